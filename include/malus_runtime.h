@@ -1,0 +1,313 @@
+/*
+ * malus_runtime.h — C ABI of libmalus_runtime_cuda.so, the sm_100a (B200)
+ * runtime behind malus's Cranelift-emitted host code.
+ *
+ * Every entry point in section 1 has the signature of the symbol the
+ * reference injects into its JIT through `RuntimeSymbols`
+ * (crates/malus-codegen-cpu/src/lib.rs:116-184); Rust `usize` is `size_t`,
+ * tensor handles are `int64_t` (an opaque pointer, 0 = none).  Section 2 is
+ * the non-JIT Rust API the CLI and tests call (crates/malus-runtime/src/
+ * lib.rs, bench.rs, metal.rs).  Section 3 holds the stdlib host functions the
+ * JIT would otherwise compile from crates/malus-stdlib/stdlib/*.ml; they keep
+ * the .ml names and signatures, so the BwdSlot table (codegen-cpu
+ * lib.rs:189-220) points at them directly.  Section 4 is new in this build:
+ * fused optimizer, data parallelism, the compiled nanoGPT step, and
+ * diagnostics.
+ *
+ * Conventions (same as the reference):
+ *  - every op returns a NEW handle with refcount 1 owned by the caller; inputs
+ *    are borrowed;
+ *  - all work is asynchronous on one CUDA stream; host reads synchronise;
+ *  - errors print "malus: ..." to stderr and abort() (panic-only model,
+ *    reference docs/adr/0006-panic-only-error-model.md).
+ */
+#ifndef MALUS_RUNTIME_H
+#define MALUS_RUNTIME_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Dtype tags: crates/malus-runtime/src/metal.rs:18-60.  Only F32 (0), I32 (5)
+ * and I64 (6) are allocatable (metal.rs:375-378). */
+enum { MALUS_F32 = 0, MALUS_I32 = 5, MALUS_I64 = 6 };
+
+/* ===================== 1. RuntimeSymbols (JIT-injected) ================== */
+
+/* metal.rs:340-347 tensor_alloc_gpu: shape[ndims] row-major; data may be NULL
+ * (uninitialised) or point to len*elem_size host bytes copied to the device. */
+int64_t tensor_alloc_gpu(int32_t dtype, const size_t* shape, size_t ndims, const float* data);
+/* metal.rs:458-484 */
+int64_t tensor_alloc_zeros_gpu(const size_t* shape, size_t ndims);
+/* metal.rs:486-492 */
+int64_t tensor_alloc_ones_gpu(const size_t* shape, size_t ndims);
+/* metal.rs:555-558: tensor_free == tensor_release. All accept 0. */
+void tensor_free(int64_t h);
+/* metal.rs:498-507 */
+void tensor_retain(int64_t h);
+/* metal.rs:509-551: decrement; aborts on over-release. */
+void tensor_release(int64_t h);
+/* metal.rs:560-588 */
+void tensor_print(int64_t h);
+/* metal.rs:651-672 (tensor_dim accepts negative i) */
+int64_t tensor_len(int64_t h);
+int64_t tensor_ndim(int64_t h);
+int64_t tensor_dim(int64_t h, int64_t i);
+/* metal.rs:1860-1931: launch a registered builtin kernel; out has the shape of
+ * handles[0]. */
+int64_t kernel_dispatch(uint64_t kernel_id, const int64_t* handles, size_t count);
+/* metal.rs:1944-2065: launch a registered explicit kernel with caller
+ * grid/tg, explicit out shape (out_ndim 0 = inherit handles[0]), uniforms. */
+int64_t kernel_dispatch_v2(uint64_t kernel_id, const int64_t* handles, size_t hc,
+                           const size_t* grid, const size_t* tg, const size_t* out_shape,
+                           size_t out_ndim, int32_t out_dtype, const void* uniforms,
+                           size_t uniforms_bytes);
+/* metal.rs:676-694: wait for all queued work; abort on a device error. */
+void gpu_barrier(void);
+/* metal.rs:820-962: (2,2), (3,3) batched and (3,2) broadcast f32 matmul. */
+int64_t tensor_matmul(int64_t a, int64_t b);
+/* metal.rs:1419-1435 zero-copy reshape; metal.rs:1407-1417 permute (0 args =
+ * 2-D transpose, 2 args = swap, rank args = full permutation). */
+int64_t tensor_reshape(int64_t h, const size_t* dims, size_t ndims);
+int64_t tensor_permute(int64_t h, const size_t* perm, size_t ndims);
+/* metal.rs:1601-1612: [T,T], 0 on/below the diagonal, -1e9 above. */
+int64_t tensor_causal_mask(int64_t t);
+/* metal.rs:1715-1737: Philox4x32-10 + Box-Muller N(0,1), per-call key. */
+int64_t tensor_randn(const size_t* shape, size_t ndims);
+/* metal.rs:1741-1749 / 1751-1759: share the randn call counter. */
+float malus_rand_uniform(void);
+int64_t malus_rand_int(int64_t n);
+/* metal.rs:1763-1769: flat f32 read (synchronises). */
+float malus_tensor_get_f32(int64_t h, int64_t idx);
+
+/* Tape: crates/malus-runtime/src/tape.rs:208-774. op_tag values follow
+ * OpTag (tape.rs:14-44); slots follow BwdSlot (tape.rs:92-125). */
+void tape_record_binop(int32_t op_tag, int64_t a, int64_t b, int64_t out);
+void tape_record_unary(int32_t op_tag, int64_t x, int64_t out);
+void tape_record_reduce(int32_t op_tag, int64_t x, int64_t out, int64_t axis, int64_t keepdim);
+void tape_record_perm(int32_t op_tag, int64_t x, int64_t out, const size_t* dims, size_t ndims);
+/* var_h / softmax_h ownership is transferred to the tape (tape.rs:289-336). */
+void tape_record_layernorm(int32_t op_tag, int64_t x, int64_t out, int64_t var_h, int64_t axis);
+void tape_record_cross_entropy(int32_t op_tag, int64_t logits, int64_t out, int64_t softmax_h,
+                               int64_t targets);
+void tape_record_embedding(int32_t op_tag, int64_t weight, int64_t indices, int64_t out);
+void tape_register_leaf(int64_t h);
+void tape_pause(void);
+void tape_resume(void);
+void tape_clear(void);
+int64_t tape_get_grad(int64_t h);
+void backward(int64_t loss);
+void tape_zero_grad(const int64_t* handles, size_t count);
+void tape_register_backward_fn(int32_t slot, size_t fnptr);
+
+/* buffer.rs:11-50: host i32 staging buffer; freeze uploads an i32 tensor. */
+int64_t malus_buffer_i32(int64_t len);
+int64_t malus_buffer_get_i32(int64_t buf, int64_t idx);
+void malus_buffer_set_i32(int64_t buf, int64_t idx, int64_t val);
+void malus_buffer_free(int64_t buf);
+int64_t malus_buffer_freeze_i32(int64_t buf);
+
+/* lib.rs:33 gradient-check recorder; bench.rs:22-38 warm-median step timer. */
+void malus_record_diff(float v);
+void bench_step_begin(void);
+void bench_step_end(void);
+
+/* strio.rs (out of scope for the training hot path: BASELINE uses synthetic
+ * token ids).  Provided so a JIT link table resolves: strings are host byte
+ * boxes, read_file reads a whole file. */
+int64_t malus_str_box(const uint8_t* bytes, size_t len);
+int64_t malus_read_file(int64_t path_box);
+int64_t malus_str_len(int64_t s);
+int64_t malus_str_char_at(int64_t s, int64_t i);
+int64_t malus_str_from_char(int64_t c);
+
+/* ===================== 2. Runtime API used by the CLI / tests ============ */
+
+/* metal.rs:309-336 runtime_init(id -> source).  This runtime has no MSL
+ * compiler: each id is bound to a native kernel by NAME (the builtin names of
+ * crates/malus-syntax/src/ast.rs:59-81 and codegen-gpu lib.rs:373-418, or a
+ * stdlib kernel name such as "__softmax_kernel").  Unknown names abort. */
+void malus_runtime_init(const uint64_t* ids, const char* const* names, size_t n);
+int64_t malus_cpu_compute_count(void);          /* lib.rs:14 (always 0 here) */
+void malus_cpu_compute_reset(void);             /* lib.rs:19 */
+float malus_gradcheck_max_diff(void);           /* lib.rs:48 */
+void malus_gradcheck_reset(void);               /* lib.rs:53 */
+void malus_rc_counts(int64_t* retains, int64_t* releases, int64_t* allocs); /* lib.rs:81 */
+void malus_rc_reset(void);                      /* lib.rs:90 */
+/* metal.rs:149-183: hits, misses, pooled bytes, peak device bytes. */
+void malus_pool_stats(int64_t* hits, int64_t* misses, int64_t* pooled_bytes, int64_t* peak_bytes);
+void malus_pool_reset(void);                    /* metal.rs:175 */
+void malus_set_mem_budget(int64_t bytes);       /* metal.rs:148 */
+void bench_enable(void);                        /* bench.rs:18 */
+/* bench.rs:51-70: warm median over steps after 3 warm-up steps, in ms; -1 if
+ * fewer than 4 steps were recorded.  n_steps receives the timed count. */
+double bench_report(int64_t* n_steps);
+void bench_reset(void);                         /* bench.rs:72 */
+/* Test helper mirroring tape.rs:733-750 tape_reset: drops leaves, grads, tape. */
+void malus_tape_reset(void);
+/* Number of live leaves / leaf grads (tape.rs:791-797 registry_lens). */
+void malus_tape_registry_lens(int64_t* leaves, int64_t* grads);
+
+/* Raw device pointer of a handle (for zero-copy interop: the data of a
+ * handle lives in HBM on the current device). */
+void* malus_tensor_data(int64_t h);
+int32_t malus_tensor_dtype(int64_t h);
+/* Copy a tensor to / from host memory (synchronous). */
+void malus_tensor_read(int64_t h, void* dst, size_t bytes);
+void malus_tensor_write(int64_t h, const void* src, size_t bytes);
+/* Wrap caller-owned device memory as a handle (not pooled; never freed). */
+int64_t malus_tensor_wrap(int32_t dtype, void* dev_ptr, const size_t* shape, size_t ndims);
+/* Reset the Philox call counter (metal.rs:1713-1715 is thread-local; the
+ * reference resets it only per thread start). */
+void malus_rng_reset(uint64_t counter);
+/* Select the CUDA device for this process (default: LOCAL_RANK or 0). */
+void malus_set_device(int32_t dev);
+/* Device kernel launches issued by this runtime since the last reset. */
+int64_t malus_launch_count(void);
+void malus_launch_count_reset(void);
+/* Current stream as a cudaStream_t (for callers that share the stream). */
+void* malus_stream(void);
+
+/* ===================== 3. Native stdlib host functions ==================== */
+/* Each replaces the same-named `fn` in crates/malus-stdlib/stdlib/*.ml. */
+
+/* broadcast_binop.ml:82-112 (NumPy right-aligned broadcasting) */
+int64_t __broadcast_add_fwd(int64_t a, int64_t b);
+int64_t __broadcast_sub_fwd(int64_t a, int64_t b);
+int64_t __broadcast_mul_fwd(int64_t a, int64_t b);
+int64_t __broadcast_div_fwd(int64_t a, int64_t b);
+/* softmax.ml:30-40 */
+int64_t __softmax_fwd(int64_t x, int64_t axis);
+/* layernorm.ml:60-72: returns a tuple box (calloc'd, refcount 1 at +0,
+ * normed handle at +8, variance handle (keepdim at axis) at +16). */
+int64_t __layernorm_fwd(int64_t x, int64_t axis);
+/* cross_entropy.ml:18-28: tuple box (loss [1] at +8, probs [N,C] at +16). */
+int64_t __cross_entropy_fwd(int64_t logits, int64_t targets);
+/* embedding.ml:18-23 */
+int64_t __embedding_fwd(int64_t weight, int64_t indices);
+/* gelu.ml:12-14 */
+int64_t __gelu_fwd(int64_t x);
+/* reduce_*.ml: axis reductions (any axis length: no 1024 cap). */
+int64_t __reduce_sum_fwd(int64_t x, int64_t axis, int64_t keepdim);
+int64_t __reduce_mean_fwd(int64_t x, int64_t axis, int64_t keepdim);
+int64_t __reduce_max_fwd(int64_t x, int64_t axis, int64_t keepdim);
+int64_t __reduce_var_fwd(int64_t x, int64_t axis, int64_t keepdim);
+/* reduce_all.ml:9-12 (any length) */
+int64_t __reduce_all_sum_fwd(int64_t x);
+/* permute.ml: rank-generic permute (perm padded to 8 entries). */
+int64_t __permute_nd_fwd(int64_t x, int64_t p0, int64_t p1, int64_t p2, int64_t p3,
+                         int64_t p4, int64_t p5, int64_t p6, int64_t p7);
+int64_t __transpose_2d_fwd(int64_t x);
+/* unary_bwd.ml: scale / fill_like / eq */
+int64_t __scale_fwd(int64_t x, float c);
+int64_t __fill_like_fwd(int64_t x, float c);
+int64_t __eq_fwd(int64_t a, int64_t b);
+/* reduce_bwd.ml:22-38 */
+int64_t __expand_axis_fwd(int64_t small, int64_t x_template, int64_t axis);
+/* elementwise_bwd.ml:8-22 */
+int64_t __sum_to_shape_bwd(int64_t dout, int64_t target);
+/* transformer_bwd.ml:6-12 */
+int64_t __rsqrt_eps_fwd(int64_t v, float eps);
+
+/* The 30 BwdSlot functions (tape.rs:92-125 / codegen-cpu lib.rs:189-220). */
+int64_t __add_bwd_a(int64_t dout, int64_t a);
+int64_t __add_bwd_b(int64_t dout, int64_t b);
+int64_t __sub_bwd_a(int64_t dout, int64_t a);
+int64_t __sub_bwd_b(int64_t dout, int64_t b);
+int64_t __mul_bwd_a(int64_t dout, int64_t a, int64_t b);
+int64_t __mul_bwd_b(int64_t dout, int64_t a, int64_t b);
+int64_t __div_bwd_a(int64_t dout, int64_t a, int64_t b);
+int64_t __div_bwd_b(int64_t dout, int64_t a, int64_t b);
+int64_t __sigmoid_bwd(int64_t s, int64_t dout);
+int64_t __relu_bwd(int64_t x, int64_t dout);
+int64_t __tanh_bwd(int64_t t, int64_t dout);
+int64_t __sqrt_bwd(int64_t s, int64_t dout);
+int64_t __abs_bwd(int64_t x, int64_t dout);
+/* reduce_bwd.ml:73-76: reads dout[0] ON THE DEVICE (no host sync). */
+int64_t __sum_bwd(int64_t x, int64_t dout);
+int64_t __reduce_sum_axis_bwd(int64_t x, int64_t dout, int64_t axis);
+int64_t __reduce_mean_axis_bwd(int64_t x, int64_t dout, int64_t axis);
+int64_t __reduce_max_axis_bwd(int64_t x, int64_t y, int64_t dout, int64_t axis);
+int64_t __reduce_var_axis_bwd(int64_t x, int64_t dout, int64_t axis);
+/* transformer_bwd.ml:15-20, fused into one kernel */
+int64_t __softmax_bwd(int64_t s, int64_t dout, int64_t axis);
+/* transformer_bwd.ml:24-36 with the host-side (tape.rs:1162-1186) per-row
+ * variance semantics; fused into one kernel */
+int64_t __layernorm_bwd(int64_t y, int64_t var_h, int64_t dout, int64_t axis);
+int64_t __gelu_bwd(int64_t x, int64_t dout);
+/* transformer_bwd.ml:66-75; dout[0] read on the device */
+int64_t __cross_entropy_bwd(int64_t probs, int64_t targets, int64_t dout);
+/* transformer_bwd.ml:83-98; deterministic sort-then-segmented-sum */
+int64_t __embedding_bwd(int64_t weight, int64_t indices, int64_t dout);
+/* matmul_bwd.ml:15-29; transposed-operand GEMMs (no materialised transpose) */
+int64_t __matmul_bwd_a(int64_t a, int64_t b, int64_t dout);
+int64_t __matmul_bwd_b(int64_t a, int64_t b, int64_t dout);
+
+/* ===================== 4. New in this build ============================== */
+
+/* Fused multi-tensor AdamW, the exact f32 operation order of
+ * examples/nanogpt.ml:80-91 (L2-coupled weight decay):
+ *   g = grad*grad_scale + wd*p; m = b1*m + (1-b1)*g; v = b2*v + ((1-b2)*g)*g;
+ *   p = p - (lr*(m/bc1)) / (sqrt(v/bc2) + eps),  bc = 1 - beta**step (f32 powf).
+ * Updates params, ms, vs IN PLACE (the reference re-registers a new leaf per
+ * step; observable values are identical).  grads[i] == 0 means "no grad
+ * accumulated" (tape_get_grad returns zeros). grad_scale is 1/world for DP. */
+void malus_adamw_multi(const int64_t* params, const int64_t* grads, const int64_t* ms,
+                       const int64_t* vs, size_t n, float lr, float beta1, float beta2,
+                       float eps, float wd, int64_t step, float grad_scale);
+
+/* Data parallelism (one process per GPU, NCCL over NVLink).  nccl_id is the
+ * 128-byte ncclUniqueId produced by malus_dp_unique_id on rank 0 and shared
+ * out of band.  Returns 0 on success, a negative error otherwise. */
+int32_t malus_dp_unique_id(uint8_t* out128);
+int32_t malus_dp_init(int32_t rank, int32_t world, const uint8_t* nccl_id, int32_t timeout_ms);
+/* In-place sum-allreduce of a contiguous f32 device buffer on the DP stream. */
+int32_t malus_dp_allreduce_f32(void* dev_ptr, size_t count);
+int32_t malus_dp_finish(void);   /* wait for outstanding collectives */
+int32_t malus_dp_destroy(void);
+int32_t malus_dp_world(void);
+
+/* The compiled nanoGPT training step (replaces the per-step call sequence of
+ * examples/nanogpt.ml:167-191 / nanogpt_modular.ml with one entry point). */
+typedef struct malus_gpt_config {
+  int32_t vocab, n_layer, n_head, n_embd, block_size, batch;
+  int32_t tied;          /* 1: LM head is wte^T (GPT-2 weight tying) */
+  float lr, beta1, beta2, eps, wd, init_std;
+  int32_t mode;          /* 0: tape (reference call sequence), 1: fused B200 step */
+  int32_t use_graph;     /* 1: capture the fused step in a CUDA graph */
+  uint64_t seed;         /* Philox call counter start for the weight init */
+} malus_gpt_config;
+int64_t malus_gpt_create(const malus_gpt_config* cfg);
+void malus_gpt_destroy(int64_t model);
+/* One training step on host token ids x/y (int32, batch*block_size each).
+ * Copies the ids to the device, runs forward, backward, (DP allreduce) and
+ * AdamW, and returns the loss (synchronises). */
+float malus_gpt_step(int64_t model, const int32_t* x, const int32_t* y);
+/* Same step with ids already on the device; the loss stays on the device
+ * (read it with malus_gpt_last_loss). */
+void malus_gpt_step_device(int64_t model, const int32_t* x_dev, const int32_t* y_dev);
+float malus_gpt_last_loss(int64_t model);
+/* Number of parameter tensors and their handles (layout order of
+ * nanogpt_modular.ml: per block [ln1,wq,wk,wv,wo,ln2,w1,w2], then
+ * [wte,wpe,ln_f,lm_head]). */
+int32_t malus_gpt_num_params(int64_t model);
+int64_t malus_gpt_param(int64_t model, int32_t i);
+int64_t malus_gpt_num_elements(int64_t model);
+
+/* Device diagnostics: last asynchronous error word written by a kernel whose
+ * bounded wait ran out (0 = none); cleared by reading. */
+int32_t malus_device_error(void);
+
+/* Live per-kernel-class timing with CUDA events on the runtime stream (for
+ * roofline figures).  Classes: 0 tcgen05 GEMM, 1 GEMM operand split,
+ * 2 SIMT GEMM.  Enabling resets the records. */
+void malus_prof_enable(int32_t on);
+void malus_prof_report(int32_t cls, int64_t* count, double* ms, double* flops, double* bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MALUS_RUNTIME_H */

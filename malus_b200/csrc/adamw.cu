@@ -1,0 +1,104 @@
+// Fused multi-tensor AdamW: one launch updates every parameter.
+//
+// The reference composes the update from ~14 elementwise launches per
+// parameter (examples/nanogpt.ml:80-91):
+//   g  = grad + wd * p                      (L2-coupled weight decay)
+//   m  = beta1 * m + (1 - beta1) * g
+//   v  = beta2 * v + (1 - beta2) * g * g    (left to right: ((1-b2)*g)*g)
+//   p' = p - lr * (m / bc1) / (sqrt(v / bc2) + eps)
+// with bc = 1 - beta**t computed on the host in f32.  This kernel performs the
+// same f32 operations in the same order with explicit round-to-nearest
+// intrinsics (no FMA contraction), so its result is bit-identical to the
+// composed sequence.  The data-parallel 1/world average is one more multiply
+// applied to the raw gradient first (exact when world is a power of two).
+#include "common.cuh"
+
+namespace malus {
+namespace {
+
+struct SegTable {
+  AdamSeg seg[64];
+  int64_t start[65];  // prefix of float4-chunk counts
+};
+
+__device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, float lr, float b1,
+                                         float b2, float eps, float wd, float c1, float c2,
+                                         float bc1, float bc2, float gs) {
+  if (gs != 1.0f) g = __fmul_rn(g, gs);
+  float gg = __fadd_rn(g, __fmul_rn(wd, p));
+  m = __fadd_rn(__fmul_rn(b1, m), __fmul_rn(c1, gg));
+  v = __fadd_rn(__fmul_rn(b2, v), __fmul_rn(__fmul_rn(c2, gg), gg));
+  float mh = __fdiv_rn(m, bc1);
+  float vh = __fdiv_rn(v, bc2);
+  float upd = __fdiv_rn(__fmul_rn(lr, mh), __fadd_rn(__fsqrt_rn(vh), eps));
+  p = __fsub_rn(p, upd);
+}
+
+__global__ void k_adamw(SegTable t, int nseg, int64_t total4, float lr, float b1, float b2,
+                        float eps, float wd, float c1, float c2, float bc1, float bc2, float gs) {
+  int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  int64_t step = (int64_t)gridDim.x * blockDim.x;
+  int s = 0;
+  for (int64_t q = tid; q < total4; q += step) {
+    while (s + 1 < nseg && q >= t.start[s + 1]) ++s;
+    while (s > 0 && q < t.start[s]) --s;
+    const AdamSeg& sg = t.seg[s];
+    int64_t e0 = (q - t.start[s]) * 4;
+    for (int u = 0; u < 4; ++u) {
+      int64_t e = e0 + u;
+      if (e >= sg.n) break;
+      float p = sg.p[e], m = sg.m[e], v = sg.v[e];
+      float g = sg.g ? sg.g[e] : 0.0f;
+      adam_one(p, g, m, v, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      sg.p[e] = p;
+      sg.m[e] = m;
+      sg.v[e] = v;
+    }
+  }
+}
+
+}  // namespace
+
+void adamw_multi(const AdamSeg* segs, int nseg, float lr, float b1, float b2, float eps, float wd,
+                 float bc1, float bc2, float grad_scale) {
+  float c1 = 1.0f - b1, c2 = 1.0f - b2;  // the host-side (1.0 - beta) literals
+  for (int base = 0; base < nseg; base += 64) {
+    int n = std::min(64, nseg - base);
+    SegTable t;
+    int64_t acc = 0;
+    for (int i = 0; i < n; ++i) {
+      t.seg[i] = segs[base + i];
+      t.start[i] = acc;
+      acc += (segs[base + i].n + 3) / 4;
+    }
+    t.start[n] = acc;
+    if (acc == 0) continue;
+    k_adamw<<<grid_for((size_t)acc, 256), 256, 0, stream()>>>(t, n, acc, lr, b1, b2, eps, wd, c1,
+                                                              c2, bc1, bc2, grad_scale);
+    count_launch();
+    after_launch("k_adamw");
+  }
+}
+
+}  // namespace malus
+
+extern "C" void malus_adamw_multi(const int64_t* params, const int64_t* grads, const int64_t* ms,
+                                  const int64_t* vs, size_t n, float lr, float beta1, float beta2,
+                                  float eps, float wd, int64_t step, float grad_scale) {
+  using namespace malus;
+  std::vector<AdamSeg> segs;
+  segs.reserve(n);
+  for (size_t i = 0; i < n; ++i) {
+    auto* p = tb(params[i]);
+    if (tb(ms[i])->len != p->len || tb(vs[i])->len != p->len)
+      panic("adamw: moment %zu has %zu/%zu elements, parameter has %zu", i, tb(ms[i])->len,
+            tb(vs[i])->len, p->len);
+    if (grads[i] && tb(grads[i])->len != p->len)
+      panic("adamw: grad %zu has %zu elements, parameter has %zu", i, tb(grads[i])->len, p->len);
+    segs.push_back(AdamSeg{fptr(params[i]), grads[i] ? fptr(grads[i]) : nullptr, fptr(ms[i]),
+                           fptr(vs[i]), (int64_t)p->len});
+  }
+  float bc1 = 1.0f - powf(beta1, (float)step);
+  float bc2 = 1.0f - powf(beta2, (float)step);
+  adamw_multi(segs.data(), (int)segs.size(), lr, beta1, beta2, eps, wd, bc1, bc2, grad_scale);
+}

@@ -1,0 +1,172 @@
+// Internal definitions shared by the runtime's translation units.
+//
+// A tensor handle is a pointer to TensorBuffer (the handle layout of the
+// reference is opaque too: crates/malus-runtime/src/metal.rs:280-296).  Data
+// always lives in HBM, row-major and contiguous; reshape aliases share one
+// Storage (metal.rs:1388-1403).  All device work is ordered on one CUDA
+// stream, which is what makes the pool's immediate reuse of a freed buffer
+// safe: a later kernel on the same stream cannot start before the kernels
+// that last touched the buffer.
+#pragma once
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <initializer_list>
+#include <vector>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+#include "../../include/malus_runtime.h"
+
+namespace malus {
+
+[[noreturn]] void panic(const char* fmt, ...);
+
+#define MALUS_CUDA(call)                                                      \
+  do {                                                                        \
+    cudaError_t e_ = (call);                                                  \
+    if (e_ != cudaSuccess)                                                    \
+      ::malus::panic("CUDA error %s at %s:%d: %s", cudaGetErrorName(e_),      \
+                     __FILE__, __LINE__, cudaGetErrorString(e_));             \
+  } while (0)
+
+constexpr int kMaxRank = 8;
+
+struct Storage {
+  void* ptr;
+  size_t bytes;      // allocated (pool bucket) size
+  int aliases;       // number of TensorBuffers sharing this storage
+  bool owned;        // false for malus_tensor_wrap'd memory
+};
+
+struct TensorBuffer {
+  Storage* st;
+  int32_t dtype;
+  int32_t ndim;
+  size_t len;
+  size_t shape[kMaxRank];
+  std::atomic<int64_t> rc;
+};
+
+inline TensorBuffer* tb(int64_t h) {
+  if (h == 0) panic("null tensor handle");
+  return reinterpret_cast<TensorBuffer*>(h);
+}
+inline float* fptr(int64_t h) { return static_cast<float*>(tb(h)->st->ptr); }
+inline void* vptr(int64_t h) { return tb(h)->st->ptr; }
+size_t dtype_size(int32_t dtype);
+
+// ---- runtime core (runtime.cu) ----
+cudaStream_t stream();
+int64_t alloc(int32_t dtype, const size_t* shape, int ndim);       // uninitialised
+int64_t alloc_like(int64_t h);                                     // same shape, f32
+int64_t alloc_f32(std::initializer_list<size_t> shape);
+void* scratch_alloc(size_t bytes);                                 // pooled raw device memory
+void scratch_free(void* p);
+void count_launch(int n = 1);
+void after_launch(const char* what);
+bool sync_dispatch();
+int32_t* device_error_word();
+bool prof_on();
+int prof_begin(int cls, double flops, double bytes);
+void prof_end(int id);
+
+// Shape helpers
+struct Shape {
+  int ndim = 0;
+  size_t d[kMaxRank] = {0};
+  size_t numel() const { size_t n = 1; for (int i = 0; i < ndim; ++i) n *= d[i]; return n; }
+};
+inline Shape shape_of(int64_t h) {
+  Shape s; auto* t = tb(h); s.ndim = t->ndim;
+  for (int i = 0; i < t->ndim; ++i) s.d[i] = t->shape[i];
+  return s;
+}
+inline int64_t alloc_shape(const Shape& s, int32_t dtype = MALUS_F32) {
+  return alloc(dtype, s.d, s.ndim);
+}
+bool same_shape(int64_t a, int64_t b);
+int normalize_axis(int64_t axis, int ndim);
+// outer / axis / inner decomposition (softmax.ml:1-7 convention)
+void split_axis(const Shape& s, int axis, size_t* outer, size_t* axis_sz, size_t* inner);
+
+// ---- launch geometry ----
+constexpr int kNumSMs = 148;
+inline unsigned grid_for(size_t work_items, int threads, int max_blocks_per_sm = 8) {
+  size_t b = (work_items + threads - 1) / threads;
+  size_t cap = (size_t)kNumSMs * max_blocks_per_sm;
+  if (b > cap) b = cap;
+  if (b == 0) b = 1;
+  return (unsigned)b;
+}
+
+// ---- elementwise (elementwise.cu) ----
+enum BinOp : int { kAdd = 0, kSub = 1, kMul = 2, kDiv = 3 };
+int64_t binary_broadcast(int op, int64_t a, int64_t b);          // NumPy broadcast result
+void binary_same(int op, const float* a, const float* b, float* out, size_t n);
+enum ScalarOp : int { kSAdd, kSSub, kSRSub, kSMul, kSDiv, kSRDiv, kSFill };
+void scalar_op_dev(int op, const float* a, const float* s_dev, float* out, size_t n);
+void scalar_op_imm(int op, const float* a, float s, float* out, size_t n);
+enum UnaryOp : int { kRelu, kSigmoid, kTanh, kExp, kLog, kSqrt, kAbs, kGelu, kRsqrtEps, kNeg };
+void unary_op(int op, const float* a, float* out, size_t n, float param = 0.f);
+enum UnaryBwdOp : int { kSigmoidBwd, kReluBwd, kTanhBwd, kSqrtBwd, kAbsBwd, kGeluBwd, kEq };
+void unary_bwd(int op, const float* x, const float* dout, float* out, size_t n);
+void fill_from_dev_scalar(float* out, const float* s_dev, size_t n);
+void expand_axis(const float* small, float* out, size_t outer, size_t axis_sz, size_t inner);
+// the XOR user kernel `sigmoid_backward` (examples/xor.ml:1-2)
+void sigmoid_backward_user(const float* g, const float* s, float* out, size_t n);
+
+// ---- reductions (reduce.cu) ----
+enum RedOp : int { kRSum = 0, kRMean = 1, kRMax = 2, kRVar = 3 };
+void reduce_axis(int op, const float* x, float* out, size_t outer, size_t axis_sz, size_t inner);
+
+// ---- row kernels (rows.cu) ----
+void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner);
+void softmax_bwd(const float* s, const float* dout, float* dx, size_t outer, size_t axis_sz,
+                 size_t inner);
+void layernorm_fwd(const float* x, float* y, float* var, size_t outer, size_t axis_sz,
+                   size_t inner, float eps);
+void layernorm_bwd(const float* y, const float* var, const float* dout, float* dx, size_t outer,
+                   size_t axis_sz, size_t inner, float eps);
+// probs [N,V] written; loss[0] = mean nll
+void xent_fwd(const float* logits, const void* targets, int tgt_dtype, float* probs, float* loss,
+              size_t n, size_t v);
+void xent_bwd(const float* probs, const void* targets, int tgt_dtype, const float* dout_dev,
+              float* dx, size_t n, size_t v);
+void xent_nll_gather(const float* probs, const void* targets, int tgt_dtype, float* out, size_t n,
+                     size_t v);
+void embedding_fwd(const float* w, const void* idx, int idx_dtype, float* out, size_t n,
+                   size_t vocab, size_t dim);
+void embedding_bwd(const float* dout, const void* idx, int idx_dtype, float* dw, size_t n,
+                   size_t vocab, size_t dim);
+void permute_nd(const float* x, float* out, const Shape& in_shape, const int* perm);
+
+// ---- GEMM (gemm.cu) ----
+// C[b] (MxN) = alpha * op(A[b]) * op(B[b]) + beta * C[b], f32 semantics via
+// 3xTF32 on tcgen05 (large shapes) or exact-f32 SIMT (small shapes).
+// A is MxK: a_trans=false -> A stored row-major [M][lda] ; true -> stored [K][lda] (A^T)
+// B is KxN: b_trans=false -> B stored row-major [K][ldb] ; true -> stored [N][ldb] (B^T)
+struct GemmArgs {
+  int M, N, K, batch;
+  const float* A; int64_t lda; int64_t strideA; bool a_trans;
+  const float* B; int64_t ldb; int64_t strideB; bool b_trans;
+  float* C; int64_t ldc; int64_t strideC;
+  float alpha = 1.f, beta = 0.f;
+};
+void gemm(const GemmArgs& g);
+void gemm_simt(const GemmArgs& g);
+int gemm_backend_for(const GemmArgs& g);   // 0 = SIMT, 1 = tcgen05
+void gemm_force_backend(int b);            // -1 = auto (tests)
+
+// ---- optimizer (adamw.cu) ----
+struct AdamSeg { float* p; const float* g; float* m; float* v; int64_t n; };
+void adamw_multi(const AdamSeg* segs, int nseg, float lr, float b1, float b2, float eps, float wd,
+                 float bc1, float bc2, float grad_scale);
+
+// ---- tape (tape.cpp) ----
+void tape_on_release(int64_t h);
+
+}  // namespace malus

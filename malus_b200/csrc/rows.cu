@@ -1,0 +1,957 @@
+// Row kernels: softmax, layernorm, cross-entropy, embedding and permute.
+//
+// Reference semantics:
+//   softmax      stdlib/softmax.ml:9-28        (max, exp(x-max), sum, divide)
+//   softmax VJP  stdlib/backward/transformer_bwd.ml:15-20  s*(dout - sum(dout*s))
+//   layernorm    metal.rs:1487-1533 (host twin) / layernorm.ml:8-34 (no affine,
+//                population variance, eps 1e-5); the saved variance is per
+//                group with keepdim at the axis
+//   layernorm VJP tape.rs:1162-1186 (host twin): (1/sigma)(dy - mean(dy) - y*mean(dy*y))
+//   cross-entropy cross_entropy.ml:13-28 / metal.rs:1555-1598: probs = softmax,
+//                nll = -log(probs[t]), loss = mean(nll)
+//   CE VJP       transformer_bwd.ml:57-75: (p - onehot) * dout[0] / N
+//   embedding    embedding.ml:11-23 gather; VJP transformer_bwd.ml:83-98
+//   permute      permute.ml (materialising N-D permute)
+//
+// The reference launches one thread per element (or one threadgroup of
+// `axis` threads per row, with O(axis^2) work).  Here rows are owned by a warp
+// (short rows, held in registers) or a block (long rows), reductions use warp
+// shuffles, and every pass is a coalesced stream over HBM.
+#include "common.cuh"
+
+namespace malus {
+namespace {
+
+__device__ __forceinline__ float wsum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float wmax(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// block-wide reduction helpers (blockDim multiple of 32, <= 1024)
+__device__ float bsum(float v, float* sh) {
+  v = wsum(v);
+  int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  float r = (l < (int)(blockDim.x >> 5)) ? sh[l] : 0.0f;
+  r = wsum(r);
+  return r;
+}
+__device__ float bmax(float v, float* sh) {
+  v = wmax(v);
+  int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  float r = (l < (int)(blockDim.x >> 5)) ? sh[l] : -INFINITY;
+  r = wmax(r);
+  return r;
+}
+
+// ------------------------------------------------------------------ softmax
+// One warp per contiguous row; the row is kept in registers (<= 32*PER).
+template <int PER>
+__global__ void k_softmax_warp(const float* __restrict__ x, float* __restrict__ y, size_t rows,
+                               int len) {
+  int lane = threadIdx.x & 31;
+  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (size_t r = warp; r < rows; r += nw) {
+    const float* xr = x + r * (size_t)len;
+    float v[PER];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      v[k] = i < len ? xr[i] : -INFINITY;
+      m = fmaxf(m, v[k]);
+    }
+    m = wmax(m);
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      v[k] = i < len ? expf(v[k] - m) : 0.0f;
+      s += v[k];
+    }
+    s = wsum(s);
+    float* yr = y + r * (size_t)len;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      if (i < len) yr[i] = v[k] / s;
+    }
+  }
+}
+
+// Long rows: one block per row, three passes (max, sum, write).
+__global__ void k_softmax_block(const float* __restrict__ x, float* __restrict__ y, size_t rows,
+                                size_t len) {
+  __shared__ float sh[32];
+  for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* xr = x + r * len;
+    float m = -INFINITY;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) m = fmaxf(m, xr[i]);
+    m = bmax(m, sh);
+    float s = 0.0f;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) s += expf(xr[i] - m);
+    s = bsum(s, sh);
+    float* yr = y + r * len;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) yr[i] = expf(xr[i] - m) / s;
+    __syncthreads();
+  }
+}
+
+// Strided softmax (axis not innermost): thread per (outer, inner) group.
+__global__ void k_softmax_strided(const float* __restrict__ x, float* __restrict__ y, size_t outer,
+                                  size_t axis_sz, size_t inner) {
+  size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (g >= outer * inner) return;
+  size_t o = g / inner, i = g % inner;
+  const float* b = x + o * axis_sz * inner + i;
+  float* yb = y + o * axis_sz * inner + i;
+  float m = -INFINITY;
+  for (size_t a = 0; a < axis_sz; ++a) m = fmaxf(m, b[a * inner]);
+  float s = 0.0f;
+  for (size_t a = 0; a < axis_sz; ++a) s += expf(b[a * inner] - m);
+  for (size_t a = 0; a < axis_sz; ++a) yb[a * inner] = expf(b[a * inner] - m) / s;
+}
+
+template <int PER>
+__global__ void k_softmax_bwd_warp(const float* __restrict__ s, const float* __restrict__ g,
+                                   float* __restrict__ dx, size_t rows, int len) {
+  int lane = threadIdx.x & 31;
+  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (size_t r = warp; r < rows; r += nw) {
+    const float* sr = s + r * (size_t)len;
+    const float* gr = g + r * (size_t)len;
+    float sv[PER], gv[PER];
+    float dot = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      sv[k] = i < len ? sr[i] : 0.0f;
+      gv[k] = i < len ? gr[i] : 0.0f;
+      dot += gv[k] * sv[k];
+    }
+    dot = wsum(dot);
+    float* dr = dx + r * (size_t)len;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      if (i < len) dr[i] = sv[k] * (gv[k] - dot);
+    }
+  }
+}
+
+__global__ void k_softmax_bwd_block(const float* __restrict__ s, const float* __restrict__ g,
+                                    float* __restrict__ dx, size_t rows, size_t len) {
+  __shared__ float sh[32];
+  for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* sr = s + r * len;
+    const float* gr = g + r * len;
+    float dot = 0.0f;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) dot += gr[i] * sr[i];
+    dot = bsum(dot, sh);
+    float* dr = dx + r * len;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) dr[i] = sr[i] * (gr[i] - dot);
+    __syncthreads();
+  }
+}
+
+__global__ void k_softmax_bwd_strided(const float* __restrict__ s, const float* __restrict__ g,
+                                      float* __restrict__ dx, size_t outer, size_t axis_sz,
+                                      size_t inner) {
+  size_t gi = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (gi >= outer * inner) return;
+  size_t o = gi / inner, i = gi % inner;
+  size_t base = o * axis_sz * inner + i;
+  float dot = 0.0f;
+  for (size_t a = 0; a < axis_sz; ++a) dot += g[base + a * inner] * s[base + a * inner];
+  for (size_t a = 0; a < axis_sz; ++a) {
+    size_t k = base + a * inner;
+    dx[k] = s[k] * (g[k] - dot);
+  }
+}
+
+// ---------------------------------------------------------------- layernorm
+template <int PER>
+__global__ void k_layernorm_warp(const float* __restrict__ x, float* __restrict__ y,
+                                 float* __restrict__ var_out, size_t rows, int len, float eps) {
+  int lane = threadIdx.x & 31;
+  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (size_t r = warp; r < rows; r += nw) {
+    const float* xr = x + r * (size_t)len;
+    float v[PER];
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      v[k] = i < len ? xr[i] : 0.0f;
+      s += v[k];
+    }
+    float mean = wsum(s) / (float)len;
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      float d = i < len ? v[k] - mean : 0.0f;
+      q += d * d;
+    }
+    float var = wsum(q) / (float)len;
+    float sigma = sqrtf(var + eps);
+    float* yr = y + r * (size_t)len;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      if (i < len) yr[i] = (v[k] - mean) / sigma;
+    }
+    if (lane == 0 && var_out) var_out[r] = var;
+  }
+}
+
+__global__ void k_layernorm_block(const float* __restrict__ x, float* __restrict__ y,
+                                  float* __restrict__ var_out, size_t rows, size_t len, float eps) {
+  __shared__ float sh[32];
+  for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* xr = x + r * len;
+    float s = 0.0f;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) s += xr[i];
+    float mean = bsum(s, sh) / (float)len;
+    float q = 0.0f;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
+      float d = xr[i] - mean;
+      q += d * d;
+    }
+    float var = bsum(q, sh) / (float)len;
+    float sigma = sqrtf(var + eps);
+    float* yr = y + r * len;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) yr[i] = (xr[i] - mean) / sigma;
+    if (threadIdx.x == 0 && var_out) var_out[r] = var;
+    __syncthreads();
+  }
+}
+
+__global__ void k_layernorm_strided(const float* __restrict__ x, float* __restrict__ y,
+                                    float* __restrict__ var_out, size_t outer, size_t axis_sz,
+                                    size_t inner, float eps) {
+  size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (g >= outer * inner) return;
+  size_t o = g / inner, i = g % inner;
+  size_t base = o * axis_sz * inner + i;
+  float s = 0.0f;
+  for (size_t a = 0; a < axis_sz; ++a) s += x[base + a * inner];
+  float mean = s / (float)axis_sz;
+  float q = 0.0f;
+  for (size_t a = 0; a < axis_sz; ++a) {
+    float d = x[base + a * inner] - mean;
+    q += d * d;
+  }
+  float var = q / (float)axis_sz;
+  float sigma = sqrtf(var + eps);
+  for (size_t a = 0; a < axis_sz; ++a) y[base + a * inner] = (x[base + a * inner] - mean) / sigma;
+  if (var_out) var_out[g] = var;
+}
+
+template <int PER>
+__global__ void k_layernorm_bwd_warp(const float* __restrict__ y, const float* __restrict__ var,
+                                     const float* __restrict__ g, float* __restrict__ dx,
+                                     size_t rows, int len, float eps) {
+  int lane = threadIdx.x & 31;
+  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (size_t r = warp; r < rows; r += nw) {
+    const float* yr = y + r * (size_t)len;
+    const float* gr = g + r * (size_t)len;
+    float yv[PER], gv[PER];
+    float sg = 0.0f, sgy = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      yv[k] = i < len ? yr[i] : 0.0f;
+      gv[k] = i < len ? gr[i] : 0.0f;
+      sg += gv[k];
+      sgy += gv[k] * yv[k];
+    }
+    float mg = wsum(sg) / (float)len;
+    float mgy = wsum(sgy) / (float)len;
+    float inv = 1.0f / sqrtf(var[r] + eps);
+    float* dr = dx + r * (size_t)len;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      if (i < len) dr[i] = ((gv[k] - mg) - yv[k] * mgy) * inv;
+    }
+  }
+}
+
+__global__ void k_layernorm_bwd_block(const float* __restrict__ y, const float* __restrict__ var,
+                                      const float* __restrict__ g, float* __restrict__ dx,
+                                      size_t rows, size_t len, float eps) {
+  __shared__ float sh[32];
+  for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* yr = y + r * len;
+    const float* gr = g + r * len;
+    float sg = 0.0f, sgy = 0.0f;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
+      sg += gr[i];
+      sgy += gr[i] * yr[i];
+    }
+    float mg = bsum(sg, sh) / (float)len;
+    float mgy = bsum(sgy, sh) / (float)len;
+    float inv = 1.0f / sqrtf(var[r] + eps);
+    float* dr = dx + r * len;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x)
+      dr[i] = ((gr[i] - mg) - yr[i] * mgy) * inv;
+    __syncthreads();
+  }
+}
+
+__global__ void k_layernorm_bwd_strided(const float* __restrict__ y, const float* __restrict__ var,
+                                        const float* __restrict__ g, float* __restrict__ dx,
+                                        size_t outer, size_t axis_sz, size_t inner, float eps) {
+  size_t gi = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (gi >= outer * inner) return;
+  size_t o = gi / inner, i = gi % inner;
+  size_t base = o * axis_sz * inner + i;
+  float sg = 0.0f, sgy = 0.0f;
+  for (size_t a = 0; a < axis_sz; ++a) {
+    size_t k = base + a * inner;
+    sg += g[k];
+    sgy += g[k] * y[k];
+  }
+  float mg = sg / (float)axis_sz, mgy = sgy / (float)axis_sz;
+  float inv = 1.0f / sqrtf(var[gi] + eps);
+  for (size_t a = 0; a < axis_sz; ++a) {
+    size_t k = base + a * inner;
+    dx[k] = ((g[k] - mg) - y[k] * mgy) * inv;
+  }
+}
+
+// ------------------------------------------------------------ cross-entropy
+__device__ __forceinline__ int64_t load_index(const void* p, int dtype, size_t i) {
+  return dtype == MALUS_I64 ? ((const int64_t*)p)[i] : (int64_t)((const int32_t*)p)[i];
+}
+
+template <int PER>
+__global__ void k_xent_fwd_warp(const float* __restrict__ logits, const void* __restrict__ tgt,
+                                int tdt, float* __restrict__ probs, float* __restrict__ nll,
+                                size_t rows, int V, int32_t* err) {
+  int lane = threadIdx.x & 31;
+  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  for (size_t r = warp; r < rows; r += nw) {
+    const float* xr = logits + r * (size_t)V;
+    float v[PER];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      v[k] = i < V ? xr[i] : -INFINITY;
+      m = fmaxf(m, v[k]);
+    }
+    m = wmax(m);
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      v[k] = i < V ? expf(v[k] - m) : 0.0f;
+      s += v[k];
+    }
+    s = wsum(s);
+    int64_t t = load_index(tgt, tdt, r);
+    bool bad = t < 0 || t >= V;
+    float pt = 0.0f;
+    float* pr = probs + r * (size_t)V;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      if (i < V) {
+        float p = v[k] / s;
+        pr[i] = p;
+        if (i == t) pt = p;
+      }
+    }
+    pt = wsum(pt);
+    if (lane == 0) {
+      if (bad) { atomicExch(err, 3); nll[r] = 0.0f; }
+      else nll[r] = -logf(pt);
+    }
+  }
+}
+
+__global__ void k_xent_fwd_block(const float* __restrict__ logits, const void* __restrict__ tgt,
+                                 int tdt, float* __restrict__ probs, float* __restrict__ nll,
+                                 size_t rows, size_t V, int32_t* err) {
+  __shared__ float sh[32];
+  __shared__ float pt_sh;
+  for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* xr = logits + r * V;
+    float m = -INFINITY;
+    for (size_t i = threadIdx.x; i < V; i += blockDim.x) m = fmaxf(m, xr[i]);
+    m = bmax(m, sh);
+    float s = 0.0f;
+    for (size_t i = threadIdx.x; i < V; i += blockDim.x) s += expf(xr[i] - m);
+    s = bsum(s, sh);
+    int64_t t = load_index(tgt, tdt, r);
+    bool bad = t < 0 || (size_t)t >= V;
+    float* pr = probs + r * V;
+    for (size_t i = threadIdx.x; i < V; i += blockDim.x) {
+      float p = expf(xr[i] - m) / s;
+      pr[i] = p;
+      if ((int64_t)i == t) pt_sh = p;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      if (bad) { atomicExch(err, 3); nll[r] = 0.0f; }
+      else nll[r] = -logf(pt_sh);
+    }
+    __syncthreads();
+  }
+}
+
+// loss[0] = (sum_i nll[i]) / n  — one block, fixed order, deterministic
+__global__ void k_mean_1block(const float* __restrict__ v, float* __restrict__ out, size_t n) {
+  __shared__ float sh[32];
+  float s = 0.0f;
+  for (size_t i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
+  s = bsum(s, sh);
+  if (threadIdx.x == 0) out[0] = s / (float)n;
+}
+
+// cross_entropy.ml:13-16: out[i] = -log(probs[i*V + t_i])
+__global__ void k_xent_nll_gather(const float* __restrict__ probs, const void* __restrict__ tgt,
+                                  int tdt, float* __restrict__ out, size_t n, size_t V,
+                                  int32_t* err) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int64_t t = load_index(tgt, tdt, i);
+  if (t < 0 || (size_t)t >= V) { atomicExch(err, 3); out[i] = 0.0f; return; }
+  out[i] = -logf(probs[i * V + (size_t)t]);
+}
+
+__global__ void k_xent_bwd(const float* __restrict__ probs, const void* __restrict__ tgt, int tdt,
+                           const float* __restrict__ dout, float* __restrict__ dx, size_t rows,
+                           size_t V) {
+  float scale = dout[0] / (float)rows;
+  size_t n = rows * V;
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t f = tid; f < n; f += stride) {
+    size_t i = f / V, j = f - i * V;
+    float g = probs[f];
+    if ((int64_t)j == load_index(tgt, tdt, i)) g = g - 1.0f;
+    dx[f] = g * scale;
+  }
+}
+
+// ---------------------------------------------------------------- embedding
+// out[t, :] = w[idx[t], :]  — one warp per row, 16-byte copies when aligned.
+__global__ void k_embedding_fwd(const float* __restrict__ w, const void* __restrict__ idx, int idt,
+                                float* __restrict__ out, size_t n, size_t V, size_t D,
+                                int32_t* err) {
+  int lane = threadIdx.x & 31;
+  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  bool vec = (D % 4 == 0) && (((uintptr_t)w & 15) == 0) && (((uintptr_t)out & 15) == 0);
+  for (size_t t = warp; t < n; t += nw) {
+    int64_t row = load_index(idx, idt, t);
+    float* o = out + t * D;
+    if (row < 0 || (size_t)row >= V) {
+      if (lane == 0) atomicExch(err, 4);
+      for (size_t c = lane; c < D; c += 32) o[c] = 0.0f;
+      continue;
+    }
+    const float* src = w + (size_t)row * D;
+    if (vec) {
+      const float4* s4 = reinterpret_cast<const float4*>(src);
+      float4* o4 = reinterpret_cast<float4*>(o);
+      for (size_t c = lane; c < D / 4; c += 32) o4[c] = s4[c];
+    } else {
+      for (size_t c = lane; c < D; c += 32) o[c] = src[c];
+    }
+  }
+}
+
+// Embedding VJP, deterministic sort-then-segmented-sum.
+// K1: each block sorts a chunk of CH token keys (id<<32 | t) in shared memory
+//     (bitonic), stores them, and writes the run length of each id present in
+//     the chunk to counts[id * nch + chunk].
+constexpr int kEmbChunk = 1024;
+
+__global__ void k_emb_chunk_sort(const void* __restrict__ idx, int idt, size_t n, size_t V,
+                                 int nch, unsigned long long* __restrict__ keys,
+                                 int* __restrict__ counts, int32_t* err) {
+  __shared__ unsigned long long sk[kEmbChunk];
+  int c = blockIdx.x;
+  size_t base = (size_t)c * kEmbChunk;
+  for (int j = threadIdx.x; j < kEmbChunk; j += blockDim.x) {
+    size_t t = base + j;
+    unsigned long long key = ~0ull;
+    if (t < n) {
+      int64_t id = load_index(idx, idt, t);
+      if (id < 0 || (size_t)id >= V) atomicExch(err, 4);
+      else key = ((unsigned long long)id << 32) | (unsigned long long)(uint32_t)t;
+    }
+    sk[j] = key;
+  }
+  __syncthreads();
+  for (int k = 2; k <= kEmbChunk; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < kEmbChunk; i += blockDim.x) {
+        int ixj = i ^ j;
+        if (ixj > i) {
+          unsigned long long a = sk[i], b = sk[ixj];
+          bool up = (i & k) == 0;
+          if ((a > b) == up) { sk[i] = b; sk[ixj] = a; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int j = threadIdx.x; j < kEmbChunk; j += blockDim.x) {
+    unsigned long long key = sk[j];
+    keys[base + j] = key;
+    if (key == ~0ull) continue;
+    uint32_t id = (uint32_t)(key >> 32);
+    bool start = j == 0 || (uint32_t)(sk[j - 1] >> 32) != id;
+    if (start) {
+      int lo = j, hi = kEmbChunk;  // first index with id' > id
+      while (lo < hi) {
+        int mid = (lo + hi) >> 1;
+        if (sk[mid] != ~0ull && (uint32_t)(sk[mid] >> 32) <= id) lo = mid + 1;
+        else hi = mid;
+      }
+      counts[(size_t)id * nch + c] = lo - j;
+    }
+  }
+}
+
+// K2: exclusive scan of counts (length m) -> offs (length m+1); 3 phases.
+constexpr int kScanTile = 4096;
+__global__ void k_scan_tile_sums(const int* __restrict__ in, size_t m, int* __restrict__ sums) {
+  __shared__ float sh[32];
+  size_t base = (size_t)blockIdx.x * kScanTile;
+  int s = 0;
+  for (int j = threadIdx.x; j < kScanTile; j += blockDim.x) {
+    size_t k = base + j;
+    if (k < m) s += in[k];
+  }
+  // integer block sum via float-free path
+  __shared__ int shi[32];
+  (void)sh;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) shi[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    int v = threadIdx.x < (blockDim.x >> 5) ? shi[threadIdx.x] : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) sums[blockIdx.x] = v;
+  }
+}
+
+__global__ void k_scan_sums_serial(int* __restrict__ sums, int nt, int* __restrict__ total_out) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    int run = 0;
+    for (int i = 0; i < nt; ++i) { int v = sums[i]; sums[i] = run; run += v; }
+    *total_out = run;
+  }
+}
+
+__global__ void k_scan_tile_apply(const int* __restrict__ in, size_t m, const int* __restrict__ sums,
+                                  int* __restrict__ out) {
+  // each block scans its tile: 1024 threads x 4 items
+  __shared__ int warp_tot[32];
+  size_t base = (size_t)blockIdx.x * kScanTile;
+  int t = threadIdx.x;
+  int v[4];
+  int local = 0;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    size_t k = base + (size_t)t * 4 + q;
+    v[q] = k < m ? in[k] : 0;
+    local += v[q];
+  }
+  int lane = t & 31, w = t >> 5;
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    int x = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+    int xi = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, xi, o);
+      if (lane >= o) xi += y;
+    }
+    warp_tot[lane] = xi - x;  // exclusive
+  }
+  __syncthreads();
+  int run = sums[blockIdx.x] + warp_tot[w] + (incl - local);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    size_t k = base + (size_t)t * 4 + q;
+    if (k < m) out[k] = run;
+    run += v[q];
+  }
+}
+
+// K3: place each chunk's sorted tokens at their global positions.
+__global__ void k_emb_scatter(const unsigned long long* __restrict__ keys, size_t n, int nch,
+                              const int* __restrict__ offs, int* __restrict__ order) {
+  __shared__ unsigned long long sk[kEmbChunk];
+  int c = blockIdx.x;
+  size_t base = (size_t)c * kEmbChunk;
+  for (int j = threadIdx.x; j < kEmbChunk; j += blockDim.x) sk[j] = keys[base + j];
+  __syncthreads();
+  for (int j = threadIdx.x; j < kEmbChunk; j += blockDim.x) {
+    unsigned long long key = sk[j];
+    if (key == ~0ull) continue;
+    uint32_t id = (uint32_t)(key >> 32);
+    int lo = 0, hi = j;  // first index with id' >= id
+    while (lo < hi) {
+      int mid = (lo + hi) >> 1;
+      if ((uint32_t)(sk[mid] >> 32) < id) lo = mid + 1;
+      else hi = mid;
+    }
+    order[offs[(size_t)id * nch + c] + (j - lo)] = (int)(uint32_t)key;
+  }
+}
+
+// K4: dw[v, :] = sum over the run of v (token order) of dout[t, :].
+__global__ void k_emb_segsum(const float* __restrict__ dout, const int* __restrict__ order,
+                             const int* __restrict__ offs, int nch, size_t V, size_t D,
+                             float* __restrict__ dw) {
+  size_t v = blockIdx.x;
+  size_t c4 = (blockIdx.y * (size_t)blockDim.x + threadIdx.x) * 4;
+  if (v >= V || c4 >= D) return;
+  int beg = offs[v * nch], end = offs[(v + 1) * nch];
+  bool vec = (D % 4 == 0) && (((uintptr_t)dout & 15) == 0) && (((uintptr_t)dw & 15) == 0);
+  if (vec) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int k = beg; k < end; ++k) {
+      float4 x = *reinterpret_cast<const float4*>(dout + (size_t)order[k] * D + c4);
+      acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+    }
+    *reinterpret_cast<float4*>(dw + v * D + c4) = acc;
+  } else {
+    for (int q = 0; q < 4 && c4 + q < D; ++q) {
+      float acc = 0.0f;
+      for (int k = beg; k < end; ++k) acc += dout[(size_t)order[k] * D + c4 + q];
+      dw[v * D + c4 + q] = acc;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ permute
+struct PermMeta {
+  int ndim;
+  int64_t out_shape[kMaxRank];
+  int64_t in_stride_for_out_dim[kMaxRank];  // input stride of the input dim perm[d]
+};
+
+// Innermost dim preserved: copy contiguous rows of length L (warp per row).
+__global__ void k_permute_rows(const float* __restrict__ x, float* __restrict__ out, size_t nrows,
+                               size_t L, PermMeta m) {
+  int lane = threadIdx.x & 31;
+  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  bool vec = (L % 4 == 0) && (((uintptr_t)x & 15) == 0) && (((uintptr_t)out & 15) == 0);
+  for (size_t r = warp; r < nrows; r += nw) {
+    size_t rem = r;
+    int64_t src = 0;
+    for (int d = m.ndim - 2; d >= 0; --d) {
+      int64_t i = (int64_t)(rem % (size_t)m.out_shape[d]);
+      rem /= (size_t)m.out_shape[d];
+      src += i * m.in_stride_for_out_dim[d];
+    }
+    const float* s = x + src;
+    float* o = out + r * L;
+    if (vec) {
+      for (size_t c = lane; c < L / 4; c += 32)
+        reinterpret_cast<float4*>(o)[c] = reinterpret_cast<const float4*>(s)[c];
+    } else {
+      for (size_t c = lane; c < L; c += 32) o[c] = s[c];
+    }
+  }
+}
+
+// Batched transpose of the last two dims: in [B, R, C] -> out [B, C, R].
+__global__ void k_transpose_tiled(const float* __restrict__ x, float* __restrict__ out, size_t R,
+                                  size_t C) {
+  __shared__ float tile[32][33];
+  size_t b = blockIdx.z;
+  size_t r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const float* xb = x + b * R * C;
+  float* ob = out + b * R * C;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    size_t r = r0 + k, c = c0 + threadIdx.x;
+    if (r < R && c < C) tile[k][threadIdx.x] = xb[r * C + c];
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    size_t c = c0 + k, r = r0 + threadIdx.x;
+    if (r < R && c < C) ob[c * R + r] = tile[threadIdx.x][k];
+  }
+}
+
+__global__ void k_permute_general(const float* __restrict__ x, float* __restrict__ out, size_t n,
+                                  PermMeta m) {
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t f = tid; f < n; f += stride) {
+    size_t rem = f;
+    int64_t src = 0;
+    for (int d = m.ndim - 1; d >= 0; --d) {
+      int64_t i = (int64_t)(rem % (size_t)m.out_shape[d]);
+      rem /= (size_t)m.out_shape[d];
+      src += i * m.in_stride_for_out_dim[d];
+    }
+    out[f] = x[src];
+  }
+}
+
+}  // namespace
+
+#define LAUNCH_ROWS_WARP(KERN, LEN, ROWS, ...)                                   \
+  do {                                                                           \
+    unsigned blocks_ = grid_for((ROWS) * 32, 256);                               \
+    if ((LEN) <= 32) KERN<1><<<blocks_, 256, 0, stream()>>>(__VA_ARGS__);        \
+    else if ((LEN) <= 128) KERN<4><<<blocks_, 256, 0, stream()>>>(__VA_ARGS__);  \
+    else if ((LEN) <= 256) KERN<8><<<blocks_, 256, 0, stream()>>>(__VA_ARGS__);  \
+    else if ((LEN) <= 512) KERN<16><<<blocks_, 256, 0, stream()>>>(__VA_ARGS__); \
+    else KERN<32><<<blocks_, 256, 0, stream()>>>(__VA_ARGS__);                   \
+    count_launch();                                                              \
+    after_launch(#KERN);                                                         \
+  } while (0)
+
+static unsigned row_blocks(size_t rows) {
+  return (unsigned)std::max<size_t>(1, std::min<size_t>(rows, (size_t)kNumSMs * 8));
+}
+
+void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner) {
+  if (!outer || !axis_sz || !inner) return;
+  if (inner == 1 && axis_sz <= 1024) {
+    LAUNCH_ROWS_WARP(k_softmax_warp, axis_sz, outer, x, y, outer, (int)axis_sz);
+  } else if (inner == 1) {
+    k_softmax_block<<<row_blocks(outer), 512, 0, stream()>>>(x, y, outer, axis_sz);
+    count_launch();
+    after_launch("k_softmax_block");
+  } else {
+    size_t g = outer * inner;
+    k_softmax_strided<<<(unsigned)((g + 255) / 256), 256, 0, stream()>>>(x, y, outer, axis_sz, inner);
+    count_launch();
+    after_launch("k_softmax_strided");
+  }
+}
+
+void softmax_bwd(const float* s, const float* g, float* dx, size_t outer, size_t axis_sz,
+                 size_t inner) {
+  if (!outer || !axis_sz || !inner) return;
+  if (inner == 1 && axis_sz <= 1024) {
+    LAUNCH_ROWS_WARP(k_softmax_bwd_warp, axis_sz, outer, s, g, dx, outer, (int)axis_sz);
+  } else if (inner == 1) {
+    k_softmax_bwd_block<<<row_blocks(outer), 512, 0, stream()>>>(s, g, dx, outer, axis_sz);
+    count_launch();
+    after_launch("k_softmax_bwd_block");
+  } else {
+    size_t gg = outer * inner;
+    k_softmax_bwd_strided<<<(unsigned)((gg + 255) / 256), 256, 0, stream()>>>(s, g, dx, outer,
+                                                                             axis_sz, inner);
+    count_launch();
+    after_launch("k_softmax_bwd_strided");
+  }
+}
+
+void layernorm_fwd(const float* x, float* y, float* var, size_t outer, size_t axis_sz,
+                   size_t inner, float eps) {
+  if (!outer || !axis_sz || !inner) return;
+  if (inner == 1 && axis_sz <= 1024) {
+    LAUNCH_ROWS_WARP(k_layernorm_warp, axis_sz, outer, x, y, var, outer, (int)axis_sz, eps);
+  } else if (inner == 1) {
+    k_layernorm_block<<<row_blocks(outer), 512, 0, stream()>>>(x, y, var, outer, axis_sz, eps);
+    count_launch();
+    after_launch("k_layernorm_block");
+  } else {
+    size_t g = outer * inner;
+    k_layernorm_strided<<<(unsigned)((g + 255) / 256), 256, 0, stream()>>>(x, y, var, outer,
+                                                                           axis_sz, inner, eps);
+    count_launch();
+    after_launch("k_layernorm_strided");
+  }
+}
+
+void layernorm_bwd(const float* y, const float* var, const float* g, float* dx, size_t outer,
+                   size_t axis_sz, size_t inner, float eps) {
+  if (!outer || !axis_sz || !inner) return;
+  if (inner == 1 && axis_sz <= 1024) {
+    LAUNCH_ROWS_WARP(k_layernorm_bwd_warp, axis_sz, outer, y, var, g, dx, outer, (int)axis_sz, eps);
+  } else if (inner == 1) {
+    k_layernorm_bwd_block<<<row_blocks(outer), 512, 0, stream()>>>(y, var, g, dx, outer, axis_sz, eps);
+    count_launch();
+    after_launch("k_layernorm_bwd_block");
+  } else {
+    size_t gg = outer * inner;
+    k_layernorm_bwd_strided<<<(unsigned)((gg + 255) / 256), 256, 0, stream()>>>(
+        y, var, g, dx, outer, axis_sz, inner, eps);
+    count_launch();
+    after_launch("k_layernorm_bwd_strided");
+  }
+}
+
+void xent_fwd(const float* logits, const void* tgt, int tdt, float* probs, float* loss, size_t n,
+              size_t v) {
+  if (!n) {
+    scalar_op_imm(kSFill, nullptr, NAN, loss, 1);
+    return;
+  }
+  float* nll = (float*)scratch_alloc(n * sizeof(float));
+  if (v <= 1024) {
+    LAUNCH_ROWS_WARP(k_xent_fwd_warp, v, n, logits, tgt, tdt, probs, nll, n, (int)v,
+                     device_error_word());
+  } else {
+    k_xent_fwd_block<<<row_blocks(n), 512, 0, stream()>>>(logits, tgt, tdt, probs, nll, n, v,
+                                                          device_error_word());
+    count_launch();
+    after_launch("k_xent_fwd_block");
+  }
+  k_mean_1block<<<1, 1024, 0, stream()>>>(nll, loss, n);
+  count_launch();
+  after_launch("k_mean_1block");
+  scratch_free(nll);
+}
+
+void xent_nll_gather(const float* probs, const void* tgt, int tdt, float* out, size_t n, size_t v) {
+  if (!n) return;
+  k_xent_nll_gather<<<(unsigned)((n + 255) / 256), 256, 0, stream()>>>(probs, tgt, tdt, out, n, v,
+                                                                      device_error_word());
+  count_launch();
+  after_launch("k_xent_nll_gather");
+}
+
+void xent_bwd(const float* probs, const void* tgt, int tdt, const float* dout_dev, float* dx,
+              size_t n, size_t v) {
+  size_t total = n * v;
+  if (!total) return;
+  k_xent_bwd<<<grid_for(total, 256), 256, 0, stream()>>>(probs, tgt, tdt, dout_dev, dx, n, v);
+  count_launch();
+  after_launch("k_xent_bwd");
+}
+
+void embedding_fwd(const float* w, const void* idx, int idt, float* out, size_t n, size_t vocab,
+                   size_t dim) {
+  if (!n || !dim) return;
+  k_embedding_fwd<<<grid_for(n * 32, 256), 256, 0, stream()>>>(w, idx, idt, out, n, vocab, dim,
+                                                              device_error_word());
+  count_launch();
+  after_launch("k_embedding_fwd");
+}
+
+// Exclusive scan of m ints: out[0..m] (out[m] = total).
+static void exclusive_scan_int(const int* in, int* out, size_t m) {
+  int nt = (int)((m + kScanTile - 1) / kScanTile);
+  if (nt == 0) nt = 1;
+  int* sums = (int*)scratch_alloc((size_t)nt * sizeof(int));
+  k_scan_tile_sums<<<nt, 1024, 0, stream()>>>(in, m, sums);
+  k_scan_sums_serial<<<1, 32, 0, stream()>>>(sums, nt, out + m);
+  k_scan_tile_apply<<<nt, 1024, 0, stream()>>>(in, m, sums, out);
+  count_launch(3);
+  after_launch("exclusive_scan_int");
+  scratch_free(sums);
+}
+
+void embedding_bwd(const float* dout, const void* idx, int idt, float* dw, size_t n, size_t V,
+                   size_t D) {
+  if (!V || !D) return;
+  if (!n) {
+    MALUS_CUDA(cudaMemsetAsync(dw, 0, V * D * sizeof(float), stream()));
+    return;
+  }
+  int nch = (int)((n + kEmbChunk - 1) / kEmbChunk);
+  size_t m = V * (size_t)nch;
+  auto* keys = (unsigned long long*)scratch_alloc((size_t)nch * kEmbChunk * 8);
+  int* counts = (int*)scratch_alloc(m * sizeof(int));
+  int* offs = (int*)scratch_alloc((m + 1) * sizeof(int));
+  int* order = (int*)scratch_alloc(n * sizeof(int));
+  MALUS_CUDA(cudaMemsetAsync(counts, 0, m * sizeof(int), stream()));
+  k_emb_chunk_sort<<<nch, 512, 0, stream()>>>(idx, idt, n, V, nch, keys, counts,
+                                              device_error_word());
+  count_launch();
+  after_launch("k_emb_chunk_sort");
+  exclusive_scan_int(counts, offs, m);
+  k_emb_scatter<<<nch, 512, 0, stream()>>>(keys, n, nch, offs, order);
+  count_launch();
+  after_launch("k_emb_scatter");
+  unsigned threads = (unsigned)std::min<size_t>(256, std::max<size_t>(32, ((D + 3) / 4 + 31) / 32 * 32));
+  dim3 grid((unsigned)V, (unsigned)(((D + 3) / 4 + threads - 1) / threads));
+  k_emb_segsum<<<grid, threads, 0, stream()>>>(dout, order, offs, nch, V, D, dw);
+  count_launch();
+  after_launch("k_emb_segsum");
+  scratch_free(keys);
+  scratch_free(counts);
+  scratch_free(offs);
+  scratch_free(order);
+}
+
+void permute_nd(const float* x, float* out, const Shape& s, const int* perm) {
+  size_t n = s.numel();
+  if (!n) return;
+  int r = s.ndim;
+  int64_t in_stride[kMaxRank];
+  int64_t st = 1;
+  for (int d = r - 1; d >= 0; --d) { in_stride[d] = st; st *= (int64_t)s.d[d]; }
+  PermMeta m;
+  m.ndim = r;
+  for (int d = 0; d < r; ++d) {
+    m.out_shape[d] = (int64_t)s.d[perm[d]];
+    m.in_stride_for_out_dim[d] = in_stride[perm[d]];
+  }
+  bool identity = true;
+  for (int d = 0; d < r; ++d) identity &= perm[d] == d;
+  if (identity) {
+    MALUS_CUDA(cudaMemcpyAsync(out, x, n * 4, cudaMemcpyDeviceToDevice, stream()));
+    return;
+  }
+  if (perm[r - 1] == r - 1) {
+    size_t L = s.d[r - 1];
+    size_t nrows = n / L;
+    k_permute_rows<<<grid_for(nrows * 32, 256), 256, 0, stream()>>>(x, out, nrows, L, m);
+    count_launch();
+    after_launch("k_permute_rows");
+    return;
+  }
+  // last two dims swapped, leading dims in order: batched tiled transpose
+  bool lead_identity = r >= 2 && perm[r - 1] == r - 2 && perm[r - 2] == r - 1;
+  for (int d = 0; d < r - 2 && lead_identity; ++d) lead_identity &= perm[d] == d;
+  if (lead_identity) {
+    size_t R = s.d[r - 2], C = s.d[r - 1];
+    size_t B = n / (R * C);
+    dim3 grid((unsigned)((C + 31) / 32), (unsigned)((R + 31) / 32), (unsigned)B);
+    k_transpose_tiled<<<grid, dim3(32, 8), 0, stream()>>>(x, out, R, C);
+    count_launch();
+    after_launch("k_transpose_tiled");
+    return;
+  }
+  k_permute_general<<<grid_for(n, 256), 256, 0, stream()>>>(x, out, n, m);
+  count_launch();
+  after_launch("k_permute_general");
+}
+
+}  // namespace malus

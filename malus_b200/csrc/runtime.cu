@@ -1,0 +1,734 @@
+// Runtime core: device selection, the stream, the buffer pool, tensor handle
+// lifetime, host access, RNG, host staging buffers, counters and the bench
+// timer.  Semantics follow crates/malus-runtime/src/metal.rs (allocation,
+// refcounting, reshape aliasing, Philox RNG, causal mask), buffer.rs,
+// bench.rs and lib.rs; the mechanisms are CUDA-native:
+//  - one non-blocking stream per process (process-per-GPU, so the
+//    reference's single-consumer context, ADR-0033, holds);
+//  - a stream-ordered exact-size free-list pool: a buffer released on the
+//    host can be handed out again at once, because every later use is
+//    queued behind every earlier use on the same stream (this replaces the
+//    generation gating of metal.rs:364-456);
+//  - host reads synchronise the stream (replaces flush_if_pending).
+#include "common.cuh"
+
+#include <cmath>
+#include <cstdarg>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+namespace malus {
+
+void panic(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  fprintf(stderr, "malus: ");
+  vfprintf(stderr, fmt, ap);
+  fprintf(stderr, "\n");
+  va_end(ap);
+  fflush(stderr);
+  abort();
+}
+
+size_t dtype_size(int32_t dtype) {
+  switch (dtype) {
+    case 0: case 5: case 9: return 4;
+    case 1: case 2: case 4: case 8: return 2;
+    case 3: case 7: return 1;
+    case 6: case 10: return 8;
+    default: panic("unknown dtype tag %d", dtype);
+  }
+}
+
+// ------------------------------------------------------------------ context
+namespace {
+struct Context {
+  bool init = false;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int32_t* d_error = nullptr;  // device error word (bounded waits)
+  std::mutex mu;
+};
+Context g_ctx;
+
+std::atomic<int64_t> g_launches{0};
+std::atomic<int64_t> g_retains{0}, g_releases{0}, g_allocs{0};
+bool g_sync_dispatch = false;
+
+void ensure_init() {
+  if (g_ctx.init) return;
+  std::lock_guard<std::mutex> lk(g_ctx.mu);
+  if (g_ctx.init) return;
+  int dev = 0;
+  if (const char* s = getenv("MALUS_DEVICE")) dev = atoi(s);
+  else if (const char* s = getenv("LOCAL_RANK")) dev = atoi(s);
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+    panic("no CUDA device available (this runtime has no CPU fallback)");
+  if (dev >= n) dev = dev % n;
+  MALUS_CUDA(cudaSetDevice(dev));
+  MALUS_CUDA(cudaStreamCreateWithFlags(&g_ctx.stream, cudaStreamNonBlocking));
+  MALUS_CUDA(cudaMalloc(&g_ctx.d_error, 256));
+  MALUS_CUDA(cudaMemset(g_ctx.d_error, 0, 256));
+  const char* sd = getenv("MALUS_SYNC_DISPATCH");
+  g_sync_dispatch = sd && sd[0] == '1';
+  g_ctx.device = dev;
+  g_ctx.init = true;
+}
+}  // namespace
+
+cudaStream_t stream() {
+  ensure_init();
+  return g_ctx.stream;
+}
+int32_t* device_error_word() { ensure_init(); return g_ctx.d_error; }
+bool sync_dispatch() { return g_sync_dispatch; }
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+void after_launch(const char* what) {
+  cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess) panic("kernel launch failed (%s): %s", what, cudaGetErrorString(e));
+  if (g_sync_dispatch) {
+    e = cudaStreamSynchronize(g_ctx.stream);
+    if (e != cudaSuccess) panic("kernel %s failed: %s", what, cudaGetErrorString(e));
+  }
+}
+
+// --------------------------------------------------------------------- pool
+namespace {
+struct Pool {
+  std::mutex mu;
+  std::unordered_map<size_t, std::vector<void*>> free_lists;
+  int64_t hits = 0, misses = 0, pooled = 0, live = 0, peak = 0;
+  int64_t budget = -1;
+};
+Pool g_pool;
+
+size_t bucket_of(size_t bytes) {
+  if (bytes == 0) bytes = 1;  // metal.rs:389-392: 1-byte placeholder for empty tensors
+  return (bytes + 511) & ~size_t(511);
+}
+
+int64_t budget_bytes() {
+  if (g_pool.budget < 0) {
+    const char* s = getenv("MALUS_MEM_BUDGET_MB");
+    g_pool.budget = s ? (int64_t)atoll(s) << 20 : 0;  // 0 = unlimited
+  }
+  return g_pool.budget;
+}
+
+bool capturing() {
+  cudaStreamCaptureStatus st;
+  if (cudaStreamIsCapturing(g_ctx.stream, &st) != cudaSuccess) return false;
+  return st != cudaStreamCaptureStatusNone;
+}
+
+void trim_pool_locked() {
+  if (capturing()) return;
+  MALUS_CUDA(cudaStreamSynchronize(g_ctx.stream));
+  for (auto& kv : g_pool.free_lists)
+    for (void* p : kv.second) {
+      MALUS_CUDA(cudaFree(p));
+      g_pool.pooled -= (int64_t)kv.first;
+    }
+  g_pool.free_lists.clear();
+}
+
+void* pool_get(size_t bytes, size_t* bucket_out) {
+  ensure_init();
+  size_t b = bucket_of(bytes);
+  *bucket_out = b;
+  std::lock_guard<std::mutex> lk(g_pool.mu);
+  auto it = g_pool.free_lists.find(b);
+  if (it != g_pool.free_lists.end() && !it->second.empty()) {
+    void* p = it->second.back();
+    it->second.pop_back();
+    g_pool.hits++;
+    g_pool.pooled -= (int64_t)b;
+    g_pool.live += (int64_t)b;
+    return p;
+  }
+  g_pool.misses++;
+  int64_t bud = budget_bytes();
+  if (bud > 0 && g_pool.live + g_pool.pooled + (int64_t)b > bud) trim_pool_locked();
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, b);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    trim_pool_locked();
+    e = cudaMalloc(&p, b);
+    if (e != cudaSuccess) panic("out of device memory allocating %zu bytes", b);
+  }
+  g_pool.live += (int64_t)b;
+  if (g_pool.live + g_pool.pooled > g_pool.peak) g_pool.peak = g_pool.live + g_pool.pooled;
+  return p;
+}
+
+void pool_put(void* p, size_t bucket) {
+  std::lock_guard<std::mutex> lk(g_pool.mu);
+  g_pool.free_lists[bucket].push_back(p);
+  g_pool.live -= (int64_t)bucket;
+  g_pool.pooled += (int64_t)bucket;
+}
+}  // namespace
+
+// Raw pooled workspace for kernels (split operands, sort keys, partial sums).
+// Freed back to the pool right after the launches that use it are queued:
+// the stream order protects it exactly like a tensor buffer.
+static std::mutex g_scratch_mu;
+static std::unordered_map<void*, size_t>& scratch_map() {
+  static auto* m = new std::unordered_map<void*, size_t>();
+  return *m;
+}
+void* scratch_alloc(size_t bytes) {
+  size_t b;
+  void* p = pool_get(bytes, &b);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  scratch_map()[p] = b;
+  return p;
+}
+void scratch_free(void* p) {
+  if (!p) return;
+  size_t b;
+  {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    auto it = scratch_map().find(p);
+    if (it == scratch_map().end()) panic("scratch_free of an unknown pointer");
+    b = it->second;
+    scratch_map().erase(it);
+  }
+  pool_put(p, b);
+}
+
+// ----------------------------------------------------------- tensor handles
+static int64_t make_handle(int32_t dtype, const size_t* shape, int ndim, Storage* st, size_t len) {
+  auto* t = new TensorBuffer();
+  t->st = st;
+  t->dtype = dtype;
+  t->ndim = ndim;
+  t->len = len;
+  for (int i = 0; i < ndim; ++i) t->shape[i] = shape[i];
+  t->rc.store(1, std::memory_order_relaxed);
+  g_allocs.fetch_add(1, std::memory_order_relaxed);
+  return reinterpret_cast<int64_t>(t);
+}
+
+int64_t alloc(int32_t dtype, const size_t* shape, int ndim) {
+  if (dtype != MALUS_F32 && dtype != MALUS_I32 && dtype != MALUS_I64)
+    panic("unsupported dtype tag %d; supported: f32, i32, i64", dtype);
+  if (ndim > kMaxRank) panic("rank %d exceeds the maximum of %d", ndim, kMaxRank);
+  size_t n = 1;
+  for (int i = 0; i < ndim; ++i) n *= shape[i];
+  size_t bytes = n * dtype_size(dtype);
+  auto* st = new Storage();
+  st->ptr = pool_get(bytes, &st->bytes);
+  st->aliases = 1;
+  st->owned = true;
+  return make_handle(dtype, shape, ndim, st, n);
+}
+
+int64_t alloc_like(int64_t h) {
+  auto* t = tb(h);
+  return alloc(MALUS_F32, t->shape, t->ndim);
+}
+
+int64_t alloc_f32(std::initializer_list<size_t> shape) {
+  size_t s[kMaxRank];
+  int n = 0;
+  for (size_t d : shape) s[n++] = d;
+  return alloc(MALUS_F32, s, n);
+}
+
+bool same_shape(int64_t a, int64_t b) {
+  auto *x = tb(a), *y = tb(b);
+  if (x->ndim != y->ndim) return false;
+  for (int i = 0; i < x->ndim; ++i)
+    if (x->shape[i] != y->shape[i]) return false;
+  return true;
+}
+
+int normalize_axis(int64_t axis, int ndim) {
+  int64_t a = axis < 0 ? axis + ndim : axis;
+  if (a < 0 || a >= ndim) panic("axis %lld is out of range for tensor with %d dimensions",
+                                (long long)axis, ndim);
+  return (int)a;
+}
+
+void split_axis(const Shape& s, int axis, size_t* outer, size_t* axis_sz, size_t* inner) {
+  size_t o = 1, in = 1;
+  for (int i = 0; i < axis; ++i) o *= s.d[i];
+  for (int i = axis + 1; i < s.ndim; ++i) in *= s.d[i];
+  *outer = o;
+  *axis_sz = s.d[axis];
+  *inner = in;
+}
+
+static void release_storage(Storage* st) {
+  if (--st->aliases > 0) return;
+  if (st->owned) pool_put(st->ptr, st->bytes);
+  delete st;
+}
+
+}  // namespace malus
+
+using namespace malus;
+
+// ============================================================ C ABI: section 1
+extern "C" {
+
+int64_t tensor_alloc_gpu(int32_t dtype, const size_t* shape, size_t ndims, const float* data) {
+  int64_t h = alloc(dtype, shape, (int)ndims);
+  auto* t = tb(h);
+  if (data && t->len > 0) {
+    MALUS_CUDA(cudaMemcpyAsync(t->st->ptr, data, t->len * dtype_size(dtype),
+                               cudaMemcpyHostToDevice, stream()));
+    // The source is caller-owned pageable memory that may die right after
+    // this call; the copy above is staged before it returns, which is what
+    // the reference's immediate memcpy into a shared buffer guarantees.
+  }
+  return h;
+}
+
+int64_t tensor_alloc_zeros_gpu(const size_t* shape, size_t ndims) {
+  int64_t h = alloc(MALUS_F32, shape, (int)ndims);
+  auto* t = tb(h);
+  MALUS_CUDA(cudaMemsetAsync(t->st->ptr, 0, std::max<size_t>(t->len * 4, 1), stream()));
+  return h;
+}
+
+int64_t tensor_alloc_ones_gpu(const size_t* shape, size_t ndims) {
+  int64_t h = alloc(MALUS_F32, shape, (int)ndims);
+  auto* t = tb(h);
+  if (t->len) scalar_op_imm(kSFill, nullptr, 1.0f, fptr(h), t->len);
+  return h;
+}
+
+void tensor_retain(int64_t h) {
+  if (h == 0) return;
+  g_retains.fetch_add(1, std::memory_order_relaxed);
+  tb(h)->rc.fetch_add(1, std::memory_order_relaxed);
+}
+
+void tensor_release(int64_t h) {
+  if (h == 0) return;
+  g_releases.fetch_add(1, std::memory_order_relaxed);
+  auto* t = tb(h);
+  int64_t prev = t->rc.fetch_sub(1, std::memory_order_acq_rel);
+  if (prev <= 0)
+    panic("over-release of tensor handle %#llx (refcount already zero) — likely a "
+          "borrow-inference or tape-retain bug", (unsigned long long)h);
+  if (prev == 1) {
+    tape_on_release(h);
+    release_storage(t->st);
+    delete t;
+  }
+}
+
+void tensor_free(int64_t h) { tensor_release(h); }
+
+int64_t tensor_len(int64_t h) { return (int64_t)tb(h)->len; }
+int64_t tensor_ndim(int64_t h) { return (int64_t)tb(h)->ndim; }
+int64_t tensor_dim(int64_t h, int64_t i) {
+  auto* t = tb(h);
+  int64_t idx = i < 0 ? i + t->ndim : i;
+  if (idx < 0 || idx >= t->ndim)
+    panic("tensor_dim index %lld out of range for rank-%d tensor", (long long)i, t->ndim);
+  return (int64_t)t->shape[idx];
+}
+
+static void print_rec(const void* data, int32_t dtype, const size_t* shape, int ndim, size_t off) {
+  auto pv = [&](size_t i) {
+    if (dtype == MALUS_I32) printf("%d", ((const int32_t*)data)[i]);
+    else if (dtype == MALUS_I64) printf("%lld", (long long)((const int64_t*)data)[i]);
+    else printf("%g", (double)((const float*)data)[i]);
+  };
+  if (ndim == 0) { pv(off); return; }
+  size_t stride = 1;
+  for (int i = 1; i < ndim; ++i) stride *= shape[i];
+  printf("[");
+  for (size_t i = 0; i < shape[0]; ++i) {
+    if (i) printf(", ");
+    if (ndim == 1) pv(off + i);
+    else print_rec(data, dtype, shape + 1, ndim - 1, off + i * stride);
+  }
+  printf("]");
+}
+
+void tensor_print(int64_t h) {
+  if (h == 0) { printf("[]"); return; }
+  auto* t = tb(h);
+  std::vector<char> buf(std::max<size_t>(t->len * dtype_size(t->dtype), 1));
+  malus_tensor_read(h, buf.data(), t->len * dtype_size(t->dtype));
+  print_rec(buf.data(), t->dtype, t->shape, t->ndim, 0);
+  fflush(stdout);
+}
+
+void gpu_barrier(void) {
+  cudaError_t e = cudaStreamSynchronize(stream());
+  if (e != cudaSuccess)
+    panic("GPU stream failed: %s (set MALUS_SYNC_DISPATCH=1 to attribute the failing op)",
+          cudaGetErrorString(e));
+}
+
+float malus_tensor_get_f32(int64_t h, int64_t idx) {
+  auto* t = tb(h);
+  if (idx < 0 || (size_t)idx >= t->len)
+    panic("tensor_get_f32 index %lld out of range for length %zu", (long long)idx, t->len);
+  float v;
+  MALUS_CUDA(cudaMemcpyAsync(&v, (const float*)t->st->ptr + idx, 4, cudaMemcpyDeviceToHost,
+                             stream()));
+  gpu_barrier();
+  return v;
+}
+
+int64_t tensor_reshape(int64_t h, const size_t* dims, size_t ndims) {
+  auto* t = tb(h);
+  size_t n = 1;
+  for (size_t i = 0; i < ndims; ++i) n *= dims[i];
+  if (n != t->len)
+    panic("reshape element count mismatch: input has %zu elements, target would have %zu",
+          t->len, n);
+  if (ndims > (size_t)kMaxRank) panic("reshape rank %zu exceeds %d", ndims, kMaxRank);
+  t->st->aliases++;
+  return make_handle(t->dtype, dims, (int)ndims, t->st, t->len);
+}
+
+int64_t tensor_causal_mask(int64_t tsz) {
+  size_t T = (size_t)tsz;
+  std::vector<float> d(T * T, 0.0f);
+  for (size_t i = 0; i < T; ++i)
+    for (size_t j = i + 1; j < T; ++j) d[i * T + j] = -1e9f;
+  size_t shape[2] = {T, T};
+  int64_t h = tensor_alloc_gpu(MALUS_F32, shape, 2, d.data());
+  gpu_barrier();  // d is a stack vector; make sure the copy has consumed it
+  return h;
+}
+
+}  // extern "C"
+
+// -------------------------------------------------------------------- RNG
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy
+// as 1, 2, 3", SC'11), keyed by a per-call counter, followed by the
+// Box-Muller transform in double precision — the generator of
+// metal.rs:1692-1737 so that seeded weights are reproducible bit for bit.
+namespace {
+thread_local uint64_t t_rng_counter = 0;
+
+struct Philox {
+  static constexpr uint32_t kMul0 = 0xD2511F53u, kMul1 = 0xCD9E8D57u;
+  static constexpr uint32_t kWeyl0 = 0x9E3779B9u, kWeyl1 = 0xBB67AE85u;
+  static void run(uint32_t c[4], uint32_t k0, uint32_t k1) {
+    for (int r = 0; r < 10; ++r) {
+      uint64_t p0 = (uint64_t)c[0] * kMul0;
+      uint64_t p1 = (uint64_t)c[2] * kMul1;
+      uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+      uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+      uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+      c[0] = n0; c[1] = lo1; c[2] = n2; c[3] = lo0;
+      k0 += kWeyl0;
+      k1 += kWeyl1;
+    }
+  }
+};
+
+void randn_fill(float* out, size_t n, uint64_t call_idx) {
+  uint32_t k0 = (uint32_t)call_idx, k1 = (uint32_t)(call_idx >> 32);
+  size_t pairs = (n + 1) / 2;
+  auto work = [&](size_t lo, size_t hi) {
+    for (size_t k = lo; k < hi; ++k) {
+      uint32_t c[4] = {(uint32_t)k, (uint32_t)((uint64_t)k >> 32), 0u, 0u};
+      Philox::run(c, k0, k1);
+      double u1 = ((double)c[0] + 0.5) / 4294967296.0;
+      double u2 = ((double)c[1] + 0.5) / 4294967296.0;
+      double mag = std::sqrt(-2.0 * std::log(u1));
+      double ang = 2.0 * M_PI * u2;
+      out[2 * k] = (float)(mag * std::cos(ang));
+      if (2 * k + 1 < n) out[2 * k + 1] = (float)(mag * std::sin(ang));
+    }
+  };
+  unsigned nt = pairs > (1u << 20) ? std::min(16u, std::max(1u, std::thread::hardware_concurrency())) : 1;
+  if (nt <= 1) { work(0, pairs); return; }
+  std::vector<std::thread> th;
+  size_t chunk = (pairs + nt - 1) / nt;
+  for (unsigned i = 0; i < nt; ++i) {
+    size_t lo = i * chunk, hi = std::min(pairs, lo + chunk);
+    if (lo < hi) th.emplace_back(work, lo, hi);
+  }
+  for (auto& t : th) t.join();
+}
+}  // namespace
+
+extern "C" {
+
+int64_t tensor_randn(const size_t* shape, size_t ndims) {
+  size_t n = 1;
+  for (size_t i = 0; i < ndims; ++i) n *= shape[i];
+  uint64_t call_idx = t_rng_counter++;
+  std::vector<float> d(std::max<size_t>(n, 1));
+  randn_fill(d.data(), n, call_idx);
+  int64_t h = tensor_alloc_gpu(MALUS_F32, shape, ndims, d.data());
+  gpu_barrier();
+  return h;
+}
+
+float malus_rand_uniform(void) {
+  uint64_t call_idx = t_rng_counter++;
+  uint32_t c[4] = {0, 0, 0, 0};
+  Philox::run(c, (uint32_t)call_idx, (uint32_t)(call_idx >> 32));
+  return (float)((double)c[0] / 4294967296.0);
+}
+
+int64_t malus_rand_int(int64_t n) {
+  uint64_t call_idx = t_rng_counter++;
+  uint32_t c[4] = {1, 0, 0, 0};
+  Philox::run(c, (uint32_t)call_idx, (uint32_t)(call_idx >> 32));
+  return (int64_t)((uint64_t)c[0] % (uint64_t)n);
+}
+
+void malus_rng_reset(uint64_t counter) { t_rng_counter = counter; }
+
+// ------------------------------------------------------ host i32 buffers
+// buffer.rs:11-50: a host Vec<i32>; freeze copies it into an i32 tensor.
+struct HostBuf { std::vector<int32_t> v; };
+
+int64_t malus_buffer_i32(int64_t len) {
+  auto* b = new HostBuf();
+  b->v.assign((size_t)len, 0);
+  return reinterpret_cast<int64_t>(b);
+}
+int64_t malus_buffer_get_i32(int64_t buf, int64_t idx) {
+  auto* b = reinterpret_cast<HostBuf*>(buf);
+  if (idx < 0 || (size_t)idx >= b->v.size()) panic("buffer index %lld out of range", (long long)idx);
+  return b->v[(size_t)idx];
+}
+void malus_buffer_set_i32(int64_t buf, int64_t idx, int64_t val) {
+  auto* b = reinterpret_cast<HostBuf*>(buf);
+  if (idx < 0 || (size_t)idx >= b->v.size()) panic("buffer index %lld out of range", (long long)idx);
+  b->v[(size_t)idx] = (int32_t)val;
+}
+void malus_buffer_free(int64_t buf) { delete reinterpret_cast<HostBuf*>(buf); }
+int64_t malus_buffer_freeze_i32(int64_t buf) {
+  auto* b = reinterpret_cast<HostBuf*>(buf);
+  size_t shape[1] = {b->v.size()};
+  int64_t h = tensor_alloc_gpu(MALUS_I32, shape, 1, reinterpret_cast<const float*>(b->v.data()));
+  return h;
+}
+
+// ------------------------------------------------------------ strings
+// strio.rs: boxed host byte strings (not on the training hot path).
+struct StrBox { std::string s; };
+int64_t malus_str_box(const uint8_t* bytes, size_t len) {
+  auto* s = new StrBox();
+  s->s.assign(reinterpret_cast<const char*>(bytes), len);
+  return reinterpret_cast<int64_t>(s);
+}
+int64_t malus_read_file(int64_t path_box) {
+  auto* p = reinterpret_cast<StrBox*>(path_box);
+  FILE* f = fopen(p->s.c_str(), "rb");
+  if (!f) panic("read_file: cannot open '%s'", p->s.c_str());
+  auto* s = new StrBox();
+  char buf[65536];
+  size_t r;
+  while ((r = fread(buf, 1, sizeof buf, f)) > 0) s->s.append(buf, r);
+  fclose(f);
+  return reinterpret_cast<int64_t>(s);
+}
+int64_t malus_str_len(int64_t s) { return (int64_t)reinterpret_cast<StrBox*>(s)->s.size(); }
+int64_t malus_str_char_at(int64_t s, int64_t i) {
+  auto* b = reinterpret_cast<StrBox*>(s);
+  if (i < 0 || (size_t)i >= b->s.size()) panic("str_char_at index %lld out of range", (long long)i);
+  return (int64_t)(uint8_t)b->s[(size_t)i];
+}
+int64_t malus_str_from_char(int64_t c) {
+  auto* s = new StrBox();
+  s->s.assign(1, (char)c);
+  return reinterpret_cast<int64_t>(s);
+}
+
+// -------------------------------------------------------- counters etc.
+static int64_t g_cpu_compute = 0;   // lib.rs:1-21: this runtime never computes on the CPU
+int64_t malus_cpu_compute_count(void) { return g_cpu_compute; }
+void malus_cpu_compute_reset(void) { g_cpu_compute = 0; }
+
+static float g_gradcheck_max = 0.0f;
+void malus_record_diff(float v) {
+  float a = std::fabs(v);
+  if (a > g_gradcheck_max || std::isnan(a)) g_gradcheck_max = a;
+}
+float malus_gradcheck_max_diff(void) { return g_gradcheck_max; }
+void malus_gradcheck_reset(void) { g_gradcheck_max = 0.0f; }
+
+void malus_rc_counts(int64_t* r, int64_t* rel, int64_t* a) {
+  if (r) *r = g_retains.load();
+  if (rel) *rel = g_releases.load();
+  if (a) *a = g_allocs.load();
+}
+void malus_rc_reset(void) { g_retains = 0; g_releases = 0; g_allocs = 0; }
+
+void malus_pool_stats(int64_t* hits, int64_t* misses, int64_t* pooled, int64_t* peak) {
+  std::lock_guard<std::mutex> lk(g_pool.mu);
+  if (hits) *hits = g_pool.hits;
+  if (misses) *misses = g_pool.misses;
+  if (pooled) *pooled = g_pool.pooled;
+  if (peak) *peak = g_pool.peak;
+}
+void malus_pool_reset(void) {
+  ensure_init();
+  std::lock_guard<std::mutex> lk(g_pool.mu);
+  trim_pool_locked();
+  g_pool.hits = g_pool.misses = 0;
+  g_pool.peak = g_pool.live;
+}
+void malus_set_mem_budget(int64_t bytes) {
+  std::lock_guard<std::mutex> lk(g_pool.mu);
+  g_pool.budget = bytes < 0 ? -1 : bytes;
+}
+
+void* malus_tensor_data(int64_t h) { return vptr(h); }
+int32_t malus_tensor_dtype(int64_t h) { return tb(h)->dtype; }
+void malus_tensor_read(int64_t h, void* dst, size_t bytes) {
+  auto* t = tb(h);
+  size_t have = t->len * dtype_size(t->dtype);
+  if (bytes > have) panic("tensor_read of %zu bytes from a %zu-byte tensor", bytes, have);
+  if (bytes) MALUS_CUDA(cudaMemcpyAsync(dst, t->st->ptr, bytes, cudaMemcpyDeviceToHost, stream()));
+  gpu_barrier();
+}
+void malus_tensor_write(int64_t h, const void* src, size_t bytes) {
+  auto* t = tb(h);
+  size_t have = t->len * dtype_size(t->dtype);
+  if (bytes > have) panic("tensor_write of %zu bytes into a %zu-byte tensor", bytes, have);
+  if (bytes) MALUS_CUDA(cudaMemcpyAsync(t->st->ptr, src, bytes, cudaMemcpyHostToDevice, stream()));
+  gpu_barrier();
+}
+int64_t malus_tensor_wrap(int32_t dtype, void* dev_ptr, const size_t* shape, size_t ndims) {
+  auto* st = new Storage();
+  st->ptr = dev_ptr;
+  st->bytes = 0;
+  st->aliases = 1;
+  st->owned = false;
+  size_t n = 1;
+  for (size_t i = 0; i < ndims; ++i) n *= shape[i];
+  return make_handle(dtype, shape, (int)ndims, st, n);
+}
+void malus_set_device(int32_t dev) {
+  if (g_ctx.init) {
+    if (dev != g_ctx.device) panic("malus_set_device(%d) after the runtime bound device %d", dev, g_ctx.device);
+    return;
+  }
+  char buf[16];
+  snprintf(buf, sizeof buf, "%d", dev);
+  setenv("MALUS_DEVICE", buf, 1);
+  ensure_init();
+}
+int64_t malus_launch_count(void) { return g_launches.load(); }
+void malus_launch_count_reset(void) { g_launches = 0; }
+void* malus_stream(void) { return (void*)stream(); }
+
+int32_t malus_device_error(void) {
+  int32_t v = 0;
+  MALUS_CUDA(cudaMemcpyAsync(&v, device_error_word(), 4, cudaMemcpyDeviceToHost, stream()));
+  gpu_barrier();
+  if (v) MALUS_CUDA(cudaMemsetAsync(device_error_word(), 0, 4, stream()));
+  return v;
+}
+
+// ------------------------------------------------------------- bench timer
+// bench.rs:12-70: dormant unless enabled; each step's end waits for the GPU
+// inside the timed region; report = median of the steps after 3 warm-ups.
+static bool g_bench_on = false;
+static std::vector<double> g_bench_ms;
+static cudaEvent_t g_bench_ev0 = nullptr, g_bench_ev1 = nullptr;
+void bench_enable(void) {
+  g_bench_on = true;
+  if (!g_bench_ev0) {
+    MALUS_CUDA(cudaEventCreate(&g_bench_ev0));
+    MALUS_CUDA(cudaEventCreate(&g_bench_ev1));
+  }
+}
+void bench_step_begin(void) {
+  if (!g_bench_on) return;
+  MALUS_CUDA(cudaEventRecord(g_bench_ev0, stream()));
+}
+void bench_step_end(void) {
+  if (!g_bench_on) return;
+  MALUS_CUDA(cudaEventRecord(g_bench_ev1, stream()));
+  gpu_barrier();
+  float ms = 0;
+  MALUS_CUDA(cudaEventElapsedTime(&ms, g_bench_ev0, g_bench_ev1));
+  g_bench_ms.push_back(ms);
+}
+double bench_report(int64_t* n_steps) {
+  const size_t warm = 3;
+  if (g_bench_ms.size() <= warm) { if (n_steps) *n_steps = 0; return -1.0; }
+  std::vector<double> v(g_bench_ms.begin() + warm, g_bench_ms.end());
+  std::sort(v.begin(), v.end());
+  if (n_steps) *n_steps = (int64_t)v.size();
+  size_t n = v.size();
+  return n % 2 ? v[n / 2] : 0.5 * (v[n / 2 - 1] + v[n / 2]);
+}
+void bench_reset(void) { g_bench_ms.clear(); }
+
+}  // extern "C"
+
+// ------------------------------------------------------ live kernel timing
+// Optional per-kernel-class timing for the bench's roofline figure: when
+// enabled, launches of a class are bracketed by CUDA events on the runtime
+// stream; the report sums the event durations and the algorithmic work the
+// launcher declared.  Classes: 0 = tcgen05 GEMM, 1 = split of GEMM operands,
+// 2 = SIMT GEMM.
+namespace malus {
+namespace {
+struct ProfRec { cudaEvent_t a, b; int cls; double flops, bytes; };
+bool g_prof_on = false;
+std::vector<ProfRec> g_prof;
+std::vector<cudaEvent_t> g_ev_free;
+cudaEvent_t ev_get() {
+  if (!g_ev_free.empty()) { cudaEvent_t e = g_ev_free.back(); g_ev_free.pop_back(); return e; }
+  cudaEvent_t e;
+  MALUS_CUDA(cudaEventCreate(&e));
+  return e;
+}
+}  // namespace
+bool prof_on() { return g_prof_on; }
+int prof_begin(int cls, double flops, double bytes) {
+  if (!g_prof_on) return -1;
+  ProfRec r{ev_get(), ev_get(), cls, flops, bytes};
+  MALUS_CUDA(cudaEventRecord(r.a, stream()));
+  g_prof.push_back(r);
+  return (int)g_prof.size() - 1;
+}
+void prof_end(int id) {
+  if (id < 0) return;
+  MALUS_CUDA(cudaEventRecord(g_prof[id].b, stream()));
+}
+}  // namespace malus
+
+extern "C" {
+void malus_prof_enable(int32_t on) {
+  using namespace malus;
+  gpu_barrier();
+  for (auto& r : g_prof) { g_ev_free.push_back(r.a); g_ev_free.push_back(r.b); }
+  g_prof.clear();
+  g_prof_on = on != 0;
+}
+// Sum over recorded launches of class `cls`: count, total ms, flops, bytes.
+void malus_prof_report(int32_t cls, int64_t* count, double* ms, double* flops, double* bytes) {
+  using namespace malus;
+  gpu_barrier();
+  int64_t n = 0;
+  double t = 0, f = 0, b = 0;
+  for (auto& r : g_prof) {
+    if (r.cls != cls) continue;
+    float x = 0;
+    MALUS_CUDA(cudaEventElapsedTime(&x, r.a, r.b));
+    ++n; t += x; f += r.flops; b += r.bytes;
+  }
+  if (count) *count = n;
+  if (ms) *ms = t;
+  if (flops) *flops = f;
+  if (bytes) *bytes = b;
+}
+}  // extern "C"
