@@ -36,10 +36,16 @@ def _needs(obj: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
+# HBM-bound kernels keep the reference's separate multiply/add rounding
+# (no FMA contraction); it costs nothing when bandwidth is the bound.
+NO_FMAD = {"elementwise", "rows", "reduce"}
+
+
 def _compile(src: Path, verbose: bool) -> Path:
     obj = BUILD / (src.stem + ".o")
-    if _needs(obj, [src] + _headers()):
-        cmd = [NVCC, *ARCH, *CFLAGS, "-c", str(src), "-o", str(obj)]
+    if _needs(obj, [src] + _headers() + [Path(__file__)]):
+        extra = ["-fmad=false"] if src.stem in NO_FMAD else []
+        cmd = [NVCC, *ARCH, *CFLAGS, *extra, "-c", str(src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)

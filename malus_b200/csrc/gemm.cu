@@ -166,13 +166,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t mbar,
-                                            int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      ::"r"(dst), "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1)
-      : "memory");
-}
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t mbar,
                                             int c0, int c1, int c2) {
   asm volatile(
@@ -181,15 +174,28 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// UMMA shared-memory descriptor, 128-byte swizzle (layout type 2), version 1.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// UMMA shared-memory descriptor (version 1).  Layout type 2 is the 128-byte
+// swizzle with 16-byte granules used for K-major tiles; layout type 1 is the
+// 128-byte swizzle with 32-byte granules (4-row atom) that 32-bit (tf32)
+// MN-major tiles require.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFF);
   d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)layout << 61;
   return d;
+}
+// K-major tile: rows of 128 B (32 tf32 along K), 8-row atoms 1 KB apart.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int kk) {
+  return umma_desc(tile + kk * 32, 16, 1024, 2);
+}
+// MN-major tile: 32-element (128 B) MN chunks 4 KB apart (one TMA box each),
+// K rows 128 B apart in 4-row (512 B) atoms; one MMA consumes 8 K rows.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int kk) {
+  return umma_desc(tile + kk * 1024, 4096, 512, 1);
 }
 
 // Instruction descriptor: f32 accumulate, tf32 A/B, M=128, N=BN.
@@ -311,7 +317,6 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32(p.a_mn, p.b_mn);
       bool ok = true;
-      int done = 0;
       for (int kb = 0; kb < nk; ++kb) {
         int s = kb % STAGES;
         uint32_t ph = (uint32_t)((kb / STAGES) & 1);
@@ -322,23 +327,17 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
         uint32_t bh = smem_u32(st + 2 * kTileBytesA), bl = bh + kTileBytesB;
 #pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
-          // K-major: advance 32 B inside the 128-B swizzled row (SBO = 1 KB per 8 rows).
-          // MN-major: advance one 8-row (1 KB) K group; 32-element MN chunks are 4 KB apart.
-          uint32_t offa = p.a_mn ? kk * 1024 : kk * 32;
-          uint32_t offb = p.b_mn ? kk * 1024 : kk * 32;
-          uint64_t dah = p.a_mn ? umma_desc(ah + offa, 4096, 1024) : umma_desc(ah + offa, 16, 1024);
-          uint64_t dal = p.a_mn ? umma_desc(al + offa, 4096, 1024) : umma_desc(al + offa, 16, 1024);
-          uint64_t dbh = p.b_mn ? umma_desc(bh + offb, 4096, 1024) : umma_desc(bh + offb, 16, 1024);
-          uint64_t dbl = p.b_mn ? umma_desc(bl + offb, 4096, 1024) : umma_desc(bl + offb, 16, 1024);
+          uint64_t dah = p.a_mn ? desc_mnmajor(ah, kk) : desc_kmajor(ah, kk);
+          uint64_t dal = p.a_mn ? desc_mnmajor(al, kk) : desc_kmajor(al, kk);
+          uint64_t dbh = p.b_mn ? desc_mnmajor(bh, kk) : desc_kmajor(bh, kk);
+          uint64_t dbl = p.b_mn ? desc_mnmajor(bl, kk) : desc_kmajor(bl, kk);
           uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
           mma_tf32(tmem, dal, dbh, idesc, acc0);   // small terms first
           mma_tf32(tmem, dah, dbl, idesc, 1u);
           mma_tf32(tmem, dah, dbh, idesc, 1u);
         }
         mma_commit(smem_u32(&empty[s]));   // frees the stage when these MMAs finish
-        done = kb + 1;
       }
-      (void)done;
       // Signal the epilogue (also on abort, so no MMA is in flight at exit).
       mma_commit(smem_u32(accb));
       if (!ok) {
@@ -448,16 +447,18 @@ void load_encoder() {
   });
 }
 
-// 3-D f32 map {d0 (contiguous), d1, d2}, box {b0, b1, 1}, 128-B swizzle.
+// 3-D f32 map {d0 (contiguous), d1, d2}, box {b0, b1, 1}, 128-B swizzle with
+// 16-byte granules (K-major tiles) or 32-byte granules (MN-major tiles).
 CUtensorMap make_map(const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t pitch_bytes,
-                     uint64_t plane_bytes, uint32_t b0, uint32_t b1) {
+                     uint64_t plane_bytes, uint32_t b0, uint32_t b1, bool mn_major) {
   CUtensorMap m;
   cuuint64_t dims[3] = {d0, d1, d2};
   cuuint64_t strides[2] = {pitch_bytes, plane_bytes};
   cuuint32_t box[3] = {b0, b1, 1};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) panic("cuTensorMapEncodeTiled failed (%d)", (int)r);
   return m;
@@ -511,18 +512,18 @@ static void gemm_tc(const GemmArgs& g) {
   CUtensorMap mah, mal, mbh, mbl;
   uint64_t apb = (uint64_t)ap * 4, bpb = (uint64_t)bp * 4;
   if (!a_mn) {
-    mah = make_map(ah, ac, ar, abatch, apb, apb * ar, 32, BM);
-    mal = make_map(al, ac, ar, abatch, apb, apb * ar, 32, BM);
+    mah = make_map(ah, ac, ar, abatch, apb, apb * ar, 32, BM, false);
+    mal = make_map(al, ac, ar, abatch, apb, apb * ar, 32, BM, false);
   } else {
-    mah = make_map(ah, ac, ar, abatch, apb, apb * ar, 32, 32);
-    mal = make_map(al, ac, ar, abatch, apb, apb * ar, 32, 32);
+    mah = make_map(ah, ac, ar, abatch, apb, apb * ar, 32, 32, true);
+    mal = make_map(al, ac, ar, abatch, apb, apb * ar, 32, 32, true);
   }
   if (!b_mn) {
-    mbh = make_map(bh, bc, br, bbatch, bpb, bpb * br, 32, BN);
-    mbl = make_map(bl, bc, br, bbatch, bpb, bpb * br, 32, BN);
+    mbh = make_map(bh, bc, br, bbatch, bpb, bpb * br, 32, BN, false);
+    mbl = make_map(bl, bc, br, bbatch, bpb, bpb * br, 32, BN, false);
   } else {
-    mbh = make_map(bh, bc, br, bbatch, bpb, bpb * br, 32, 32);
-    mbl = make_map(bl, bc, br, bbatch, bpb, bpb * br, 32, 32);
+    mbh = make_map(bh, bc, br, bbatch, bpb, bpb * br, 32, 32, true);
+    mbl = make_map(bl, bc, br, bbatch, bpb, bpb * br, 32, 32, true);
   }
   TcParams p;
   p.M = g.M; p.N = g.N; p.K = g.K;

@@ -17,8 +17,12 @@ G = json.loads((Path(__file__).parent / "golden" / "reference_golden.json").read
 ADD, SUB, MUL, DIV, SIGMOID, RELU, ABS, SUM, TRANSPOSE, MATMUL = 1, 2, 3, 4, 5, 6, 11, 12, 13, 0
 
 
+_LIVE = []  # keeps tensors alive until the test ends (inline temporaries would be freed early)
+
+
 def T(M, a, leaf=False, rt=None):
     t = M.Tensor.from_numpy(np.asarray(a, np.float32))
+    _LIVE.append(t)
     if leaf:
         rt.tape_register_leaf(t.h)
     return t
@@ -33,6 +37,7 @@ def reset(rt):
     rt.malus_tape_reset()
     yield
     rt.malus_tape_reset()
+    _LIVE.clear()
 
 
 @pytest.mark.parametrize("name,tag", [("backward_add", ADD), ("backward_sub", SUB),
