@@ -307,6 +307,26 @@ int32_t malus_device_error(void);
 void malus_prof_enable(int32_t on);
 void malus_prof_report(int32_t cls, int64_t* count, double* ms, double* flops, double* bytes);
 
+/* Embedding backward that allocates nothing.  This entry point has no
+ * counterpart in the reference.  It is for callers that cannot call cudaMalloc
+ * where they need the op (inside a stream capture that must not gain memory
+ * nodes, inside another framework's memory arena, or under a fully committed
+ * memory budget).  It computes dweight[vocab, dim] from dout[n, dim] and
+ * indices[n] (i32 when index_dtype is 5, i64 when 6) with the same
+ * deterministic sort-then-segmented-sum as __embedding_bwd, on the caller's
+ * stream (NULL = the legacy default stream).  All inputs and the output are
+ * caller-owned device pointers; the scratch is a fixed 4,982,016-byte device array
+ * inside this library, present on every GPU that loads it until the process
+ * exits.  Limits: n <= 65536 and vocab * ceil(n / 1024) <= 524288; larger
+ * sizes return a negative error with a message on stderr.  The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  All calls share the array, so
+ * calls that overlap on the GPU race; ordered calls (one stream) are safe.
+ * Returns 0 on success. */
+int32_t malus_embedding_bwd_noalloc(const float* dout, const void* indices, int32_t index_dtype,
+                                    size_t n, size_t vocab, size_t dim, float* dweight,
+                                    void* stream);
+
 #ifdef __cplusplus
 }
 #endif

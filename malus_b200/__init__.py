@@ -174,6 +174,7 @@ SIGNATURES: dict[str, tuple] = {
     "malus_gpt_num_elements": (i64, [i64]),
     "malus_device_error": (i32, []),
     "malus_prof_enable": (None, [i32]),
+    "malus_embedding_bwd_noalloc": (i32, [vp, vp, i32, sz, sz, sz, vp, vp]),
     "malus_prof_report": (None, [i32, P_i64, C.POINTER(C.c_double), C.POINTER(C.c_double),
                                  C.POINTER(C.c_double)]),
 }

@@ -143,6 +143,9 @@ void embedding_fwd(const float* w, const void* idx, int idx_dtype, float* out, s
 void embedding_bwd(const float* dout, const void* idx, int idx_dtype, float* dw, size_t n,
                    size_t vocab, size_t dim);
 void permute_nd(const float* x, float* out, const Shape& in_shape, const int* perm);
+size_t embedding_bwd_ws_bytes(size_t n, size_t vocab);
+int embedding_bwd_ws(const float* dout, const void* idx, int idx_dtype, float* dw, size_t n,
+                     size_t vocab, size_t dim, void* workspace, cudaStream_t st);
 
 // ---- GEMM (gemm.cu) ----
 // C[b] (MxN) = alpha * op(A[b]) * op(B[b]) + beta * C[b], f32 semantics via
