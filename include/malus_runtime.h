@@ -297,6 +297,39 @@ int32_t malus_gpt_num_params(int64_t model);
 int64_t malus_gpt_param(int64_t model, int32_t i);
 int64_t malus_gpt_num_elements(int64_t model);
 
+/* tcgen05 3xTF32 GEMM on pre-split tf32 operand planes, with fused epilogues.
+ * Each f32 operand x is given as two planes hi = tf32_rn(x), lo = tf32_rn(x -
+ * hi) (malus_tf32_split makes them).  An operand is a stack of nz row-major
+ * slices of rows x cols (row pitch in floats, multiple of 4; slice stride
+ * zstride): K-major operands are stored {rows = M (or N), cols = K}, MN-major
+ * ones {rows = K, cols = M (or N)}.  zmode picks the slice for each tile:
+ * 0 none, 1 the problem batch index, 2 k / seg, 3 m-or-n / seg.  The output
+ * element (z, m, n) lives at oz(z) + om(m) + on(n), each term
+ * (i / div) * hi + (i % div) * lo (div 0: i * lo).  Epilogues: 0 store
+ * (alpha, beta), 1 residual add (out = aux + acc), 2 GELU (out = acc, planes
+ * of gelu(acc)), 3 GELU derivative (planes of acc * gelu'(aux)); out_hi/out_lo,
+ * when set, receive the tf32 planes of the stored value.  New in this build (the
+ * reference's matmul is an MPS call, metal.rs:805-962). */
+typedef struct malus_tc_operand {
+  const float* hi; const float* lo;
+  int64_t rows, cols, pitch;
+  int32_t nz; int64_t zstride;
+  int32_t mn_major, zmode, seg;
+} malus_tc_operand;
+typedef struct malus_tc_layout { int64_t d1, s1, d2, s2, s3; } malus_tc_layout;
+typedef struct malus_tc_problem {
+  int32_t M, N, K, batch;
+  malus_tc_operand a, b;
+  int32_t epi;
+  malus_tc_layout oz, om, on;
+  float* out; float* out_hi; float* out_lo;
+  const float* aux;
+  float alpha, beta;
+} malus_tc_problem;
+void malus_tc_gemm(const malus_tc_problem* p);
+void malus_tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t batch,
+                      int64_t sstride, float* hi, float* lo, int64_t pitch);
+
 /* Device diagnostics: last asynchronous error word written by a kernel whose
  * bounded wait ran out (0 = none); cleared by reading. */
 int32_t malus_device_error(void);

@@ -23,6 +23,21 @@ P_sz, P_i64, P_u64, P_f32, P_u8, P_i32 = (C.POINTER(C.c_size_t), C.POINTER(C.c_i
                                           C.POINTER(C.c_uint8), C.POINTER(C.c_int32))
 
 
+class TcOperand(C.Structure):
+    _fields_ = [("hi", vp), ("lo", vp), ("rows", i64), ("cols", i64), ("pitch", i64),
+                ("nz", i32), ("zstride", i64), ("mn_major", i32), ("zmode", i32), ("seg", i32)]
+
+
+class TcLayout(C.Structure):
+    _fields_ = [("d1", i64), ("s1", i64), ("d2", i64), ("s2", i64), ("s3", i64)]
+
+
+class TcProblem(C.Structure):
+    _fields_ = [("M", i32), ("N", i32), ("K", i32), ("batch", i32), ("a", TcOperand), ("b", TcOperand),
+                ("epi", i32), ("oz", TcLayout), ("om", TcLayout), ("on", TcLayout),
+                ("out", vp), ("out_hi", vp), ("out_lo", vp), ("aux", vp), ("alpha", f32), ("beta", f32)]
+
+
 class GptConfig(C.Structure):
     _fields_ = [("vocab", i32), ("n_layer", i32), ("n_head", i32), ("n_embd", i32),
                 ("block_size", i32), ("batch", i32), ("tied", i32),
@@ -173,6 +188,8 @@ SIGNATURES: dict[str, tuple] = {
     "malus_gpt_param": (i64, [i64, i32]),
     "malus_gpt_num_elements": (i64, [i64]),
     "malus_device_error": (i32, []),
+    "malus_tc_gemm": (None, [C.POINTER(TcProblem)]),
+    "malus_tf32_split": (None, [vp, i64, i64, i64, i64, i64, vp, vp, i64]),
     "malus_prof_enable": (None, [i32]),
     "malus_embedding_bwd_noalloc": (i32, [vp, vp, i32, sz, sz, sz, vp, vp]),
     "malus_prof_report": (None, [i32, P_i64, C.POINTER(C.c_double), C.POINTER(C.c_double),

@@ -160,6 +160,45 @@ struct GemmArgs {
   float alpha = 1.f, beta = 0.f;
 };
 void gemm(const GemmArgs& g);
+
+// Low-level tcgen05 GEMM on pre-split tf32 planes (hi/lo), for callers that
+// produce their operands already split.  Each operand is a stack of nz
+// row-major slices (rows x cols, row pitch in floats, slice stride zstride);
+// a K-major operand is stored {rows = M or N, cols = K}, an MN-major one
+// {rows = K, cols = M or N}.  zmode selects what the third TMA coordinate
+// follows: nothing, the problem batch index, k / seg (K segments spread over
+// slices) or mn / seg (M or N segments spread over slices).
+enum TcZMode : int { kZNone = 0, kZBatch = 1, kZKSeg = 2, kZMNSeg = 3 };
+struct TcOperand {
+  const float* hi;
+  const float* lo;
+  int64_t rows, cols, pitch;
+  int nz;
+  int64_t zstride;
+  bool mn_major;
+  int zmode;
+  int seg;
+};
+// out offset = Z(z) + R(m) + Cc(n); each term maps an index i through two
+// optional divisions: q1 = i / d1, r1 = i % d1 (d1 = 0: q1 = 0, r1 = i);
+// q2 = r1 / d2, r2 = r1 % d2 (d2 = 0: q2 = 0, r2 = r1); term = q1*s1 + q2*s2 + r2*s3.
+struct TcLayout { int64_t d1, s1, d2, s2, s3; };
+enum TcEpi : int { kEpiStore = 0, kEpiResid = 1, kEpiGelu = 2, kEpiGeluBwd = 3 };
+struct TcProblem {
+  int M, N, K, batch;
+  TcOperand a, b;
+  int epi;
+  TcLayout oz, om, on;
+  float* out;       // f32 output (Store/Resid: result; Gelu: pre-activation; GeluBwd: optional)
+  float* out_hi;    // optional tf32 planes of the result (Gelu/GeluBwd: of the activation/derivative)
+  float* out_lo;
+  const float* aux; // Resid: residual input; GeluBwd: pre-activation
+  float alpha = 1.f, beta = 0.f;
+};
+void gemm_tc_planes(const TcProblem& p);
+// hi/lo planes of a stack of `batch` row-major slices (rows x cols, ld, sstride)
+void tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t batch,
+                int64_t sstride, float* hi, float* lo, int64_t pitch);
 void gemm_simt(const GemmArgs& g);
 int gemm_backend_for(const GemmArgs& g);   // 0 = SIMT, 1 = tcgen05
 void gemm_force_backend(int b);            // -1 = auto (tests)

@@ -115,6 +115,21 @@ void gemm_simt(const GemmArgs& g) {
 }
 
 // =============================================================== tcgen05
+//
+// Persistent 3xTF32 GEMM.  One CTA per SM walks a static list of 128x128
+// output tiles.  Warp 0 streams operand tiles with TMA into a 3-stage
+// shared-memory ring, warp 1 issues tcgen05.mma into one of two TMEM
+// accumulators (2 x 128 columns), and warps 2-5 drain the other accumulator
+// (tcgen05.ld -> registers -> global) while the next tile is being computed.
+// Each f32 operand arrives as two tf32 planes (hi = rn(x), lo = rn(x - hi));
+// the accumulator receives lo*hi + hi*lo + hi*hi per k-step.
+//
+// The epilogue writes through a mixed-radix address map out(z, m, n) =
+// Z(z) + Mr(m) + Nc(n), each term (i / div) * hi + (i % div) * lo, which
+// expresses plain row-major outputs, batched outputs, the attention head
+// fold/unfold and N-segmented outputs without extra copies; and it can fuse a
+// residual add, GELU (storing the pre-activation), the GELU derivative, and
+// the tf32 split of its own output (so the next GEMM reads ready planes).
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
@@ -123,7 +138,9 @@ constexpr int kTileBytesB = BN * BK * 4;  // 16 KB
 constexpr int kStageBytes = 2 * kTileBytesA + 2 * kTileBytesB;
 constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 constexpr int kThreadsTC = 192;   // warp0 TMA, warp1 MMA+TMEM, warps2-5 epilogue
+constexpr uint32_t kTmemCols = 2 * BN;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on every wait
+constexpr float kGeluC0 = 0.7978845608028654f, kGeluC1 = 0.044715f;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -161,6 +178,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile 
       return false;
     }
   }
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t a) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes)
@@ -217,48 +237,149 @@ __device__ __forceinline__ void mma_commit(uint32_t mbar) {
       : "memory");
 }
 
-struct TcParams {
-  int M, N, K;
-  bool a_mn, b_mn;          // operand is MN-major (stored transposed)
-  bool a_batched, b_batched;
-  float* C;
-  int64_t ldc, strideC;
-  float alpha, beta;
+__device__ __forceinline__ float tf32_rn(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+__device__ __forceinline__ int64_t lay(const TcLayout& L, int64_t i) {
+  int64_t off = 0;
+  if (L.d1) { off = (i / L.d1) * L.s1; i %= L.d1; }
+  if (L.d2) { off += (i / L.d2) * L.s2; i %= L.d2; }
+  return off + i * L.s3;
+}
+
+struct TcKernelParams {
+  TcProblem pr;
+  int tiles_m, tiles_n, nk;
   int32_t* err;
 };
 
-// A map: K-major -> dims {K, M, batch}, box {32, 128, 1}
-//        MN-major -> dims {M, K, batch}, box {32, 32, 1} issued BM/32 times
+// Operand coordinates for k-block k0 of tile (z, m0/n0).
+__device__ __forceinline__ void operand_coords(int zmode, int seg, int z, int k0, int mn0,
+                                               int* kc, int* mnc, int* zc) {
+  *kc = k0;
+  *mnc = mn0;
+  *zc = 0;
+  if (zmode == kZBatch) *zc = z;
+  else if (zmode == kZKSeg) { *zc = k0 / seg; *kc = k0 % seg; }
+  else if (zmode == kZMNSeg) { *zc = mn0 / seg; *mnc = mn0 % seg; }
+}
+
+
+__device__ __forceinline__ float gelu_f(float v) {
+  float x3 = v * v * v;
+  return 0.5f * v * (1.0f + tanhf(kGeluC0 * (v + kGeluC1 * x3)));
+}
+__device__ __forceinline__ float gelu_grad(float x) {
+  float x3 = x * x * x;
+  float t = tanhf(kGeluC0 * (x + kGeluC1 * x3));
+  float gp = kGeluC0 * (1.0f + 3.0f * kGeluC1 * x * x);
+  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * gp;
+}
+
+// One output element: value v (the accumulator) at offset o.
+template <int EPI>
+__device__ __forceinline__ void epi_store1(const TcProblem& p, int64_t o, float v) {
+  if (p.alpha != 1.0f) v *= p.alpha;
+  float split_src;
+  if (EPI == kEpiStore) {
+    if (p.beta != 0.0f) v += p.beta * p.out[o];
+    p.out[o] = v;
+    split_src = v;
+  } else if (EPI == kEpiResid) {
+    v = p.aux[o] + v;
+    p.out[o] = v;
+    split_src = v;
+  } else if (EPI == kEpiGelu) {
+    p.out[o] = v;                 // pre-activation, kept for the GELU derivative
+    split_src = gelu_f(v);
+  } else {                        // kEpiGeluBwd: v = dL/d(gelu out); aux = pre-activation
+    split_src = v * gelu_grad(p.aux[o]);
+    if (p.out) p.out[o] = split_src;
+  }
+  if (p.out_hi) {
+    float h = tf32_rn(split_src);
+    p.out_hi[o] = h;
+    p.out_lo[o] = tf32_rn(split_src - h);
+  }
+}
+
+// Four consecutive output elements at 16-byte aligned offset o.
+template <int EPI>
+__device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4 v) {
+  if (p.alpha != 1.0f) { v.x *= p.alpha; v.y *= p.alpha; v.z *= p.alpha; v.w *= p.alpha; }
+  float4 s;
+  if (EPI == kEpiStore) {
+    if (p.beta != 0.0f) {
+      float4 q = *reinterpret_cast<const float4*>(p.out + o);
+      v.x += p.beta * q.x; v.y += p.beta * q.y; v.z += p.beta * q.z; v.w += p.beta * q.w;
+    }
+    *reinterpret_cast<float4*>(p.out + o) = v;
+    s = v;
+  } else if (EPI == kEpiResid) {
+    float4 q = *reinterpret_cast<const float4*>(p.aux + o);
+    v.x = q.x + v.x; v.y = q.y + v.y; v.z = q.z + v.z; v.w = q.w + v.w;
+    *reinterpret_cast<float4*>(p.out + o) = v;
+    s = v;
+  } else if (EPI == kEpiGelu) {
+    *reinterpret_cast<float4*>(p.out + o) = v;
+    s = make_float4(gelu_f(v.x), gelu_f(v.y), gelu_f(v.z), gelu_f(v.w));
+  } else {
+    float4 x = *reinterpret_cast<const float4*>(p.aux + o);
+    s = make_float4(v.x * gelu_grad(x.x), v.y * gelu_grad(x.y), v.z * gelu_grad(x.z),
+                    v.w * gelu_grad(x.w));
+    if (p.out) *reinterpret_cast<float4*>(p.out + o) = s;
+  }
+  if (p.out_hi) {
+    float4 h = make_float4(tf32_rn(s.x), tf32_rn(s.y), tf32_rn(s.z), tf32_rn(s.w));
+    float4 l = make_float4(tf32_rn(s.x - h.x), tf32_rn(s.y - h.y), tf32_rn(s.z - h.z),
+                           tf32_rn(s.w - h.w));
+    *reinterpret_cast<float4*>(p.out_hi + o) = h;
+    *reinterpret_cast<float4*>(p.out_lo + o) = l;
+  }
+}
+
+template <int EPI>
 __global__ void __launch_bounds__(kThreadsTC, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
           const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
-          TcParams p) {
+          const TcKernelParams kp) {
   extern __shared__ uint8_t smem_raw[];
+  const TcProblem& p = kp.pr;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* bar_area = smem + STAGES * kStageBytes;
   uint64_t* full = (uint64_t*)bar_area;
   uint64_t* empty = full + STAGES;
-  uint64_t* accb = empty + STAGES;
-  uint32_t* tmem_slot = (uint32_t*)(accb + 1);
+  uint64_t* accf = empty + STAGES;
+  uint64_t* acce = accf + 2;
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
-  const int nk = (p.K + BK - 1) / BK;
+  const int per_batch = kp.tiles_m * kp.tiles_n;
+  const int total = per_batch * p.batch;
+  const int nk = kp.nk;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    mbar_init(smem_u32(accb), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&accf[b]), 1);
+      mbar_init(smem_u32(&acce[b]), 4);
+    }
+    mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"((uint32_t)BN));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -269,96 +390,117 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        int s = kb % STAGES;
-        uint32_t ph = (uint32_t)((kb / STAGES) & 1);
-        if (kb >= STAGES) {
-          if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err, 11)) break;
-        }
-        uint8_t* st = smem + s * kStageBytes;
-        uint32_t fb = smem_u32(&full[s]);
-        mbar_expect_tx(fb, kStageBytes);
-        int k0 = kb * BK;
-        int za = p.a_batched ? bz : 0, zb = p.b_batched ? bz : 0;
-        if (!p.a_mn) {
-          tma_load_3d(smem_u32(st), &mAh, fb, k0, m0, za);
-          tma_load_3d(smem_u32(st + kTileBytesA), &mAl, fb, k0, m0, za);
-        } else {
-          for (int j = 0; j < BM / 32; ++j) {
-            tma_load_3d(smem_u32(st + j * 4096), &mAh, fb, m0 + 32 * j, k0, za);
-            tma_load_3d(smem_u32(st + kTileBytesA + j * 4096), &mAl, fb, m0 + 32 * j, k0, za);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        int z = tile / per_batch, rem = tile % per_batch;
+        int m0 = (rem / kp.tiles_n) * BM, n0 = (rem % kp.tiles_n) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          int s = it % STAGES;
+          uint32_t ph = (it / STAGES) & 1;
+          if (it >= STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, kp.err, 11)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * kStageBytes;
+          uint32_t fb = smem_u32(&full[s]);
+          mbar_expect_tx(fb, kStageBytes);
+          int k0 = kb * BK, kc, mnc, zc;
+          operand_coords(p.a.zmode, p.a.seg, z, k0, m0, &kc, &mnc, &zc);
+          if (!p.a.mn_major) {
+            tma_load_3d(smem_u32(st), &mAh, fb, kc, mnc, zc);
+            tma_load_3d(smem_u32(st + kTileBytesA), &mAl, fb, kc, mnc, zc);
+          } else {
+            for (int j = 0; j < BM / 32; ++j) {
+              tma_load_3d(smem_u32(st + j * 4096), &mAh, fb, mnc + 32 * j, kc, zc);
+              tma_load_3d(smem_u32(st + kTileBytesA + j * 4096), &mAl, fb, mnc + 32 * j, kc, zc);
+            }
+          }
+          uint8_t* sb = st + 2 * kTileBytesA;
+          operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
+          if (!p.b.mn_major) {
+            tma_load_3d(smem_u32(sb), &mBh, fb, kc, mnc, zc);
+            tma_load_3d(smem_u32(sb + kTileBytesB), &mBl, fb, kc, mnc, zc);
+          } else {
+            for (int j = 0; j < BN / 32; ++j) {
+              tma_load_3d(smem_u32(sb + j * 4096), &mBh, fb, mnc + 32 * j, kc, zc);
+              tma_load_3d(smem_u32(sb + kTileBytesB + j * 4096), &mBl, fb, mnc + 32 * j, kc, zc);
+            }
           }
         }
-        uint8_t* sb = st + 2 * kTileBytesA;
-        if (!p.b_mn) {
-          tma_load_3d(smem_u32(sb), &mBh, fb, k0, n0, zb);
-          tma_load_3d(smem_u32(sb + kTileBytesB), &mBl, fb, k0, n0, zb);
-        } else {
-          for (int j = 0; j < BN / 32; ++j) {
-            tma_load_3d(smem_u32(sb + j * 4096), &mBh, fb, n0 + 32 * j, k0, zb);
-            tma_load_3d(smem_u32(sb + kTileBytesB + j * 4096), &mBl, fb, n0 + 32 * j, k0, zb);
-          }
-        }
-        issued = kb + 1;
       }
-      // Drain: every stage that was filled must have landed before exit.
       if (*abort_flag) {
-        for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb) {
-          int s = kb % STAGES;
-          uint32_t ph = (uint32_t)((kb / STAGES) & 1);
+        // every issued stage must land before the CTA exits
+        uint32_t lo = it > (uint32_t)STAGES ? it - STAGES : 0;
+        for (uint32_t q = lo; q < it; ++q) {
           uint64_t t0 = gtimer();
-          while (!mbar_try(smem_u32(&full[s]), ph) && gtimer() - t0 < kWaitNs) {}
+          while (!mbar_try(smem_u32(&full[q % STAGES]), (q / STAGES) & 1) && gtimer() - t0 < kWaitNs) {}
         }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(p.a_mn, p.b_mn);
-      bool ok = true;
-      for (int kb = 0; kb < nk; ++kb) {
-        int s = kb % STAGES;
-        uint32_t ph = (uint32_t)((kb / STAGES) & 1);
-        if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.err, 12)) { ok = false; break; }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        uint8_t* st = smem + s * kStageBytes;
-        uint32_t ah = smem_u32(st), al = smem_u32(st + kTileBytesA);
-        uint32_t bh = smem_u32(st + 2 * kTileBytesA), bl = bh + kTileBytesB;
-#pragma unroll
-        for (int kk = 0; kk < BK / 8; ++kk) {
-          uint64_t dah = p.a_mn ? desc_mnmajor(ah, kk) : desc_kmajor(ah, kk);
-          uint64_t dal = p.a_mn ? desc_mnmajor(al, kk) : desc_kmajor(al, kk);
-          uint64_t dbh = p.b_mn ? desc_mnmajor(bh, kk) : desc_kmajor(bh, kk);
-          uint64_t dbl = p.b_mn ? desc_mnmajor(bl, kk) : desc_kmajor(bl, kk);
-          uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
-          mma_tf32(tmem, dal, dbh, idesc, acc0);   // small terms first
-          mma_tf32(tmem, dah, dbl, idesc, 1u);
-          mma_tf32(tmem, dah, dbh, idesc, 1u);
+      const uint32_t idesc = idesc_tf32(p.a.mn_major, p.b.mn_major);
+      uint32_t it = 0, local = 0;
+      bool ok = true, issued = false;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++local) {
+        uint32_t b = local & 1, u = local >> 1;
+        if (u >= 1 && !mbar_wait(smem_u32(&acce[b]), (u - 1) & 1, abort_flag, kp.err, 14)) {
+          ok = false;
+          break;
         }
-        mma_commit(smem_u32(&empty[s]));   // frees the stage when these MMAs finish
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t dacc = tmem + b * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          int s = it % STAGES;
+          uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, kp.err, 12)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          uint8_t* st = smem + s * kStageBytes;
+          uint32_t ah = smem_u32(st), al = smem_u32(st + kTileBytesA);
+          uint32_t bh = smem_u32(st + 2 * kTileBytesA), bl = bh + kTileBytesB;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            uint64_t dah = p.a.mn_major ? desc_mnmajor(ah, kk) : desc_kmajor(ah, kk);
+            uint64_t dal = p.a.mn_major ? desc_mnmajor(al, kk) : desc_kmajor(al, kk);
+            uint64_t dbh = p.b.mn_major ? desc_mnmajor(bh, kk) : desc_kmajor(bh, kk);
+            uint64_t dbl = p.b.mn_major ? desc_mnmajor(bl, kk) : desc_kmajor(bl, kk);
+            uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
+            mma_tf32(dacc, dal, dbh, idesc, acc0);   // small terms first
+            mma_tf32(dacc, dah, dbl, idesc, 1u);
+            mma_tf32(dacc, dah, dbh, idesc, 1u);
+          }
+          issued = true;
+          mma_commit(smem_u32(&empty[s]));   // frees the stage when these MMAs finish
+        }
+        if (ok) mma_commit(smem_u32(&accf[b]));
       }
-      // Signal the epilogue (also on abort, so no MMA is in flight at exit).
-      mma_commit(smem_u32(accb));
-      if (!ok) {
+      if (!ok && issued) {
+        // no MMA may be in flight when TMEM is freed
+        mma_commit(smem_u32(drain));
         uint64_t t0 = gtimer();
-        while (!mbar_try(smem_u32(accb), 0) && gtimer() - t0 < kWaitNs) {}
+        while (!mbar_try(smem_u32(drain), 0) && gtimer() - t0 < kWaitNs) {}
       }
+      if (!ok) *abort_flag = 1;
     }
   } else {
     // ---------------- epilogue: TMEM -> registers -> global ----------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
-    bool ok = mbar_wait(smem_u32(accb), 0, abort_flag, p.err, 13);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ok && !*abort_flag) {
+    uint32_t local = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+      uint32_t b = local & 1, u = local >> 1;
+      if (!mbar_wait(smem_u32(&accf[b]), u & 1, abort_flag, kp.err, 13)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      int z = tile / per_batch, rem = tile % per_batch;
+      int m0 = (rem / kp.tiles_n) * BM, n0 = (rem % kp.tiles_n) * BN;
       const int m = m0 + row;
-      float* crow = p.C + (int64_t)bz * p.strideC + (int64_t)m * p.ldc;
-      const bool vec = (p.ldc % 4 == 0) && ((((uintptr_t)p.C) & 15) == 0) && (p.strideC % 4 == 0);
+      const int64_t zm_off = lay(p.oz, z) + lay(p.om, m);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
-        uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
+        uint32_t taddr = tmem + b * BN + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
             "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -372,33 +514,33 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         if (m < p.M) {
           const int nb = n0 + c0;
-          if (vec && nb + 32 <= p.N) {
+          // contiguous run of 32 columns when the column map is unit-stride inside
+          // 32-aligned groups
+          const bool contig = (p.on.d1 % 32 == 0) && (p.on.d2 % 32 == 0) && p.on.s3 == 1;
+          const int64_t base = zm_off + lay(p.on, nb);
+          const bool vec = contig && nb + 32 <= p.N && (base & 3) == 0;
+          if (vec) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
               float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
                                      __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-              float4* dst = reinterpret_cast<float4*>(crow + nb + j);
-              if (p.alpha != 1.0f) { v.x *= p.alpha; v.y *= p.alpha; v.z *= p.alpha; v.w *= p.alpha; }
-              if (p.beta != 0.0f) {
-                float4 o = *dst;
-                v.x += p.beta * o.x; v.y += p.beta * o.y; v.z += p.beta * o.z; v.w += p.beta * o.w;
-              }
-              *dst = v;
+              epi_store4<EPI>(p, base + j, v);
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               int n = nb + j;
               if (n < p.N) {
-                float v = __uint_as_float(r[j]);
-                if (p.alpha != 1.0f) v *= p.alpha;
-                if (p.beta != 0.0f) v += p.beta * crow[n];
-                crow[n] = v;
+                int64_t o = contig ? base + j : zm_off + lay(p.on, n);
+                epi_store1<EPI>(p, o, __uint_as_float(r[j]));
               }
             }
           }
         }
       }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acce[b]));
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -406,31 +548,36 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"((uint32_t)BN));
+                 "r"(kTmemCols));
   }
 }
 
-// ---- operand split: hi = tf32_rn(x), lo = tf32_rn(x - hi), padded pitch ----
-__device__ __forceinline__ float tf32_rn(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-
-__global__ void k_split_tf32(const float* __restrict__ src, int64_t rows, int64_t cols,
-                             int64_t ld, int64_t sstride, float* __restrict__ hi,
-                             float* __restrict__ lo, int64_t pitch, int64_t total) {
-  int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  int64_t step = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t f = tid; f < total; f += step) {
-    int64_t c = f % pitch;
-    int64_t rb = f / pitch;        // batch*rows + r
-    int64_t r = rb % rows, b = rb / rows;
-    float x = c < cols ? src[b * sstride + r * ld + c] : 0.0f;
-    float h = tf32_rn(x);
-    hi[f] = h;
-    lo[f] = tf32_rn(x - h);
+// ---- operand split: hi = tf32_rn(x), lo = tf32_rn(x - hi); one block per
+// row chunk of 1024 columns, pitch padded to a multiple of 4 (zero-filled) ----
+__global__ void k_split_tf32(const float* __restrict__ src, int64_t rows, int64_t cols, int64_t ld,
+                             int64_t sstride, float* __restrict__ hi, float* __restrict__ lo,
+                             int64_t pitch, bool vec) {
+  int64_t row = blockIdx.x;                 // batch * rows + r
+  int64_t c = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * 4;
+  if (c >= pitch) return;
+  int64_t b = row / rows, r = row - b * rows;
+  const float* s = src + b * sstride + r * ld;
+  float x[4];
+  if (vec && c + 4 <= cols) {
+    float4 v = *reinterpret_cast<const float4*>(s + c);
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) x[q] = c + q < cols ? s[c + q] : 0.0f;
   }
+  float h[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    h[q] = tf32_rn(x[q]);
+    l[q] = tf32_rn(x[q] - h[q]);
+  }
+  *reinterpret_cast<float4*>(hi + row * pitch + c) = make_float4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<float4*>(lo + row * pitch + c) = make_float4(l[0], l[1], l[2], l[3]);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -464,7 +611,30 @@ CUtensorMap make_map(const float* base, uint64_t d0, uint64_t d1, uint64_t d2, u
   return m;
 }
 
+// Map of one operand plane.  Stored matrix: nz slices of rows x cols with the
+// given pitch; K-major operands are {cols=K, rows=MN}, MN-major {cols=MN, rows=K}.
+CUtensorMap operand_map(const TcOperand& o, const float* plane) {
+  uint64_t pb = (uint64_t)o.pitch * 4;
+  uint64_t zb = (uint64_t)o.zstride * 4;
+  if (o.nz > 1 && (zb % 16 != 0)) panic("gemm operand slice stride %lld is not 16-byte aligned", (long long)o.zstride);
+  if (o.nz <= 1) zb = pb * (uint64_t)o.rows;
+  return make_map(plane, (uint64_t)o.cols, (uint64_t)o.rows, (uint64_t)std::max(1, o.nz), pb,
+                  std::max<uint64_t>(zb, 16), 32, o.mn_major ? 32 : BM, o.mn_major);
+}
+
 int g_force_backend = -1;
+
+template <int EPI>
+void launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
+               const CUtensorMap& bl, const TcKernelParams& kp, int grid) {
+  static bool attr = false;
+  if (!attr) {
+    MALUS_CUDA(cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kSmemBytes));
+    attr = true;
+  }
+  k_gemm_tc<EPI><<<grid, kThreadsTC, kSmemBytes, stream()>>>(ah, al, bh, bl, kp);
+}
 
 }  // namespace
 
@@ -484,62 +654,73 @@ int gemm_backend_for(const GemmArgs& g) {
   return 1;
 }
 
-static void gemm_tc(const GemmArgs& g) {
+void tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t batch,
+                int64_t sstride, float* hi, float* lo, int64_t pitch) {
+  int64_t nrow = rows * batch;
+  if (!nrow || !pitch) return;
+  bool vec = (ld % 4 == 0) && (sstride % 4 == 0) && (((uintptr_t)src & 15) == 0);
+  dim3 grid((unsigned)nrow, (unsigned)((pitch + 1023) / 1024));
+  k_split_tf32<<<grid, 256, 0, stream()>>>(src, rows, cols, ld, sstride, hi, lo, pitch, vec);
+  count_launch();
+  after_launch("k_split_tf32");
+}
+
+void gemm_tc_planes(const TcProblem& pr) {
+  if (pr.M <= 0 || pr.N <= 0 || pr.batch <= 0) return;
+  if (pr.K <= 0) panic("gemm_tc_planes with K=0");
   load_encoder();
-  static bool attr_set = false;
-  if (!attr_set) {
-    MALUS_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    attr_set = true;
+  CUtensorMap ah = operand_map(pr.a, pr.a.hi), al = operand_map(pr.a, pr.a.lo);
+  CUtensorMap bh = operand_map(pr.b, pr.b.hi), bl = operand_map(pr.b, pr.b.lo);
+  TcKernelParams kp;
+  kp.pr = pr;
+  kp.tiles_m = (pr.M + BM - 1) / BM;
+  kp.tiles_n = (pr.N + BN - 1) / BN;
+  kp.nk = (pr.K + BK - 1) / BK;
+  kp.err = device_error_word();
+  int total = kp.tiles_m * kp.tiles_n * pr.batch;
+  int grid = std::min(total, kNumSMs);
+  double flops = 2.0 * pr.M * (double)pr.N * pr.K * pr.batch;
+  int pid = prof_begin(0, flops, 8.0 * ((double)pr.M * pr.K + (double)pr.N * pr.K) * pr.batch +
+                                     4.0 * (double)pr.M * pr.N * pr.batch);
+  switch (pr.epi) {
+    case kEpiStore: launch_tc<kEpiStore>(ah, al, bh, bl, kp, grid); break;
+    case kEpiResid: launch_tc<kEpiResid>(ah, al, bh, bl, kp, grid); break;
+    case kEpiGelu: launch_tc<kEpiGelu>(ah, al, bh, bl, kp, grid); break;
+    default: launch_tc<kEpiGeluBwd>(ah, al, bh, bl, kp, grid); break;
   }
-  // Operand A as stored: rows x cols = (a_trans ? K x M : M x K)
+  count_launch();
+  after_launch("k_gemm_tc");
+  prof_end(pid);
+}
+
+// tensor_matmul / VJP path: split both operands into workspace planes, then one
+// persistent GEMM with a plain row-major (batched) output.
+static void gemm_tc(const GemmArgs& g) {
   int64_t ar = g.a_trans ? g.K : g.M, ac = g.a_trans ? g.M : g.K;
   int64_t br = g.b_trans ? g.N : g.K, bc = g.b_trans ? g.K : g.N;
   int64_t ap = (ac + 3) & ~int64_t(3), bp = (bc + 3) & ~int64_t(3);
   int64_t abatch = g.strideA ? g.batch : 1, bbatch = g.strideB ? g.batch : 1;
   int64_t an = abatch * ar * ap, bn = bbatch * br * bp;
   float* ws = (float*)scratch_alloc((size_t)(2 * an + 2 * bn) * sizeof(float) + 256);
-  float *ah = ws, *al = ws + an, *bh = ws + 2 * an, *bl = bh + bn;
+  float *ahp = ws, *alp = ws + an, *bhp = ws + 2 * an, *blp = bhp + bn;
   int pid = prof_begin(1, 0.0, 12.0 * (double)(an + bn));
-  k_split_tf32<<<grid_for((size_t)an, 256), 256, 0, stream()>>>(g.A, ar, ac, g.lda, g.strideA, ah, al,
-                                                               ap, an);
-  k_split_tf32<<<grid_for((size_t)bn, 256), 256, 0, stream()>>>(g.B, br, bc, g.ldb, g.strideB, bh, bl,
-                                                               bp, bn);
-  count_launch(2);
-  after_launch("k_split_tf32");
+  tf32_split(g.A, ar, ac, g.lda, abatch, g.strideA, ahp, alp, ap);
+  tf32_split(g.B, br, bc, g.ldb, bbatch, g.strideB, bhp, blp, bp);
   prof_end(pid);
-  // A: K-major (not transposed) -> {K, M, batch} box {32, 128}; MN-major -> {M, K, batch} box {32, 32}
-  bool a_mn = g.a_trans, b_mn = !g.b_trans;
-  CUtensorMap mah, mal, mbh, mbl;
-  uint64_t apb = (uint64_t)ap * 4, bpb = (uint64_t)bp * 4;
-  if (!a_mn) {
-    mah = make_map(ah, ac, ar, abatch, apb, apb * ar, 32, BM, false);
-    mal = make_map(al, ac, ar, abatch, apb, apb * ar, 32, BM, false);
-  } else {
-    mah = make_map(ah, ac, ar, abatch, apb, apb * ar, 32, 32, true);
-    mal = make_map(al, ac, ar, abatch, apb, apb * ar, 32, 32, true);
-  }
-  if (!b_mn) {
-    mbh = make_map(bh, bc, br, bbatch, bpb, bpb * br, 32, BN, false);
-    mbl = make_map(bl, bc, br, bbatch, bpb, bpb * br, 32, BN, false);
-  } else {
-    mbh = make_map(bh, bc, br, bbatch, bpb, bpb * br, 32, 32, true);
-    mbl = make_map(bl, bc, br, bbatch, bpb, bpb * br, 32, 32, true);
-  }
-  TcParams p;
-  p.M = g.M; p.N = g.N; p.K = g.K;
-  p.a_mn = a_mn; p.b_mn = b_mn;
-  p.a_batched = g.strideA != 0; p.b_batched = g.strideB != 0;
-  p.C = g.C; p.ldc = g.ldc; p.strideC = g.strideC;
-  p.alpha = g.alpha; p.beta = g.beta;
-  p.err = device_error_word();
-  dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
-  pid = prof_begin(0, 2.0 * g.M * (double)g.N * g.K * g.batch,
-                   4.0 * ((double)g.M * g.N * g.batch * (g.beta != 0.0f ? 2 : 1)) +
-                       8.0 * (double)(an + bn));
-  k_gemm_tc<<<grid, kThreadsTC, kSmemBytes, stream()>>>(mah, mal, mbh, mbl, p);
-  count_launch();
-  after_launch("k_gemm_tc");
-  prof_end(pid);
+  TcProblem pr{};
+  pr.M = g.M; pr.N = g.N; pr.K = g.K; pr.batch = g.batch;
+  pr.a = TcOperand{ahp, alp, ar, ac, ap, (int)abatch, ar * ap, g.a_trans,
+                   g.strideA ? kZBatch : kZNone, 0};
+  pr.b = TcOperand{bhp, blp, br, bc, bp, (int)bbatch, br * bp, !g.b_trans,
+                   g.strideB ? kZBatch : kZNone, 0};
+  pr.epi = kEpiStore;
+  pr.oz = TcLayout{0, 0, 0, 0, g.batch > 1 ? g.strideC : 0};
+  pr.om = TcLayout{0, 0, 0, 0, g.ldc};
+  pr.on = TcLayout{0, 0, 0, 0, 1};
+  pr.out = g.C;
+  pr.alpha = g.alpha;
+  pr.beta = g.beta;
+  gemm_tc_planes(pr);
   scratch_free(ws);
 }
 
@@ -550,3 +731,29 @@ void gemm(const GemmArgs& g) {
 }
 
 }  // namespace malus
+
+extern "C" void malus_tc_gemm(const malus_tc_problem* q) {
+  using namespace malus;
+  auto op = [](const malus_tc_operand& o) {
+    return TcOperand{o.hi, o.lo, o.rows, o.cols, o.pitch, o.nz, o.zstride, o.mn_major != 0,
+                     o.zmode, o.seg};
+  };
+  TcProblem p{};
+  p.M = q->M; p.N = q->N; p.K = q->K; p.batch = q->batch;
+  p.a = op(q->a);
+  p.b = op(q->b);
+  p.epi = q->epi;
+  auto L = [](const malus_tc_layout& l) { return TcLayout{l.d1, l.s1, l.d2, l.s2, l.s3}; };
+  p.oz = L(q->oz);
+  p.om = L(q->om);
+  p.on = L(q->on);
+  p.out = q->out; p.out_hi = q->out_hi; p.out_lo = q->out_lo; p.aux = q->aux;
+  p.alpha = q->alpha; p.beta = q->beta;
+  gemm_tc_planes(p);
+}
+
+extern "C" void malus_tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld,
+                                 int64_t batch, int64_t sstride, float* hi, float* lo,
+                                 int64_t pitch) {
+  malus::tf32_split(src, rows, cols, ld, batch, sstride, hi, lo, pitch);
+}

@@ -1,0 +1,187 @@
+"""GPU: the plane-level tcgen05 GEMM (malus_tc_gemm) against float64 numpy:
+every epilogue, the head fold/unfold output maps, N- and K-segmented
+operands, batching, and all four operand major-ness combinations."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+_LIVE = []
+
+
+@pytest.fixture(autouse=True)
+def _free():
+    yield
+    _LIVE.clear()
+
+
+def dev(M, a):
+    t = M.Tensor.from_numpy(np.ascontiguousarray(a, np.float32))
+    _LIVE.append(t)
+    return t
+
+
+def ptr(lib, t):
+    return lib.malus_tensor_data(t.h)
+
+
+def planes(M, lib, x):
+    """x: [nz, rows, cols] or [rows, cols] -> (hi, lo, pitch) device planes."""
+    x = np.asarray(x, np.float32)
+    if x.ndim == 2:
+        x = x[None]
+    nz, rows, cols = x.shape
+    pitch = (cols + 3) // 4 * 4
+    src = dev(M, x)
+    hi = dev(M, np.zeros((nz, rows, pitch), np.float32))
+    lo = dev(M, np.zeros((nz, rows, pitch), np.float32))
+    lib.malus_tf32_split(ptr(lib, src), rows, cols, cols, nz, rows * cols, ptr(lib, hi), ptr(lib, lo), pitch)
+    return hi, lo, pitch, nz, rows, cols
+
+
+def operand(M, lib, x, mn_major, zmode=0, seg=0):
+    hi, lo, pitch, nz, rows, cols = planes(M, lib, x)
+    return M.TcOperand(ptr(lib, hi), ptr(lib, lo), rows, cols, pitch, nz, rows * pitch,
+                       int(mn_major), zmode, seg)
+
+
+def lay(d1=0, s1=0, d2=0, s2=0, s3=0):
+    """index i -> (i//d1)*s1 + ((i%d1)//d2)*s2 + (i%d2)*s3 (d = 0 skips a level)"""
+    import malus_b200 as M
+    return M.TcLayout(d1, s1, d2, s2, s3)
+
+
+def run(M, lib, Mm, N, K, batch, a, b, epi=0, oz=None, om=None, on=None, out=None, out_hi=None,
+        out_lo=None, aux=None, alpha=1.0, beta=0.0):
+    p = M.TcProblem()
+    p.M, p.N, p.K, p.batch = Mm, N, K, batch
+    p.a, p.b = a, b
+    p.epi = epi
+    p.oz = oz or lay()
+    p.om = om or lay(s3=N)
+    p.on = on or lay(s3=1)
+    p.out = ptr(lib, out) if out is not None else None
+    p.out_hi = ptr(lib, out_hi) if out_hi is not None else None
+    p.out_lo = ptr(lib, out_lo) if out_lo is not None else None
+    p.aux = ptr(lib, aux) if aux is not None else None
+    p.alpha, p.beta = alpha, beta
+    lib.malus_tc_gemm(C.byref(p))
+
+
+def err(got, ref, a, b):
+    scale = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
+    return float(np.max(np.abs(got - ref) / np.maximum(scale, 1e-30)))
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("Mm,N,K", [(300, 200, 130), (512, 384, 384), (1024, 65, 384), (129, 1536, 64)])
+def test_majors(M, rt, rng, a_mn, b_mn, Mm, N, K):
+    A = rng.standard_normal((Mm, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    ao = operand(M, rt, A.T if a_mn else A, a_mn)
+    bo = operand(M, rt, B if b_mn else B.T, b_mn)
+    out = dev(M, np.zeros((Mm, N)))
+    run(M, rt, Mm, N, K, 1, ao, bo, out=out)
+    ref = A.astype(np.float64) @ B
+    assert err(out.numpy(), ref, A, B) < 1e-4
+
+
+def test_store_beta_and_planes(M, rt, rng):
+    A = rng.standard_normal((256, 128)).astype(np.float32)
+    B = rng.standard_normal((128, 256)).astype(np.float32)
+    C0 = rng.standard_normal((256, 256)).astype(np.float32)
+    out = dev(M, C0)
+    hi = dev(M, np.zeros((256, 256)))
+    lo = dev(M, np.zeros((256, 256)))
+    run(M, rt, 256, 256, 128, 1, operand(M, rt, A, False), operand(M, rt, B, True), out=out,
+        out_hi=hi, out_lo=lo, alpha=0.5, beta=1.0)
+    ref = 0.5 * (A.astype(np.float64) @ B) + C0
+    got = out.numpy()
+    assert err(got, ref, A, B) < 1e-4
+    assert np.max(np.abs(hi.numpy().astype(np.float64) + lo.numpy() - got)) <= 1e-6 * np.max(np.abs(got))
+
+
+def test_residual_gelu_gelubwd(M, rt, rng):
+    Mm, N, K = 384, 512, 128
+    A = rng.standard_normal((Mm, K)).astype(np.float32) * 0.5
+    B = rng.standard_normal((K, N)).astype(np.float32) * 0.5
+    ref = A.astype(np.float64) @ B
+    R = rng.standard_normal((Mm, N)).astype(np.float32)
+    ao, bo = operand(M, rt, A, False), operand(M, rt, B, True)
+    out = dev(M, np.zeros((Mm, N)))
+    resid = dev(M, R)
+    run(M, rt, Mm, N, K, 1, ao, bo, epi=1, out=out, aux=resid)
+    assert err(out.numpy() - R, ref, A, B) < 2e-4
+    pre = dev(M, np.zeros((Mm, N)))
+    hi, lo = dev(M, np.zeros((Mm, N))), dev(M, np.zeros((Mm, N)))
+    run(M, rt, Mm, N, K, 1, ao, bo, epi=2, out=pre, out_hi=hi, out_lo=lo)
+    assert err(pre.numpy(), ref, A, B) < 1e-4
+    g = 0.5 * ref * (1 + np.tanh(0.7978845608028654 * (ref + 0.044715 * ref ** 3)))
+    assert np.max(np.abs(hi.numpy().astype(np.float64) + lo.numpy() - g)) < 1e-4
+    X = rng.standard_normal((Mm, N)).astype(np.float32)
+    xs = dev(M, X)
+    d = dev(M, np.zeros((Mm, N)))
+    run(M, rt, Mm, N, K, 1, ao, bo, epi=3, out=d, out_hi=hi, out_lo=lo, aux=xs)
+    x = X.astype(np.float64)
+    t = np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3))
+    gp = 0.7978845608028654 * (1 + 3 * 0.044715 * x * x)
+    dref = ref * (0.5 * (1 + t) + 0.5 * x * (1 - t * t) * gp)
+    assert np.max(np.abs(d.numpy() - dref) / (np.abs(A) @ np.abs(B) + 1e-9)) < 2e-4
+
+
+def test_qkv_nseg_with_head_fold(M, rt, rng):
+    """x[M,C] @ [Wq|Wk|Wv] (three separate [C,C] slices) written as [3][B][H][T][hs]."""
+    Bsz, T, H, hs = 4, 64, 6, 64
+    Cc, Mm = H * hs, Bsz * T
+    X = rng.standard_normal((Mm, Cc)).astype(np.float32)
+    W = rng.standard_normal((3, Cc, Cc)).astype(np.float32)
+    ao = operand(M, rt, X, False)
+    bo = operand(M, rt, W, True, zmode=3, seg=Cc)      # MN-major, N segmented over slices
+    out = dev(M, np.zeros((3, Bsz, H, T, hs)))
+    # m = b*T + t -> b*H*T*hs + t*hs ; n = j*C + h*hs + d -> j*B*H*T*hs + h*T*hs + d
+    run(M, rt, Mm, 3 * Cc, Cc, 1, ao, bo, out=out, om=lay(T, H * T * hs, 0, 0, hs),
+        on=lay(Cc, Bsz * H * T * hs, hs, T * hs, 1))
+    got = out.numpy()
+    for j in range(3):
+        ref = (X.astype(np.float64) @ W[j]).reshape(Bsz, T, H, hs).transpose(0, 2, 1, 3)
+        scale = (np.abs(X.astype(np.float64)) @ np.abs(W[j])).reshape(Bsz, T, H, hs).transpose(0, 2, 1, 3)
+        assert np.max(np.abs(got[j] - ref) / scale) < 1e-4
+    # N-segmented B into a plain [M, 3C] output
+    out2 = dev(M, np.zeros((Mm, 3 * Cc)))
+    run(M, rt, Mm, 3 * Cc, Cc, 1, ao, bo, out=out2)
+    ref2 = np.concatenate([X.astype(np.float64) @ W[j] for j in range(3)], axis=1)
+    Wcat = np.concatenate([W[j] for j in range(3)], axis=1)
+    assert err(out2.numpy(), ref2, X, Wcat) < 1e-4
+
+
+def test_kseg_sum_of_products(M, rt, rng):
+    """dx = sum_j dq_j @ W_j^T with dq [3][M][C] and W [3][C][C] as K segments."""
+    Mm, Cc = 256, 384
+    DQ = rng.standard_normal((3, Mm, Cc)).astype(np.float32)
+    W = rng.standard_normal((3, Cc, Cc)).astype(np.float32)
+    ao = operand(M, rt, DQ, False, zmode=2, seg=Cc)    # K-major, K segmented
+    bo = operand(M, rt, W, False, zmode=2, seg=Cc)     # B^T rows = n: W_j[n][c] K-major
+    out = dev(M, np.zeros((Mm, Cc)))
+    run(M, rt, Mm, Cc, 3 * Cc, 1, ao, bo, out=out)
+    A = np.concatenate([DQ[j] for j in range(3)], axis=1)
+    Bm = np.concatenate([W[j].T for j in range(3)], axis=0)
+    ref = A.astype(np.float64) @ Bm
+    assert err(out.numpy(), ref, A, Bm) < 1e-4
+
+
+def test_batched_with_unfold(M, rt, rng):
+    """P[BH,T,T] @ V[BH,T,hs] written straight into the [B*T, H*hs] layout."""
+    Bsz, H, T, hs = 2, 3, 128, 64
+    P = rng.standard_normal((Bsz * H, T, T)).astype(np.float32)
+    V = rng.standard_normal((Bsz * H, T, hs)).astype(np.float32)
+    ao = operand(M, rt, P, False, zmode=1)
+    bo = operand(M, rt, V, True, zmode=1)              # V stored [K=T][N=hs]: MN-major
+    out = dev(M, np.zeros((Bsz * T, H * hs)))
+    # z = b*H + h -> b*T*H*hs + h*hs ; m = t -> t*H*hs ; n = d
+    run(M, rt, T, hs, T, Bsz * H, ao, bo, out=out, oz=lay(H, T * H * hs, 0, 0, hs), om=lay(s3=H * hs),
+        on=lay(s3=1))
+    ref = np.einsum("ztk,zkd->ztd", P.astype(np.float64), V).reshape(Bsz, H, T, hs).transpose(0, 2, 1, 3)
+    scale = np.einsum("ztk,zkd->ztd", np.abs(P).astype(np.float64), np.abs(V)).reshape(Bsz, H, T, hs).transpose(0, 2, 1, 3)
+    assert np.max(np.abs(out.numpy().reshape(Bsz, T, H, hs) - ref) / scale) < 1e-4
