@@ -179,7 +179,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="malus", choices=["malus", "reference"])
-    ap.add_argument("--mode", type=int, default=int(os.environ.get("MALUS_BENCH_MODE", "0")))
+    ap.add_argument("--mode", type=int, default=int(os.environ.get("MALUS_BENCH_MODE", "1")))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -295,6 +295,9 @@ float malus_gpt_last_loss(int64_t model);
  * [wte,wpe,ln_f,lm_head]). */
 int32_t malus_gpt_num_params(int64_t model);
 int64_t malus_gpt_param(int64_t model, int32_t i);
+/* Gradient of parameter i from the last step (before the update; summed over
+ * data-parallel ranks), same shape; a borrowed handle like malus_gpt_param. */
+int64_t malus_gpt_grad(int64_t model, int32_t i);
 int64_t malus_gpt_num_elements(int64_t model);
 
 /* tcgen05 3xTF32 GEMM on pre-split tf32 operand planes, with fused epilogues.

@@ -186,6 +186,7 @@ SIGNATURES: dict[str, tuple] = {
     "malus_gpt_last_loss": (f32, [i64]),
     "malus_gpt_num_params": (i32, [i64]),
     "malus_gpt_param": (i64, [i64, i32]),
+    "malus_gpt_grad": (i64, [i64, i32]),
     "malus_gpt_num_elements": (i64, [i64]),
     "malus_device_error": (i32, []),
     "malus_tc_gemm": (None, [C.POINTER(TcProblem)]),
@@ -300,6 +301,12 @@ class GPT:
     def params(self) -> list[np.ndarray]:
         lib = load()
         return [Tensor(lib.malus_gpt_param(self.h, i), owned=False).numpy()
+                for i in range(lib.malus_gpt_num_params(self.h))]
+
+    def grads(self) -> list[np.ndarray]:
+        """Gradients of the last step (before the update), in parameter order."""
+        lib = load()
+        return [Tensor(lib.malus_gpt_grad(self.h, i), owned=False).numpy()
                 for i in range(lib.malus_gpt_num_params(self.h))]
 
     def close(self):

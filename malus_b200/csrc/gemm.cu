@@ -285,15 +285,17 @@ __device__ __forceinline__ void epi_store1(const TcProblem& p, int64_t o, float 
   if (p.alpha != 1.0f) v *= p.alpha;
   float split_src;
   if (EPI == kEpiStore) {
-    if (p.beta != 0.0f) v += p.beta * p.out[o];
-    p.out[o] = v;
+    if (p.out) {                  // the f32 output is optional: planes-only callers pass none
+      if (p.beta != 0.0f) v += p.beta * p.out[o];
+      p.out[o] = v;
+    }
     split_src = v;
   } else if (EPI == kEpiResid) {
     v = p.aux[o] + v;
-    p.out[o] = v;
+    if (p.out) p.out[o] = v;
     split_src = v;
   } else if (EPI == kEpiGelu) {
-    p.out[o] = v;                 // pre-activation, kept for the GELU derivative
+    if (p.out) p.out[o] = v;      // pre-activation, kept for the GELU derivative
     split_src = gelu_f(v);
   } else {                        // kEpiGeluBwd: v = dL/d(gelu out); aux = pre-activation
     split_src = v * gelu_grad(p.aux[o]);
@@ -312,19 +314,21 @@ __device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4
   if (p.alpha != 1.0f) { v.x *= p.alpha; v.y *= p.alpha; v.z *= p.alpha; v.w *= p.alpha; }
   float4 s;
   if (EPI == kEpiStore) {
-    if (p.beta != 0.0f) {
-      float4 q = *reinterpret_cast<const float4*>(p.out + o);
-      v.x += p.beta * q.x; v.y += p.beta * q.y; v.z += p.beta * q.z; v.w += p.beta * q.w;
+    if (p.out) {
+      if (p.beta != 0.0f) {
+        float4 q = *reinterpret_cast<const float4*>(p.out + o);
+        v.x += p.beta * q.x; v.y += p.beta * q.y; v.z += p.beta * q.z; v.w += p.beta * q.w;
+      }
+      *reinterpret_cast<float4*>(p.out + o) = v;
     }
-    *reinterpret_cast<float4*>(p.out + o) = v;
     s = v;
   } else if (EPI == kEpiResid) {
     float4 q = *reinterpret_cast<const float4*>(p.aux + o);
     v.x = q.x + v.x; v.y = q.y + v.y; v.z = q.z + v.z; v.w = q.w + v.w;
-    *reinterpret_cast<float4*>(p.out + o) = v;
+    if (p.out) *reinterpret_cast<float4*>(p.out + o) = v;
     s = v;
   } else if (EPI == kEpiGelu) {
-    *reinterpret_cast<float4*>(p.out + o) = v;
+    if (p.out) *reinterpret_cast<float4*>(p.out + o) = v;
     s = make_float4(gelu_f(v.x), gelu_f(v.y), gelu_f(v.z), gelu_f(v.w));
   } else {
     float4 x = *reinterpret_cast<const float4*>(p.aux + o);
@@ -406,25 +410,32 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
           uint32_t fb = smem_u32(&full[s]);
           mbar_expect_tx(fb, kStageBytes);
           int k0 = kb * BK, kc, mnc, zc;
-          operand_coords(p.a.zmode, p.a.seg, z, k0, m0, &kc, &mnc, &zc);
-          if (!p.a.mn_major) {
+          // A 128-wide M/N tile may straddle segments (segment width a multiple
+          // of 32): MN-major tiles and K-major tiles of an MN-segmented operand
+          // are loaded as four 32-wide boxes, each with its own segment.
+          if (!p.a.mn_major && p.a.zmode != kZMNSeg) {
+            operand_coords(p.a.zmode, p.a.seg, z, k0, m0, &kc, &mnc, &zc);
             tma_load_3d(smem_u32(st), &mAh, fb, kc, mnc, zc);
             tma_load_3d(smem_u32(st + kTileBytesA), &mAl, fb, kc, mnc, zc);
           } else {
             for (int j = 0; j < BM / 32; ++j) {
-              tma_load_3d(smem_u32(st + j * 4096), &mAh, fb, mnc + 32 * j, kc, zc);
-              tma_load_3d(smem_u32(st + kTileBytesA + j * 4096), &mAl, fb, mnc + 32 * j, kc, zc);
+              operand_coords(p.a.zmode, p.a.seg, z, k0, m0 + 32 * j, &kc, &mnc, &zc);
+              int x = p.a.mn_major ? mnc : kc, y = p.a.mn_major ? kc : mnc;
+              tma_load_3d(smem_u32(st + j * 4096), &mAh, fb, x, y, zc);
+              tma_load_3d(smem_u32(st + kTileBytesA + j * 4096), &mAl, fb, x, y, zc);
             }
           }
           uint8_t* sb = st + 2 * kTileBytesA;
-          operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
-          if (!p.b.mn_major) {
+          if (!p.b.mn_major && p.b.zmode != kZMNSeg) {
+            operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
             tma_load_3d(smem_u32(sb), &mBh, fb, kc, mnc, zc);
             tma_load_3d(smem_u32(sb + kTileBytesB), &mBl, fb, kc, mnc, zc);
           } else {
             for (int j = 0; j < BN / 32; ++j) {
-              tma_load_3d(smem_u32(sb + j * 4096), &mBh, fb, mnc + 32 * j, kc, zc);
-              tma_load_3d(smem_u32(sb + kTileBytesB + j * 4096), &mBl, fb, mnc + 32 * j, kc, zc);
+              operand_coords(p.b.zmode, p.b.seg, z, k0, n0 + 32 * j, &kc, &mnc, &zc);
+              int x = p.b.mn_major ? mnc : kc, y = p.b.mn_major ? kc : mnc;
+              tma_load_3d(smem_u32(sb + j * 4096), &mBh, fb, x, y, zc);
+              tma_load_3d(smem_u32(sb + kTileBytesB + j * 4096), &mBl, fb, x, y, zc);
             }
           }
         }
@@ -618,8 +629,10 @@ CUtensorMap operand_map(const TcOperand& o, const float* plane) {
   uint64_t zb = (uint64_t)o.zstride * 4;
   if (o.nz > 1 && (zb % 16 != 0)) panic("gemm operand slice stride %lld is not 16-byte aligned", (long long)o.zstride);
   if (o.nz <= 1) zb = pb * (uint64_t)o.rows;
+  // K-major boxes are 32 (K) x 128 rows, or 32 x 32 rows when the rows are segmented
+  uint32_t box_rows = (o.mn_major || o.zmode == kZMNSeg) ? 32 : BM;
   return make_map(plane, (uint64_t)o.cols, (uint64_t)o.rows, (uint64_t)std::max(1, o.nz), pb,
-                  std::max<uint64_t>(zb, 16), 32, o.mn_major ? 32 : BM, o.mn_major);
+                  std::max<uint64_t>(zb, 16), 32, box_rows, o.mn_major);
 }
 
 int g_force_backend = -1;
@@ -668,6 +681,14 @@ void tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_
 void gemm_tc_planes(const TcProblem& pr) {
   if (pr.M <= 0 || pr.N <= 0 || pr.batch <= 0) return;
   if (pr.K <= 0) panic("gemm_tc_planes with K=0");
+  if (!pr.out && !pr.out_hi) panic("gemm_tc_planes: no output (out and out_hi are both null)");
+  if ((pr.out_hi == nullptr) != (pr.out_lo == nullptr)) panic("gemm_tc_planes: out_hi/out_lo must come together");
+  if ((pr.epi == kEpiResid || pr.epi == kEpiGeluBwd) && !pr.aux) panic("gemm_tc_planes: epilogue %d needs aux", pr.epi);
+  if ((pr.epi == kEpiGelu || pr.epi == kEpiGeluBwd) && !pr.out_hi) panic("gemm_tc_planes: GELU epilogues write planes");
+  if (!pr.a.hi || !pr.a.lo || !pr.b.hi || !pr.b.lo) panic("gemm_tc_planes: missing operand plane");
+  for (const TcOperand* o : {&pr.a, &pr.b})
+    if ((o->zmode == kZKSeg || o->zmode == kZMNSeg) && (o->seg <= 0 || o->seg % 32 != 0))
+      panic("gemm_tc_planes: segment width %d must be a positive multiple of 32", o->seg);
   load_encoder();
   CUtensorMap ah = operand_map(pr.a, pr.a.hi), al = operand_map(pr.a, pr.a.lo);
   CUtensorMap bh = operand_map(pr.b, pr.b.hi), bl = operand_map(pr.b, pr.b.lo);

@@ -30,6 +30,7 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
                         const std::vector<size_t>& grad_offsets);
 void fused_destroy(FusedStep* f);
 void fused_step(FusedStep* f, const int32_t* x_dev, const int32_t* y_dev, float* loss_dev);
+void fused_after_update(FusedStep* f);
 }  // namespace malus
 
 using namespace malus;
@@ -43,7 +44,7 @@ struct Model {
   malus_gpt_config cfg;
   int C, H, hs, T, B, V, L, C4;
   size_t M;
-  std::vector<int64_t> params, ms, vs;
+  std::vector<int64_t> params, ms, vs, gradv;   // gradv: views of the gradient buffer
   std::vector<size_t> offs;   // element offsets into the fused buffers
   std::vector<size_t> sizes;
   size_t total = 0;
@@ -196,18 +197,18 @@ void tape_step(Model& m) {
   // gradients -> (DP all-reduce) -> fused AdamW
   std::vector<int64_t> grads(nparam);
   for (size_t i = 0; i < nparam; ++i) grads[i] = tape_get_grad(m.params[i]);
+  // gather into the fused gradient buffer (readable with malus_gpt_grad; one
+  // all-reduce over it under data parallelism)
+  for (size_t i = 0; i < nparam; ++i) {
+    MALUS_CUDA(cudaMemcpyAsync(m.gbuf + m.offs[i], fptr(grads[i]), m.sizes[i] * 4,
+                               cudaMemcpyDeviceToDevice, stream()));
+    tensor_release(grads[i]);
+    grads[i] = wrap(m.gbuf + m.offs[i], {m.sizes[i]});
+  }
   float gscale = 1.0f;
   if (dp_world() > 1) {
-    for (size_t i = 0; i < nparam; ++i) {
-      MALUS_CUDA(cudaMemcpyAsync(m.gbuf + m.offs[i], fptr(grads[i]), m.sizes[i] * 4,
-                                 cudaMemcpyDeviceToDevice, stream()));
-    }
     if (dp_allreduce_async(m.gbuf, m.total) != 0) panic("data-parallel all-reduce failed");
     dp_join();
-    for (size_t i = 0; i < nparam; ++i) {
-      tensor_release(grads[i]);
-      grads[i] = wrap(m.gbuf + m.offs[i], {m.sizes[i]});
-    }
     gscale = 1.0f / (float)dp_world();
   }
   m.step++;
@@ -266,6 +267,7 @@ int64_t malus_gpt_create(const malus_gpt_config* cfgp) {
     m->params.push_back(malus_tensor_wrap(MALUS_F32, m->pbuf + m->offs[i], s, shapes[i].size()));
     m->ms.push_back(malus_tensor_wrap(MALUS_F32, m->mbuf + m->offs[i], s, shapes[i].size()));
     m->vs.push_back(malus_tensor_wrap(MALUS_F32, m->vbuf + m->offs[i], s, shapes[i].size()));
+    m->gradv.push_back(malus_tensor_wrap(MALUS_F32, m->gbuf + m->offs[i], s, shapes[i].size()));
   }
   // initialisation in the reference's RNG call order: per block wq,wk,wv,wo,w1,w2,
   // then wte, wpe, (lm_head); LN gains are ones
@@ -319,6 +321,7 @@ void malus_gpt_destroy(int64_t h) {
   for (int64_t p : m->params) tensor_release(p);
   for (int64_t p : m->ms) tensor_release(p);
   for (int64_t p : m->vs) tensor_release(p);
+  for (int64_t p : m->gradv) tensor_release(p);
   tensor_release(m->x_h);
   tensor_release(m->y_h);
   tensor_release(m->pos_h);
@@ -344,6 +347,7 @@ void malus_gpt_step_device(int64_t h, const int32_t* x_dev, const int32_t* y_dev
     AdamSeg seg{m->pbuf, m->gbuf, m->mbuf, m->vbuf, (int64_t)m->total};
     adamw_multi(&seg, 1, m->cfg.lr, m->cfg.beta1, m->cfg.beta2, m->cfg.eps, m->cfg.wd, bc1, bc2,
                 gscale);
+    fused_after_update(m->fused);
   } else {
     tape_step(*m);
   }
@@ -371,6 +375,7 @@ float malus_gpt_last_loss(int64_t h) {
 
 int32_t malus_gpt_num_params(int64_t h) { return (int32_t)reinterpret_cast<Model*>(h)->params.size(); }
 int64_t malus_gpt_param(int64_t h, int32_t i) { return reinterpret_cast<Model*>(h)->params.at((size_t)i); }
+int64_t malus_gpt_grad(int64_t h, int32_t i) { return reinterpret_cast<Model*>(h)->gradv.at((size_t)i); }
 int64_t malus_gpt_num_elements(int64_t h) {
   auto* m = reinterpret_cast<Model*>(h);
   int64_t n = 0;

@@ -76,7 +76,8 @@ def err(got, ref, a, b):
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
-@pytest.mark.parametrize("Mm,N,K", [(300, 200, 130), (512, 384, 384), (1024, 65, 384), (129, 1536, 64)])
+@pytest.mark.parametrize("Mm,N,K", [(300, 200, 130), (512, 384, 384), (1024, 65, 384), (129, 1536, 64),
+                                    (32, 16, 16), (32, 32, 16), (64, 16, 32), (40, 24, 20)])
 def test_majors(M, rt, rng, a_mn, b_mn, Mm, N, K):
     A = rng.standard_normal((Mm, K)).astype(np.float32)
     B = rng.standard_normal((K, N)).astype(np.float32)
@@ -101,6 +102,18 @@ def test_store_beta_and_planes(M, rt, rng):
     got = out.numpy()
     assert err(got, ref, A, B) < 1e-4
     assert np.max(np.abs(hi.numpy().astype(np.float64) + lo.numpy() - got)) <= 1e-6 * np.max(np.abs(got))
+
+
+def test_planes_only_output(M, rt, rng):
+    """out = NULL: only the tf32 planes of the product are written."""
+    A = rng.standard_normal((256, 128)).astype(np.float32)
+    B = rng.standard_normal((128, 192)).astype(np.float32)
+    hi = dev(M, np.zeros((256, 192)))
+    lo = dev(M, np.zeros((256, 192)))
+    run(M, rt, 256, 192, 128, 1, operand(M, rt, A, False), operand(M, rt, B, True), out=None,
+        out_hi=hi, out_lo=lo)
+    got = hi.numpy().astype(np.float64) + lo.numpy()
+    assert err(got, A.astype(np.float64) @ B, A, B) < 1e-4
 
 
 def test_residual_gelu_gelubwd(M, rt, rng):
@@ -131,9 +144,9 @@ def test_residual_gelu_gelubwd(M, rt, rng):
     assert np.max(np.abs(d.numpy() - dref) / (np.abs(A) @ np.abs(B) + 1e-9)) < 2e-4
 
 
-def test_qkv_nseg_with_head_fold(M, rt, rng):
+@pytest.mark.parametrize("Bsz,T,H,hs", [(4, 64, 6, 64), (4, 32, 4, 16)])
+def test_qkv_nseg_with_head_fold(M, rt, rng, Bsz, T, H, hs):
     """x[M,C] @ [Wq|Wk|Wv] (three separate [C,C] slices) written as [3][B][H][T][hs]."""
-    Bsz, T, H, hs = 4, 64, 6, 64
     Cc, Mm = H * hs, Bsz * T
     X = rng.standard_normal((Mm, Cc)).astype(np.float32)
     W = rng.standard_normal((3, Cc, Cc)).astype(np.float32)
@@ -185,3 +198,27 @@ def test_batched_with_unfold(M, rt, rng):
     ref = np.einsum("ztk,zkd->ztd", P.astype(np.float64), V).reshape(Bsz, H, T, hs).transpose(0, 2, 1, 3)
     scale = np.einsum("ztk,zkd->ztd", np.abs(P).astype(np.float64), np.abs(V)).reshape(Bsz, H, T, hs).transpose(0, 2, 1, 3)
     assert np.max(np.abs(out.numpy().reshape(Bsz, T, H, hs) - ref) / scale) < 1e-4
+
+
+@pytest.mark.parametrize("side", ["a", "b"])
+@pytest.mark.parametrize("mn", [False, True])
+@pytest.mark.parametrize("seg,nseg", [(64, 3), (96, 3), (32, 5)])
+def test_mnseg_tiles_straddle_segments(M, rt, rng, side, mn, seg, nseg):
+    """M- or N-segmented operands whose segments are narrower than a 128-wide tile."""
+    K, other = 80, 200
+    S = rng.standard_normal((nseg, seg, K)).astype(np.float32)    # segment j: rows j*seg.. of the MN x K matrix
+    full = np.concatenate(list(S), axis=0)                        # [nseg*seg, K]
+    X = rng.standard_normal((other, K)).astype(np.float32)
+    stored = np.ascontiguousarray(S.transpose(0, 2, 1)) if mn else S   # MN-major: [K][seg] per segment
+    so = operand(M, rt, stored, mn, zmode=3, seg=seg)
+    if side == "a":
+        xo = operand(M, rt, X.T, True)                            # B: [K][N] MN-major
+        Mm, N, A, B = nseg * seg, other, full, X.T
+        out = dev(M, np.zeros((Mm, N)))
+        run(M, rt, Mm, N, K, 1, so, xo, out=out)
+    else:
+        xo = operand(M, rt, X, False)                             # A: [M][K] K-major
+        Mm, N, A, B = other, nseg * seg, X, full.T
+        out = dev(M, np.zeros((Mm, N)))
+        run(M, rt, Mm, N, K, 1, xo, so, out=out)
+    assert err(out.numpy(), A.astype(np.float64) @ B, A, B) < 1e-4
