@@ -137,7 +137,11 @@ constexpr int kTileBytesA = BM * BK * 4;  // 16 KB
 constexpr int kTileBytesB = BN * BK * 4;  // 16 KB
 constexpr int kStageBytes = 2 * kTileBytesA + 2 * kTileBytesB;
 constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-constexpr int kThreadsTC = 192;   // warp0 TMA, warp1 MMA+TMEM, warps2-5 epilogue
+// Epilogue warps: 8 (two per TMEM lane quarter, half the columns each) when the
+// epilogue reads an auxiliary input, whose load latency the extra warps hide;
+// 4 otherwise, leaving L2 bandwidth to the operand loads.
+__host__ __device__ constexpr int epi_warps(int epi) { return (epi == 1 || epi == 3) ? 8 : 4; }
+__host__ __device__ constexpr int threads_tc(int epi) { return 64 + 32 * epi_warps(epi); }
 constexpr uint32_t kTmemCols = 2 * BN;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on every wait
 constexpr float kGeluC0 = 0.7978845608028654f, kGeluC1 = 0.044715f;
@@ -243,16 +247,20 @@ __device__ __forceinline__ float tf32_rn(float x) {
   return __uint_as_float(r);
 }
 
-__device__ __forceinline__ int64_t lay(const TcLayout& L, int64_t i) {
+// Indices (z < batch, m < M, n < N: all int) and radices fit 32 bits: 32-bit division.
+__device__ __forceinline__ int64_t lay(const TcLayout& L, int64_t idx) {
+  uint32_t i = (uint32_t)idx;
   int64_t off = 0;
-  if (L.d1) { off = (i / L.d1) * L.s1; i %= L.d1; }
-  if (L.d2) { off += (i / L.d2) * L.s2; i %= L.d2; }
-  return off + i * L.s3;
+  if (L.d1) { uint32_t d = (uint32_t)L.d1, q = i / d; off = (int64_t)q * L.s1; i -= q * d; }
+  if (L.d2) { uint32_t d = (uint32_t)L.d2, q = i / d; off += (int64_t)q * L.s2; i -= q * d; }
+  return off + (int64_t)i * L.s3;
 }
 
 struct TcKernelParams {
   TcProblem pr;
   int tiles_m, tiles_n, nk;
+  int splits;      // K slices per tile (split-K); > 1 writes raw partial tiles to ws
+  float* ws;       // [tile][split][BM][BN] partial accumulators when splits > 1
   int32_t* err;
 };
 
@@ -310,7 +318,7 @@ __device__ __forceinline__ void epi_store1(const TcProblem& p, int64_t o, float 
 
 // Four consecutive output elements at 16-byte aligned offset o.
 template <int EPI>
-__device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4 v) {
+__device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4 v, float4 aux4) {
   if (p.alpha != 1.0f) { v.x *= p.alpha; v.y *= p.alpha; v.z *= p.alpha; v.w *= p.alpha; }
   float4 s;
   if (EPI == kEpiStore) {
@@ -323,7 +331,7 @@ __device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4
     }
     s = v;
   } else if (EPI == kEpiResid) {
-    float4 q = *reinterpret_cast<const float4*>(p.aux + o);
+    const float4 q = aux4;
     v.x = q.x + v.x; v.y = q.y + v.y; v.z = q.z + v.z; v.w = q.w + v.w;
     if (p.out) *reinterpret_cast<float4*>(p.out + o) = v;
     s = v;
@@ -331,7 +339,7 @@ __device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4
     if (p.out) *reinterpret_cast<float4*>(p.out + o) = v;
     s = make_float4(gelu_f(v.x), gelu_f(v.y), gelu_f(v.z), gelu_f(v.w));
   } else {
-    float4 x = *reinterpret_cast<const float4*>(p.aux + o);
+    const float4 x = aux4;
     s = make_float4(v.x * gelu_grad(x.x), v.y * gelu_grad(x.y), v.z * gelu_grad(x.z),
                     v.w * gelu_grad(x.w));
     if (p.out) *reinterpret_cast<float4*>(p.out + o) = s;
@@ -346,7 +354,7 @@ __device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(kThreadsTC, 1)
+__global__ void __launch_bounds__(threads_tc(EPI), 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
           const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
           const TcKernelParams kp) {
@@ -364,7 +372,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per_batch = kp.tiles_m * kp.tiles_n;
-  const int total = per_batch * p.batch;
+  const int splits = kp.splits;
+  const int total = per_batch * p.batch * splits;   // work units: (tile, K slice)
   const int nk = kp.nk;
 
   if (threadIdx.x == 0) {
@@ -374,7 +383,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&accf[b]), 1);
-      mbar_init(smem_u32(&acce[b]), 4);
+      mbar_init(smem_u32(&acce[b]), epi_warps(EPI));
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -396,10 +405,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
+        int tile = unit / splits, sl = unit % splits;
         int z = tile / per_batch, rem = tile % per_batch;
         int m0 = (rem / kp.tiles_n) * BM, n0 = (rem % kp.tiles_n) * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int kb_lo = sl * nk / splits, kb_hi = (sl + 1) * nk / splits;
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           int s = it % STAGES;
           uint32_t ph = (it / STAGES) & 1;
           if (it >= STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, kp.err, 11)) {
@@ -455,7 +466,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       const uint32_t idesc = idesc_tf32(p.a.mn_major, p.b.mn_major);
       uint32_t it = 0, local = 0;
       bool ok = true, issued = false;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++local) {
+      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x, ++local) {
         uint32_t b = local & 1, u = local >> 1;
         if (u >= 1 && !mbar_wait(smem_u32(&acce[b]), (u - 1) & 1, abort_flag, kp.err, 14)) {
           ok = false;
@@ -463,7 +474,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t dacc = tmem + b * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int sl = unit % splits;
+        const int kb_lo = sl * nk / splits, kb_hi = (sl + 1) * nk / splits;
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           int s = it % STAGES;
           uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, kp.err, 12)) { ok = false; break; }
@@ -477,7 +490,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
             uint64_t dal = p.a.mn_major ? desc_mnmajor(al, kk) : desc_kmajor(al, kk);
             uint64_t dbh = p.b.mn_major ? desc_mnmajor(bh, kk) : desc_kmajor(bh, kk);
             uint64_t dbl = p.b.mn_major ? desc_mnmajor(bl, kk) : desc_kmajor(bl, kk);
-            uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
+            uint32_t acc0 = (kb > kb_lo || kk > 0) ? 1u : 0u;
             mma_tf32(dacc, dal, dbh, idesc, acc0);   // small terms first
             mma_tf32(dacc, dah, dbl, idesc, 1u);
             mma_tf32(dacc, dah, dbh, idesc, 1u);
@@ -497,19 +510,26 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     }
   } else {
     // ---------------- epilogue: TMEM -> registers -> global ----------------
+    // Warp w reads TMEM lane quarter (w % 4) (its 32 tile rows, one per lane)
+    // and, with 8 epilogue warps, column half (w - 2) / 4.  Auxiliary inputs of a 32-column
+    // chunk are loaded before any of its stores so the loads overlap.
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    constexpr int kCols = BN * 4 / epi_warps(EPI);      // columns per epilogue warp
+    const int chalf = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
+    const bool contig = (p.on.d1 % 32 == 0) && (p.on.d2 % 32 == 0) && p.on.s3 == 1;
     uint32_t local = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+    for (int unit = blockIdx.x; unit < total; unit += gridDim.x, ++local) {
       uint32_t b = local & 1, u = local >> 1;
       if (!mbar_wait(smem_u32(&accf[b]), u & 1, abort_flag, kp.err, 13)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int tile = unit / splits;
       int z = tile / per_batch, rem = tile % per_batch;
       int m0 = (rem / kp.tiles_n) * BM, n0 = (rem % kp.tiles_n) * BN;
       const int m = m0 + row;
       const int64_t zm_off = lay(p.oz, z) + lay(p.om, m);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = chalf * kCols; c0 < (chalf + 1) * kCols; c0 += 32) {
         uint32_t r[32];
         uint32_t taddr = tmem + b * BN + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
         asm volatile(
@@ -523,30 +543,35 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
               "=r"(r[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (m < p.M) {
-          const int nb = n0 + c0;
-          // contiguous run of 32 columns when the column map is unit-stride inside
-          // 32-aligned groups
-          const bool contig = (p.on.d1 % 32 == 0) && (p.on.d2 % 32 == 0) && p.on.s3 == 1;
-          const int64_t base = zm_off + lay(p.on, nb);
-          const bool vec = contig && nb + 32 <= p.N && (base & 3) == 0;
-          if (vec) {
+        if (splits > 1) {
+          // raw partial tile, row-major [BM][BN]; k_splitk_reduce applies the epilogue
+          float4* dst = reinterpret_cast<float4*>(kp.ws + (size_t)unit * (BM * BN) + row * BN + c0);
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+          for (int j = 0; j < 32; j += 4)
+            dst[j / 4] = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
                                      __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-              epi_store4<EPI>(p, base + j, v);
-            }
-          } else {
+          continue;
+        }
+        if (m >= p.M) continue;
+        const int nb = n0 + c0;
+        const int64_t base = zm_off + lay(p.on, nb);
+        if (contig && nb + 32 <= p.N && (base & 3) == 0) {
+          float4 ax[8];
+          if (EPI == kEpiResid || EPI == kEpiGeluBwd) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              int n = nb + j;
-              if (n < p.N) {
-                int64_t o = contig ? base + j : zm_off + lay(p.on, n);
-                epi_store1<EPI>(p, o, __uint_as_float(r[j]));
-              }
-            }
+            for (int j = 0; j < 8; ++j) ax[j] = __ldg(reinterpret_cast<const float4*>(p.aux + base) + j);
           }
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            epi_store4<EPI>(p, base + 4 * j,
+                            make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                        __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])),
+                            ax[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < p.N)
+              epi_store1<EPI>(p, contig ? base + j : zm_off + lay(p.on, nb + j), __uint_as_float(r[j]));
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -560,6 +585,42 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols));
+  }
+}
+
+// ---- split-K: sum the K slices of each tile in slice order (deterministic),
+// then the same epilogue as the GEMM.  One thread per 4 columns of a tile row.
+template <int EPI>
+__global__ void k_splitk_reduce(const TcKernelParams kp) {
+  const TcProblem& p = kp.pr;
+  const int per_batch = kp.tiles_m * kp.tiles_n;
+  const int64_t chunks = (int64_t)per_batch * p.batch * (BM * BN / 4);
+  const bool contig4 = (p.on.d1 % 4 == 0) && (p.on.d2 % 4 == 0) && p.on.s3 == 1;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < chunks;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int tile = (int)(q / (BM * BN / 4));
+    const int e = (int)(q % (BM * BN / 4)) * 4;    // element offset inside the tile
+    const int r = e / BN, c = e % BN;
+    const int z = tile / per_batch, rem = tile % per_batch;
+    const int m = (rem / kp.tiles_n) * BM + r, n = (rem % kp.tiles_n) * BN + c;
+    if (m >= p.M || n >= p.N) continue;
+    const float4* src = reinterpret_cast<const float4*>(kp.ws + (size_t)tile * kp.splits * (BM * BN) + e);
+    float4 v = src[0];
+    for (int sl = 1; sl < kp.splits; ++sl) {
+      float4 t = src[(size_t)sl * (BM * BN / 4)];
+      v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+    }
+    const int64_t zm = lay(p.oz, z) + lay(p.om, m);
+    const int64_t base = zm + lay(p.on, n);
+    if (contig4 && n + 4 <= p.N && (base & 3) == 0) {
+      float4 ax = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (EPI == kEpiResid || EPI == kEpiGeluBwd) ax = *reinterpret_cast<const float4*>(p.aux + base);
+      epi_store4<EPI>(p, base, v, ax);
+    } else {
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+      for (int j = 0; j < 4 && n + j < p.N; ++j)
+        epi_store1<EPI>(p, contig4 ? base + j : zm + lay(p.on, n + j), vv[j]);
+    }
   }
 }
 
@@ -637,6 +698,30 @@ CUtensorMap operand_map(const TcOperand& o, const float* plane) {
 
 int g_force_backend = -1;
 
+// K slices for a problem of `tiles` output tiles and nk k-blocks: split only
+// when the tiles fill less than half the SMs and every slice keeps >= 8 k-blocks
+// (the weight gradients dW = X^T dY, whose K is the token count).
+int splitk_for(int tiles, int nk) {
+  if (tiles * 2 > kNumSMs || nk < 16) return 1;
+  return std::max(1, std::min({kNumSMs / tiles, nk / 8, 64}));
+}
+
+// Device workspace for split-K partials, grown on demand (never shrinks).
+float* splitk_workspace(size_t floats) {
+  static float* buf[16] = {};
+  static size_t cap[16] = {};
+  int dev = 0;
+  MALUS_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 16) panic("split-K workspace: device index %d out of range", dev);
+  if (floats > cap[dev]) {
+    MALUS_CUDA(cudaStreamSynchronize(stream()));   // the old buffer may still be in use
+    if (buf[dev]) MALUS_CUDA(cudaFree(buf[dev]));
+    MALUS_CUDA(cudaMalloc(&buf[dev], floats * sizeof(float)));
+    cap[dev] = floats;
+  }
+  return buf[dev];
+}
+
 template <int EPI>
 void launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
                const CUtensorMap& bl, const TcKernelParams& kp, int grid) {
@@ -646,7 +731,12 @@ void launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& 
                                     kSmemBytes));
     attr = true;
   }
-  k_gemm_tc<EPI><<<grid, kThreadsTC, kSmemBytes, stream()>>>(ah, al, bh, bl, kp);
+  k_gemm_tc<EPI><<<grid, threads_tc(EPI), kSmemBytes, stream()>>>(ah, al, bh, bl, kp);
+  if (kp.splits > 1) {
+    int64_t chunks = (int64_t)kp.tiles_m * kp.tiles_n * kp.pr.batch * (BM * BN / 4);
+    unsigned g = (unsigned)std::min<int64_t>((chunks + 255) / 256, (int64_t)kNumSMs * 8);
+    k_splitk_reduce<EPI><<<g, 256, 0, stream()>>>(kp);
+  }
 }
 
 }  // namespace
@@ -698,7 +788,10 @@ void gemm_tc_planes(const TcProblem& pr) {
   kp.tiles_n = (pr.N + BN - 1) / BN;
   kp.nk = (pr.K + BK - 1) / BK;
   kp.err = device_error_word();
-  int total = kp.tiles_m * kp.tiles_n * pr.batch;
+  int tiles = kp.tiles_m * kp.tiles_n * pr.batch;
+  kp.splits = splitk_for(tiles, kp.nk);
+  kp.ws = kp.splits > 1 ? splitk_workspace((size_t)tiles * kp.splits * BM * BN) : nullptr;
+  int total = tiles * kp.splits;
   int grid = std::min(total, kNumSMs);
   double flops = 2.0 * pr.M * (double)pr.N * pr.K * pr.batch;
   int pid = prof_begin(0, flops, 8.0 * ((double)pr.M * pr.K + (double)pr.N * pr.K) * pr.batch +
@@ -709,7 +802,7 @@ void gemm_tc_planes(const TcProblem& pr) {
     case kEpiGelu: launch_tc<kEpiGelu>(ah, al, bh, bl, kp, grid); break;
     default: launch_tc<kEpiGeluBwd>(ah, al, bh, bl, kp, grid); break;
   }
-  count_launch();
+  count_launch(kp.splits > 1 ? 2 : 1);
   after_launch("k_gemm_tc");
   prof_end(pid);
 }

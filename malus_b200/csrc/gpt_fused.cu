@@ -118,7 +118,9 @@ __global__ void k_ln_fwd_split(const float* __restrict__ x, const float* __restr
 
 // Layernorm backward through the gain, plus the residual stream:
 //   dy = dz * g ; y = (x - mean)/sigma ; dx = ((dy - mean(dy)) - y*mean(dy*y)) / sqrt(var+eps)
-//   gout = resid + dx (f32 and optional tf32 planes); gain partials part[blk][c] += dz*y.
+//   gout = resid + dx (f32 and optional tf32 planes); gain partials part[blk][c] = sum dz*y.
+// One warp per row; lane l owns columns l + 32k, so each lane keeps its gain
+// partials in registers across rows; all of a row's loads are issued before use.
 template <int PER>
 __global__ void k_ln_bwd_fused(const float* __restrict__ x, const float* __restrict__ mean_in,
                                const float* __restrict__ var_in, const float* __restrict__ g,
@@ -127,48 +129,57 @@ __global__ void k_ln_bwd_fused(const float* __restrict__ x, const float* __restr
                                float* __restrict__ gout_lo, float* __restrict__ part, int M,
                                int C) {
   extern __shared__ float sacc[];  // [warps][C]
-  int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  int nwb = blockDim.x >> 5;
-  float* acc = sacc + (size_t)wib * C;
-  for (int i = lane; i < C; i += 32) acc[i] = 0.0f;
-  int warp = blockIdx.x * nwb + wib;
-  int nw = gridDim.x * nwb;
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int nwb = blockDim.x >> 5;
+  const int warp = blockIdx.x * nwb + wib;
+  const int nw = gridDim.x * nwb;
+  float gk[PER], gacc[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    int i = lane + 32 * k;
+    gk[k] = i < C ? g[i] : 0.0f;
+    gacc[k] = 0.0f;
+  }
   for (int r = warp; r < M; r += nw) {
-    const float* xr = x + (size_t)r * C;
-    const float* dr = dz + (size_t)r * C;
-    float mean = mean_in[r], var = var_in[r];
-    float sigma = sqrtf(var + kEps);
-    float inv = 1.0f / sqrtf(var + kEps);
-    float yv[PER], dy[PER];
+    const size_t ro = (size_t)r * C;
+    float xv[PER], dv[PER], rv[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      int i = lane + 32 * k;
+      xv[k] = i < C ? x[ro + i] : 0.0f;
+      dv[k] = i < C ? dz[ro + i] : 0.0f;
+      rv[k] = (resid && i < C) ? resid[ro + i] : 0.0f;
+    }
+    const float mean = mean_in[r], var = var_in[r];
+    const float sigma = sqrtf(var + kEps);
+    const float inv = 1.0f / sigma;
     float sg = 0.0f, sgy = 0.0f;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int i = lane + 32 * k;
-      if (i < C) {
-        float y = (xr[i] - mean) / sigma;
-        float d = dr[i];
-        acc[i] += d * y;
-        yv[k] = y;
-        dy[k] = d * g[i];
-      } else {
-        yv[k] = 0.0f;
-        dy[k] = 0.0f;
-      }
-      sg += dy[k];
-      sgy += dy[k] * yv[k];
+      float y = i < C ? (xv[k] - mean) / sigma : 0.0f;
+      gacc[k] += dv[k] * y;
+      xv[k] = y;                  // y from here on
+      dv[k] = dv[k] * gk[k];      // dy from here on
+      sg += dv[k];
+      sgy += dv[k] * y;
     }
-    float mg = wsum(sg) / (float)C, mgy = wsum(sgy) / (float)C;
+    const float mg = wsum(sg) / (float)C, mgy = wsum(sgy) / (float)C;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int i = lane + 32 * k;
       if (i < C) {
-        size_t o = (size_t)r * C + i;
-        float v = ((dy[k] - mg) - yv[k] * mgy) * inv;
-        if (resid) v = resid[o] + v;
-        gout[o] = v;
-        if (gout_hi) split_store(gout_hi, gout_lo, o, v);
+        float v = ((dv[k] - mg) - xv[k] * mgy) * inv;
+        if (resid) v = rv[k] + v;
+        gout[ro + i] = v;
+        if (gout_hi) split_store(gout_hi, gout_lo, ro + i, v);
       }
     }
+  }
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    int i = lane + 32 * k;
+    if (i < C) sacc[(size_t)wib * C + i] = gacc[k];
   }
   __syncthreads();
   // block partial = sum over its warps (fixed order)
@@ -179,12 +190,25 @@ __global__ void k_ln_bwd_fused(const float* __restrict__ x, const float* __restr
   }
 }
 
+// out[c] = sum_b part[b][c] in a fixed order: 8 row groups per column, then
+// the 8 group sums in order.  Block = 32 columns x 8 row groups.
 __global__ void k_colsum(const float* __restrict__ part, float* __restrict__ out, int nblk, int C) {
-  int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
+  __shared__ float sh[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + tx;
   float s = 0.0f;
-  for (int b = 0; b < nblk; ++b) s += part[(size_t)b * C + c];
-  out[c] = s;
+  if (c < C) {
+#pragma unroll 4
+    for (int b = ty; b < nblk; b += 8) s += part[(size_t)b * C + c];
+  }
+  sh[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < C) {
+    float t = sh[0][tx];
+#pragma unroll
+    for (int q = 1; q < 8; ++q) t += sh[q][tx];
+    out[c] = t;
+  }
 }
 
 // Causal softmax of one row of S (already scaled): P planes.  -1e9 above the
@@ -411,7 +435,7 @@ void ln_bwd(FusedStep* f, const float* x, const float* mean, const float* var, c
   size_t smem = (size_t)(threads / 32) * f->C * sizeof(float);
   PER_DISPATCH(f->C, (k_ln_bwd_fused<P_><<<f->part_blocks, threads, smem, stream()>>>(
                           x, mean, var, g, dz, resid, gout, gpl.hi, gpl.lo, f->part, f->M, f->C)));
-  k_colsum<<<(f->C + 255) / 256, 256, 0, stream()>>>(f->part, dgain, f->part_blocks, f->C);
+  k_colsum<<<(f->C + 31) / 32, 256, 0, stream()>>>(f->part, dgain, f->part_blocks, f->C);
   count_launch(2);
   after_launch("k_ln_bwd_fused");
 }

@@ -143,10 +143,75 @@ def cases(b: Bench, rng):
         W = b.T(rng.standard_normal((kk, nn), dtype=np.float32))
         yield f"matmul {mm}x{kk}x{nn} ({label})", (lambda A=A, W=W: lib.tensor_matmul(A.h, W.h)), \
             (mm * kk + kk * nn + mm * nn) * F, 2.0 * mm * nn * kk
+    yield from plane_cases(b, rng)
     Q = b.T(rng.standard_normal((384, 256, 64), dtype=np.float32))
     Kt = b.T(rng.standard_normal((384, 64, 256), dtype=np.float32))
     yield "bmm 384x256x64x256 (QK^T)", lambda: lib.tensor_matmul(Q.h, Kt.h), \
         (2 * 384 * 256 * 64 + 384 * 256 * 256) * F, 2.0 * 384 * 256 * 256 * 64
+
+
+def plane_cases(b: Bench, rng):
+    """The fused step's GEMMs at the C4 shapes, on pre-split tf32 planes through
+    malus_tc_gemm (operands and outputs exactly as the step lays them out)."""
+    lib = b.lib
+    Mt, Cc, H, T, hs = 16384, 384, 6, 256, 64
+    C4, Bz = 4 * Cc, 64
+
+    def buf(*shape, rand=True):
+        a = rng.standard_normal(shape, dtype=np.float32) * 0.1 if rand else np.zeros(shape, np.float32)
+        return lib.malus_tensor_data(b.T(a).h)
+
+    def op(rows, cols, mn, nz=1, zmode=0, seg=0):
+        return M.TcOperand(buf(nz, rows, cols), buf(nz, rows, cols), rows, cols, cols, nz, rows * cols,
+                           int(mn), zmode, seg)
+
+    def L(d1=0, s1=0, d2=0, s2=0, s3=0):
+        return M.TcLayout(d1, s1, d2, s2, s3)
+
+    def prob(Mm, N, K, batch, a, bb, epi=0, oz=None, om=None, on=None, out=False, planes=False, aux=False,
+             alpha=1.0):
+        q = M.TcProblem()
+        q.M, q.N, q.K, q.batch, q.a, q.b, q.epi = Mm, N, K, batch, a, bb, epi
+        q.oz, q.om, q.on = oz or L(), om or L(s3=N), on or L(s3=1)
+        n_out = Mm * N * batch
+        q.out = buf(n_out, rand=False) if out else None
+        if planes:
+            q.out_hi, q.out_lo = buf(n_out, rand=False), buf(n_out, rand=False)
+        q.aux = buf(n_out) if aux else None
+        q.alpha, q.beta = alpha, 0.0
+        return q
+
+    def run(q):
+        lib.malus_tc_gemm(C.byref(q))
+        return 0
+
+    def nbytes(q, Mm, N, K, batch, n_out_arrays, aux):
+        return (8 * (Mm * K + N * K) * batch + 4 * Mm * N * batch * (n_out_arrays + int(aux)))
+
+    cases_ = [
+        ("tc QKV (planes out, head fold)", prob(Mt, 3 * Cc, Cc, 1, op(Mt, Cc, False),
+                                                op(Cc, Cc, True, 3, 3, Cc), planes=True,
+                                                om=L(T, H * T * hs, 0, 0, hs),
+                                                on=L(Cc, Bz * H * T * hs, hs, T * hs, 1)), (Mt, 3 * Cc, Cc, 1, 2, False)),
+        ("tc attn S=QK^T (f32 out)", prob(T, T, hs, Bz * H, op(T, hs, False, Bz * H, 1),
+                                          op(T, hs, False, Bz * H, 1), out=True, oz=L(s3=T * T),
+                                          om=L(s3=T), alpha=0.125), (T, T, hs, Bz * H, 1, False)),
+        ("tc attn O=PV (planes, unfold)", prob(T, hs, T, Bz * H, op(T, T, False, Bz * H, 1),
+                                               op(T, hs, True, Bz * H, 1), planes=True,
+                                               oz=L(H, T * Cc, 0, 0, hs), om=L(s3=Cc)), (T, hs, T, Bz * H, 2, False)),
+        ("tc proj + residual", prob(Mt, Cc, Cc, 1, op(Mt, Cc, False), op(Cc, Cc, True), epi=1, out=True,
+                                    aux=True), (Mt, Cc, Cc, 1, 1, True)),
+        ("tc MLP up + GELU", prob(Mt, C4, Cc, 1, op(Mt, Cc, False), op(Cc, C4, True), epi=2, out=True,
+                                  planes=True), (Mt, C4, Cc, 1, 3, False)),
+        ("tc MLP down + residual", prob(Mt, Cc, C4, 1, op(Mt, C4, False), op(C4, Cc, True), epi=1,
+                                        out=True, aux=True), (Mt, Cc, C4, 1, 1, True)),
+        ("tc GELU backward", prob(Mt, C4, Cc, 1, op(Mt, Cc, False), op(C4, Cc, False), epi=3, planes=True,
+                                  aux=True), (Mt, C4, Cc, 1, 2, True)),
+        ("tc dW1 = xn^T dh (split-K)", prob(Cc, C4, Mt, 1, op(Mt, Cc, True), op(Mt, C4, True), out=True),
+         (Cc, C4, Mt, 1, 1, False)),
+    ]
+    for name, q, (Mm, N, K, batch, nout, aux) in cases_:
+        yield name, (lambda q=q: run(q)), nbytes(q, Mm, N, K, batch, nout, aux), 2.0 * Mm * N * K * batch
 
 
 def main():

@@ -222,3 +222,70 @@ def test_mnseg_tiles_straddle_segments(M, rt, rng, side, mn, seg, nseg):
         out = dev(M, np.zeros((Mm, N)))
         run(M, rt, Mm, N, K, 1, xo, so, out=out)
     assert err(out.numpy(), A.astype(np.float64) @ B, A, B) < 1e-4
+
+
+@pytest.mark.parametrize("Mm,N,K", [(384, 1536, 16384), (65, 384, 16384), (384, 384, 4096), (200, 100, 2000)])
+def test_splitk_weight_gradient_shapes(M, rt, rng, Mm, N, K):
+    """dW = X^T dY: few output tiles and a long K are computed as K slices; the
+    slices are summed in a fixed order, so two runs agree bit for bit."""
+    X = rng.standard_normal((K, Mm)).astype(np.float32)
+    D = rng.standard_normal((K, N)).astype(np.float32)
+    ao = operand(M, rt, X, True)           # A = X^T: X stored [K][M], MN-major
+    bo = operand(M, rt, D, True)           # B = dY stored [K][N], MN-major
+    out = dev(M, np.zeros((Mm, N)))
+    run(M, rt, Mm, N, K, 1, ao, bo, out=out)
+    got = out.numpy()
+    A = X.T
+    assert err(got, A.astype(np.float64) @ D, A, D) < 1e-4
+    out2 = dev(M, np.zeros((Mm, N)))
+    run(M, rt, Mm, N, K, 1, ao, bo, out=out2)
+    assert np.array_equal(got, out2.numpy())
+
+
+def test_splitk_nseg_output_and_epilogues(M, rt, rng):
+    """Split-K with the dWqkv output map (N segments into three [C][C] slices),
+    alpha/beta, and the residual / GELU / GELU-backward epilogues."""
+    Cc, K = 96, 8192
+    X = rng.standard_normal((K, Cc)).astype(np.float32) * 0.1
+    D = rng.standard_normal((3, K, Cc)).astype(np.float32) * 0.1
+    ao = operand(M, rt, X, True)
+    bo = operand(M, rt, D, True, zmode=3, seg=Cc)
+    out = dev(M, np.zeros((3, Cc, Cc)))
+    run(M, rt, Cc, 3 * Cc, K, 1, ao, bo, out=out, om=lay(s3=Cc), on=lay(Cc, Cc * Cc, 0, 0, 1))
+    for j in range(3):
+        assert err(out.numpy()[j], X.T.astype(np.float64) @ D[j], X.T, D[j]) < 1e-4
+    B = D[0]
+    ref = X.T.astype(np.float64) @ B
+    bo1 = operand(M, rt, B, True)
+    C0 = rng.standard_normal((Cc, Cc)).astype(np.float32)
+    o = dev(M, C0)
+    run(M, rt, Cc, Cc, K, 1, ao, bo1, out=o, alpha=0.5, beta=2.0)
+    assert err(o.numpy() - 2.0 * C0, 0.5 * ref, X.T, B) < 2e-4
+    R = dev(M, C0)
+    o = dev(M, np.zeros((Cc, Cc)))
+    run(M, rt, Cc, Cc, K, 1, ao, bo1, epi=1, out=o, aux=R)
+    assert err(o.numpy() - C0, ref, X.T, B) < 2e-4
+    hi, lo = dev(M, np.zeros((Cc, Cc))), dev(M, np.zeros((Cc, Cc)))
+    run(M, rt, Cc, Cc, K, 1, ao, bo1, epi=2, out=o, out_hi=hi, out_lo=lo)
+    g = 0.5 * ref * (1 + np.tanh(0.7978845608028654 * (ref + 0.044715 * ref ** 3)))
+    assert np.max(np.abs(hi.numpy().astype(np.float64) + lo.numpy() - g)) < 1e-4 * np.max(np.abs(ref))
+    run(M, rt, Cc, Cc, K, 1, ao, bo1, epi=3, out=o, out_hi=hi, out_lo=lo, aux=R)
+    x = C0.astype(np.float64)
+    t = np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3))
+    gp = 0.7978845608028654 * (1 + 3 * 0.044715 * x * x)
+    dref = ref * (0.5 * (1 + t) + 0.5 * x * (1 - t * t) * gp)
+    scale = (np.abs(X.T).astype(np.float64) @ np.abs(B)) * np.max(np.abs(0.5 * (1 + t) + 0.5 * x * (1 - t * t) * gp))
+    assert np.max(np.abs(o.numpy() - dref) / scale) < 2e-4
+
+
+def test_splitk_batched(M, rt, rng):
+    """Batched problems with one tile each and a long K also take K slices."""
+    Z, Mm, N, K = 3, 64, 48, 4096
+    A = rng.standard_normal((Z, Mm, K)).astype(np.float32)
+    B = rng.standard_normal((Z, K, N)).astype(np.float32)
+    ao = operand(M, rt, A, False, zmode=1)
+    bo = operand(M, rt, B, True, zmode=1)
+    out = dev(M, np.zeros((Z, Mm, N)))
+    run(M, rt, Mm, N, K, Z, ao, bo, out=out, oz=lay(s3=Mm * N))
+    for z in range(Z):
+        assert err(out.numpy()[z], A[z].astype(np.float64) @ B[z], A[z], B[z]) < 1e-4
