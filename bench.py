@@ -112,10 +112,13 @@ class ClockSampler:
 
 
 def traffic_from_profiles(kernel: str):
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
+    capture of this bench command (profiles/roofline_traffic.json)."""
     p = ROOT / "profiles" / "roofline_traffic.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return d.get(kernel)
+        e = d.get(kernel)
+        return e.get("bytes_per_launch") if isinstance(e, dict) else e
     return None
 
 
@@ -275,6 +278,7 @@ def main():
                     "achieved": round(algo, 2), "peak": round(f32_peak, 2), "unit": "TFLOP/s",
                     "frac": round(algo / f32_peak, 4),
                     "traffic": traffic_from_profiles("k_gemm_tc"),
+                    "algorithmic_bytes_per_launch": round(by_k.value / cnt.value),
                     "launches_per_step": cnt.value / args.steps,
                     "gemm_share_of_step": round(ms_k.value / dt_ms, 4) if world == 1 else None,
                     "executed_tf32_tflops": round(3.0 * algo, 2),

@@ -794,8 +794,11 @@ void gemm_tc_planes(const TcProblem& pr) {
   int total = tiles * kp.splits;
   int grid = std::min(total, kNumSMs);
   double flops = 2.0 * pr.M * (double)pr.N * pr.K * pr.batch;
+  // algorithmic bytes: both operands' hi/lo planes once, each output array and aux once
+  const double mn = (double)pr.M * pr.N * pr.batch;
+  const int arrays = (pr.out ? 1 : 0) + (pr.out_hi ? 2 : 0) + (pr.aux ? 1 : 0);
   int pid = prof_begin(0, flops, 8.0 * ((double)pr.M * pr.K + (double)pr.N * pr.K) * pr.batch +
-                                     4.0 * (double)pr.M * pr.N * pr.batch);
+                                     4.0 * mn * arrays);
   switch (pr.epi) {
     case kEpiStore: launch_tc<kEpiStore>(ah, al, bh, bl, kp, grid); break;
     case kEpiResid: launch_tc<kEpiResid>(ah, al, bh, bl, kp, grid); break;
