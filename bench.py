@@ -206,15 +206,8 @@ def main():
     lib = M.load()
     lib.malus_set_device(local)
     if world > 1:
-        idb = (C.c_uint8 * 128)()
-        if rank == 0:
-            assert lib.malus_dp_unique_id(idb) == 0
-        t = torch.tensor(list(bytes(idb)), dtype=torch.uint8, device="cuda")
-        dist.broadcast(t, 0)
-        idb = (C.c_uint8 * 128)(*t.cpu().tolist())
-        rc = lib.malus_dp_init(rank, world, idb, 120000)
-        if rc != 0:
-            raise RuntimeError(f"malus_dp_init failed: {rc}")
+        from malus_b200.dist import init_data_parallel
+        init_data_parallel(lib, rank, world, timeout_ms=120000)
 
     cfg = dict(C4)
     model = M.GPT(**cfg, **OPT, mode=args.mode, seed=0)

@@ -268,6 +268,8 @@ int32_t malus_dp_init(int32_t rank, int32_t world, const uint8_t* nccl_id, int32
 int32_t malus_dp_allreduce_f32(void* dev_ptr, size_t count);
 int32_t malus_dp_finish(void);   /* wait for outstanding collectives */
 int32_t malus_dp_destroy(void);
+/* Abort the communicator without contacting peers (after one is known lost). */
+int32_t malus_dp_abort(void);
 int32_t malus_dp_world(void);
 
 /* The compiled nanoGPT training step (replaces the per-step call sequence of
@@ -299,6 +301,16 @@ int64_t malus_gpt_param(int64_t model, int32_t i);
  * data-parallel ranks), same shape; a borrowed handle like malus_gpt_param. */
 int64_t malus_gpt_grad(int64_t model, int32_t i);
 int64_t malus_gpt_num_elements(int64_t model);
+/* Host-only (no device work): the fused parameter/gradient buffer layout for a
+ * config.  Writes offsets[i] and sizes[i] (elements) for the first n tensors,
+ * *total = buffer length in elements (slices 256-byte aligned); returns the
+ * tensor count. */
+int32_t malus_gpt_layout(const malus_gpt_config* cfg, int64_t* offsets, int64_t* sizes, int32_t n,
+                         int64_t* total);
+/* Host-only: the data-parallel all-reduce buckets of the fused step in issue
+ * order ([lo, hi) element ranges of the gradient buffer: each layer, last
+ * first, then embeddings / final norm / head); returns the bucket count. */
+int32_t malus_gpt_dp_buckets(const malus_gpt_config* cfg, int64_t* lo, int64_t* hi, int32_t n);
 
 /* tcgen05 3xTF32 GEMM on pre-split tf32 operand planes, with fused epilogues.
  * Each f32 operand x is given as two planes hi = tf32_rn(x), lo = tf32_rn(x -

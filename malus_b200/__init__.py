@@ -178,6 +178,7 @@ SIGNATURES: dict[str, tuple] = {
     "malus_dp_allreduce_f32": (i32, [vp, sz]),
     "malus_dp_finish": (i32, []),
     "malus_dp_destroy": (i32, []),
+    "malus_dp_abort": (i32, []),
     "malus_dp_world": (i32, []),
     "malus_gpt_create": (i64, [C.POINTER(GptConfig)]),
     "malus_gpt_destroy": (None, [i64]),
@@ -188,6 +189,8 @@ SIGNATURES: dict[str, tuple] = {
     "malus_gpt_param": (i64, [i64, i32]),
     "malus_gpt_grad": (i64, [i64, i32]),
     "malus_gpt_num_elements": (i64, [i64]),
+    "malus_gpt_layout": (i32, [C.POINTER(GptConfig), P_i64, P_i64, i32, P_i64]),
+    "malus_gpt_dp_buckets": (i32, [C.POINTER(GptConfig), P_i64, P_i64, i32]),
     "malus_device_error": (i32, []),
     "malus_tc_gemm": (None, [C.POINTER(TcProblem)]),
     "malus_tf32_split": (None, [vp, i64, i64, i64, i64, i64, vp, vp, i64]),

@@ -211,4 +211,10 @@ void adamw_multi(const AdamSeg* segs, int nseg, float lr, float b1, float b2, fl
 // ---- tape (tape.cpp) ----
 void tape_on_release(int64_t h);
 
+// nanoGPT fused-buffer layout and its data-parallel all-reduce buckets (gpt.cu)
+size_t gpt_layout(const malus_gpt_config& c, std::vector<std::vector<size_t>>& shapes,
+                  std::vector<size_t>& offs, std::vector<size_t>& sizes);
+std::vector<std::pair<size_t, size_t>> gpt_dp_buckets(int n_layer, const std::vector<size_t>& offs,
+                                                      const std::vector<size_t>& sizes);
+
 }  // namespace malus

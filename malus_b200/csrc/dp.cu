@@ -172,4 +172,10 @@ int32_t malus_dp_destroy(void) {
 
 int32_t malus_dp_world(void) { return g_world; }
 
+// Local teardown after a peer is known to be gone: ncclCommAbort needs no peer.
+int32_t malus_dp_abort(void) {
+  abort_comm();
+  return 0;
+}
+
 }  // extern "C"

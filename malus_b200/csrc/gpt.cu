@@ -217,23 +217,29 @@ void tape_step(Model& m) {
   for (int64_t g : grads) tensor_release(g);
 }
 
+// Under data parallelism, wait (bounded) for this step's collectives before a
+// blocking host read: a lost peer aborts the communicator (its NCCL kernels
+// end) and the process reports the failure instead of blocking forever.
+void dp_drain_or_die() {
+  if (dp_world() <= 1) return;
+  int r = malus_dp_finish();
+  if (r != 0) panic("data-parallel step failed: a peer was lost or timed out (%d)", r);
+}
+
 }  // namespace
 
-extern "C" {
+namespace malus {
 
-int64_t malus_gpt_create(const malus_gpt_config* cfgp) {
-  auto* m = new Model();
-  m->cfg = *cfgp;
-  auto& c = m->cfg;
-  m->C = c.n_embd; m->H = c.n_head; m->T = c.block_size; m->B = c.batch; m->V = c.vocab;
-  m->L = c.n_layer; m->C4 = 4 * c.n_embd;
-  if (m->C % m->H) panic("n_embd %d not divisible by n_head %d", m->C, m->H);
-  m->hs = m->C / m->H;
-  m->M = (size_t)m->B * m->T;
-  size_t C = m->C, C4 = m->C4, V = m->V, T = m->T;
-  // parameter layout (nanogpt_modular.ml:112-125, 150-162)
-  std::vector<std::vector<size_t>> shapes;
-  for (int l = 0; l < m->L; ++l) {
+// Parameter layout of the fused buffers (nanogpt_modular.ml:112-125, 150-162):
+// per block [ln1, wq, wk, wv, wo, ln2, w1, w2], then [wte, wpe, ln_f, (lm_head)],
+// each slice 256-byte aligned.  Returns the buffer length in elements.
+size_t gpt_layout(const malus_gpt_config& c, std::vector<std::vector<size_t>>& shapes,
+                  std::vector<size_t>& offs, std::vector<size_t>& sizes) {
+  const size_t C = c.n_embd, C4 = 4 * (size_t)c.n_embd, V = c.vocab, T = c.block_size;
+  shapes.clear();
+  offs.clear();
+  sizes.clear();
+  for (int l = 0; l < c.n_layer; ++l) {
     shapes.push_back({C});
     for (int j = 0; j < 4; ++j) shapes.push_back({C, C});
     shapes.push_back({C});
@@ -248,10 +254,67 @@ int64_t malus_gpt_create(const malus_gpt_config* cfgp) {
   for (auto& s : shapes) {
     size_t n = 1;
     for (size_t d : s) n *= d;
-    m->offs.push_back(off);
-    m->sizes.push_back(n);
-    off += (n + 63) & ~size_t(63);  // 256-byte aligned slices
+    offs.push_back(off);
+    sizes.push_back(n);
+    off += (n + 63) & ~size_t(63);
   }
+  return off;
+}
+
+// All-reduce buckets of the fused step in issue order: each layer's slice as soon
+// as its backward is done (last layer first), then embeddings, final norm, head.
+std::vector<std::pair<size_t, size_t>> gpt_dp_buckets(int n_layer, const std::vector<size_t>& offs,
+                                                      const std::vector<size_t>& sizes) {
+  std::vector<std::pair<size_t, size_t>> b;
+  for (int l = n_layer - 1; l >= 0; --l) {
+    size_t first = (size_t)l * 8, last = first + 7;
+    b.push_back({offs[first], offs[last] + sizes[last]});
+  }
+  size_t top = (size_t)n_layer * 8;
+  b.push_back({offs[top], offs.back() + sizes.back()});
+  return b;
+}
+
+}  // namespace malus
+
+extern "C" {
+
+int32_t malus_gpt_layout(const malus_gpt_config* cfg, int64_t* offsets, int64_t* sizes, int32_t n,
+                         int64_t* total) {
+  std::vector<std::vector<size_t>> shapes;
+  std::vector<size_t> o, z;
+  size_t t = gpt_layout(*cfg, shapes, o, z);
+  for (size_t i = 0; i < o.size() && (int32_t)i < n; ++i) {
+    if (offsets) offsets[i] = (int64_t)o[i];
+    if (sizes) sizes[i] = (int64_t)z[i];
+  }
+  if (total) *total = (int64_t)t;
+  return (int32_t)o.size();
+}
+
+int32_t malus_gpt_dp_buckets(const malus_gpt_config* cfg, int64_t* lo, int64_t* hi, int32_t n) {
+  std::vector<std::vector<size_t>> shapes;
+  std::vector<size_t> o, z;
+  gpt_layout(*cfg, shapes, o, z);
+  auto b = gpt_dp_buckets(cfg->n_layer, o, z);
+  for (size_t i = 0; i < b.size() && (int32_t)i < n; ++i) {
+    if (lo) lo[i] = (int64_t)b[i].first;
+    if (hi) hi[i] = (int64_t)b[i].second;
+  }
+  return (int32_t)b.size();
+}
+
+int64_t malus_gpt_create(const malus_gpt_config* cfgp) {
+  auto* m = new Model();
+  m->cfg = *cfgp;
+  auto& c = m->cfg;
+  m->C = c.n_embd; m->H = c.n_head; m->T = c.block_size; m->B = c.batch; m->V = c.vocab;
+  m->L = c.n_layer; m->C4 = 4 * c.n_embd;
+  if (m->C % m->H) panic("n_embd %d not divisible by n_head %d", m->C, m->H);
+  m->hs = m->C / m->H;
+  m->M = (size_t)m->B * m->T;
+  std::vector<std::vector<size_t>> shapes;
+  size_t off = gpt_layout(c, shapes, m->offs, m->sizes);
   m->total = off;
   MALUS_CUDA(cudaMalloc(&m->pbuf, off * 4));
   MALUS_CUDA(cudaMalloc(&m->mbuf, off * 4));
@@ -361,6 +424,7 @@ float malus_gpt_step(int64_t h, const int32_t* x, const int32_t* y) {
   MALUS_CUDA(cudaMemcpyAsync(m->y_dev, m->y_pin, m->M * 4, cudaMemcpyHostToDevice, stream()));
   malus_gpt_step_device(h, m->x_dev, m->y_dev);
   MALUS_CUDA(cudaMemcpyAsync(m->loss_pin, m->loss_dev, 4, cudaMemcpyDeviceToHost, stream()));
+  dp_drain_or_die();
   gpu_barrier();
   return m->loss_pin[0];
 }
@@ -369,6 +433,7 @@ float malus_gpt_last_loss(int64_t h) {
   auto* m = reinterpret_cast<Model*>(h);
   float v;
   MALUS_CUDA(cudaMemcpyAsync(&v, m->loss_dev, 4, cudaMemcpyDeviceToHost, stream()));
+  dp_drain_or_die();
   gpu_barrier();
   return v;
 }

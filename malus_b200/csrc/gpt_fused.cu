@@ -363,6 +363,7 @@ struct FusedStep {
   float scale;
   std::vector<float*> params;
   std::vector<size_t> sizes, goff;
+  std::vector<std::pair<size_t, size_t>> buckets;   // DP all-reduce ranges, issue order
   float* gbuf;
   std::vector<float*> allocs;
   // weight planes (mirror of the parameter layout) and the padded LM head planes
@@ -481,6 +482,7 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
   f->gbuf = gbuf;
   f->goff = goff;
   f->poff = goff;   // parameters and gradients share the slice layout
+  f->buckets = gpt_dp_buckets(f->L, goff, sizes);
   size_t total = goff.back() + ((sizes.back() + 63) & ~size_t(63));
   f->wpl = palloc(f, total);
   if (!cfg.tied) f->lmpl = palloc(f, (size_t)f->C * f->Vp);
@@ -658,8 +660,9 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     ln_bwd(f, f->x[l], f->mean1[l], f->var1[l], P(b), f->dxn, g2, g3, g3p, G(b));
     if (dp_world() > 1) {
       // this layer's gradients are final: reduce them while earlier layers run
-      size_t lo = f->goff[b], hi = f->goff[b + 7] + f->sizes[b + 7];
-      if (dp_allreduce_async(f->gbuf + lo, hi - lo) != 0) panic("data-parallel all-reduce failed");
+      const auto& bk = f->buckets[(size_t)(Lc - 1 - l)];
+      if (dp_allreduce_async(f->gbuf + bk.first, bk.second - bk.first) != 0)
+        panic("data-parallel all-reduce failed (peer lost or timed out)");
     }
   }
   // embeddings: x0 = wte[tok] + wpe[pos]
@@ -673,9 +676,9 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
   }
   reduce_axis(kRSum, g3, G(top + 1), 1, B, (size_t)T * C);   // dwpe = sum over batch
   if (dp_world() > 1) {
-    size_t lo = f->goff[top];
-    size_t hi = f->goff.back() + f->sizes.back();
-    if (dp_allreduce_async(f->gbuf + lo, hi - lo) != 0) panic("data-parallel all-reduce failed");
+    const auto& bk = f->buckets.back();
+    if (dp_allreduce_async(f->gbuf + bk.first, bk.second - bk.first) != 0)
+      panic("data-parallel all-reduce failed (peer lost or timed out)");
     dp_join();
   }
 }
