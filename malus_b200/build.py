@@ -25,6 +25,26 @@ CFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
           "--expt-relaxed-constexpr", f"-I{ROOT / 'include'}"]
 
 
+def _nccl_dir() -> Path | None:
+    """The NCCL that torch itself loads (the nvidia-nccl wheel), so that this
+    library and torch share one libnccl.so.2 whichever is loaded first."""
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia")
+        for base in (spec.submodule_search_locations if spec else []):
+            d = Path(base) / "nccl"
+            if (d / "lib" / "libnccl.so.2").exists() and (d / "include" / "nccl.h").exists():
+                return d
+    except Exception:
+        pass
+    return None
+
+
+NCCL = _nccl_dir()
+if NCCL is not None:
+    CFLAGS.append(f"-I{NCCL / 'include'}")
+
+
 def _headers() -> list[Path]:
     return sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
 
@@ -61,8 +81,12 @@ def build(verbose: bool = False) -> Path:
     srcs = sorted(CSRC.glob("*.cu"))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
-    if _needs(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lnccl"]
+    if _needs(LIB, objs + [Path(__file__)]):
+        if NCCL is not None:
+            nccl = [f"-L{NCCL / 'lib'}", "-l:libnccl.so.2", "-Xlinker", f"-rpath={NCCL / 'lib'}"]
+        else:
+            nccl = ["-lnccl"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), *nccl]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
