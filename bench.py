@@ -184,6 +184,8 @@ def main():
     ap.add_argument("--impl", default="malus", choices=["malus", "reference"])
     ap.add_argument("--mode", type=int, default=int(os.environ.get("MALUS_BENCH_MODE", "1")))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", type=int, default=int(os.environ.get("MALUS_BENCH_GRAPH", "1")),
+                    help="replay the fused step as one CUDA graph (mode 1)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -210,7 +212,7 @@ def main():
         init_data_parallel(lib, rank, world, timeout_ms=120000)
 
     cfg = dict(C4)
-    model = M.GPT(**cfg, **OPT, mode=args.mode, seed=0)
+    model = M.GPT(**cfg, **OPT, mode=args.mode, use_graph=args.graph if args.mode == 1 else 0, seed=0)
     m = cfg["batch"] * cfg["block_size"]
     rng = np.random.default_rng(1000 + rank)
     nb = args.steps + args.warmup
@@ -316,6 +318,7 @@ def main():
                            "model": "char-nanoGPT", "global_batch": cfg["batch"] * world,
                            "seq_len": cfg["block_size"], "parallelism": f"dp{world}",
                            "mode": "fused" if args.mode == 1 else "tape",
+                           "cuda_graph": bool(args.graph and args.mode == 1),
                            "l2": "working set (activations, several GB) exceeds the 126 MB L2"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
                 "clocks": clk.summary(), "loss_last": loss_last,

@@ -34,8 +34,17 @@ __device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, 
   p = __fsub_rn(p, upd);
 }
 
+// bc_tab (optional): host-computed bias corrections per step, [2*(t-1)] = 1 - b1**t,
+// [2*(t-1)+1] = 1 - b2**t, indexed by the device step counter *step_dev, so a
+// captured CUDA graph replays with the current step's values.
 __global__ void k_adamw(SegTable t, int nseg, int64_t total4, float lr, float b1, float b2,
-                        float eps, float wd, float c1, float c2, float bc1, float bc2, float gs) {
+                        float eps, float wd, float c1, float c2, float bc1, float bc2, float gs,
+                        const float* __restrict__ bc_tab, const int64_t* __restrict__ step_dev) {
+  if (bc_tab) {
+    const int64_t st = *step_dev;
+    bc1 = bc_tab[2 * (st - 1)];
+    bc2 = bc_tab[2 * (st - 1) + 1];
+  }
   int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   int64_t step = (int64_t)gridDim.x * blockDim.x;
   int s = 0;
@@ -61,6 +70,12 @@ __global__ void k_adamw(SegTable t, int nseg, int64_t total4, float lr, float b1
 
 void adamw_multi(const AdamSeg* segs, int nseg, float lr, float b1, float b2, float eps, float wd,
                  float bc1, float bc2, float grad_scale) {
+  adamw_multi_tab(segs, nseg, lr, b1, b2, eps, wd, bc1, bc2, grad_scale, nullptr, nullptr);
+}
+
+void adamw_multi_tab(const AdamSeg* segs, int nseg, float lr, float b1, float b2, float eps,
+                     float wd, float bc1, float bc2, float grad_scale, const float* bc_tab,
+                     const int64_t* step_dev) {
   float c1 = 1.0f - b1, c2 = 1.0f - b2;  // the host-side (1.0 - beta) literals
   for (int base = 0; base < nseg; base += 64) {
     int n = std::min(64, nseg - base);
@@ -74,7 +89,8 @@ void adamw_multi(const AdamSeg* segs, int nseg, float lr, float b1, float b2, fl
     t.start[n] = acc;
     if (acc == 0) continue;
     k_adamw<<<grid_for((size_t)acc, 256), 256, 0, stream()>>>(t, n, acc, lr, b1, b2, eps, wd, c1,
-                                                              c2, bc1, bc2, grad_scale);
+                                                              c2, bc1, bc2, grad_scale, bc_tab,
+                                                              step_dev);
     count_launch();
     after_launch("k_adamw");
   }

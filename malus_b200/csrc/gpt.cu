@@ -26,11 +26,11 @@ void dp_join();
 int dp_world();
 struct FusedStep;
 FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& params,
-                        const std::vector<size_t>& sizes, float* grad_base,
-                        const std::vector<size_t>& grad_offsets);
+                        const std::vector<size_t>& sizes, float* gbuf,
+                        const std::vector<size_t>& goff, float* pbuf, float* mbuf, float* vbuf,
+                        size_t total_elems);
 void fused_destroy(FusedStep* f);
-void fused_step(FusedStep* f, const int32_t* x_dev, const int32_t* y_dev, float* loss_dev);
-void fused_after_update(FusedStep* f);
+void fused_train_step(FusedStep* f, const int32_t* x_dev, const int32_t* y_dev, float* loss_dev);
 }  // namespace malus
 
 using namespace malus;
@@ -371,7 +371,7 @@ int64_t malus_gpt_create(const malus_gpt_config* cfgp) {
   if (c.mode == 1) {
     std::vector<float*> ps;
     for (size_t i = 0; i < m->params.size(); ++i) ps.push_back(m->pbuf + m->offs[i]);
-    m->fused = fused_create(c, ps, m->sizes, m->gbuf, m->offs);
+    m->fused = fused_create(c, ps, m->sizes, m->gbuf, m->offs, m->pbuf, m->mbuf, m->vbuf, m->total);
   }
   gpu_barrier();
   return reinterpret_cast<int64_t>(m);
@@ -402,15 +402,7 @@ void malus_gpt_step_device(int64_t h, const int32_t* x_dev, const int32_t* y_dev
     MALUS_CUDA(cudaMemcpyAsync(m->y_dev, y_dev, m->M * 4, cudaMemcpyDeviceToDevice, stream()));
   if (m->cfg.mode == 1) {
     m->step++;
-    fused_step(m->fused, m->x_dev, m->y_dev, m->loss_dev);
-    float gscale = 1.0f;
-    if (dp_world() > 1) gscale = 1.0f / (float)dp_world();
-    float bc1 = 1.0f - powf(m->cfg.beta1, (float)m->step);
-    float bc2 = 1.0f - powf(m->cfg.beta2, (float)m->step);
-    AdamSeg seg{m->pbuf, m->gbuf, m->mbuf, m->vbuf, (int64_t)m->total};
-    adamw_multi(&seg, 1, m->cfg.lr, m->cfg.beta1, m->cfg.beta2, m->cfg.eps, m->cfg.wd, bc1, bc2,
-                gscale);
-    fused_after_update(m->fused);
+    fused_train_step(m->fused, m->x_dev, m->y_dev, m->loss_dev);
   } else {
     tape_step(*m);
   }

@@ -346,6 +346,20 @@ __global__ void k_add_inplace(float* __restrict__ a, const float* __restrict__ b
   for (; i < n; i += st) a[i] = a[i] + b[i];
 }
 
+__global__ void k_step_inc(int64_t* step) { *step += 1; }
+
+// dwpe[t][c] = sum over b = 0..B-1 (in that order) of g[b][t][c]: the order in
+// which the embedding VJP scatters the position ids b*T + t.
+__global__ void k_dwpe(const float* __restrict__ g, float* __restrict__ out, int B, size_t TC) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t st = (size_t)gridDim.x * blockDim.x;
+  for (; i < TC; i += st) {
+    float s = 0.0f;
+    for (int b = 0; b < B; ++b) s += g[(size_t)b * TC + i];
+    out[i] = s;
+  }
+}
+
 TcLayout L(int64_t d1 = 0, int64_t s1 = 0, int64_t d2 = 0, int64_t s2 = 0, int64_t s3 = 0) {
   return TcLayout{d1, s1, d2, s2, s3};
 }
@@ -381,6 +395,17 @@ struct FusedStep {
   float *S, *dP, *dxf, *dxn, *g_a, *g_b, *part, *emb_tmp;
   Planes g_a_pl, g_b_pl, dh, dO, dqkv, dS;
   int part_blocks;
+  void* emb_ws = nullptr;      // embedding-VJP workspace (no allocation inside a step)
+  // optimizer state (the model's fused buffers) and the device step counter
+  float *pbuf = nullptr, *mbuf = nullptr, *vbuf = nullptr;
+  size_t total = 0;
+  int64_t* step_dev = nullptr;
+  float* bc_tab = nullptr;     // [2 * bc_cap] host-computed 1 - beta**t
+  int64_t bc_cap = 0;
+  int64_t host_step = 0;
+  // CUDA graph of one whole training step (captured after the first eager step)
+  cudaGraphExec_t exec = nullptr;
+  int64_t graph_launches = 0;
 };
 
 namespace {
@@ -464,10 +489,35 @@ void split_weights(FusedStep* f) {
 
 }  // namespace
 
+namespace {
+
+// Bias-correction table for steps 1..cap: the same f32 powf the host computes.
+void fill_bc_table(FusedStep* f, int64_t cap) {
+  std::vector<float> h((size_t)cap * 2);
+  for (int64_t t = 1; t <= cap; ++t) {
+    h[2 * (t - 1)] = 1.0f - powf(f->cfg.beta1, (float)t);
+    h[2 * (t - 1) + 1] = 1.0f - powf(f->cfg.beta2, (float)t);
+  }
+  if (f->bc_tab) {
+    MALUS_CUDA(cudaStreamSynchronize(stream()));
+    MALUS_CUDA(cudaFree(f->bc_tab));
+  }
+  MALUS_CUDA(cudaMalloc(&f->bc_tab, h.size() * sizeof(float)));
+  MALUS_CUDA(cudaMemcpy(f->bc_tab, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+  f->bc_cap = cap;
+}
+
+}  // namespace
+
 FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& params,
                         const std::vector<size_t>& sizes, float* gbuf,
-                        const std::vector<size_t>& goff) {
+                        const std::vector<size_t>& goff, float* pbuf, float* mbuf, float* vbuf,
+                        size_t total_elems) {
   auto* f = new FusedStep();
+  f->pbuf = pbuf;
+  f->mbuf = mbuf;
+  f->vbuf = vbuf;
+  f->total = total_elems;
   f->cfg = cfg;
   f->V = cfg.vocab; f->L = cfg.n_layer; f->H = cfg.n_head; f->C = cfg.n_embd;
   f->T = cfg.block_size; f->B = cfg.batch;
@@ -523,6 +573,10 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
   f->part_blocks = kNumSMs * 2;
   f->part = dalloc(f, (size_t)f->part_blocks * C);
   f->emb_tmp = dalloc(f, (size_t)f->V * C);
+  f->emb_ws = dalloc(f, (embedding_bwd_ws_bytes(M, f->V) + 3) / 4);
+  MALUS_CUDA(cudaMalloc(&f->step_dev, sizeof(int64_t)));
+  MALUS_CUDA(cudaMemset(f->step_dev, 0, sizeof(int64_t)));
+  fill_bc_table(f, 1 << 16);
   MALUS_CUDA(cudaFuncSetAttribute(k_ln_bwd_fused<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024));
   MALUS_CUDA(cudaFuncSetAttribute(k_ln_bwd_fused<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024));
   split_weights(f);
@@ -530,7 +584,11 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
 }
 
 void fused_destroy(FusedStep* f) {
+  cudaStreamSynchronize(stream());
+  if (f->exec) cudaGraphExecDestroy(f->exec);
   for (float* p : f->allocs) cudaFree(p);
+  cudaFree(f->step_dev);
+  cudaFree(f->bc_tab);
   delete f;
 }
 
@@ -666,15 +724,17 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     }
   }
   // embeddings: x0 = wte[tok] + wpe[pos]
+  float* dwte = f->cfg.tied ? f->emb_tmp : G(top);
+  int er = embedding_bwd_ws(g3, xt, MALUS_I32, dwte, M, V, C, f->emb_ws, stream());
+  if (er != 0) panic("fused step: embedding backward failed (%d)", er);
   if (f->cfg.tied) {
-    embedding_bwd(g3, xt, MALUS_I32, f->emb_tmp, M, V, C);
     k_add_inplace<<<grid_for((size_t)V * C, 256), 256, 0, stream()>>>(G(top), f->emb_tmp, (size_t)V * C);
     count_launch();
     after_launch("k_add_inplace");
-  } else {
-    embedding_bwd(g3, xt, MALUS_I32, G(top), M, V, C);
   }
-  reduce_axis(kRSum, g3, G(top + 1), 1, B, (size_t)T * C);   // dwpe = sum over batch
+  k_dwpe<<<grid_for((size_t)T * C, 256), 256, 0, stream()>>>(g3, G(top + 1), B, (size_t)T * C);
+  count_launch();
+  after_launch("k_dwpe");
   if (dp_world() > 1) {
     const auto& bk = f->buckets.back();
     if (dp_allreduce_async(f->gbuf + bk.first, bk.second - bk.first) != 0)
@@ -685,5 +745,58 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
 
 // Called after AdamW updates the parameters: refresh the weight planes.
 void fused_after_update(FusedStep* f) { split_weights(f); }
+
+namespace {
+
+// One whole training step on the runtime stream: step counter, forward,
+// backward (with the data-parallel all-reduces), AdamW, weight re-split.
+// Nothing in here allocates or reads the host, so it can be captured.
+void fused_body(FusedStep* f, const int32_t* x, const int32_t* y, float* loss) {
+  k_step_inc<<<1, 1, 0, stream()>>>(f->step_dev);
+  count_launch();
+  after_launch("k_step_inc");
+  fused_step(f, x, y, loss);
+  float gscale = dp_world() > 1 ? 1.0f / (float)dp_world() : 1.0f;
+  AdamSeg seg{f->pbuf, f->gbuf, f->mbuf, f->vbuf, (int64_t)f->total};
+  adamw_multi_tab(&seg, 1, f->cfg.lr, f->cfg.beta1, f->cfg.beta2, f->cfg.eps, f->cfg.wd, 0.0f, 0.0f,
+                  gscale, f->bc_tab, f->step_dev);
+  fused_after_update(f);
+}
+
+}  // namespace
+
+// The training step of mode 1.  With cfg.use_graph the first step runs eagerly
+// (it sizes the workspaces and sets kernel attributes); the second is captured
+// into a CUDA graph that every later step replays.  Kernel timing (prof) and
+// synchronous dispatch force the eager path.
+void fused_train_step(FusedStep* f, const int32_t* x, const int32_t* y, float* loss) {
+  f->host_step++;
+  if (f->host_step > f->bc_cap) {
+    if (f->exec) {                  // the table moves: the graph must be captured again
+      MALUS_CUDA(cudaStreamSynchronize(stream()));
+      MALUS_CUDA(cudaGraphExecDestroy(f->exec));
+      f->exec = nullptr;
+    }
+    fill_bc_table(f, f->bc_cap * 4);
+  }
+  const bool graph = f->cfg.use_graph && !prof_on() && !sync_dispatch() && f->host_step > 1;
+  if (!graph) {
+    fused_body(f, x, y, loss);
+    return;
+  }
+  if (!f->exec) {
+    cudaGraph_t g = nullptr;
+    int64_t before = malus_launch_count();
+    MALUS_CUDA(cudaStreamBeginCapture(stream(), cudaStreamCaptureModeThreadLocal));
+    fused_body(f, x, y, loss);
+    MALUS_CUDA(cudaStreamEndCapture(stream(), &g));
+    f->graph_launches = malus_launch_count() - before;
+    count_launch(-(int)f->graph_launches);     // captured, not launched
+    MALUS_CUDA(cudaGraphInstantiate(&f->exec, g, 0));
+    MALUS_CUDA(cudaGraphDestroy(g));
+  }
+  MALUS_CUDA(cudaGraphLaunch(f->exec, stream()));
+  count_launch((int)f->graph_launches);
+}
 
 }  // namespace malus

@@ -25,6 +25,7 @@ def main():
     ap.add_argument("--mode", choices=["parity", "leave"], required=True)
     ap.add_argument("--out", required=True)
     ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--graph", type=int, default=0)
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -41,7 +42,7 @@ def main():
                     prefix="dpw")
     m = CFG["batch"] * CFG["block_size"]
     xs, ys = shard_tokens(11, rank, CFG["vocab"], m, args.steps)
-    g = M.GPT(**CFG, lr=1e-3, mode=1)
+    g = M.GPT(**CFG, lr=1e-3, mode=1, use_graph=args.graph)
     out = Path(args.out)
     if args.mode == "parity":
         losses = []

@@ -33,23 +33,25 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def torchrun(mode, out, steps=3, timeout=240):
+def torchrun(mode, out, steps=3, timeout=240, graph=0):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     env.pop("MALUS_DEVICE", None)          # each rank binds its LOCAL_RANK
     cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port",
-           str(free_port()), str(WORKER), "--mode", mode, "--out", str(out), "--steps", str(steps)]
+           str(free_port()), str(WORKER), "--mode", mode, "--out", str(out), "--steps", str(steps),
+           "--graph", str(graph)]
     r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
 
 
 @needs2
-def test_dp2_matches_single_gpu_double_batch(M, tmp_path):
+@pytest.mark.parametrize("graph", [0, 1])
+def test_dp2_matches_single_gpu_double_batch(M, tmp_path, graph):
     from malus_b200.dist import shard_tokens
     sys.path.insert(0, str(ROOT / "tests"))
     from dp_worker import CFG
-    steps = 3
-    torchrun("parity", tmp_path, steps)
+    steps = 4
+    torchrun("parity", tmp_path, steps, graph=graph)
     l0, l1 = np.load(tmp_path / "losses0.npy"), np.load(tmp_path / "losses1.npy")
     p2 = np.load(tmp_path / "params0.npz")
     m = CFG["batch"] * CFG["block_size"]
