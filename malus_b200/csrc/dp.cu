@@ -137,7 +137,10 @@ int32_t malus_dp_finish(void) {
   dp_join();
   auto t0 = std::chrono::steady_clock::now();
   while (true) {
+    // collectives run on the DP stream, or on the main stream inside a
+    // replayed CUDA graph of the step: wait (bounded) for both
     cudaError_t q = cudaStreamQuery(g_dp_stream);
+    if (q == cudaSuccess) q = cudaStreamQuery(stream());
     if (q == cudaSuccess) return 0;
     if (q != cudaErrorNotReady) return -6;
     ncclResult_t st;
