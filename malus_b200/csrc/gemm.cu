@@ -136,7 +136,10 @@ constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
 constexpr int kTileBytesA = BM * BK * 4;  // 16 KB
 constexpr int kTileBytesB = BN * BK * 4;  // 16 KB
 constexpr int kStageBytes = 2 * kTileBytesA + 2 * kTileBytesB;
-constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kEpiPitch = 36;     // GELU staging row pitch (floats): 16-B aligned, conflict-free float4
+constexpr int kEpiWarpFloats = 32 * kEpiPitch;
+constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+                           4 * kEpiWarpFloats * 4 /*GELU epilogue staging*/;
 // Epilogue warps: 8 (two per TMEM lane quarter, half the columns each) when the
 // epilogue reads an auxiliary input, whose load latency the extra warps hide;
 // 4 otherwise, leaving L2 bandwidth to the operand loads.
@@ -195,6 +198,14 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
       ::"r"(dst), "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t mbar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(dst), "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 
@@ -261,6 +272,7 @@ struct TcKernelParams {
   int tiles_m, tiles_n, nk;
   int splits;      // K slices per tile (split-K); > 1 writes raw partial tiles to ws
   float* ws;       // [tile][split][BM][BN] partial accumulators when splits > 1
+  int a_chunked, b_chunked;   // MN-major operand loaded as one {32, 32 K, 4 chunks} box per plane
   int32_t* err;
 };
 
@@ -424,7 +436,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
           // A 128-wide M/N tile may straddle segments (segment width a multiple
           // of 32): MN-major tiles and K-major tiles of an MN-segmented operand
           // are loaded as four 32-wide boxes, each with its own segment.
-          if (!p.a.mn_major && p.a.zmode != kZMNSeg) {
+          if (kp.a_chunked) {
+            operand_coords(p.a.zmode, p.a.seg, z, k0, m0, &kc, &mnc, &zc);
+            tma_load_4d(smem_u32(st), &mAh, fb, 0, kc, mnc >> 5, zc);
+            tma_load_4d(smem_u32(st + kTileBytesA), &mAl, fb, 0, kc, mnc >> 5, zc);
+          } else if (!p.a.mn_major && p.a.zmode != kZMNSeg) {
             operand_coords(p.a.zmode, p.a.seg, z, k0, m0, &kc, &mnc, &zc);
             tma_load_3d(smem_u32(st), &mAh, fb, kc, mnc, zc);
             tma_load_3d(smem_u32(st + kTileBytesA), &mAl, fb, kc, mnc, zc);
@@ -437,7 +453,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
             }
           }
           uint8_t* sb = st + 2 * kTileBytesA;
-          if (!p.b.mn_major && p.b.zmode != kZMNSeg) {
+          if (kp.b_chunked) {
+            operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
+            tma_load_4d(smem_u32(sb), &mBh, fb, 0, kc, mnc >> 5, zc);
+            tma_load_4d(smem_u32(sb + kTileBytesB), &mBl, fb, 0, kc, mnc >> 5, zc);
+          } else if (!p.b.mn_major && p.b.zmode != kZMNSeg) {
             operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
             tma_load_3d(smem_u32(sb), &mBh, fb, kc, mnc, zc);
             tma_load_3d(smem_u32(sb + kTileBytesB), &mBl, fb, kc, mnc, zc);
@@ -527,7 +547,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       int z = tile / per_batch, rem = tile % per_batch;
       int m0 = (rem / kp.tiles_n) * BM, n0 = (rem % kp.tiles_n) * BN;
       const int m = m0 + row;
-      const int64_t zm_off = lay(p.oz, z) + lay(p.om, m);
+      const int64_t zm_z = lay(p.oz, z);
+      const int64_t zm_off = zm_z + lay(p.om, m);
 #pragma unroll 1
       for (int c0 = chalf * kCols; c0 < (chalf + 1) * kCols; c0 += 32) {
         uint32_t r[32];
@@ -550,6 +571,40 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
           for (int j = 0; j < 32; j += 4)
             dst[j / 4] = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
                                      __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          continue;
+        }
+        if (EPI == kEpiGelu && contig) {
+          // GELU writes three arrays: transpose the 32x32 chunk through smem so
+          // each store instruction covers 4 rows x 128 contiguous bytes
+          float* wst = reinterpret_cast<float*>(bar_area + 256) + quarter * kEpiWarpFloats;
+          float4* wrow = reinterpret_cast<float4*>(wst + lane * kEpiPitch);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            wrow[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                  __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          __syncwarp();
+          const int rsub = lane >> 3, csub = (lane & 7) * 4;
+          const int nb = n0 + c0 + csub;
+          const int64_t n_off = lay(p.on, nb);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const int rr = 4 * t + rsub;
+            const int mm = m0 + quarter * 32 + rr;
+            const float4 v = *reinterpret_cast<const float4*>(wst + rr * kEpiPitch + csub);
+            if (mm < p.M) {
+              const int64_t zm = zm_z + lay(p.om, mm);
+              const int64_t base = zm + n_off;
+              if (nb + 4 <= p.N && (base & 3) == 0) {
+                epi_store4<EPI>(p, base, v, v);
+              } else {
+                const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  if (nb + j < p.N) epi_store1<EPI>(p, base + j, vv[j]);
+              }
+            }
+          }
+          __syncwarp();
           continue;
         }
         if (m >= p.M) continue;
@@ -685,11 +740,36 @@ CUtensorMap make_map(const float* base, uint64_t d0, uint64_t d1, uint64_t d2, u
 
 // Map of one operand plane.  Stored matrix: nz slices of rows x cols with the
 // given pitch; K-major operands are {cols=K, rows=MN}, MN-major {cols=MN, rows=K}.
+// An MN-major operand whose columns are whole 32-element chunks (and whose
+// segments, if any, are whole 128-wide tiles) is read as one box per plane:
+// a 4-D view {32 columns, K rows, column chunks, slices} with box {32, 32, 4, 1}
+// lands in shared memory as [chunk][k][32], the same swizzled layout that four
+// 32-wide boxes produce.  The view never addresses past a row's columns.
+bool mn_chunked(const TcOperand& o) {
+  return o.mn_major && o.cols % 32 == 0 && (o.zmode != kZMNSeg || o.seg % 128 == 0);
+}
+
+CUtensorMap chunked_map(const TcOperand& o, const float* plane, uint64_t pitch_bytes,
+                        uint64_t plane_bytes) {
+  CUtensorMap m;
+  cuuint64_t dims[4] = {32, (cuuint64_t)o.rows, (cuuint64_t)(o.cols / 32),
+                        (cuuint64_t)std::max(1, o.nz)};
+  cuuint64_t strides[3] = {pitch_bytes, 128, plane_bytes};
+  cuuint32_t box[4] = {32, 32, 4, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)plane, dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) panic("cuTensorMapEncodeTiled (chunked MN-major view) failed (%d)", (int)r);
+  return m;
+}
+
 CUtensorMap operand_map(const TcOperand& o, const float* plane) {
   uint64_t pb = (uint64_t)o.pitch * 4;
   uint64_t zb = (uint64_t)o.zstride * 4;
   if (o.nz > 1 && (zb % 16 != 0)) panic("gemm operand slice stride %lld is not 16-byte aligned", (long long)o.zstride);
   if (o.nz <= 1) zb = pb * (uint64_t)o.rows;
+  if (mn_chunked(o)) return chunked_map(o, plane, pb, std::max<uint64_t>(zb, 16));
   // K-major boxes are 32 (K) x 128 rows, or 32 x 32 rows when the rows are segmented
   uint32_t box_rows = (o.mn_major || o.zmode == kZMNSeg) ? 32 : BM;
   return make_map(plane, (uint64_t)o.cols, (uint64_t)o.rows, (uint64_t)std::max(1, o.nz), pb,
@@ -790,6 +870,8 @@ void gemm_tc_planes(const TcProblem& pr) {
   kp.err = device_error_word();
   int tiles = kp.tiles_m * kp.tiles_n * pr.batch;
   kp.splits = splitk_for(tiles, kp.nk);
+  kp.a_chunked = mn_chunked(pr.a) ? 1 : 0;
+  kp.b_chunked = mn_chunked(pr.b) ? 1 : 0;
   kp.ws = kp.splits > 1 ? splitk_workspace((size_t)tiles * kp.splits * BM * BN) : nullptr;
   int total = tiles * kp.splits;
   int grid = std::min(total, kNumSMs);
