@@ -323,8 +323,12 @@ int32_t malus_gpt_dp_buckets(const malus_gpt_config* cfg, int64_t* lo, int64_t* 
  * (i / div) * hi + (i % div) * lo (div 0: i * lo).  Epilogues: 0 store
  * (alpha, beta), 1 residual add (out = aux + acc), 2 GELU (out = acc, planes
  * of gelu(acc)), 3 GELU derivative (planes of acc * gelu'(aux)); out_hi/out_lo,
- * when set, receive the tf32 planes of the stored value.  New in this build (the
- * reference's matmul is an MPS call, metal.rs:805-962). */
+ * when set, receive the tf32 planes of the stored value.  causal (per batch
+ * slice, for attention matrices): 0 none; 1 only output tiles that reach the
+ * lower triangle n <= m are computed (the rest of the output is not written);
+ * 2 A is lower-triangular (A(m,k) = 0 for k > m: the K range stops at the
+ * diagonal); 3 A is upper-triangular (A(m,k) = 0 for k < m).  New in this build
+ * (the reference's matmul is an MPS call, metal.rs:805-962). */
 typedef struct malus_tc_operand {
   const float* hi; const float* lo;
   int64_t rows, cols, pitch;
@@ -340,6 +344,7 @@ typedef struct malus_tc_problem {
   float* out; float* out_hi; float* out_lo;
   const float* aux;
   float alpha, beta;
+  int32_t causal;
 } malus_tc_problem;
 void malus_tc_gemm(const malus_tc_problem* p);
 void malus_tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t batch,

@@ -194,7 +194,9 @@ struct TcProblem {
   float* out_lo;
   const float* aux; // Resid: residual input; GeluBwd: pre-activation
   float alpha = 1.f, beta = 0.f;
+  int causal = 0;   // kCausal*: skip work on the zero side of an attention mask
 };
+enum { kCausalNone = 0, kCausalOut = 1, kCausalALower = 2, kCausalAUpper = 3 };
 void gemm_tc_planes(const TcProblem& p);
 // hi/lo planes of a stack of `batch` row-major slices (rows x cols, ld, sstride)
 void tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t batch,

@@ -276,6 +276,29 @@ struct TcKernelParams {
   int32_t* err;
 };
 
+// Work unit -> tile and K-block range, honouring split-K and the causal modes.
+// Returns false for output tiles wholly above the diagonal (kCausalOut).
+struct Unit {
+  int z, m0, n0, kb_lo, kb_hi;
+};
+__device__ __forceinline__ bool unit_of(const TcKernelParams& kp, int unit, Unit& u) {
+  const TcProblem& p = kp.pr;
+  const int per_batch = kp.tiles_m * kp.tiles_n;
+  const int tile = unit / kp.splits, sl = unit % kp.splits;
+  u.z = tile / per_batch;
+  const int rem = tile % per_batch;
+  u.m0 = (rem / kp.tiles_n) * BM;
+  u.n0 = (rem % kp.tiles_n) * BN;
+  if (p.causal == kCausalOut && u.n0 > u.m0 + BM - 1) return false;
+  int lo = 0, hi = kp.nk;
+  if (p.causal == kCausalALower) hi = min(kp.nk, (u.m0 + BM + BK - 1) / BK);
+  if (p.causal == kCausalAUpper) lo = u.m0 / BK;
+  const int len = hi - lo;
+  u.kb_lo = lo + sl * len / kp.splits;
+  u.kb_hi = lo + (sl + 1) * len / kp.splits;
+  return u.kb_hi > u.kb_lo;
+}
+
 // Operand coordinates for k-block k0 of tile (z, m0/n0).
 __device__ __forceinline__ void operand_coords(int zmode, int seg, int z, int k0, int mn0,
                                                int* kc, int* mnc, int* zc) {
@@ -418,11 +441,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       uint32_t it = 0;
       bool ok = true;
       for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
-        int tile = unit / splits, sl = unit % splits;
-        int z = tile / per_batch, rem = tile % per_batch;
-        int m0 = (rem / kp.tiles_n) * BM, n0 = (rem % kp.tiles_n) * BN;
-        const int kb_lo = sl * nk / splits, kb_hi = (sl + 1) * nk / splits;
-        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+        Unit un;
+        if (!unit_of(kp, unit, un)) continue;
+        const int z = un.z, m0 = un.m0, n0 = un.n0;
+        for (int kb = un.kb_lo; kb < un.kb_hi; ++kb, ++it) {
           int s = it % STAGES;
           uint32_t ph = (it / STAGES) & 1;
           if (it >= STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, kp.err, 11)) {
@@ -486,16 +508,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       const uint32_t idesc = idesc_tf32(p.a.mn_major, p.b.mn_major);
       uint32_t it = 0, local = 0;
       bool ok = true, issued = false;
-      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x, ++local) {
+      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
+        Unit un;
+        if (!unit_of(kp, unit, un)) continue;
         uint32_t b = local & 1, u = local >> 1;
+        ++local;
         if (u >= 1 && !mbar_wait(smem_u32(&acce[b]), (u - 1) & 1, abort_flag, kp.err, 14)) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t dacc = tmem + b * BN;
-        const int sl = unit % splits;
-        const int kb_lo = sl * nk / splits, kb_hi = (sl + 1) * nk / splits;
+        const int kb_lo = un.kb_lo, kb_hi = un.kb_hi;
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           int s = it % STAGES;
           uint32_t ph = (it / STAGES) & 1;
@@ -539,13 +563,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     const int row = quarter * 32 + lane;
     const bool contig = (p.on.d1 % 32 == 0) && (p.on.d2 % 32 == 0) && p.on.s3 == 1;
     uint32_t local = 0;
-    for (int unit = blockIdx.x; unit < total; unit += gridDim.x, ++local) {
+    for (int unit = blockIdx.x; unit < total; unit += gridDim.x) {
+      Unit un;
+      if (!unit_of(kp, unit, un)) continue;
       uint32_t b = local & 1, u = local >> 1;
+      ++local;
       if (!mbar_wait(smem_u32(&accf[b]), u & 1, abort_flag, kp.err, 13)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int tile = unit / splits;
-      int z = tile / per_batch, rem = tile % per_batch;
-      int m0 = (rem / kp.tiles_n) * BM, n0 = (rem % kp.tiles_n) * BN;
+      const int z = un.z, m0 = un.m0, n0 = un.n0;
       const int m = m0 + row;
       const int64_t zm_z = lay(p.oz, z);
       const int64_t zm_off = zm_z + lay(p.om, m);
@@ -856,6 +881,7 @@ void gemm_tc_planes(const TcProblem& pr) {
   if ((pr.epi == kEpiResid || pr.epi == kEpiGeluBwd) && !pr.aux) panic("gemm_tc_planes: epilogue %d needs aux", pr.epi);
   if ((pr.epi == kEpiGelu || pr.epi == kEpiGeluBwd) && !pr.out_hi) panic("gemm_tc_planes: GELU epilogues write planes");
   if (!pr.a.hi || !pr.a.lo || !pr.b.hi || !pr.b.lo) panic("gemm_tc_planes: missing operand plane");
+  if (pr.causal < 0 || pr.causal > kCausalAUpper) panic("gemm_tc_planes: causal mode %d", pr.causal);
   for (const TcOperand* o : {&pr.a, &pr.b})
     if ((o->zmode == kZKSeg || o->zmode == kZMNSeg) && (o->seg <= 0 || o->seg % 32 != 0))
       panic("gemm_tc_planes: segment width %d must be a positive multiple of 32", o->seg);
@@ -869,13 +895,30 @@ void gemm_tc_planes(const TcProblem& pr) {
   kp.nk = (pr.K + BK - 1) / BK;
   kp.err = device_error_word();
   int tiles = kp.tiles_m * kp.tiles_n * pr.batch;
-  kp.splits = splitk_for(tiles, kp.nk);
+  kp.splits = pr.causal ? 1 : splitk_for(tiles, kp.nk);
   kp.a_chunked = mn_chunked(pr.a) ? 1 : 0;
   kp.b_chunked = mn_chunked(pr.b) ? 1 : 0;
   kp.ws = kp.splits > 1 ? splitk_workspace((size_t)tiles * kp.splits * BM * BN) : nullptr;
   int total = tiles * kp.splits;
-  int grid = std::min(total, kNumSMs);
+  // Static round-robin over units: for causal problems the per-batch pattern of
+  // skipped tiles / short K ranges has period 2 or 4, so an odd grid (147)
+  // spreads the light and heavy units evenly over the CTAs.
+  int grid = std::min(total, pr.causal ? kNumSMs - 1 : kNumSMs);
   double flops = 2.0 * pr.M * (double)pr.N * pr.K * pr.batch;
+  if (pr.causal) {   // the work actually done: tiles and K ranges the mask leaves
+    double f = 0.0;
+    for (int tm = 0; tm < kp.tiles_m; ++tm)
+      for (int tn = 0; tn < kp.tiles_n; ++tn) {
+        int m0 = tm * BM, n0 = tn * BN;
+        if (pr.causal == kCausalOut && n0 > m0 + BM - 1) continue;
+        int lo = 0, hi = kp.nk;
+        if (pr.causal == kCausalALower) hi = std::min(kp.nk, (m0 + BM + BK - 1) / BK);
+        if (pr.causal == kCausalAUpper) lo = m0 / BK;
+        double k = std::min(hi * BK, pr.K) - lo * BK;
+        f += 2.0 * std::min(BM, pr.M - m0) * std::min(BN, pr.N - n0) * std::max(0.0, k);
+      }
+    flops = f * pr.batch;
+  }
   // algorithmic bytes: both operands' hi/lo planes once, each output array and aux once
   const double mn = (double)pr.M * pr.N * pr.batch;
   const int arrays = (pr.out ? 1 : 0) + (pr.out_hi ? 2 : 0) + (pr.aux ? 1 : 0);
@@ -948,6 +991,7 @@ extern "C" void malus_tc_gemm(const malus_tc_problem* q) {
   p.on = L(q->on);
   p.out = q->out; p.out_hi = q->out_hi; p.out_lo = q->out_lo; p.aux = q->aux;
   p.alpha = q->alpha; p.beta = q->beta;
+  p.causal = q->causal;
   gemm_tc_planes(p);
 }
 

@@ -227,7 +227,9 @@ __global__ void k_softmax_causal_split(const float* __restrict__ S, float* __res
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int j = lane + 32 * k;
-      v[k] = j < T ? sr[j] + (j > i ? -1e9f : 0.0f) : -INFINITY;
+      // masked scores (j > i; not computed by the causal S GEMM) would be
+      // s - 1e9, whose exp underflows to exactly 0: -inf gives the same 0
+      v[k] = j <= i ? sr[j] : -INFINITY;
       m = fmaxf(m, v[k]);
     }
     m = wmax(m);
@@ -235,7 +237,7 @@ __global__ void k_softmax_causal_split(const float* __restrict__ S, float* __res
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int j = lane + 32 * k;
-      v[k] = j < T ? expf(v[k] - m) : 0.0f;
+      v[k] = j <= i ? expf(v[k] - m) : 0.0f;
       s += v[k];
     }
     s = wsum(s);
@@ -258,13 +260,14 @@ __global__ void k_softmax_bwd_split(const float* __restrict__ p_hi, const float*
   int nw = (gridDim.x * blockDim.x) >> 5;
   for (int r = warp; r < rows; r += nw) {
     size_t base = (size_t)r * T;
+    const int i = r % T;          // dP above the diagonal is not computed; P is 0 there
     float pv[PER], gv[PER];
     float dot = 0.0f;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int j = lane + 32 * k;
-      pv[k] = j < T ? p_hi[base + j] + p_lo[base + j] : 0.0f;
-      gv[k] = j < T ? dP[base + j] : 0.0f;
+      pv[k] = j <= i ? p_hi[base + j] + p_lo[base + j] : 0.0f;
+      gv[k] = j <= i ? dP[base + j] : 0.0f;
       dot += gv[k] * pv[k];
     }
     dot = wsum(dot);
@@ -425,7 +428,7 @@ TcOperand op(const Planes& p, int64_t rows, int64_t cols, int64_t pitch, bool mn
 
 void gemm(int M, int N, int K, int batch, const TcOperand& a, const TcOperand& b, int epi,
           TcLayout oz, TcLayout om, TcLayout on, float* out, Planes outp, const float* aux,
-          float alpha = 1.0f) {
+          float alpha = 1.0f, int causal = kCausalNone) {
   TcProblem p{};
   p.M = M; p.N = N; p.K = K; p.batch = batch;
   p.a = a; p.b = b;
@@ -433,6 +436,7 @@ void gemm(int M, int N, int K, int batch, const TcOperand& a, const TcOperand& b
   p.oz = oz; p.om = om; p.on = on;
   p.out = out; p.out_hi = outp.hi; p.out_lo = outp.lo; p.aux = aux;
   p.alpha = alpha; p.beta = 0.0f;
+  p.causal = causal;
   gemm_tc_planes(p);
 }
 
@@ -619,7 +623,8 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     // S = Q K^T * scale
     gemm(T, T, hs, BH, op(f->qkv[l], T, hs, hs, false, BH, (int64_t)T * hs, kZBatch),
          op(f->qkv[l], T, hs, hs, false, BH, (int64_t)T * hs, kZBatch, 0, MC), kEpiStore,
-         L(0, 0, 0, 0, (int64_t)TT), L(0, 0, 0, 0, T), unit, f->S, Planes{}, nullptr, f->scale);
+         L(0, 0, 0, 0, (int64_t)TT), L(0, 0, 0, 0, T), unit, f->S, Planes{}, nullptr, f->scale,
+         kCausalOut);
     PER_DISPATCH(T, (k_softmax_causal_split<P_><<<rows_grid(BH * T), 256, 0, stream()>>>(
                         f->S, f->P[l].hi, f->P[l].lo, BH * T, T)));
     count_launch();
@@ -627,7 +632,7 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     // O = P V, written unfolded to [M][C]
     gemm(T, hs, T, BH, op(f->P[l], T, T, T, false, BH, (int64_t)TT, kZBatch),
          op(f->qkv[l], T, hs, hs, true, BH, (int64_t)T * hs, kZBatch, 0, 2 * MC), kEpiStore,
-         L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, f->O[l], nullptr);
+         L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, f->O[l], nullptr, 1.0f, kCausalALower);
     // x2 = x + O Wo
     gemm(M, C, C, 1, op(f->O[l], M, C, C, false), op(W(b + 4), C, C, C, true), kEpiResid, none,
          rowC, unit, f->x2[l], Planes{}, f->x[l]);
@@ -691,11 +696,11 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     // dP = dO V^T ; dV = P^T dO
     gemm(T, T, hs, BH, op(f->dO, T, hs, hs, false, BH, (int64_t)T * hs, kZBatch),
          op(f->qkv[l], T, hs, hs, false, BH, (int64_t)T * hs, kZBatch, 0, 2 * MC), kEpiStore,
-         L(0, 0, 0, 0, (int64_t)TT), L(0, 0, 0, 0, T), unit, f->dP, Planes{}, nullptr);
+         L(0, 0, 0, 0, (int64_t)TT), L(0, 0, 0, 0, T), unit, f->dP, Planes{}, nullptr, 1.0f, kCausalOut);
     Planes dqkv2{f->dqkv.hi + 2 * MC, f->dqkv.lo + 2 * MC};
     gemm(T, hs, T, BH, op(f->P[l], T, T, T, true, BH, (int64_t)TT, kZBatch),
          op(f->dO, T, hs, hs, true, BH, (int64_t)T * hs, kZBatch), kEpiStore,
-         L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, dqkv2, nullptr);
+         L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, dqkv2, nullptr, 1.0f, kCausalAUpper);
     PER_DISPATCH(T, (k_softmax_bwd_split<P_><<<rows_grid(BH * T), 256, 0, stream()>>>(
                         f->P[l].hi, f->P[l].lo, f->dP, f->dS.hi, f->dS.lo, BH * T, T, f->scale)));
     count_launch();
@@ -704,10 +709,10 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     Planes dqkv1{f->dqkv.hi + MC, f->dqkv.lo + MC};
     gemm(T, hs, T, BH, op(f->dS, T, T, T, false, BH, (int64_t)TT, kZBatch),
          op(f->qkv[l], T, hs, hs, true, BH, (int64_t)T * hs, kZBatch, 0, MC), kEpiStore,
-         L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, f->dqkv, nullptr);
+         L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, f->dqkv, nullptr, 1.0f, kCausalALower);
     gemm(T, hs, T, BH, op(f->dS, T, T, T, true, BH, (int64_t)TT, kZBatch),
          op(f->qkv[l], T, hs, hs, true, BH, (int64_t)T * hs, kZBatch), kEpiStore,
-         L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, dqkv1, nullptr);
+         L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, dqkv1, nullptr, 1.0f, kCausalAUpper);
     // dxn1 = sum_j dqkv_j W_j^T (K segments) ; dW_j = xn1^T dqkv_j (N segments)
     gemm(M, C, 3 * C, 1, op(f->dqkv, M, C, C, false, 3, (int64_t)MC, kZKSeg, C),
          op(W(b + 1), C, C, C, false, 3, (int64_t)C * C, kZKSeg, C), kEpiStore, none, rowC, unit,

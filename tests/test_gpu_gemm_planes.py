@@ -54,7 +54,7 @@ def lay(d1=0, s1=0, d2=0, s2=0, s3=0):
 
 
 def run(M, lib, Mm, N, K, batch, a, b, epi=0, oz=None, om=None, on=None, out=None, out_hi=None,
-        out_lo=None, aux=None, alpha=1.0, beta=0.0):
+        out_lo=None, aux=None, alpha=1.0, beta=0.0, causal=0):
     p = M.TcProblem()
     p.M, p.N, p.K, p.batch = Mm, N, K, batch
     p.a, p.b = a, b
@@ -67,6 +67,7 @@ def run(M, lib, Mm, N, K, batch, a, b, epi=0, oz=None, om=None, on=None, out=Non
     p.out_lo = ptr(lib, out_lo) if out_lo is not None else None
     p.aux = ptr(lib, aux) if aux is not None else None
     p.alpha, p.beta = alpha, beta
+    p.causal = causal
     lib.malus_tc_gemm(C.byref(p))
 
 
@@ -289,3 +290,44 @@ def test_splitk_batched(M, rt, rng):
     run(M, rt, Mm, N, K, Z, ao, bo, out=out, oz=lay(s3=Mm * N))
     for z in range(Z):
         assert err(out.numpy()[z], A[z].astype(np.float64) @ B[z], A[z], B[z]) < 1e-4
+
+
+@pytest.mark.parametrize("T,hs", [(256, 64), (200, 48), (384, 32)])
+@pytest.mark.parametrize("a_mn", [False, True])
+def test_causal_triangular_a(M, rt, rng, T, hs, a_mn):
+    """Attention-shaped batched GEMMs whose A is triangular: the K range stops at
+    (lower) or starts from (upper) the diagonal; results equal the full product."""
+    Z = 3
+    for mode, tri in ((2, np.tril), (3, np.triu)):
+        A = tri(rng.standard_normal((Z, T, T)).astype(np.float32))
+        B = rng.standard_normal((Z, T, hs)).astype(np.float32)
+        ao = operand(M, rt, A.transpose(0, 2, 1) if a_mn else A, a_mn, zmode=1)
+        bo = operand(M, rt, B, True, zmode=1)
+        out = dev(M, np.zeros((Z, T, hs)))
+        run(M, rt, T, hs, T, Z, ao, bo, out=out, oz=lay(s3=T * hs), om=lay(s3=hs), causal=mode)
+        for z in range(Z):
+            assert err(out.numpy()[z], A[z].astype(np.float64) @ B[z], A[z], B[z]) < 1e-4, mode
+
+
+@pytest.mark.parametrize("T", [256, 200, 384])
+def test_causal_output_tiles(M, rt, rng, T):
+    """Only tiles reaching the lower triangle are computed; every element on or
+    below the diagonal is exact, and skipped tiles are left untouched."""
+    Z, hs = 2, 64
+    Q = rng.standard_normal((Z, T, hs)).astype(np.float32)
+    Kt = rng.standard_normal((Z, T, hs)).astype(np.float32)
+    qo = operand(M, rt, Q, False, zmode=1)
+    ko = operand(M, rt, Kt, False, zmode=1)
+    sentinel = np.full((Z, T, T), 7.0, np.float32)
+    out = dev(M, sentinel)
+    run(M, rt, T, T, hs, Z, qo, ko, out=out, oz=lay(s3=T * T), om=lay(s3=T), alpha=0.125, causal=1)
+    got = out.numpy()
+    low = np.tril(np.ones((T, T), bool))
+    for z in range(Z):
+        ref = 0.125 * (Q[z].astype(np.float64) @ Kt[z].T)
+        scale = 0.125 * (np.abs(Q[z]).astype(np.float64) @ np.abs(Kt[z]).T)
+        assert np.max((np.abs(got[z] - ref) / scale)[low]) < 1e-4
+        for tm in range(0, T, 128):
+            for tn in range(0, T, 128):
+                if tn > tm + 127:
+                    assert np.all(got[z, tm:tm + 128, tn:tn + 128] == 7.0)
