@@ -322,7 +322,9 @@ int32_t malus_gpt_dp_buckets(const malus_gpt_config* cfg, int64_t* lo, int64_t* 
  * element (z, m, n) lives at oz(z) + om(m) + on(n), each term
  * (i / div) * hi + (i % div) * lo (div 0: i * lo).  Epilogues: 0 store
  * (alpha, beta), 1 residual add (out = aux + acc), 2 GELU (out = acc, planes
- * of gelu(acc)), 3 GELU derivative (planes of acc * gelu'(aux)); out_hi/out_lo,
+ * of gelu(acc)), 3 GELU derivative (planes of acc * gelu'(aux)), 4 softmax
+ * backward (planes of alpha * P * (acc - rowv[z*M + m]) with P = aux + aux_lo,
+ * the hi/lo planes of the softmax output, acc = dP); out_hi/out_lo,
  * when set, receive the tf32 planes of the stored value.  causal (per batch
  * slice, for attention matrices): 0 none; 1 only output tiles that reach the
  * lower triangle n <= m are computed (the rest of the output is not written);
@@ -345,6 +347,8 @@ typedef struct malus_tc_problem {
   const float* aux;
   float alpha, beta;
   int32_t causal;
+  const float* aux_lo;
+  const float* rowv;
 } malus_tc_problem;
 void malus_tc_gemm(const malus_tc_problem* p);
 void malus_tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t batch,

@@ -36,7 +36,7 @@ class TcProblem(C.Structure):
     _fields_ = [("M", i32), ("N", i32), ("K", i32), ("batch", i32), ("a", TcOperand), ("b", TcOperand),
                 ("epi", i32), ("oz", TcLayout), ("om", TcLayout), ("on", TcLayout),
                 ("out", vp), ("out_hi", vp), ("out_lo", vp), ("aux", vp), ("alpha", f32), ("beta", f32),
-                ("causal", i32)]
+                ("causal", i32), ("aux_lo", vp), ("rowv", vp)]
 
 
 class GptConfig(C.Structure):

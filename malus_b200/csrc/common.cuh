@@ -183,7 +183,7 @@ struct TcOperand {
 // optional divisions: q1 = i / d1, r1 = i % d1 (d1 = 0: q1 = 0, r1 = i);
 // q2 = r1 / d2, r2 = r1 % d2 (d2 = 0: q2 = 0, r2 = r1); term = q1*s1 + q2*s2 + r2*s3.
 struct TcLayout { int64_t d1, s1, d2, s2, s3; };
-enum TcEpi : int { kEpiStore = 0, kEpiResid = 1, kEpiGelu = 2, kEpiGeluBwd = 3 };
+enum TcEpi : int { kEpiStore = 0, kEpiResid = 1, kEpiGelu = 2, kEpiGeluBwd = 3, kEpiSoftmaxBwd = 4 };
 struct TcProblem {
   int M, N, K, batch;
   TcOperand a, b;
@@ -195,6 +195,8 @@ struct TcProblem {
   const float* aux; // Resid: residual input; GeluBwd: pre-activation
   float alpha = 1.f, beta = 0.f;
   int causal = 0;   // kCausal*: skip work on the zero side of an attention mask
+  const float* aux_lo = nullptr;  // SoftmaxBwd: lo plane of P (aux = hi plane)
+  const float* rowv = nullptr;    // SoftmaxBwd: D[z * M + m] = sum_j P dP of the row
 };
 enum { kCausalNone = 0, kCausalOut = 1, kCausalALower = 2, kCausalAUpper = 3 };
 void gemm_tc_planes(const TcProblem& p);

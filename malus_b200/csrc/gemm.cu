@@ -136,14 +136,16 @@ constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
 constexpr int kTileBytesA = BM * BK * 4;  // 16 KB
 constexpr int kTileBytesB = BN * BK * 4;  // 16 KB
 constexpr int kStageBytes = 2 * kTileBytesA + 2 * kTileBytesB;
-constexpr int kEpiPitch = 36;     // GELU staging row pitch (floats): 16-B aligned, conflict-free float4
-constexpr int kEpiWarpFloats = 32 * kEpiPitch;
+constexpr int kEpiWarpFloats = 32 * 32;   // per-warp 32x32 staging block (XOR-swizzled granules)
 constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
-                           4 * kEpiWarpFloats * 4 /*GELU epilogue staging*/;
+                           8 * kEpiWarpFloats * 4 /*epilogue staging*/;
 // Epilogue warps: 8 (two per TMEM lane quarter, half the columns each) when the
 // epilogue reads an auxiliary input, whose load latency the extra warps hide;
 // 4 otherwise, leaving L2 bandwidth to the operand loads.
-__host__ __device__ constexpr int epi_warps(int epi) { return (epi == 1 || epi == 3) ? 8 : 4; }
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == 0 ? 4 : 8; }
+// Epilogues with math per element or an auxiliary input go through the
+// transposing smem stage (coalesced loads and stores, 8 warps to hide latency).
+__host__ __device__ constexpr bool epi_staged(int epi) { return epi != 0; }
 __host__ __device__ constexpr int threads_tc(int epi) { return 64 + 32 * epi_warps(epi); }
 constexpr uint32_t kTmemCols = 2 * BN;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on every wait
@@ -324,10 +326,14 @@ __device__ __forceinline__ float gelu_grad(float x) {
 
 // One output element: value v (the accumulator) at offset o.
 template <int EPI>
-__device__ __forceinline__ void epi_store1(const TcProblem& p, int64_t o, float v) {
-  if (p.alpha != 1.0f) v *= p.alpha;
+__device__ __forceinline__ void epi_store1(const TcProblem& p, int64_t o, float v, float rv = 0.0f) {
+  if (EPI != kEpiSoftmaxBwd && p.alpha != 1.0f) v *= p.alpha;
   float split_src;
-  if (EPI == kEpiStore) {
+  if (EPI == kEpiSoftmaxBwd) {    // dS = (P * (dP - D)) * scale
+    const float pv = p.aux[o] + p.aux_lo[o];
+    split_src = (pv * (v - rv)) * p.alpha;
+    if (p.out) p.out[o] = split_src;
+  } else if (EPI == kEpiStore) {
     if (p.out) {                  // the f32 output is optional: planes-only callers pass none
       if (p.beta != 0.0f) v += p.beta * p.out[o];
       p.out[o] = v;
@@ -353,10 +359,16 @@ __device__ __forceinline__ void epi_store1(const TcProblem& p, int64_t o, float 
 
 // Four consecutive output elements at 16-byte aligned offset o.
 template <int EPI>
-__device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4 v, float4 aux4) {
-  if (p.alpha != 1.0f) { v.x *= p.alpha; v.y *= p.alpha; v.z *= p.alpha; v.w *= p.alpha; }
+__device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4 v, float4 aux4,
+                                           float4 auxlo4 = float4{}, float rv = 0.0f) {
+  if (EPI != kEpiSoftmaxBwd && p.alpha != 1.0f) { v.x *= p.alpha; v.y *= p.alpha; v.z *= p.alpha; v.w *= p.alpha; }
   float4 s;
-  if (EPI == kEpiStore) {
+  if (EPI == kEpiSoftmaxBwd) {
+    const float a = p.alpha;
+    s = make_float4(((aux4.x + auxlo4.x) * (v.x - rv)) * a, ((aux4.y + auxlo4.y) * (v.y - rv)) * a,
+                    ((aux4.z + auxlo4.z) * (v.z - rv)) * a, ((aux4.w + auxlo4.w) * (v.w - rv)) * a);
+    if (p.out) *reinterpret_cast<float4*>(p.out + o) = s;
+  } else if (EPI == kEpiStore) {
     if (p.out) {
       if (p.beta != 0.0f) {
         float4 q = *reinterpret_cast<const float4*>(p.out + o);
@@ -562,6 +574,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     const int chalf = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const bool contig = (p.on.d1 % 32 == 0) && (p.on.d2 % 32 == 0) && p.on.s3 == 1;
+    const int rsub = lane >> 3, cgr = lane & 7, csub = cgr * 4;   // staged layout: lane's row group / columns
     uint32_t local = 0;
     for (int unit = blockIdx.x; unit < total; unit += gridDim.x) {
       Unit un;
@@ -574,6 +587,16 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       const int m = m0 + row;
       const int64_t zm_z = lay(p.oz, z);
       const int64_t zm_off = zm_z + lay(p.om, m);
+      int64_t zm[8];                  // staged path: output offsets of rows quarter*32 + 4t + rsub
+      float rvs[8];
+      if (epi_staged(EPI) && splits == 1) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int mm = m0 + quarter * 32 + 4 * t + rsub;
+          zm[t] = mm < p.M ? zm_z + lay(p.om, mm) : -1;
+          rvs[t] = (EPI == kEpiSoftmaxBwd && mm < p.M) ? p.rowv[(int64_t)z * p.M + mm] : 0.0f;
+        }
+      }
 #pragma unroll 1
       for (int c0 = chalf * kCols; c0 < (chalf + 1) * kCols; c0 += 32) {
         uint32_t r[32];
@@ -598,60 +621,78 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
                                      __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
           continue;
         }
-        if (EPI == kEpiGelu && contig) {
-          // GELU writes three arrays: transpose the 32x32 chunk through smem so
-          // each store instruction covers 4 rows x 128 contiguous bytes
-          float* wst = reinterpret_cast<float*>(bar_area + 256) + quarter * kEpiWarpFloats;
-          float4* wrow = reinterpret_cast<float4*>(wst + lane * kEpiPitch);
+        if (epi_staged(EPI) && contig) {
+          // transpose the 32x32 chunk through smem: granule g of row r sits at
+          // g ^ (r & 7) (conflict-free float4 both ways); each lane then owns 4
+          // consecutive columns of rows 4t + rsub, so loads and stores are
+          // 4 rows x 128 contiguous bytes per instruction
+          float* wst = reinterpret_cast<float*>(bar_area + 256) + (warp - 2) * kEpiWarpFloats;
+          float4* wrow = reinterpret_cast<float4*>(wst + lane * 32);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            wrow[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                  __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            wrow[j ^ (lane & 7)] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
           __syncwarp();
-          const int rsub = lane >> 3, csub = (lane & 7) * 4;
           const int nb = n0 + c0 + csub;
           const int64_t n_off = lay(p.on, nb);
+          const bool vec = nb + 4 <= p.N;
+          float4 ax[8], axl[8];
+          if (EPI == kEpiResid || EPI == kEpiGeluBwd || EPI == kEpiSoftmaxBwd) {
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              if (zm[t] >= 0 && vec && ((zm[t] + n_off) & 3) == 0)
+                ax[t] = __ldg(reinterpret_cast<const float4*>(p.aux + zm[t] + n_off));
+          }
+          if (EPI == kEpiSoftmaxBwd) {
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              if (zm[t] >= 0 && vec && ((zm[t] + n_off) & 3) == 0)
+                axl[t] = __ldg(reinterpret_cast<const float4*>(p.aux_lo + zm[t] + n_off));
+          }
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
             const int rr = 4 * t + rsub;
-            const int mm = m0 + quarter * 32 + rr;
-            const float4 v = *reinterpret_cast<const float4*>(wst + rr * kEpiPitch + csub);
-            if (mm < p.M) {
-              const int64_t zm = zm_z + lay(p.om, mm);
-              const int64_t base = zm + n_off;
-              if (nb + 4 <= p.N && (base & 3) == 0) {
-                epi_store4<EPI>(p, base, v, v);
-              } else {
-                const float vv[4] = {v.x, v.y, v.z, v.w};
+            const float4 v = *reinterpret_cast<const float4*>(wst + rr * 32 + ((cgr ^ (rr & 7)) << 2));
+            if (zm[t] < 0) continue;
+            const int64_t base = zm[t] + n_off;
+            const float rv = EPI == kEpiSoftmaxBwd ? rvs[t] : 0.0f;
+            if (vec && (base & 3) == 0) {
+              epi_store4<EPI>(p, base, v, ax[t], axl[t], rv);
+            } else {
+              const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                  if (nb + j < p.N) epi_store1<EPI>(p, base + j, vv[j]);
-              }
+              for (int j = 0; j < 4; ++j)
+                if (nb + j < p.N) epi_store1<EPI>(p, base + j, vv[j], rv);
             }
           }
-          __syncwarp();
+          __syncwarp();   // the staging block is rewritten by the next chunk
           continue;
         }
         if (m >= p.M) continue;
         const int nb = n0 + c0;
         const int64_t base = zm_off + lay(p.on, nb);
+        const float rv = EPI == kEpiSoftmaxBwd ? p.rowv[(int64_t)z * p.M + m] : 0.0f;
         if (contig && nb + 32 <= p.N && (base & 3) == 0) {
-          float4 ax[8];
-          if (EPI == kEpiResid || EPI == kEpiGeluBwd) {
+          float4 ax[8], axl[8];
+          if (EPI == kEpiResid || EPI == kEpiGeluBwd || EPI == kEpiSoftmaxBwd) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) ax[j] = __ldg(reinterpret_cast<const float4*>(p.aux + base) + j);
+          }
+          if (EPI == kEpiSoftmaxBwd) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) axl[j] = __ldg(reinterpret_cast<const float4*>(p.aux_lo + base) + j);
           }
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             epi_store4<EPI>(p, base + 4 * j,
                             make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
                                         __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])),
-                            ax[j]);
+                            ax[j], axl[j], rv);
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (nb + j < p.N)
-              epi_store1<EPI>(p, contig ? base + j : zm_off + lay(p.on, nb + j), __uint_as_float(r[j]));
+              epi_store1<EPI>(p, contig ? base + j : zm_off + lay(p.on, nb + j), __uint_as_float(r[j]), rv);
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -692,14 +733,17 @@ __global__ void k_splitk_reduce(const TcKernelParams kp) {
     }
     const int64_t zm = lay(p.oz, z) + lay(p.om, m);
     const int64_t base = zm + lay(p.on, n);
+    const float rv = EPI == kEpiSoftmaxBwd ? p.rowv[(int64_t)z * p.M + m] : 0.0f;
     if (contig4 && n + 4 <= p.N && (base & 3) == 0) {
-      float4 ax = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (EPI == kEpiResid || EPI == kEpiGeluBwd) ax = *reinterpret_cast<const float4*>(p.aux + base);
-      epi_store4<EPI>(p, base, v, ax);
+      float4 ax = make_float4(0.f, 0.f, 0.f, 0.f), axl = ax;
+      if (EPI == kEpiResid || EPI == kEpiGeluBwd || EPI == kEpiSoftmaxBwd)
+        ax = *reinterpret_cast<const float4*>(p.aux + base);
+      if (EPI == kEpiSoftmaxBwd) axl = *reinterpret_cast<const float4*>(p.aux_lo + base);
+      epi_store4<EPI>(p, base, v, ax, axl, rv);
     } else {
       const float vv[4] = {v.x, v.y, v.z, v.w};
       for (int j = 0; j < 4 && n + j < p.N; ++j)
-        epi_store1<EPI>(p, contig4 ? base + j : zm + lay(p.on, n + j), vv[j]);
+        epi_store1<EPI>(p, contig4 ? base + j : zm + lay(p.on, n + j), vv[j], rv);
     }
   }
 }
@@ -880,6 +924,9 @@ void gemm_tc_planes(const TcProblem& pr) {
   if ((pr.out_hi == nullptr) != (pr.out_lo == nullptr)) panic("gemm_tc_planes: out_hi/out_lo must come together");
   if ((pr.epi == kEpiResid || pr.epi == kEpiGeluBwd) && !pr.aux) panic("gemm_tc_planes: epilogue %d needs aux", pr.epi);
   if ((pr.epi == kEpiGelu || pr.epi == kEpiGeluBwd) && !pr.out_hi) panic("gemm_tc_planes: GELU epilogues write planes");
+  if (pr.epi < kEpiStore || pr.epi > kEpiSoftmaxBwd) panic("gemm_tc_planes: epilogue %d", pr.epi);
+  if (pr.epi == kEpiSoftmaxBwd && (!pr.aux || !pr.aux_lo || !pr.rowv))
+    panic("gemm_tc_planes: softmax-backward epilogue needs P planes (aux, aux_lo) and rowv");
   if (!pr.a.hi || !pr.a.lo || !pr.b.hi || !pr.b.lo) panic("gemm_tc_planes: missing operand plane");
   if (pr.causal < 0 || pr.causal > kCausalAUpper) panic("gemm_tc_planes: causal mode %d", pr.causal);
   for (const TcOperand* o : {&pr.a, &pr.b})
@@ -928,7 +975,8 @@ void gemm_tc_planes(const TcProblem& pr) {
     case kEpiStore: launch_tc<kEpiStore>(ah, al, bh, bl, kp, grid); break;
     case kEpiResid: launch_tc<kEpiResid>(ah, al, bh, bl, kp, grid); break;
     case kEpiGelu: launch_tc<kEpiGelu>(ah, al, bh, bl, kp, grid); break;
-    default: launch_tc<kEpiGeluBwd>(ah, al, bh, bl, kp, grid); break;
+    case kEpiGeluBwd: launch_tc<kEpiGeluBwd>(ah, al, bh, bl, kp, grid); break;
+    default: launch_tc<kEpiSoftmaxBwd>(ah, al, bh, bl, kp, grid); break;
   }
   count_launch(kp.splits > 1 ? 2 : 1);
   after_launch("k_gemm_tc");
@@ -992,6 +1040,8 @@ extern "C" void malus_tc_gemm(const malus_tc_problem* q) {
   p.out = q->out; p.out_hi = q->out_hi; p.out_lo = q->out_lo; p.aux = q->aux;
   p.alpha = q->alpha; p.beta = q->beta;
   p.causal = q->causal;
+  p.aux_lo = q->aux_lo;
+  p.rowv = q->rowv;
   gemm_tc_planes(p);
 }
 

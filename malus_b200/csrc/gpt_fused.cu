@@ -428,7 +428,8 @@ TcOperand op(const Planes& p, int64_t rows, int64_t cols, int64_t pitch, bool mn
 
 void gemm(int M, int N, int K, int batch, const TcOperand& a, const TcOperand& b, int epi,
           TcLayout oz, TcLayout om, TcLayout on, float* out, Planes outp, const float* aux,
-          float alpha = 1.0f, int causal = kCausalNone) {
+          float alpha = 1.0f, int causal = kCausalNone, const float* aux_lo = nullptr,
+          const float* rowv = nullptr) {
   TcProblem p{};
   p.M = M; p.N = N; p.K = K; p.batch = batch;
   p.a = a; p.b = b;
@@ -437,6 +438,8 @@ void gemm(int M, int N, int K, int batch, const TcOperand& a, const TcOperand& b
   p.out = out; p.out_hi = outp.hi; p.out_lo = outp.lo; p.aux = aux;
   p.alpha = alpha; p.beta = 0.0f;
   p.causal = causal;
+  p.aux_lo = aux_lo;
+  p.rowv = rowv;
   gemm_tc_planes(p);
 }
 

@@ -331,3 +331,33 @@ def test_causal_output_tiles(M, rt, rng, T):
             for tn in range(0, T, 128):
                 if tn > tm + 127:
                     assert np.all(got[z, tm:tm + 128, tn:tn + 128] == 7.0)
+
+
+def test_softmax_backward_epilogue(M, rt, rng):
+    """dS = scale * P * (dO V^T - D) in the GEMM epilogue, P read from its tf32
+    planes, D per row, causal tiles only (the fused attention backward)."""
+    Z, T, hs, scale = 3, 256, 64, 0.125
+    S = rng.standard_normal((Z, T, T)) + np.triu(np.full((T, T), -np.inf), 1)
+    P = np.exp(S - S.max(-1, keepdims=True))
+    P = (P / P.sum(-1, keepdims=True)).astype(np.float32)
+    dO = rng.standard_normal((Z, T, hs)).astype(np.float32)
+    V = rng.standard_normal((Z, T, hs)).astype(np.float32)
+    D = np.einsum("ztd,ztd->zt", dO.astype(np.float64), np.einsum("ztk,zkd->ztd", P.astype(np.float64), V))
+    p_hi, p_lo, _, _, _, _ = planes(M, rt, P)
+    Dd = dev(M, D.astype(np.float32))
+    hi, lo = dev(M, np.zeros((Z, T, T))), dev(M, np.zeros((Z, T, T)))
+    p = M.TcProblem()
+    p.M, p.N, p.K, p.batch = T, T, hs, Z
+    p.a, p.b = operand(M, rt, dO, False, zmode=1), operand(M, rt, V, False, zmode=1)
+    p.epi = 4
+    p.oz, p.om, p.on = lay(s3=T * T), lay(s3=T), lay(s3=1)
+    p.out_hi, p.out_lo = ptr(rt, hi), ptr(rt, lo)
+    p.aux, p.aux_lo, p.rowv = ptr(rt, p_hi), ptr(rt, p_lo), ptr(rt, Dd)
+    p.alpha, p.beta, p.causal = scale, 0.0, 1
+    rt.malus_tc_gemm(C.byref(p))
+    got = hi.numpy().astype(np.float64) + lo.numpy()
+    dP = np.einsum("ztd,zkd->ztk", dO.astype(np.float64), V)
+    ref = scale * P * (dP - D[..., None])
+    bound = scale * P * (np.einsum("ztd,zkd->ztk", np.abs(dO).astype(np.float64), np.abs(V)) + np.abs(D)[..., None])
+    low = np.tril(np.ones((T, T), bool))
+    assert np.max((np.abs(got - ref) / np.maximum(bound, 1e-30))[:, low]) < 1e-5
