@@ -143,9 +143,9 @@ constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barrier
 // epilogue reads an auxiliary input, whose load latency the extra warps hide;
 // 4 otherwise, leaving L2 bandwidth to the operand loads.
 __host__ __device__ constexpr int epi_warps(int epi) { return epi == 0 ? 4 : 8; }
-// Epilogues with math per element or an auxiliary input go through the
-// transposing smem stage (coalesced loads and stores, 8 warps to hide latency).
-__host__ __device__ constexpr bool epi_staged(int epi) { return epi != 0; }
+// Epilogues with math per element or an auxiliary input, and stores that write
+// tf32 planes, go through the transposing smem stage (coalesced loads and
+// stores); a plain f32 store writes each lane's row directly.
 __host__ __device__ constexpr int threads_tc(int epi) { return 64 + 32 * epi_warps(epi); }
 constexpr uint32_t kTmemCols = 2 * BN;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on every wait
@@ -275,6 +275,7 @@ struct TcKernelParams {
   int splits;      // K slices per tile (split-K); > 1 writes raw partial tiles to ws
   float* ws;       // [tile][split][BM][BN] partial accumulators when splits > 1
   int a_chunked, b_chunked;   // MN-major operand loaded as one {32, 32 K, 4 chunks} box per plane
+  int staged;                 // epilogue through the smem transpose (see epi_warps)
   int32_t* err;
 };
 
@@ -589,7 +590,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       const int64_t zm_off = zm_z + lay(p.om, m);
       int64_t zm[8];                  // staged path: output offsets of rows quarter*32 + 4t + rsub
       float rvs[8];
-      if (epi_staged(EPI) && splits == 1) {
+      if (kp.staged && splits == 1) {
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
           const int mm = m0 + quarter * 32 + 4 * t + rsub;
@@ -621,7 +622,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
                                      __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
           continue;
         }
-        if (epi_staged(EPI) && contig) {
+        if (kp.staged) {
           // transpose the 32x32 chunk through smem: granule g of row r sits at
           // g ^ (r & 7) (conflict-free float4 both ways); each lane then owns 4
           // consecutive columns of rows 4t + rsub, so loads and stores are
@@ -943,6 +944,10 @@ void gemm_tc_planes(const TcProblem& pr) {
   kp.err = device_error_word();
   int tiles = kp.tiles_m * kp.tiles_n * pr.batch;
   kp.splits = pr.causal ? 1 : splitk_for(tiles, kp.nk);
+  {
+    const bool contig = (pr.on.d1 % 32 == 0) && (pr.on.d2 % 32 == 0) && pr.on.s3 == 1;
+    kp.staged = contig && (pr.epi != kEpiStore || pr.out_hi != nullptr) ? 1 : 0;
+  }
   kp.a_chunked = mn_chunked(pr.a) ? 1 : 0;
   kp.b_chunked = mn_chunked(pr.b) ? 1 : 0;
   kp.ws = kp.splits > 1 ? splitk_workspace((size_t)tiles * kp.splits * BM * BN) : nullptr;
