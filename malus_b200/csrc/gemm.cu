@@ -132,13 +132,23 @@ void gemm_simt(const GemmArgs& g) {
 // the tf32 split of its own output (so the next GEMM reads ready planes).
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+constexpr int BM = 128, BK = 32;
 constexpr int kTileBytesA = BM * BK * 4;  // 16 KB
-constexpr int kTileBytesB = BN * BK * 4;  // 16 KB
-constexpr int kStageBytes = 2 * kTileBytesA + 2 * kTileBytesB;
 constexpr int kEpiWarpFloats = 32 * 32;   // per-warp 32x32 staging block (XOR-swizzled granules)
-constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
-                           8 * kEpiWarpFloats * 4 /*epilogue staging*/;
+// Tile width BN (128, 192 or 256): a wider tile reads each A k-block once for more
+// columns (less shared-memory and L2 traffic per FLOP); its larger stages
+// leave room for 2 of them instead of 3.
+template <int BN_>
+struct TileCfg {
+  static constexpr int BN = BN_;
+  static constexpr int kTileBytesB = BN * BK * 4;
+  static constexpr int kStageBytes = 2 * kTileBytesA + 2 * kTileBytesB;
+  static constexpr int STAGES = BN <= 128 ? 3 : 2;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+                                    8 * kEpiWarpFloats * 4 /*epilogue staging*/;
+  static constexpr uint32_t kTmemCols = BN <= 128 ? 256 : 512;   // two accumulators, power of 2
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
 // Epilogue warps: 8 (two per TMEM lane quarter, half the columns each) when the
 // epilogue reads an auxiliary input, whose load latency the extra warps hide;
 // 4 otherwise, leaving L2 bandwidth to the operand loads.
@@ -147,7 +157,6 @@ __host__ __device__ constexpr int epi_warps(int epi) { return epi == 0 ? 4 : 8; 
 // tf32 planes, go through the transposing smem stage (coalesced loads and
 // stores); a plain f32 store writes each lane's row directly.
 __host__ __device__ constexpr int threads_tc(int epi) { return 64 + 32 * epi_warps(epi); }
-constexpr uint32_t kTmemCols = 2 * BN;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on every wait
 constexpr float kGeluC0 = 0.7978845608028654f, kGeluC1 = 0.044715f;
 
@@ -235,10 +244,10 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int kk) {
   return umma_desc(tile + kk * 1024, 4096, 512, 1);
 }
 
-// Instruction descriptor: f32 accumulate, tf32 A/B, M=128, N=BN.
-__host__ __device__ constexpr uint32_t idesc_tf32(bool a_mn, bool b_mn) {
+// Instruction descriptor: f32 accumulate, tf32 A/B, M=128, N=n.
+__host__ __device__ constexpr uint32_t idesc_tf32(bool a_mn, bool b_mn, int n) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) |
-         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
@@ -273,7 +282,8 @@ struct TcKernelParams {
   TcProblem pr;
   int tiles_m, tiles_n, nk;
   int splits;      // K slices per tile (split-K); > 1 writes raw partial tiles to ws
-  float* ws;       // [tile][split][BM][BN] partial accumulators when splits > 1
+  float* ws;       // [tile][split][BM][bn] partial accumulators when splits > 1
+  int bn;          // tile width (the kernel's BN)
   int a_chunked, b_chunked;   // MN-major operand loaded as one {32, 32 K, 4 chunks} box per plane
   int staged;                 // epilogue through the smem transpose (see epi_warps)
   int32_t* err;
@@ -291,7 +301,7 @@ __device__ __forceinline__ bool unit_of(const TcKernelParams& kp, int unit, Unit
   u.z = tile / per_batch;
   const int rem = tile % per_batch;
   u.m0 = (rem / kp.tiles_n) * BM;
-  u.n0 = (rem % kp.tiles_n) * BN;
+  u.n0 = (rem % kp.tiles_n) * kp.bn;
   if (p.causal == kCausalOut && u.n0 > u.m0 + BM - 1) return false;
   int lo = 0, hi = kp.nk;
   if (p.causal == kCausalALower) hi = min(kp.nk, (u.m0 + BM + BK - 1) / BK);
@@ -401,11 +411,15 @@ __device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4
   }
 }
 
-template <int EPI>
+template <int EPI, int BNT>
 __global__ void __launch_bounds__(threads_tc(EPI), 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
           const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
           const TcKernelParams kp) {
+  using CF = TileCfg<BNT>;
+  constexpr int BN = CF::BN, STAGES = CF::STAGES, kStageBytes = CF::kStageBytes;
+  constexpr int kTileBytesB = CF::kTileBytesB;
+  constexpr uint32_t kTmemCols = CF::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
   const TcProblem& p = kp.pr;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -518,7 +532,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(p.a.mn_major, p.b.mn_major);
+      const uint32_t idesc = idesc_tf32(p.a.mn_major, p.b.mn_major, BN);
       uint32_t it = 0, local = 0;
       bool ok = true, issued = false;
       for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
@@ -716,20 +730,21 @@ template <int EPI>
 __global__ void k_splitk_reduce(const TcKernelParams kp) {
   const TcProblem& p = kp.pr;
   const int per_batch = kp.tiles_m * kp.tiles_n;
-  const int64_t chunks = (int64_t)per_batch * p.batch * (BM * BN / 4);
+  const int bn = kp.bn, tsz = BM * bn;
+  const int64_t chunks = (int64_t)per_batch * p.batch * (tsz / 4);
   const bool contig4 = (p.on.d1 % 4 == 0) && (p.on.d2 % 4 == 0) && p.on.s3 == 1;
   for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < chunks;
        q += (int64_t)gridDim.x * blockDim.x) {
-    const int tile = (int)(q / (BM * BN / 4));
-    const int e = (int)(q % (BM * BN / 4)) * 4;    // element offset inside the tile
-    const int r = e / BN, c = e % BN;
+    const int tile = (int)(q / (tsz / 4));
+    const int e = (int)(q % (tsz / 4)) * 4;    // element offset inside the tile
+    const int r = e / bn, c = e % bn;
     const int z = tile / per_batch, rem = tile % per_batch;
-    const int m = (rem / kp.tiles_n) * BM + r, n = (rem % kp.tiles_n) * BN + c;
+    const int m = (rem / kp.tiles_n) * BM + r, n = (rem % kp.tiles_n) * bn + c;
     if (m >= p.M || n >= p.N) continue;
-    const float4* src = reinterpret_cast<const float4*>(kp.ws + (size_t)tile * kp.splits * (BM * BN) + e);
+    const float4* src = reinterpret_cast<const float4*>(kp.ws + (size_t)tile * kp.splits * tsz + e);
     float4 v = src[0];
     for (int sl = 1; sl < kp.splits; ++sl) {
-      float4 t = src[(size_t)sl * (BM * BN / 4)];
+      float4 t = src[(size_t)sl * (tsz / 4)];
       v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
     }
     const int64_t zm = lay(p.oz, z) + lay(p.om, m);
@@ -811,21 +826,22 @@ CUtensorMap make_map(const float* base, uint64_t d0, uint64_t d1, uint64_t d2, u
 // Map of one operand plane.  Stored matrix: nz slices of rows x cols with the
 // given pitch; K-major operands are {cols=K, rows=MN}, MN-major {cols=MN, rows=K}.
 // An MN-major operand whose columns are whole 32-element chunks (and whose
-// segments, if any, are whole 128-wide tiles) is read as one box per plane:
-// a 4-D view {32 columns, K rows, column chunks, slices} with box {32, 32, 4, 1}
-// lands in shared memory as [chunk][k][32], the same swizzled layout that four
-// 32-wide boxes produce.  The view never addresses past a row's columns.
-bool mn_chunked(const TcOperand& o) {
-  return o.mn_major && o.cols % 32 == 0 && (o.zmode != kZMNSeg || o.seg % 128 == 0);
+// segments, if any, are whole tiles of width tile_mn) is read as one box per
+// plane: a 4-D view {32 columns, K rows, column chunks, slices} with box
+// {32, 32, tile_mn / 32, 1} lands in shared memory as [chunk][k][32], the same
+// swizzled layout that separate 32-wide boxes produce.  The view never
+// addresses past a row's columns.
+bool mn_chunked(const TcOperand& o, int tile_mn) {
+  return o.mn_major && o.cols % 32 == 0 && (o.zmode != kZMNSeg || o.seg % tile_mn == 0);
 }
 
 CUtensorMap chunked_map(const TcOperand& o, const float* plane, uint64_t pitch_bytes,
-                        uint64_t plane_bytes) {
+                        uint64_t plane_bytes, int tile_mn) {
   CUtensorMap m;
   cuuint64_t dims[4] = {32, (cuuint64_t)o.rows, (cuuint64_t)(o.cols / 32),
                         (cuuint64_t)std::max(1, o.nz)};
   cuuint64_t strides[3] = {pitch_bytes, 128, plane_bytes};
-  cuuint32_t box[4] = {32, 32, 4, 1};
+  cuuint32_t box[4] = {32, 32, (cuuint32_t)(tile_mn / 32), 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)plane, dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
@@ -834,19 +850,33 @@ CUtensorMap chunked_map(const TcOperand& o, const float* plane, uint64_t pitch_b
   return m;
 }
 
-CUtensorMap operand_map(const TcOperand& o, const float* plane) {
+// tile_mn: the operand's tile extent along M (A: BM) or N (B: the tile width).
+CUtensorMap operand_map(const TcOperand& o, const float* plane, int tile_mn) {
   uint64_t pb = (uint64_t)o.pitch * 4;
   uint64_t zb = (uint64_t)o.zstride * 4;
   if (o.nz > 1 && (zb % 16 != 0)) panic("gemm operand slice stride %lld is not 16-byte aligned", (long long)o.zstride);
   if (o.nz <= 1) zb = pb * (uint64_t)o.rows;
-  if (mn_chunked(o)) return chunked_map(o, plane, pb, std::max<uint64_t>(zb, 16));
-  // K-major boxes are 32 (K) x 128 rows, or 32 x 32 rows when the rows are segmented
-  uint32_t box_rows = (o.mn_major || o.zmode == kZMNSeg) ? 32 : BM;
+  if (mn_chunked(o, tile_mn)) return chunked_map(o, plane, pb, std::max<uint64_t>(zb, 16), tile_mn);
+  // K-major boxes are 32 (K) x tile_mn rows, or 32 x 32 rows when the rows are segmented
+  uint32_t box_rows = (o.mn_major || o.zmode == kZMNSeg) ? 32 : (uint32_t)tile_mn;
   return make_map(plane, (uint64_t)o.cols, (uint64_t)o.rows, (uint64_t)std::max(1, o.nz), pb,
                   std::max<uint64_t>(zb, 16), 32, box_rows, o.mn_major);
 }
 
 int g_force_backend = -1;
+
+// Tile width: 192 when N is a whole number of 192-wide tiles and the grid
+// stays full (every C4 layer GEMM: N = 384, 1152, 1536), else 128.
+int tile_width_for(const TcProblem& pr) {
+  static int forced = [] {
+    const char* e = getenv("MALUS_GEMM_BN");   // 128 or 192 (tuning)
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 128 || forced == 192 || forced == 256) return forced;
+  if (pr.causal || pr.N % 192 != 0) return 128;
+  long tiles = (long)((pr.M + BM - 1) / BM) * (pr.N / 192) * pr.batch;
+  return tiles >= kNumSMs ? 192 : 128;
+}
 
 // K slices for a problem of `tiles` output tiles and nk k-blocks: split only
 // when the tiles fill less than half the SMs and every slice keeps >= 8 k-blocks
@@ -872,18 +902,19 @@ float* splitk_workspace(size_t floats) {
   return buf[dev];
 }
 
-template <int EPI>
+template <int EPI, int BNT>
 void launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
                const CUtensorMap& bl, const TcKernelParams& kp, int grid) {
+  constexpr int smem = TileCfg<BNT>::kSmemBytes;
   static bool attr = false;
   if (!attr) {
-    MALUS_CUDA(cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    kSmemBytes));
+    MALUS_CUDA(cudaFuncSetAttribute(k_gemm_tc<EPI, BNT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    smem));
     attr = true;
   }
-  k_gemm_tc<EPI><<<grid, threads_tc(EPI), kSmemBytes, stream()>>>(ah, al, bh, bl, kp);
+  k_gemm_tc<EPI, BNT><<<grid, threads_tc(EPI), smem, stream()>>>(ah, al, bh, bl, kp);
   if (kp.splits > 1) {
-    int64_t chunks = (int64_t)kp.tiles_m * kp.tiles_n * kp.pr.batch * (BM * BN / 4);
+    int64_t chunks = (int64_t)kp.tiles_m * kp.tiles_n * kp.pr.batch * (BM * kp.bn / 4);
     unsigned g = (unsigned)std::min<int64_t>((chunks + 255) / 256, (int64_t)kNumSMs * 8);
     k_splitk_reduce<EPI><<<g, 256, 0, stream()>>>(kp);
   }
@@ -934,10 +965,12 @@ void gemm_tc_planes(const TcProblem& pr) {
     if ((o->zmode == kZKSeg || o->zmode == kZMNSeg) && (o->seg <= 0 || o->seg % 32 != 0))
       panic("gemm_tc_planes: segment width %d must be a positive multiple of 32", o->seg);
   load_encoder();
-  CUtensorMap ah = operand_map(pr.a, pr.a.hi), al = operand_map(pr.a, pr.a.lo);
-  CUtensorMap bh = operand_map(pr.b, pr.b.hi), bl = operand_map(pr.b, pr.b.lo);
+  const int BN = tile_width_for(pr);
+  CUtensorMap ah = operand_map(pr.a, pr.a.hi, BM), al = operand_map(pr.a, pr.a.lo, BM);
+  CUtensorMap bh = operand_map(pr.b, pr.b.hi, BN), bl = operand_map(pr.b, pr.b.lo, BN);
   TcKernelParams kp;
   kp.pr = pr;
+  kp.bn = BN;
   kp.tiles_m = (pr.M + BM - 1) / BM;
   kp.tiles_n = (pr.N + BN - 1) / BN;
   kp.nk = (pr.K + BK - 1) / BK;
@@ -948,8 +981,8 @@ void gemm_tc_planes(const TcProblem& pr) {
     const bool contig = (pr.on.d1 % 32 == 0) && (pr.on.d2 % 32 == 0) && pr.on.s3 == 1;
     kp.staged = contig && (pr.epi != kEpiStore || pr.out_hi != nullptr) ? 1 : 0;
   }
-  kp.a_chunked = mn_chunked(pr.a) ? 1 : 0;
-  kp.b_chunked = mn_chunked(pr.b) ? 1 : 0;
+  kp.a_chunked = mn_chunked(pr.a, BM) ? 1 : 0;
+  kp.b_chunked = mn_chunked(pr.b, BN) ? 1 : 0;
   kp.ws = kp.splits > 1 ? splitk_workspace((size_t)tiles * kp.splits * BM * BN) : nullptr;
   int total = tiles * kp.splits;
   // Static round-robin over units: for causal problems the per-batch pattern of
@@ -976,12 +1009,30 @@ void gemm_tc_planes(const TcProblem& pr) {
   const int arrays = (pr.out ? 1 : 0) + (pr.out_hi ? 2 : 0) + (pr.aux ? 1 : 0);
   int pid = prof_begin(0, flops, 8.0 * ((double)pr.M * pr.K + (double)pr.N * pr.K) * pr.batch +
                                      4.0 * mn * arrays);
-  switch (pr.epi) {
-    case kEpiStore: launch_tc<kEpiStore>(ah, al, bh, bl, kp, grid); break;
-    case kEpiResid: launch_tc<kEpiResid>(ah, al, bh, bl, kp, grid); break;
-    case kEpiGelu: launch_tc<kEpiGelu>(ah, al, bh, bl, kp, grid); break;
-    case kEpiGeluBwd: launch_tc<kEpiGeluBwd>(ah, al, bh, bl, kp, grid); break;
-    default: launch_tc<kEpiSoftmaxBwd>(ah, al, bh, bl, kp, grid); break;
+  if (BN == 256) {
+    switch (pr.epi) {
+      case kEpiStore: launch_tc<kEpiStore, 256>(ah, al, bh, bl, kp, grid); break;
+      case kEpiResid: launch_tc<kEpiResid, 256>(ah, al, bh, bl, kp, grid); break;
+      case kEpiGelu: launch_tc<kEpiGelu, 256>(ah, al, bh, bl, kp, grid); break;
+      case kEpiGeluBwd: launch_tc<kEpiGeluBwd, 256>(ah, al, bh, bl, kp, grid); break;
+      default: launch_tc<kEpiSoftmaxBwd, 256>(ah, al, bh, bl, kp, grid); break;
+    }
+  } else if (BN == 192) {
+    switch (pr.epi) {
+      case kEpiStore: launch_tc<kEpiStore, 192>(ah, al, bh, bl, kp, grid); break;
+      case kEpiResid: launch_tc<kEpiResid, 192>(ah, al, bh, bl, kp, grid); break;
+      case kEpiGelu: launch_tc<kEpiGelu, 192>(ah, al, bh, bl, kp, grid); break;
+      case kEpiGeluBwd: launch_tc<kEpiGeluBwd, 192>(ah, al, bh, bl, kp, grid); break;
+      default: launch_tc<kEpiSoftmaxBwd, 192>(ah, al, bh, bl, kp, grid); break;
+    }
+  } else {
+    switch (pr.epi) {
+      case kEpiStore: launch_tc<kEpiStore, 128>(ah, al, bh, bl, kp, grid); break;
+      case kEpiResid: launch_tc<kEpiResid, 128>(ah, al, bh, bl, kp, grid); break;
+      case kEpiGelu: launch_tc<kEpiGelu, 128>(ah, al, bh, bl, kp, grid); break;
+      case kEpiGeluBwd: launch_tc<kEpiGeluBwd, 128>(ah, al, bh, bl, kp, grid); break;
+      default: launch_tc<kEpiSoftmaxBwd, 128>(ah, al, bh, bl, kp, grid); break;
+    }
   }
   count_launch(kp.splits > 1 ? 2 : 1);
   after_launch("k_gemm_tc");

@@ -241,10 +241,12 @@ __global__ void k_softmax_causal_split(const float* __restrict__ S, float* __res
       s += v[k];
     }
     s = wsum(s);
+    // keys past the query's 128-wide tile are never read by the causal GEMMs
+    const int jend = min(T, (i / 128 + 1) * 128);
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int j = lane + 32 * k;
-      if (j < T) split_store(p_hi, p_lo, (size_t)r * T + j, v[k] / s);
+      if (j < jend) split_store(p_hi, p_lo, (size_t)r * T + j, v[k] / s);
     }
   }
 }
@@ -271,10 +273,11 @@ __global__ void k_softmax_bwd_split(const float* __restrict__ p_hi, const float*
       dot += gv[k] * pv[k];
     }
     dot = wsum(dot);
+    const int jend = min(T, (i / 128 + 1) * 128);   // as in the forward: later tiles are never read
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int j = lane + 32 * k;
-      if (j < T) split_store(ds_hi, ds_lo, base + j, (pv[k] * (gv[k] - dot)) * scale);
+      if (j < jend) split_store(ds_hi, ds_lo, base + j, (pv[k] * (gv[k] - dot)) * scale);
     }
   }
 }
