@@ -143,6 +143,81 @@ def cpu_baseline_port(cfg, steps=2, sample_batch=8):
                       f"tokens ({m} tokens/step) on the oracle's OpenMP loops"}
 
 
+def c2_cpu_ops(threads: int):
+    """The C2 op shapes through the oracle (the reference's CPU path restated) on
+    `threads` host threads: {op name: seconds} (best of 2 after one warm-up)."""
+    from oracle import pyoracle as O
+    O.set_threads(threads)
+    rng = np.random.default_rng(0)
+    n = 8192
+    x = rng.standard_normal((n, n), dtype=np.float32)
+    y = rng.standard_normal((n, n), dtype=np.float32)
+    a = rng.standard_normal((65536, 768), dtype=np.float32)
+    g = rng.standard_normal((65536, 768), dtype=np.float32)
+    lg = rng.standard_normal((65536, 65), dtype=np.float32)
+    tg = rng.integers(0, 65, 65536).astype(np.int32)
+    wte = rng.standard_normal((65, 768), dtype=np.float32)
+    de = rng.standard_normal((65536, 768), dtype=np.float32)
+    pa = rng.standard_normal(10_000_000, dtype=np.float32)
+    ga = rng.standard_normal(10_000_000, dtype=np.float32)
+    ma, va = np.zeros_like(pa), np.zeros_like(pa)
+    sm = O.softmax(a, 1)
+    ly, lv = O.layernorm(a, 1)
+    _, probs = O.xent(lg, tg)
+    cases = {
+        "add 8192^2": lambda: O.broadcast(0, x, y),
+        "mul 8192^2": lambda: O.broadcast(2, x, y),
+        "scalar*tensor 8192^2": lambda: O.broadcast(2, x, np.array([1.5], np.float32)),
+        "sigmoid 8192^2": lambda: O.unary("sigmoid", x),
+        "gelu 8192^2": lambda: O.unary("gelu", x),
+        "exp 8192^2": lambda: O.unary("exp", x),
+        "row sum 8192^2": lambda: O.reduce(0, x, 1),
+        "col sum 8192^2": lambda: O.reduce(0, x, 0),
+        "softmax 65536x768": lambda: O.softmax(a, 1),
+        "softmax bwd 65536x768": lambda: O.softmax_bwd(sm, g, 1),
+        "layernorm 65536x768": lambda: O.layernorm(a, 1),
+        "layernorm bwd 65536x768": lambda: O.layernorm_bwd(ly, lv, g, 1),
+        "cross_entropy fwd 65536x65": lambda: O.xent(lg, tg),
+        "cross_entropy bwd 65536x65": lambda: O.xent_bwd(probs, tg, 1.0),
+        "embedding fwd 65x768, 65536 ids": lambda: O.embedding(wte, tg),
+        "embedding bwd 65x768, 65536 ids": lambda: O.embedding_bwd(de, tg, 65),
+        "AdamW 10M params": lambda: O.adamw(pa, ga, ma, va, 1e-3, 0.9, 0.95, 1e-8, 0.1, 1),
+    }
+    out = {}
+    for name, fn in cases.items():
+        fn()
+        best = float("inf")
+        for _ in range(2):
+            t0 = time.perf_counter()
+            fn()
+            best = min(best, time.perf_counter() - t0)
+        out[name] = best
+    return out
+
+
+def run_ops(args):
+    """C2 op microbench: each op on the GPU (CUDA events, median of --reps) beside
+    the oracle's CPU path on 1 thread and on all host threads; GB/s = algorithmic
+    bytes / time."""
+    from malus_b200 import opbench
+    rows, peaks = opbench.run(reps=20, verbose=False)
+    ncpu = os.cpu_count() or 1
+    cpu1 = c2_cpu_ops(1)
+    cpun = c2_cpu_ops(ncpu)
+    for r in rows:
+        if r["op"] in cpu1:
+            r["cpu1_gbs"] = round(r["bytes"] / cpu1[r["op"]] / 1e9, 2)
+            r["cpun_gbs"] = round(r["bytes"] / cpun[r["op"]] / 1e9, 2)
+    print(json.dumps({"metric": "C2 op microbench", "unit": "GB/s", "peaks": peaks, "cpu_threads": ncpu,
+                      "ops": rows}))
+    print(f"| op | GPU ms | GPU GB/s | of HBM | f32 TF/s (tf32 pipe) | CPU 1-thread GB/s | CPU {ncpu}-thread GB/s |")
+    print("|---|---:|---:|---:|---:|---:|---:|")
+    for r in rows:
+        tf = f"{r['f32_tflops']} ({r['frac_tf32']})" if "f32_tflops" in r else ""
+        print(f"| {r['op']} | {r['ms']} | {r['gbs']} | {r['frac_hbm']} | {tf} | {r.get('cpu1_gbs', '')} | "
+              f"{r.get('cpun_gbs', '')} |")
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -184,6 +259,7 @@ def main():
     ap.add_argument("--impl", default="malus", choices=["malus", "reference"])
     ap.add_argument("--mode", type=int, default=int(os.environ.get("MALUS_BENCH_MODE", "1")))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ops", action="store_true", help="C2 op microbench (GPU and CPU oracle)")
     ap.add_argument("--graph", type=int, default=int(os.environ.get("MALUS_BENCH_GRAPH", "1")),
                     help="replay the fused step as one CUDA graph (mode 1)")
     args = ap.parse_args()
@@ -195,6 +271,10 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.ops:
+        if rank == 0:
+            run_ops(args)
         return
 
     import torch

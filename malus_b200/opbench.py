@@ -214,33 +214,40 @@ def plane_cases(b: Bench, rng):
         yield name, (lambda q=q: run(q)), nbytes(q, Mm, N, K, batch, nout, aux), 2.0 * Mm * N * K * batch
 
 
+def run(only: str | None = None, reps: int = 20, verbose: bool = True) -> tuple[list[dict], dict]:
+    """Time every case (or those whose name contains `only`); returns (rows, peaks)."""
+    hbm, tf32, src = _peaks()
+    b = Bench(reps)
+    rng = np.random.default_rng(0)
+    rows = []
+    for name, fn, nbytes, flops in cases(b, rng):
+        if only and only not in name:
+            continue
+        ms = b.time(fn)
+        row = {"op": name, "ms": round(ms, 4), "bytes": nbytes, "gbs": round(nbytes / ms / 1e6, 1),
+               "frac_hbm": round(nbytes / ms / 1e6 / hbm, 3)}
+        if flops:
+            row["flops"] = flops
+            row["f32_tflops"] = round(flops / ms / 1e9, 1)
+            row["tf32_executed_tflops"] = round(3 * flops / ms / 1e9, 1)
+            row["frac_tf32"] = round(3 * flops / ms / 1e9 / tf32, 3)
+        rows.append(row)
+        if verbose:
+            print(f"{name:42s} {ms:9.4f} ms  {row['gbs']:8.1f} GB/s ({row['frac_hbm']:.2f} of HBM)"
+                  + (f"  {row['f32_tflops']:6.1f} f32-TF/s, tf32 pipe {row['frac_tf32']:.2f}" if flops else ""),
+                  flush=True)
+    return rows, {"hbm_gbs": hbm, "tf32_tflops": tf32, "source": src}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None)
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--json", action="store_true")
     args = ap.parse_args()
-    hbm, tf32, src = _peaks()
-    b = Bench(args.reps)
-    rng = np.random.default_rng(0)
-    rows = []
-    for name, fn, nbytes, flops in cases(b, rng):
-        if args.only and args.only not in name:
-            continue
-        ms = b.time(fn)
-        row = {"op": name, "ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1),
-               "frac_hbm": round(nbytes / ms / 1e6 / hbm, 3)}
-        if flops:
-            row["f32_tflops"] = round(flops / ms / 1e9, 1)
-            row["tf32_executed_tflops"] = round(3 * flops / ms / 1e9, 1)
-            row["frac_tf32"] = round(3 * flops / ms / 1e9 / tf32, 3)
-        rows.append(row)
-        if not args.json:
-            print(f"{name:42s} {ms:9.4f} ms  {row['gbs']:8.1f} GB/s ({row['frac_hbm']:.2f} of HBM)"
-                  + (f"  {row['f32_tflops']:6.1f} f32-TF/s, tf32 pipe {row['frac_tf32']:.2f}" if flops else ""),
-                  flush=True)
+    rows, peaks = run(args.only, args.reps, verbose=not args.json)
     if args.json:
-        print(json.dumps({"peaks": {"hbm_gbs": hbm, "tf32_tflops": tf32, "source": src}, "ops": rows}))
+        print(json.dumps({"peaks": peaks, "ops": rows}))
 
 
 if __name__ == "__main__":

@@ -21,21 +21,24 @@ def batches(cfg, n, seed=7):
 
 def check_params(pg, po, lr):
     """Parameters after several AdamW steps.  Adam moves an element by about
-    lr * g / (|g| + eps); an element whose gradient cancels to within eps of zero
-    takes a step that rounding can change by a sizeable fraction of lr, so the
-    bound is stated in steps: no element off by more than a quarter step, and
-    each tensor within 1e-4 normwise.  Gradients are checked directly (and
-    tightly) in test_gradients_match_oracle."""
+    lr * g / (|g| + eps); an element whose gradient cancels to within rounding of
+    zero takes a step of up to ~lr in either direction, and in a model with
+    millions of elements a few always do.  So: each tensor within 1e-4 normwise,
+    at most 1e-4 of the elements off by more than a quarter step, none by more
+    than two steps.  Gradients themselves are checked tightly in
+    test_gradients_match_oracle."""
     for i, (a, b) in enumerate(zip(pg, po)):
-        d = a.ravel().astype(np.float64) - b
-        assert np.max(np.abs(d)) < 0.25 * lr, (i, np.max(np.abs(d)))
+        d = np.abs(a.ravel().astype(np.float64) - b)
         assert np.linalg.norm(d) / np.linalg.norm(b) < 1e-4, (i, np.linalg.norm(d) / np.linalg.norm(b))
+        assert np.mean(d > 0.25 * lr) <= 1e-4, (i, np.mean(d > 0.25 * lr))
+        assert d.max() < 2 * lr, (i, d.max())
 
 
-def run_pair(M, orc, cfg, steps, mode, lr=3e-4, tied=False, **kw):
+def run_pair(M, orc, cfg, steps, mode, lr=3e-4, tied=False, use_graph=0, **opt):
+    """opt: optimizer / init settings (beta1, beta2, eps, wd, ...) given to both sides."""
     orc.set_threads(os.cpu_count())
-    g = M.GPT(**cfg, tied=tied, lr=lr, mode=mode, **kw)
-    o = orc.Gpt(**cfg, tied=tied, lr=lr)
+    g = M.GPT(**cfg, tied=tied, lr=lr, mode=mode, use_graph=use_graph, **opt)
+    o = orc.Gpt(**cfg, tied=tied, lr=lr, **opt)
     init_g = g.params()
     init_o = o.params()
     for a, b in zip(init_g, init_o):
@@ -59,7 +62,8 @@ def test_tape_mode_matches_oracle(M, orc, tied):
 
 
 def test_tape_mode_c3_loss_curve(M, orc):
-    steps = int(os.environ.get("MALUS_C3_STEPS", "20"))
+    # 200 steps: the loss-curve bar (<= 0.5 % per step over 200 steps)
+    steps = int(os.environ.get("MALUS_C3_STEPS", "200"))
     lg, lo, _, _ = run_pair(M, orc, C3, steps, mode=0, lr=3e-4)
     assert np.max(np.abs(lg - lo) / lo) < 5e-3, (lg, lo)
 
@@ -82,9 +86,21 @@ def test_fused_mode_matches_oracle(M, orc, tied):
 
 
 def test_fused_mode_c3_loss_curve(M, orc):
-    steps = int(os.environ.get("MALUS_C3_STEPS", "20"))
-    lg, lo, _, _ = run_pair(M, orc, C3, steps, mode=1, lr=3e-4)
+    steps = int(os.environ.get("MALUS_C3_STEPS", "200"))
+    lg, lo, _, _ = run_pair(M, orc, C3, steps, mode=1, lr=3e-4, use_graph=1)
     assert np.max(np.abs(lg - lo) / lo) < 5e-3, (lg, lo)
+    assert lg[-1] < lg[0]                       # it trains
+
+
+def test_fused_graph_c4_architecture(M, orc):
+    """The bench's architecture (V65 L6 H6 C384 T256) through the fused step as a
+    CUDA graph, at batch 2 so the CPU oracle finishes in seconds."""
+    cfg = dict(vocab=65, n_layer=6, n_head=6, n_embd=384, block_size=256, batch=2)
+    steps = int(os.environ.get("MALUS_C4_STEPS", "5"))
+    lg, lo, pg, po = run_pair(M, orc, cfg, steps, mode=1, lr=1e-3, use_graph=1, wd=0.01, beta2=0.99)
+    assert abs(lg[0] - lo[0]) / lo[0] < 1e-5, (lg, lo)
+    assert np.max(np.abs(lg - lo) / lo) < 5e-3, (lg, lo)
+    check_params(pg, po, lr=1e-3)
 
 
 def test_fused_and_tape_modes_agree(M):
