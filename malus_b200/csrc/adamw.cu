@@ -66,7 +66,58 @@ __global__ void k_adamw(SegTable t, int nseg, int64_t total4, float lr, float b1
   }
 }
 
+__device__ __forceinline__ float tf32_rn(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// One flat buffer (n a multiple of 4, 16-byte aligned): float4 loads and
+// stores; optionally also the tf32 hi/lo planes of the updated parameters (the
+// GEMM operands of the next step), so no separate split pass is needed.
+__global__ void k_adamw_flat(float* __restrict__ p, const float* __restrict__ g,
+                             float* __restrict__ m, float* __restrict__ v, int64_t n4, float lr,
+                             float b1, float b2, float eps, float wd, float c1, float c2, float gs,
+                             const float* __restrict__ bc_tab, const int64_t* __restrict__ step_dev,
+                             float* __restrict__ hi, float* __restrict__ lo) {
+  const int64_t st = *step_dev;
+  const float bc1 = bc_tab[2 * (st - 1)], bc2 = bc_tab[2 * (st - 1) + 1];
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < n4;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    float4 pp = reinterpret_cast<float4*>(p)[q];
+    const float4 gg = reinterpret_cast<const float4*>(g)[q];
+    float4 mm = reinterpret_cast<float4*>(m)[q];
+    float4 vv = reinterpret_cast<float4*>(v)[q];
+    adam_one(pp.x, gg.x, mm.x, vv.x, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+    adam_one(pp.y, gg.y, mm.y, vv.y, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+    adam_one(pp.z, gg.z, mm.z, vv.z, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+    adam_one(pp.w, gg.w, mm.w, vv.w, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+    reinterpret_cast<float4*>(p)[q] = pp;
+    reinterpret_cast<float4*>(m)[q] = mm;
+    reinterpret_cast<float4*>(v)[q] = vv;
+    if (hi) {
+      const float4 h = make_float4(tf32_rn(pp.x), tf32_rn(pp.y), tf32_rn(pp.z), tf32_rn(pp.w));
+      reinterpret_cast<float4*>(hi)[q] = h;
+      reinterpret_cast<float4*>(lo)[q] = make_float4(tf32_rn(pp.x - h.x), tf32_rn(pp.y - h.y),
+                                                     tf32_rn(pp.z - h.z), tf32_rn(pp.w - h.w));
+    }
+  }
+}
+
 }  // namespace
+
+void adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1,
+                float b2, float eps, float wd, float grad_scale, const float* bc_tab,
+                const int64_t* step_dev, float* hi, float* lo) {
+  if (n % 4 || ((uintptr_t)p | (uintptr_t)g | (uintptr_t)m | (uintptr_t)v) & 15 ||
+      (hi && (((uintptr_t)hi | (uintptr_t)lo) & 15)))
+    panic("adamw_flat: buffers must be 16-byte aligned with a multiple of 4 elements");
+  const float c1 = 1.0f - b1, c2 = 1.0f - b2;
+  k_adamw_flat<<<grid_for((size_t)n / 4, 256), 256, 0, stream()>>>(
+      p, g, m, v, n / 4, lr, b1, b2, eps, wd, c1, c2, grad_scale, bc_tab, step_dev, hi, lo);
+  count_launch();
+  after_launch("k_adamw_flat");
+}
 
 void adamw_multi(const AdamSeg* segs, int nseg, float lr, float b1, float b2, float eps, float wd,
                  float bc1, float bc2, float grad_scale) {

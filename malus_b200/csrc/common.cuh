@@ -209,6 +209,9 @@ void gemm_force_backend(int b);            // -1 = auto (tests)
 
 // ---- optimizer (adamw.cu) ----
 struct AdamSeg { float* p; const float* g; float* m; float* v; int64_t n; };
+void adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1,
+                float b2, float eps, float wd, float grad_scale, const float* bc_tab,
+                const int64_t* step_dev, float* hi, float* lo);
 void adamw_multi_tab(const AdamSeg* segs, int nseg, float lr, float b1, float b2, float eps,
                      float wd, float bc1, float bc2, float grad_scale, const float* bc_tab,
                      const int64_t* step_dev);

@@ -74,40 +74,60 @@ __global__ void k_embed2(const float* __restrict__ wte, const float* __restrict_
   }
 }
 
+__device__ __forceinline__ float4 f4(const float* p, int i4) { return reinterpret_cast<const float4*>(p)[i4]; }
+__device__ __forceinline__ void split_store4(float* hi, float* lo, size_t o4, float4 v) {
+  const float4 h = make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
+  reinterpret_cast<float4*>(hi)[o4] = h;
+  reinterpret_cast<float4*>(lo)[o4] = make_float4(tf32_rn(v.x - h.x), tf32_rn(v.y - h.y),
+                                                  tf32_rn(v.z - h.z), tf32_rn(v.w - h.w));
+}
+
 // Layernorm (no affine, population variance, eps) times gain, written as tf32
-// planes; saves per-row mean and variance.  One warp per row, row in registers.
-template <int PER>
+// planes; saves per-row mean and variance.  One warp per row, the row in
+// registers as float4 groups (lane l owns groups l + 32k; C % 4 == 0).
+template <int P4>
 __global__ void k_ln_fwd_split(const float* __restrict__ x, const float* __restrict__ g,
                                float* __restrict__ out_hi, float* __restrict__ out_lo,
                                float* __restrict__ mean_out, float* __restrict__ var_out, int M,
                                int C) {
-  int lane = threadIdx.x & 31;
-  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int nw = (gridDim.x * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int C4 = C >> 2;
+  float4 gk[P4];
+#pragma unroll
+  for (int k = 0; k < P4; ++k) {
+    const int i4 = lane + 32 * k;
+    gk[k] = i4 < C4 ? f4(g, i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   for (int r = warp; r < M; r += nw) {
     const float* xr = x + (size_t)r * C;
-    float v[PER];
+    float4 v[P4];
     float s = 0.0f;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int i = lane + 32 * k;
-      v[k] = i < C ? xr[i] : 0.0f;
-      s += v[k];
+    for (int k = 0; k < P4; ++k) {
+      const int i4 = lane + 32 * k;
+      v[k] = i4 < C4 ? f4(xr, i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
     }
-    float mean = wsum(s) / (float)C;
+    const float mean = wsum(s) / (float)C;
     float q = 0.0f;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int i = lane + 32 * k;
-      float d = i < C ? v[k] - mean : 0.0f;
-      q += d * d;
+    for (int k = 0; k < P4; ++k) {
+      if (lane + 32 * k < C4) {
+        const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
+        q += (a * a + b * b) + (c * c + d * d);
+      }
     }
-    float var = wsum(q) / (float)C;
-    float sigma = sqrtf(var + kEps);
+    const float var = wsum(q) / (float)C;
+    const float sigma = sqrtf(var + kEps);
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int i = lane + 32 * k;
-      if (i < C) split_store(out_hi, out_lo, (size_t)r * C + i, ((v[k] - mean) / sigma) * g[i]);
+    for (int k = 0; k < P4; ++k) {
+      const int i4 = lane + 32 * k;
+      if (i4 < C4)
+        split_store4(out_hi, out_lo, (size_t)r * C4 + i4,
+                     make_float4(((v[k].x - mean) / sigma) * gk[k].x, ((v[k].y - mean) / sigma) * gk[k].y,
+                                 ((v[k].z - mean) / sigma) * gk[k].z, ((v[k].w - mean) / sigma) * gk[k].w));
     }
     if (lane == 0) {
       mean_out[r] = mean;
@@ -119,9 +139,10 @@ __global__ void k_ln_fwd_split(const float* __restrict__ x, const float* __restr
 // Layernorm backward through the gain, plus the residual stream:
 //   dy = dz * g ; y = (x - mean)/sigma ; dx = ((dy - mean(dy)) - y*mean(dy*y)) / sqrt(var+eps)
 //   gout = resid + dx (f32 and optional tf32 planes); gain partials part[blk][c] = sum dz*y.
-// One warp per row; lane l owns columns l + 32k, so each lane keeps its gain
-// partials in registers across rows; all of a row's loads are issued before use.
-template <int PER>
+// One warp per row as float4 groups; lane l owns groups l + 32k, so each lane
+// keeps its gain partials in registers across rows; a row's loads are issued
+// before use.
+template <int P4>
 __global__ void k_ln_bwd_fused(const float* __restrict__ x, const float* __restrict__ mean_in,
                                const float* __restrict__ var_in, const float* __restrict__ g,
                                const float* __restrict__ dz, const float* __restrict__ resid,
@@ -133,53 +154,61 @@ __global__ void k_ln_bwd_fused(const float* __restrict__ x, const float* __restr
   const int nwb = blockDim.x >> 5;
   const int warp = blockIdx.x * nwb + wib;
   const int nw = gridDim.x * nwb;
-  float gk[PER], gacc[PER];
+  const int C4 = C >> 2;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 gk[P4], gacc[P4];
 #pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    int i = lane + 32 * k;
-    gk[k] = i < C ? g[i] : 0.0f;
-    gacc[k] = 0.0f;
+  for (int k = 0; k < P4; ++k) {
+    const int i4 = lane + 32 * k;
+    gk[k] = i4 < C4 ? f4(g, i4) : z4;
+    gacc[k] = z4;
   }
   for (int r = warp; r < M; r += nw) {
-    const size_t ro = (size_t)r * C;
-    float xv[PER], dv[PER], rv[PER];
+    const size_t ro4 = (size_t)r * C4;
+    float4 xv[P4], dv[P4], rv[P4];
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int i = lane + 32 * k;
-      xv[k] = i < C ? x[ro + i] : 0.0f;
-      dv[k] = i < C ? dz[ro + i] : 0.0f;
-      rv[k] = (resid && i < C) ? resid[ro + i] : 0.0f;
+    for (int k = 0; k < P4; ++k) {
+      const int i4 = lane + 32 * k;
+      const bool in = i4 < C4;
+      xv[k] = in ? f4(x, ro4 + i4) : z4;
+      dv[k] = in ? f4(dz, ro4 + i4) : z4;
+      rv[k] = (resid && in) ? f4(resid, ro4 + i4) : z4;
     }
     const float mean = mean_in[r], var = var_in[r];
     const float sigma = sqrtf(var + kEps);
     const float inv = 1.0f / sigma;
     float sg = 0.0f, sgy = 0.0f;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int i = lane + 32 * k;
-      float y = i < C ? (xv[k] - mean) / sigma : 0.0f;
-      gacc[k] += dv[k] * y;
-      xv[k] = y;                  // y from here on
-      dv[k] = dv[k] * gk[k];      // dy from here on
-      sg += dv[k];
-      sgy += dv[k] * y;
+    for (int k = 0; k < P4; ++k) {
+      if (lane + 32 * k < C4) {
+        float4 y = make_float4((xv[k].x - mean) / sigma, (xv[k].y - mean) / sigma,
+                               (xv[k].z - mean) / sigma, (xv[k].w - mean) / sigma);
+        gacc[k].x += dv[k].x * y.x; gacc[k].y += dv[k].y * y.y;
+        gacc[k].z += dv[k].z * y.z; gacc[k].w += dv[k].w * y.w;
+        xv[k] = y;                                             // y from here on
+        dv[k] = make_float4(dv[k].x * gk[k].x, dv[k].y * gk[k].y, dv[k].z * gk[k].z,
+                            dv[k].w * gk[k].w);                // dy from here on
+        sg += (dv[k].x + dv[k].y) + (dv[k].z + dv[k].w);
+        sgy += (dv[k].x * y.x + dv[k].y * y.y) + (dv[k].z * y.z + dv[k].w * y.w);
+      }
     }
     const float mg = wsum(sg) / (float)C, mgy = wsum(sgy) / (float)C;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int i = lane + 32 * k;
-      if (i < C) {
-        float v = ((dv[k] - mg) - xv[k] * mgy) * inv;
-        if (resid) v = rv[k] + v;
-        gout[ro + i] = v;
-        if (gout_hi) split_store(gout_hi, gout_lo, ro + i, v);
+    for (int k = 0; k < P4; ++k) {
+      const int i4 = lane + 32 * k;
+      if (i4 < C4) {
+        float4 o = make_float4(((dv[k].x - mg) - xv[k].x * mgy) * inv, ((dv[k].y - mg) - xv[k].y * mgy) * inv,
+                               ((dv[k].z - mg) - xv[k].z * mgy) * inv, ((dv[k].w - mg) - xv[k].w * mgy) * inv);
+        if (resid) o = make_float4(rv[k].x + o.x, rv[k].y + o.y, rv[k].z + o.z, rv[k].w + o.w);
+        reinterpret_cast<float4*>(gout)[ro4 + i4] = o;
+        if (gout_hi) split_store4(gout_hi, gout_lo, ro4 + i4, o);
       }
     }
   }
 #pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    int i = lane + 32 * k;
-    if (i < C) sacc[(size_t)wib * C + i] = gacc[k];
+  for (int k = 0; k < P4; ++k) {
+    const int i4 = lane + 32 * k;
+    if (i4 < C4) reinterpret_cast<float4*>(sacc + (size_t)wib * C)[i4] = gacc[k];
   }
   __syncthreads();
   // block partial = sum over its warps (fixed order)
@@ -212,72 +241,97 @@ __global__ void k_colsum(const float* __restrict__ part, float* __restrict__ out
 }
 
 // Causal softmax of one row of S (already scaled): P planes.  -1e9 above the
-// diagonal as the reference's additive mask (metal.rs:1601-1612).
-template <int PER>
+// diagonal as the reference's additive mask (metal.rs:1601-1612).  One warp per
+// row as float4 groups (T % 4 == 0); only the groups that reach the diagonal
+// are read (the causal S GEMM does not compute the rest).
+template <int P4>
 __global__ void k_softmax_causal_split(const float* __restrict__ S, float* __restrict__ p_hi,
                                        float* __restrict__ p_lo, int rows, int T) {
-  int lane = threadIdx.x & 31;
-  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int nw = (gridDim.x * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int T4 = T >> 2;
   for (int r = warp; r < rows; r += nw) {
-    int i = r % T;
+    const int i = r % T;
     const float* sr = S + (size_t)r * T;
-    float v[PER];
+    float4 v[P4];
     float m = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int j = lane + 32 * k;
-      // masked scores (j > i; not computed by the causal S GEMM) would be
-      // s - 1e9, whose exp underflows to exactly 0: -inf gives the same 0
-      v[k] = j <= i ? sr[j] : -INFINITY;
-      m = fmaxf(m, v[k]);
+    for (int k = 0; k < P4; ++k) {
+      const int j4 = lane + 32 * k, j = 4 * j4;
+      // masked scores (j > i) would be s - 1e9, whose exp underflows to exactly
+      // 0: -inf gives the same 0
+      if (j4 < T4 && j <= i) {
+        float4 t = f4(sr, j4);
+        v[k] = make_float4(t.x, j + 1 <= i ? t.y : -INFINITY, j + 2 <= i ? t.z : -INFINITY,
+                           j + 3 <= i ? t.w : -INFINITY);
+      } else {
+        v[k] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      }
+      m = fmaxf(m, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
     }
     m = wmax(m);
     float s = 0.0f;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int j = lane + 32 * k;
-      v[k] = j <= i ? expf(v[k] - m) : 0.0f;
-      s += v[k];
+    for (int k = 0; k < P4; ++k) {
+      const int j = 4 * (lane + 32 * k);
+      v[k] = make_float4(j <= i ? expf(v[k].x - m) : 0.0f, j + 1 <= i ? expf(v[k].y - m) : 0.0f,
+                         j + 2 <= i ? expf(v[k].z - m) : 0.0f, j + 3 <= i ? expf(v[k].w - m) : 0.0f);
+      s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
     }
     s = wsum(s);
     // keys past the query's 128-wide tile are never read by the causal GEMMs
-    const int jend = min(T, (i / 128 + 1) * 128);
+    const int jend4 = min(T, (i / 128 + 1) * 128) >> 2;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int j = lane + 32 * k;
-      if (j < jend) split_store(p_hi, p_lo, (size_t)r * T + j, v[k] / s);
+    for (int k = 0; k < P4; ++k) {
+      const int j4 = lane + 32 * k;
+      if (j4 < jend4)
+        split_store4(p_hi, p_lo, (size_t)r * T4 + j4,
+                     make_float4(v[k].x / s, v[k].y / s, v[k].z / s, v[k].w / s));
     }
   }
 }
 
 // dS = scale * P * (dP - sum_j dP*P) as planes (softmax VJP, transformer_bwd.ml:15-20,
-// then the scores = qk * scale VJP).
-template <int PER>
+// then the scores = qk * scale VJP).  dP above the diagonal is not computed and
+// P is 0 there, so neither is read.
+template <int P4>
 __global__ void k_softmax_bwd_split(const float* __restrict__ p_hi, const float* __restrict__ p_lo,
                                     const float* __restrict__ dP, float* __restrict__ ds_hi,
                                     float* __restrict__ ds_lo, int rows, int T, float scale) {
-  int lane = threadIdx.x & 31;
-  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int nw = (gridDim.x * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int T4 = T >> 2;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int r = warp; r < rows; r += nw) {
-    size_t base = (size_t)r * T;
-    const int i = r % T;          // dP above the diagonal is not computed; P is 0 there
-    float pv[PER], gv[PER];
+    const size_t b4 = (size_t)r * T4;
+    const int i = r % T;
+    float4 pv[P4], gv[P4];
     float dot = 0.0f;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int j = lane + 32 * k;
-      pv[k] = j <= i ? p_hi[base + j] + p_lo[base + j] : 0.0f;
-      gv[k] = j <= i ? dP[base + j] : 0.0f;
-      dot += gv[k] * pv[k];
+    for (int k = 0; k < P4; ++k) {
+      const int j4 = lane + 32 * k, j = 4 * j4;
+      if (j4 < T4 && j <= i) {
+        const float4 h = f4(p_hi, b4 + j4), l = f4(p_lo, b4 + j4), d = f4(dP, b4 + j4);
+        pv[k] = make_float4(h.x + l.x, j + 1 <= i ? h.y + l.y : 0.0f, j + 2 <= i ? h.z + l.z : 0.0f,
+                            j + 3 <= i ? h.w + l.w : 0.0f);
+        gv[k] = make_float4(d.x, j + 1 <= i ? d.y : 0.0f, j + 2 <= i ? d.z : 0.0f, j + 3 <= i ? d.w : 0.0f);
+      } else {
+        pv[k] = z4;
+        gv[k] = z4;
+      }
+      dot += (gv[k].x * pv[k].x + gv[k].y * pv[k].y) + (gv[k].z * pv[k].z + gv[k].w * pv[k].w);
     }
     dot = wsum(dot);
-    const int jend = min(T, (i / 128 + 1) * 128);   // as in the forward: later tiles are never read
+    const int jend4 = min(T, (i / 128 + 1) * 128) >> 2;   // as in the forward: later tiles are never read
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      int j = lane + 32 * k;
-      if (j < jend) split_store(ds_hi, ds_lo, base + j, (pv[k] * (gv[k] - dot)) * scale);
+    for (int k = 0; k < P4; ++k) {
+      const int j4 = lane + 32 * k;
+      if (j4 < jend4)
+        split_store4(ds_hi, ds_lo, b4 + j4,
+                     make_float4((pv[k].x * (gv[k].x - dot)) * scale, (pv[k].y * (gv[k].y - dot)) * scale,
+                                 (pv[k].z * (gv[k].z - dot)) * scale, (pv[k].w * (gv[k].w - dot)) * scale));
     }
   }
 }
@@ -448,6 +502,19 @@ void gemm(int M, int N, int K, int batch, const TcOperand& a, const TcOperand& b
 
 unsigned rows_grid(int rows) { return grid_for((size_t)rows * 32, 256); }
 
+// float4 groups per lane for a row of LEN floats (LEN % 4 == 0, LEN <= 1024)
+#define P4_DISPATCH(LEN, CALL)                                        \
+  do {                                                                \
+    const int l4_ = (LEN) / 4;                                        \
+    if (l4_ <= 32) { constexpr int P_ = 1; CALL; }                    \
+    else if (l4_ <= 64) { constexpr int P_ = 2; CALL; }               \
+    else if (l4_ <= 96) { constexpr int P_ = 3; CALL; }               \
+    else if (l4_ <= 128) { constexpr int P_ = 4; CALL; }              \
+    else if (l4_ <= 192) { constexpr int P_ = 6; CALL; }              \
+    else if (l4_ <= 256) { constexpr int P_ = 8; CALL; }              \
+    else panic("fused step: row length %d exceeds 1024", (int)(LEN)); \
+  } while (0)
+
 #define PER_DISPATCH(LEN, CALL)                      \
   do {                                               \
     if ((LEN) <= 32) { constexpr int P_ = 1; CALL; } \
@@ -459,7 +526,7 @@ unsigned rows_grid(int rows) { return grid_for((size_t)rows * 32, 256); }
   } while (0)
 
 void ln_fwd(FusedStep* f, const float* x, const float* g, Planes out, float* mean, float* var) {
-  PER_DISPATCH(f->C, (k_ln_fwd_split<P_><<<rows_grid(f->M), 256, 0, stream()>>>(
+  P4_DISPATCH(f->C, (k_ln_fwd_split<P_><<<rows_grid(f->M), 256, 0, stream()>>>(
                           x, g, out.hi, out.lo, mean, var, f->M, f->C)));
   count_launch();
   after_launch("k_ln_fwd_split");
@@ -469,7 +536,7 @@ void ln_bwd(FusedStep* f, const float* x, const float* mean, const float* var, c
             const float* dz, const float* resid, float* gout, Planes gpl, float* dgain) {
   int threads = 256;
   size_t smem = (size_t)(threads / 32) * f->C * sizeof(float);
-  PER_DISPATCH(f->C, (k_ln_bwd_fused<P_><<<f->part_blocks, threads, smem, stream()>>>(
+  P4_DISPATCH(f->C, (k_ln_bwd_fused<P_><<<f->part_blocks, threads, smem, stream()>>>(
                           x, mean, var, g, dz, resid, gout, gpl.hi, gpl.lo, f->part, f->M, f->C)));
   k_colsum<<<(f->C + 31) / 32, 256, 0, stream()>>>(f->part, dgain, f->part_blocks, f->C);
   count_launch(2);
@@ -534,7 +601,7 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
   f->M = f->B * f->T; f->hs = f->C / f->H; f->C4 = 4 * f->C; f->BH = f->B * f->H;
   f->Vp = (f->V + 3) & ~3;
   f->scale = 1.0f / sqrtf((float)f->hs);
-  if (f->C % 32 || f->hs % 4 || f->T > 1024 || f->C > 1024 || f->Vp > 1024)
+  if (f->C % 32 || f->hs % 4 || f->T % 4 || f->T > 1024 || f->C > 1024 || f->Vp > 1024)
     panic("fused step needs n_embd %% 32 == 0, head size %% 4 == 0, T, C, vocab <= 1024 "
           "(got C=%d hs=%d T=%d V=%d)", f->C, f->hs, f->T, f->V);
   f->params = params;
@@ -587,8 +654,7 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
   MALUS_CUDA(cudaMalloc(&f->step_dev, sizeof(int64_t)));
   MALUS_CUDA(cudaMemset(f->step_dev, 0, sizeof(int64_t)));
   fill_bc_table(f, 1 << 16);
-  MALUS_CUDA(cudaFuncSetAttribute(k_ln_bwd_fused<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024));
-  MALUS_CUDA(cudaFuncSetAttribute(k_ln_bwd_fused<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024));
+
   split_weights(f);
   return f;
 }
@@ -631,7 +697,7 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
          op(f->qkv[l], T, hs, hs, false, BH, (int64_t)T * hs, kZBatch, 0, MC), kEpiStore,
          L(0, 0, 0, 0, (int64_t)TT), L(0, 0, 0, 0, T), unit, f->S, Planes{}, nullptr, f->scale,
          kCausalOut);
-    PER_DISPATCH(T, (k_softmax_causal_split<P_><<<rows_grid(BH * T), 256, 0, stream()>>>(
+    P4_DISPATCH(T, (k_softmax_causal_split<P_><<<rows_grid(BH * T), 256, 0, stream()>>>(
                         f->S, f->P[l].hi, f->P[l].lo, BH * T, T)));
     count_launch();
     after_launch("k_softmax_causal_split");
@@ -707,7 +773,7 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     gemm(T, hs, T, BH, op(f->P[l], T, T, T, true, BH, (int64_t)TT, kZBatch),
          op(f->dO, T, hs, hs, true, BH, (int64_t)T * hs, kZBatch), kEpiStore,
          L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, dqkv2, nullptr, 1.0f, kCausalAUpper);
-    PER_DISPATCH(T, (k_softmax_bwd_split<P_><<<rows_grid(BH * T), 256, 0, stream()>>>(
+    P4_DISPATCH(T, (k_softmax_bwd_split<P_><<<rows_grid(BH * T), 256, 0, stream()>>>(
                         f->P[l].hi, f->P[l].lo, f->dP, f->dS.hi, f->dS.lo, BH * T, T, f->scale)));
     count_launch();
     after_launch("k_softmax_bwd_split");
@@ -768,10 +834,15 @@ void fused_body(FusedStep* f, const int32_t* x, const int32_t* y, float* loss) {
   after_launch("k_step_inc");
   fused_step(f, x, y, loss);
   float gscale = dp_world() > 1 ? 1.0f / (float)dp_world() : 1.0f;
-  AdamSeg seg{f->pbuf, f->gbuf, f->mbuf, f->vbuf, (int64_t)f->total};
-  adamw_multi_tab(&seg, 1, f->cfg.lr, f->cfg.beta1, f->cfg.beta2, f->cfg.eps, f->cfg.wd, 0.0f, 0.0f,
-                  gscale, f->bc_tab, f->step_dev);
-  fused_after_update(f);
+  // AdamW over the whole fused buffer, writing the tf32 planes of every updated
+  // parameter (the weight planes share the parameter layout); only the padded
+  // untied LM head is re-split separately
+  adamw_flat(f->pbuf, f->gbuf, f->mbuf, f->vbuf, (int64_t)f->total, f->cfg.lr, f->cfg.beta1,
+             f->cfg.beta2, f->cfg.eps, f->cfg.wd, gscale, f->bc_tab, f->step_dev, f->wpl.hi, f->wpl.lo);
+  if (!f->cfg.tied) {
+    size_t top = (size_t)f->L * 8;
+    tf32_split(f->params[top + 3], f->C, f->V, f->V, 1, 0, f->lmpl.hi, f->lmpl.lo, f->Vp);
+  }
 }
 
 }  // namespace
