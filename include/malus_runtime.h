@@ -268,6 +268,15 @@ int32_t malus_dp_init(int32_t rank, int32_t world, const uint8_t* nccl_id, int32
 int32_t malus_dp_allreduce_f32(void* dev_ptr, size_t count);
 int32_t malus_dp_finish(void);   /* wait for outstanding collectives */
 int32_t malus_dp_destroy(void);
+/* User kernel bodies.  malus_runtime_init accepts, for any id, either a native
+ * kernel name or the MSL text that malus-codegen-gpu emits for a `kernel`
+ * (crates/malus-codegen-gpu/src/lib.rs:432-1006; the reference's runtime_init
+ * takes exactly that id -> MSL map, crates/malus-runtime/src/metal.rs:300-336);
+ * the text is translated to CUDA C++ and compiled with NVRTC for sm_100a, once
+ * per distinct source.  Host-only helpers: the translation itself (returns its
+ * length, or -1 with the reason in out) and a compile check (0 = compiled). */
+int32_t malus_jit_translate(const char* msl, char* out, size_t cap);
+int32_t malus_jit_compile_check(const char* msl, char* log, size_t cap);
 /* Abort the communicator without contacting peers (after one is known lost). */
 int32_t malus_dp_abort(void);
 int32_t malus_dp_world(void);

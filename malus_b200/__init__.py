@@ -179,6 +179,8 @@ SIGNATURES: dict[str, tuple] = {
     "malus_dp_allreduce_f32": (i32, [vp, sz]),
     "malus_dp_finish": (i32, []),
     "malus_dp_destroy": (i32, []),
+    "malus_jit_translate": (i32, [C.c_char_p, C.c_char_p, sz]),
+    "malus_jit_compile_check": (i32, [C.c_char_p, C.c_char_p, sz]),
     "malus_dp_abort": (i32, []),
     "malus_dp_world": (i32, []),
     "malus_gpt_create": (i64, [C.POINTER(GptConfig)]),

@@ -86,7 +86,9 @@ def build(verbose: bool = False) -> Path:
             nccl = [f"-L{NCCL / 'lib'}", "-l:libnccl.so.2", "-Xlinker", f"-rpath={NCCL / 'lib'}"]
         else:
             nccl = ["-lnccl"]
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), *nccl]
+        cuda_lib = Path(NVCC).resolve().parent.parent / "lib64"
+        nvrtc = [f"-L{cuda_lib}", "-lnvrtc", "-Xlinker", f"-rpath={cuda_lib}"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), *nccl, *nvrtc]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -11,8 +11,9 @@
 //    function supplies them (uniforms are 4-byte f32/i32 in declaration
 //    order, codegen-cpu lib.rs:2261-2297);
 //  * the XOR example's user kernel "sigmoid_backward" (examples/xor.ml:1-2).
-// Arbitrary user kernel bodies need the CUDA emitter + NVRTC path, which is
-// not part of this runtime.
+// A source text (containing `kernel void`) instead of a name is a user kernel
+// body as codegen-gpu emits it: nvrtc.cu translates it to CUDA C++ and compiles
+// it with NVRTC for sm_100a.
 #include "common.cuh"
 
 #include <mutex>
@@ -21,6 +22,12 @@
 
 namespace malus {
 void binary_project_into_a(int op, int64_t ha, int64_t hb, float* out);
+struct JitKernel;
+bool looks_like_msl(const char* s);
+JitKernel* jit_compile(const std::string& msl);
+void jit_dispatch_implicit(JitKernel* k, const int64_t* h, size_t count, int64_t out);
+void jit_dispatch_explicit(JitKernel* k, const int64_t* h, size_t hc, const size_t* grid, const size_t* tg,
+                           int64_t out, const void* u, size_t ub);
 }
 using namespace malus;
 
@@ -71,6 +78,13 @@ const std::unordered_map<std::string, int>& names() {
 
 std::mutex g_reg_mu;
 std::unordered_map<uint64_t, int> g_registry;
+std::unordered_map<uint64_t, JitKernel*> g_jit;   // ids bound to compiled user kernels
+
+JitKernel* jit_of(uint64_t id) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_jit.find(id);
+  return it == g_jit.end() ? nullptr : it->second;
+}
 
 int lookup(uint64_t id) {
   std::lock_guard<std::mutex> lk(g_reg_mu);
@@ -105,18 +119,30 @@ void groups_of(const size_t* grid, int32_t axis, int32_t inner, size_t* outer) {
 extern "C" {
 
 void malus_runtime_init(const uint64_t* ids, const char* const* nm, size_t n) {
-  std::lock_guard<std::mutex> lk(g_reg_mu);
   for (size_t i = 0; i < n; ++i) {
+    if (looks_like_msl(nm[i])) {           // a kernel body: translate + NVRTC
+      JitKernel* k = jit_compile(nm[i]);
+      std::lock_guard<std::mutex> lk(g_reg_mu);
+      g_jit[ids[i]] = k;
+      g_registry.erase(ids[i]);
+      continue;
+    }
+    std::lock_guard<std::mutex> lk(g_reg_mu);
     auto it = names().find(nm[i]);
-    if (it == names().end())
-      panic("runtime_init: no native kernel named '%s' (user kernel bodies need the NVRTC path)", nm[i]);
+    if (it == names().end()) panic("runtime_init: no native kernel named '%s'", nm[i]);
     g_registry[ids[i]] = it->second;
+    g_jit.erase(ids[i]);
   }
 }
 
 int64_t kernel_dispatch(uint64_t kernel_id, const int64_t* h, size_t count) {
-  int k = lookup(kernel_id);
   if (count == 0) panic("kernel_dispatch: no inputs");
+  if (JitKernel* jk = jit_of(kernel_id)) {
+    int64_t o = alloc_like(h[0]);
+    jit_dispatch_implicit(jk, h, count, o);
+    return o;
+  }
+  int k = lookup(kernel_id);
   int64_t out = alloc_like(h[0]);
   size_t n = tb(h[0])->len;
   auto need = [&](size_t c) { if (count < c) panic("kernel_dispatch: kernel needs %zu inputs", c); };
@@ -151,7 +177,8 @@ int64_t kernel_dispatch_v2(uint64_t kernel_id, const int64_t* h, size_t hc, cons
                            const size_t* tg, const size_t* out_shape, size_t out_ndim,
                            int32_t out_dtype, const void* u, size_t ub) {
   if (!grid || !tg) panic("kernel_dispatch_v2 grid/tg must not be null");
-  int k = lookup(kernel_id);
+  JitKernel* jk = jit_of(kernel_id);
+  int k = jk ? -1 : lookup(kernel_id);
   int64_t out;
   if (out_ndim == 0) {
     if (hc == 0) panic("kernel_dispatch_v2: out_ndim==0 but no tensor inputs");
@@ -159,6 +186,10 @@ int64_t kernel_dispatch_v2(uint64_t kernel_id, const int64_t* h, size_t hc, cons
     out = alloc(out_dtype >= 0 ? out_dtype : f->dtype, f->shape, f->ndim);
   } else {
     out = alloc(out_dtype, out_shape, (int)out_ndim);
+  }
+  if (jk) {
+    jit_dispatch_explicit(jk, h, hc, grid, tg, out, u, ub);
+    return out;
   }
   size_t on = tb(out)->len;
   if (on == 0) return out;

@@ -169,14 +169,20 @@ def test_refcounts_balance_over_backward(M, rt, rng):
     assert deltas[0] == deltas[1] == deltas[2] == 0
 
 
-def _register_xor_kernels(rt):
-    names = [b"sigmoid", b"malus_mul_scalar", b"sigmoid_backward"]
+def _register_xor_kernels(rt, msl=False):
+    if msl:     # the sources codegen-gpu emits, compiled by NVRTC
+        import msl_kernels as K
+        names = [K.SIGMOID.encode(), K.MUL_SCALAR.encode(), K.SIGMOID_BWD.encode()]
+    else:       # native kernels bound by name
+        names = [b"sigmoid", b"malus_mul_scalar", b"sigmoid_backward"]
     rt.malus_runtime_init((C.c_uint64 * 3)(900, 901, 902), (C.c_char_p * 3)(*names), 3)
 
 
-def test_xor_through_the_abi(M, rt, orc):
-    """examples/xor.ml, 10k full-batch SGD steps, every op a C-ABI call."""
-    _register_xor_kernels(rt)
+@pytest.mark.parametrize("msl", [False, True], ids=["native", "nvrtc"])
+def test_xor_through_the_abi(M, rt, orc, msl):
+    """examples/xor.ml, 10k full-batch SGD steps, every op a C-ABI call; the
+    three kernels bound natively or compiled from their MSL by NVRTC."""
+    _register_xor_kernels(rt, msl)
     L = rt
     f = lambda a: M.Tensor.from_numpy(np.asarray(a, np.float32))
     x = f([[0, 0], [0, 1], [1, 0], [1, 1]])
