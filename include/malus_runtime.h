@@ -277,6 +277,14 @@ int32_t malus_dp_destroy(void);
  * length, or -1 with the reason in out) and a compile check (0 = compiled). */
 int32_t malus_jit_translate(const char* msl, char* out, size_t cap);
 int32_t malus_jit_compile_check(const char* msl, char* log, size_t cap);
+/* Fused causal attention forward (tcgen05, 3xTF32): from the tf32 planes of
+ * q|k|v laid out [3][B][H][T][hs], writes P = causal_softmax(q k^T * scale) as
+ * planes [B*H][T][T] (keys up to each query's 128-wide tile) and O = P v as
+ * head-unfolded planes [B*T][H*hs].  Needs T % 128 == 0 and hs in {32, 64}
+ * (returns -1 otherwise).  New in this build; replaces the reference's
+ * bmm + scale + mask + softmax + bmm sequence of the attention block. */
+int32_t malus_attn_fwd(const float* qkv_hi, const float* qkv_lo, int32_t B, int32_t H, int32_t T,
+                       int32_t hs, float scale, float* p_hi, float* p_lo, float* o_hi, float* o_lo);
 /* Abort the communicator without contacting peers (after one is known lost). */
 int32_t malus_dp_abort(void);
 int32_t malus_dp_world(void);

@@ -18,6 +18,7 @@
 //    which is bit-identical to the reference's CPU loop
 //    (tensor_matmul_cpu, metal.rs:699-800).
 #include "common.cuh"
+#include "tc_common.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -131,6 +132,7 @@ void gemm_simt(const GemmArgs& g) {
 // residual add, GELU (storing the pre-activation), the GELU derivative, and
 // the tf32 split of its own output (so the next GEMM reads ready planes).
 namespace {
+using namespace malus::tc;
 
 constexpr int BM = 128, BK = 32;
 constexpr int kTileBytesA = BM * BK * 4;  // 16 KB
@@ -157,117 +159,9 @@ __host__ __device__ constexpr int epi_warps(int epi) { return epi == 0 ? 4 : 8; 
 // tf32 planes, go through the transposing smem stage (coalesced loads and
 // stores); a plain f32 store writes each lane's row directly.
 __host__ __device__ constexpr int threads_tc(int epi) { return 64 + 32 * epi_warps(epi); }
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on every wait
 constexpr float kGeluC0 = 0.7978845608028654f, kGeluC1 = 0.044715f;
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ uint64_t gtimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count));
-}
-__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(a), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait. Returns false (and records `code`) when the bound runs out
-// or another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int* abort_flag,
-                                          int32_t* err, int code) {
-  if (mbar_try(a, parity)) return true;
-  uint64_t t0 = gtimer();
-  while (true) {
-    if (mbar_try(a, parity)) return true;
-    if (*abort_flag) return false;
-    if (gtimer() - t0 > kWaitNs) {
-      *abort_flag = 1;
-      atomicExch(err, code);
-      return false;
-    }
-  }
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t a) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t mbar,
-                                            int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
-      ::"r"(dst), "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
 
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t mbar,
-                                            int c0, int c1, int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
-      ::"r"(dst), "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-
-// UMMA shared-memory descriptor (version 1).  Layout type 2 is the 128-byte
-// swizzle with 16-byte granules used for K-major tiles; layout type 1 is the
-// 128-byte swizzle with 32-byte granules (4-row atom) that 32-bit (tf32)
-// MN-major tiles require.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
-                                              uint32_t layout) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)layout << 61;
-  return d;
-}
-// K-major tile: rows of 128 B (32 tf32 along K), 8-row atoms 1 KB apart.
-__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int kk) {
-  return umma_desc(tile + kk * 32, 16, 1024, 2);
-}
-// MN-major tile: 32-element (128 B) MN chunks 4 KB apart (one TMA box each),
-// K rows 128 B apart in 4-row (512 B) atoms; one MMA consumes 8 K rows.
-__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int kk) {
-  return umma_desc(tile + kk * 1024, 4096, 512, 1);
-}
-
-// Instruction descriptor: f32 accumulate, tf32 A/B, M=128, N=n.
-__host__ __device__ constexpr uint32_t idesc_tf32(bool a_mn, bool b_mn, int n) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) |
-         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
-      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void mma_commit(uint32_t mbar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
-      : "memory");
-}
-
-__device__ __forceinline__ float tf32_rn(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
 
 // Indices (z < batch, m < M, n < N: all int) and radices fit 32 bits: 32-bit division.
 __device__ __forceinline__ int64_t lay(const TcLayout& L, int64_t idx) {
@@ -805,6 +699,26 @@ void load_encoder() {
     g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
   });
 }
+
+}  // namespace
+
+// Generic f32 tensor map (rank 2..5; strides in bytes for dims 1..rank-1).
+CUtensorMap encode_f32_map(int rank, const void* base, const uint64_t* dims, const uint64_t* strides,
+                           const uint32_t* box, int swizzle) {
+  load_encoder();
+  CUtensorMap m;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) { d[i] = dims[i]; b[i] = box[i]; es[i] = 1; }
+  for (int i = 0; i + 1 < rank; ++i) st[i] = strides[i];
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, (void*)base, d, st, b, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) panic("cuTensorMapEncodeTiled (rank %d) failed (%d)", rank, (int)r);
+  return m;
+}
+
+namespace {
 
 // 3-D f32 map {d0 (contiguous), d1, d2}, box {b0, b1, 1}, 128-B swizzle with
 // 16-byte granules (K-major tiles) or 32-byte granules (MN-major tiles).

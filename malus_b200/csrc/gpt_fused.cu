@@ -23,6 +23,9 @@
 namespace malus {
 
 int dp_allreduce_async(float* ptr, size_t count);
+bool attn_fwd_supported(int T, int hs);
+void attn_fwd(const float* qkv_hi, const float* qkv_lo, int B, int H, int T, int hs, float scale,
+              float* p_hi, float* p_lo, float* o_hi, float* o_lo);
 void dp_join();
 int dp_world();
 
@@ -692,6 +695,11 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
          op(W(b + 1), C, C, C, true, 3, (int64_t)C * C, kZMNSeg, C), kEpiStore, none,
          L(T, (int64_t)H * T * hs, 0, 0, hs), L(C, (int64_t)B * H * T * hs, hs, (int64_t)T * hs, 1),
          nullptr, f->qkv[l], nullptr);
+    if (attn_fwd_supported(T, hs)) {
+      // S, causal softmax and O = P V in one kernel (P planes kept for the backward)
+      attn_fwd(f->qkv[l].hi, f->qkv[l].lo, B, H, T, hs, f->scale, f->P[l].hi, f->P[l].lo, f->O[l].hi,
+               f->O[l].lo);
+    } else {
     // S = Q K^T * scale
     gemm(T, T, hs, BH, op(f->qkv[l], T, hs, hs, false, BH, (int64_t)T * hs, kZBatch),
          op(f->qkv[l], T, hs, hs, false, BH, (int64_t)T * hs, kZBatch, 0, MC), kEpiStore,
@@ -705,6 +713,7 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     gemm(T, hs, T, BH, op(f->P[l], T, T, T, false, BH, (int64_t)TT, kZBatch),
          op(f->qkv[l], T, hs, hs, true, BH, (int64_t)T * hs, kZBatch, 0, 2 * MC), kEpiStore,
          L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, f->O[l], nullptr, 1.0f, kCausalALower);
+    }
     // x2 = x + O Wo
     gemm(M, C, C, 1, op(f->O[l], M, C, C, false), op(W(b + 4), C, C, C, true), kEpiResid, none,
          rowC, unit, f->x2[l], Planes{}, f->x[l]);

@@ -212,6 +212,18 @@ def plane_cases(b: Bench, rng):
     ]
     for name, q, (Mm, N, K, batch, nout, aux) in cases_:
         yield name, (lambda q=q: run(q)), nbytes(q, Mm, N, K, batch, nout, aux), 2.0 * Mm * N * K * batch
+    # fused causal attention forward at the C4 shape: q|k|v planes in, P and O planes out
+    qh, ql = buf(3, Bz, H, T, hs), buf(3, Bz, H, T, hs)
+    ph, pl = buf(Bz * H, T, T, rand=False), buf(Bz * H, T, T, rand=False)
+    oh, ol = buf(Mt, Cc, rand=False), buf(Mt, Cc, rand=False)
+
+    def attn():
+        lib.malus_attn_fwd(qh, ql, Bz, H, T, hs, C.c_float(0.125), ph, pl, oh, ol)
+        return 0
+    causal = 0.75   # key blocks up to the diagonal (T = 256, 128-row query blocks)
+    yield ("attn fwd fused (causal, C4)", attn,
+           8 * 3 * Mt * Cc + 8 * Bz * H * T * T * causal + 8 * Mt * Cc,
+           2.0 * 2 * Bz * H * T * T * hs * causal)
 
 
 def run(only: str | None = None, reps: int = 20, verbose: bool = True) -> tuple[list[dict], dict]:
