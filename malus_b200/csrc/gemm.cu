@@ -134,23 +134,38 @@ void gemm_simt(const GemmArgs& g) {
 namespace {
 using namespace malus::tc;
 
-constexpr int BM = 128, BK = 32;
-constexpr int kTileBytesA = BM * BK * 4;  // 16 KB
+constexpr int BM = 128;
 constexpr int kEpiWarpFloats = 32 * 32;   // per-warp 32x32 staging block (XOR-swizzled granules)
-// Tile width BN (128, 192 or 256): a wider tile reads each A k-block once for more
-// columns (less shared-memory and L2 traffic per FLOP); its larger stages
-// leave room for 2 of them instead of 3.
-template <int BN_>
+// Tile shape: width BN (128 or 192) and k-block depth BK (32 or 16).  A wider
+// tile reads each A k-block once for more columns (less shared-memory and L2
+// traffic per FLOP); a shallower k-block makes stages smaller, so more of them
+// fit and the TMA latency is covered further ahead.  K-major tiles use the
+// 128-byte swizzle (BK 32) or the 64-byte swizzle (BK 16); MN-major tiles the
+// 32-byte-granule 128-byte swizzle with BK rows per 32-column chunk.
+template <int BN_, int BK_>
 struct TileCfg {
-  static constexpr int BN = BN_;
+  static constexpr int BN = BN_, BK = BK_;
+  static constexpr int kTileBytesA = BM * BK * 4;
   static constexpr int kTileBytesB = BN * BK * 4;
   static constexpr int kStageBytes = 2 * kTileBytesA + 2 * kTileBytesB;
-  static constexpr int STAGES = BN <= 128 ? 3 : 2;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
-                                    8 * kEpiWarpFloats * 4 /*epilogue staging*/;
+  static constexpr int kFixed = 1024 /*align*/ + 256 /*barriers*/ + 8 * kEpiWarpFloats * 4 /*staging*/;
+  static constexpr int STAGES = (232448 - kFixed) / kStageBytes > 6 ? 6 : (232448 - kFixed) / kStageBytes;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kFixed;
   static constexpr uint32_t kTmemCols = BN <= 128 ? 256 : 512;   // two accumulators, power of 2
-  static_assert(kSmemBytes <= 232448, "shared memory");
+  static constexpr int kChunkBytes = BK * 128;   // one 32-wide MN chunk (or 32-row K-major box)
+  static_assert(STAGES >= 2 && kSmemBytes <= 232448, "shared memory");
 };
+
+// Shared-memory descriptors for a k-block of depth BK.
+template <int BK>
+__device__ __forceinline__ uint64_t desc_k(uint32_t tile, int kk) {
+  return BK == 32 ? umma_desc(tile + kk * 32, 16, 1024, 2)    // 128-B swizzle, 8-row atoms 1 KB
+                  : umma_desc(tile + kk * 32, 16, 512, 4);    // 64-B swizzle, 8-row atoms 512 B
+}
+template <int BK>
+__device__ __forceinline__ uint64_t desc_mn(uint32_t tile, int kk) {
+  return umma_desc(tile + kk * 1024, BK * 128, 512, 1);       // chunks BK rows x 128 B apart
+}
 // Epilogue warps: 8 (two per TMEM lane quarter, half the columns each) when the
 // epilogue reads an auxiliary input, whose load latency the extra warps hide;
 // 4 otherwise, leaving L2 bandwidth to the operand loads.
@@ -178,6 +193,7 @@ struct TcKernelParams {
   int splits;      // K slices per tile (split-K); > 1 writes raw partial tiles to ws
   float* ws;       // [tile][split][BM][bn] partial accumulators when splits > 1
   int bn;          // tile width (the kernel's BN)
+  int bk;          // k-block depth (the kernel's BK)
   int a_chunked, b_chunked;   // MN-major operand loaded as one {32, 32 K, 4 chunks} box per plane
   int staged;                 // epilogue through the smem transpose (see epi_warps)
   int32_t* err;
@@ -198,8 +214,8 @@ __device__ __forceinline__ bool unit_of(const TcKernelParams& kp, int unit, Unit
   u.n0 = (rem % kp.tiles_n) * kp.bn;
   if (p.causal == kCausalOut && u.n0 > u.m0 + BM - 1) return false;
   int lo = 0, hi = kp.nk;
-  if (p.causal == kCausalALower) hi = min(kp.nk, (u.m0 + BM + BK - 1) / BK);
-  if (p.causal == kCausalAUpper) lo = u.m0 / BK;
+  if (p.causal == kCausalALower) hi = min(kp.nk, (u.m0 + BM + kp.bk - 1) / kp.bk);
+  if (p.causal == kCausalAUpper) lo = u.m0 / kp.bk;
   const int len = hi - lo;
   u.kb_lo = lo + sl * len / kp.splits;
   u.kb_hi = lo + (sl + 1) * len / kp.splits;
@@ -305,14 +321,14 @@ __device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4
   }
 }
 
-template <int EPI, int BNT>
+template <int EPI, int BNT, int BKT>
 __global__ void __launch_bounds__(threads_tc(EPI), 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
           const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
           const TcKernelParams kp) {
-  using CF = TileCfg<BNT>;
-  constexpr int BN = CF::BN, STAGES = CF::STAGES, kStageBytes = CF::kStageBytes;
-  constexpr int kTileBytesB = CF::kTileBytesB;
+  using CF = TileCfg<BNT, BKT>;
+  constexpr int BN = CF::BN, BK = CF::BK, STAGES = CF::STAGES, kStageBytes = CF::kStageBytes;
+  constexpr int kTileBytesA = CF::kTileBytesA, kTileBytesB = CF::kTileBytesB, kChunk = CF::kChunkBytes;
   constexpr uint32_t kTmemCols = CF::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
   const TcProblem& p = kp.pr;
@@ -391,8 +407,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
             for (int j = 0; j < BM / 32; ++j) {
               operand_coords(p.a.zmode, p.a.seg, z, k0, m0 + 32 * j, &kc, &mnc, &zc);
               int x = p.a.mn_major ? mnc : kc, y = p.a.mn_major ? kc : mnc;
-              tma_load_3d(smem_u32(st + j * 4096), &mAh, fb, x, y, zc);
-              tma_load_3d(smem_u32(st + kTileBytesA + j * 4096), &mAl, fb, x, y, zc);
+              tma_load_3d(smem_u32(st + j * kChunk), &mAh, fb, x, y, zc);
+              tma_load_3d(smem_u32(st + kTileBytesA + j * kChunk), &mAl, fb, x, y, zc);
             }
           }
           uint8_t* sb = st + 2 * kTileBytesA;
@@ -408,8 +424,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
             for (int j = 0; j < BN / 32; ++j) {
               operand_coords(p.b.zmode, p.b.seg, z, k0, n0 + 32 * j, &kc, &mnc, &zc);
               int x = p.b.mn_major ? mnc : kc, y = p.b.mn_major ? kc : mnc;
-              tma_load_3d(smem_u32(sb + j * 4096), &mBh, fb, x, y, zc);
-              tma_load_3d(smem_u32(sb + kTileBytesB + j * 4096), &mBl, fb, x, y, zc);
+              tma_load_3d(smem_u32(sb + j * kChunk), &mBh, fb, x, y, zc);
+              tma_load_3d(smem_u32(sb + kTileBytesB + j * kChunk), &mBl, fb, x, y, zc);
             }
           }
         }
@@ -451,10 +467,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
           uint32_t bh = smem_u32(st + 2 * kTileBytesA), bl = bh + kTileBytesB;
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
-            uint64_t dah = p.a.mn_major ? desc_mnmajor(ah, kk) : desc_kmajor(ah, kk);
-            uint64_t dal = p.a.mn_major ? desc_mnmajor(al, kk) : desc_kmajor(al, kk);
-            uint64_t dbh = p.b.mn_major ? desc_mnmajor(bh, kk) : desc_kmajor(bh, kk);
-            uint64_t dbl = p.b.mn_major ? desc_mnmajor(bl, kk) : desc_kmajor(bl, kk);
+            uint64_t dah = p.a.mn_major ? desc_mn<BK>(ah, kk) : desc_k<BK>(ah, kk);
+            uint64_t dal = p.a.mn_major ? desc_mn<BK>(al, kk) : desc_k<BK>(al, kk);
+            uint64_t dbh = p.b.mn_major ? desc_mn<BK>(bh, kk) : desc_k<BK>(bh, kk);
+            uint64_t dbl = p.b.mn_major ? desc_mn<BK>(bl, kk) : desc_k<BK>(bl, kk);
             uint32_t acc0 = (kb > kb_lo || kk > 0) ? 1u : 0u;
             mma_tf32(dacc, dal, dbh, idesc, acc0);   // small terms first
             mma_tf32(dacc, dah, dbl, idesc, 1u);
@@ -720,8 +736,9 @@ CUtensorMap encode_f32_map(int rank, const void* base, const uint64_t* dims, con
 
 namespace {
 
-// 3-D f32 map {d0 (contiguous), d1, d2}, box {b0, b1, 1}, 128-B swizzle with
-// 16-byte granules (K-major tiles) or 32-byte granules (MN-major tiles).
+// 3-D f32 map {d0 (contiguous), d1, d2}, box {b0, b1, 1}: K-major tiles use the
+// 128-byte (b0 = 32) or 64-byte (b0 = 16) swizzle with 16-byte granules,
+// MN-major tiles the 128-byte swizzle with 32-byte granules.
 CUtensorMap make_map(const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t pitch_bytes,
                      uint64_t plane_bytes, uint32_t b0, uint32_t b1, bool mn_major) {
   CUtensorMap m;
@@ -731,7 +748,8 @@ CUtensorMap make_map(const float* base, uint64_t d0, uint64_t d1, uint64_t d2, u
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                 : (b0 == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B),
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) panic("cuTensorMapEncodeTiled failed (%d)", (int)r);
   return m;
@@ -750,12 +768,12 @@ bool mn_chunked(const TcOperand& o, int tile_mn) {
 }
 
 CUtensorMap chunked_map(const TcOperand& o, const float* plane, uint64_t pitch_bytes,
-                        uint64_t plane_bytes, int tile_mn) {
+                        uint64_t plane_bytes, int tile_mn, int bk) {
   CUtensorMap m;
   cuuint64_t dims[4] = {32, (cuuint64_t)o.rows, (cuuint64_t)(o.cols / 32),
                         (cuuint64_t)std::max(1, o.nz)};
   cuuint64_t strides[3] = {pitch_bytes, 128, plane_bytes};
-  cuuint32_t box[4] = {32, 32, (cuuint32_t)(tile_mn / 32), 1};
+  cuuint32_t box[4] = {32, (cuuint32_t)bk, (cuuint32_t)(tile_mn / 32), 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)plane, dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
@@ -764,33 +782,25 @@ CUtensorMap chunked_map(const TcOperand& o, const float* plane, uint64_t pitch_b
   return m;
 }
 
-// tile_mn: the operand's tile extent along M (A: BM) or N (B: the tile width).
-CUtensorMap operand_map(const TcOperand& o, const float* plane, int tile_mn) {
+// tile_mn: the operand's tile extent along M (A: BM) or N (B: the tile width);
+// bk: the k-block depth.
+CUtensorMap operand_map(const TcOperand& o, const float* plane, int tile_mn, int bk) {
   uint64_t pb = (uint64_t)o.pitch * 4;
   uint64_t zb = (uint64_t)o.zstride * 4;
   if (o.nz > 1 && (zb % 16 != 0)) panic("gemm operand slice stride %lld is not 16-byte aligned", (long long)o.zstride);
   if (o.nz <= 1) zb = pb * (uint64_t)o.rows;
-  if (mn_chunked(o, tile_mn)) return chunked_map(o, plane, pb, std::max<uint64_t>(zb, 16), tile_mn);
-  // K-major boxes are 32 (K) x tile_mn rows, or 32 x 32 rows when the rows are segmented
-  uint32_t box_rows = (o.mn_major || o.zmode == kZMNSeg) ? 32 : (uint32_t)tile_mn;
+  if (mn_chunked(o, tile_mn)) return chunked_map(o, plane, pb, std::max<uint64_t>(zb, 16), tile_mn, bk);
+  // K-major boxes are bk (K) x tile_mn rows, or bk x 32 rows when the rows are
+  // segmented; MN-major boxes 32 columns x bk rows
+  if (o.mn_major)
+    return make_map(plane, (uint64_t)o.cols, (uint64_t)o.rows, (uint64_t)std::max(1, o.nz), pb,
+                    std::max<uint64_t>(zb, 16), 32, (uint32_t)bk, true);
+  uint32_t box_rows = o.zmode == kZMNSeg ? 32 : (uint32_t)tile_mn;
   return make_map(plane, (uint64_t)o.cols, (uint64_t)o.rows, (uint64_t)std::max(1, o.nz), pb,
-                  std::max<uint64_t>(zb, 16), 32, box_rows, o.mn_major);
+                  std::max<uint64_t>(zb, 16), (uint32_t)bk, box_rows, false);
 }
 
 int g_force_backend = -1;
-
-// Tile width: 192 when N is a whole number of 192-wide tiles and the grid
-// stays full (every C4 layer GEMM: N = 384, 1152, 1536), else 128.
-int tile_width_for(const TcProblem& pr) {
-  static int forced = [] {
-    const char* e = getenv("MALUS_GEMM_BN");   // 128 or 192 (tuning)
-    return e ? atoi(e) : 0;
-  }();
-  if (forced == 128 || forced == 192 || forced == 256) return forced;
-  if (pr.causal || pr.N % 192 != 0) return 128;
-  long tiles = (long)((pr.M + BM - 1) / BM) * (pr.N / 192) * pr.batch;
-  return tiles >= kNumSMs ? 192 : 128;
-}
 
 // K slices for a problem of `tiles` output tiles and nk k-blocks: split only
 // when the tiles fill less than half the SMs and every slice keeps >= 8 k-blocks
@@ -798,6 +808,28 @@ int tile_width_for(const TcProblem& pr) {
 int splitk_for(int tiles, int nk) {
   if (tiles * 2 > kNumSMs || nk < 16) return 1;
   return std::max(1, std::min({kNumSMs / tiles, nk / 8, 64}));
+}
+
+// Tile shape (measured on the C4 GEMMs): width 192 when N is a whole number of
+// 192-wide tiles and the grid is either full or split along K (every C4 layer
+// GEMM: N = 384, 1152, 1536), else 128.  k-block depth 16 with the 192-wide
+// tile (four stages instead of two) except for stores of tf32 planes, which
+// measured faster at 32; 32 with the 128-wide tile.  MALUS_GEMM_BN / _BK
+// override for tuning.
+struct TileShape { int bn, bk; };
+TileShape tile_shape_for(const TcProblem& pr) {
+  static int forced_bn = [] { const char* e = getenv("MALUS_GEMM_BN"); return e ? atoi(e) : 0; }();
+  static int forced_bk = [] { const char* e = getenv("MALUS_GEMM_BK"); return e ? atoi(e) : 0; }();
+  int bn = 128;
+  if (forced_bn == 128 || forced_bn == 192) {
+    bn = forced_bn;
+  } else if (!pr.causal && pr.N % 192 == 0) {
+    long tiles = (long)((pr.M + BM - 1) / BM) * (pr.N / 192) * pr.batch;
+    if (tiles >= kNumSMs || splitk_for((int)tiles, (pr.K + 15) / 16) > 1) bn = 192;
+  }
+  int bk = (bn == 192 && !(pr.epi == kEpiStore && pr.out_hi)) ? 16 : 32;
+  if (forced_bk == 16 || forced_bk == 32) bk = forced_bk;
+  return {bn, bk};
 }
 
 // Device workspace for split-K partials, grown on demand (never shrinks).
@@ -816,17 +848,17 @@ float* splitk_workspace(size_t floats) {
   return buf[dev];
 }
 
-template <int EPI, int BNT>
+template <int EPI, int BNT, int BKT>
 void launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
                const CUtensorMap& bl, const TcKernelParams& kp, int grid) {
-  constexpr int smem = TileCfg<BNT>::kSmemBytes;
+  constexpr int smem = TileCfg<BNT, BKT>::kSmemBytes;
   static bool attr = false;
   if (!attr) {
-    MALUS_CUDA(cudaFuncSetAttribute(k_gemm_tc<EPI, BNT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    MALUS_CUDA(cudaFuncSetAttribute(k_gemm_tc<EPI, BNT, BKT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     smem));
     attr = true;
   }
-  k_gemm_tc<EPI, BNT><<<grid, threads_tc(EPI), smem, stream()>>>(ah, al, bh, bl, kp);
+  k_gemm_tc<EPI, BNT, BKT><<<grid, threads_tc(EPI), smem, stream()>>>(ah, al, bh, bl, kp);
   if (kp.splits > 1) {
     int64_t chunks = (int64_t)kp.tiles_m * kp.tiles_n * kp.pr.batch * (BM * kp.bn / 4);
     unsigned g = (unsigned)std::min<int64_t>((chunks + 255) / 256, (int64_t)kNumSMs * 8);
@@ -879,12 +911,14 @@ void gemm_tc_planes(const TcProblem& pr) {
     if ((o->zmode == kZKSeg || o->zmode == kZMNSeg) && (o->seg <= 0 || o->seg % 32 != 0))
       panic("gemm_tc_planes: segment width %d must be a positive multiple of 32", o->seg);
   load_encoder();
-  const int BN = tile_width_for(pr);
-  CUtensorMap ah = operand_map(pr.a, pr.a.hi, BM), al = operand_map(pr.a, pr.a.lo, BM);
-  CUtensorMap bh = operand_map(pr.b, pr.b.hi, BN), bl = operand_map(pr.b, pr.b.lo, BN);
+  const TileShape ts = tile_shape_for(pr);
+  const int BN = ts.bn, BK = ts.bk;
+  CUtensorMap ah = operand_map(pr.a, pr.a.hi, BM, BK), al = operand_map(pr.a, pr.a.lo, BM, BK);
+  CUtensorMap bh = operand_map(pr.b, pr.b.hi, BN, BK), bl = operand_map(pr.b, pr.b.lo, BN, BK);
   TcKernelParams kp;
   kp.pr = pr;
   kp.bn = BN;
+  kp.bk = BK;
   kp.tiles_m = (pr.M + BM - 1) / BM;
   kp.tiles_n = (pr.N + BN - 1) / BN;
   kp.nk = (pr.K + BK - 1) / BK;
@@ -923,31 +957,19 @@ void gemm_tc_planes(const TcProblem& pr) {
   const int arrays = (pr.out ? 1 : 0) + (pr.out_hi ? 2 : 0) + (pr.aux ? 1 : 0);
   int pid = prof_begin(0, flops, 8.0 * ((double)pr.M * pr.K + (double)pr.N * pr.K) * pr.batch +
                                      4.0 * mn * arrays);
-  if (BN == 256) {
-    switch (pr.epi) {
-      case kEpiStore: launch_tc<kEpiStore, 256>(ah, al, bh, bl, kp, grid); break;
-      case kEpiResid: launch_tc<kEpiResid, 256>(ah, al, bh, bl, kp, grid); break;
-      case kEpiGelu: launch_tc<kEpiGelu, 256>(ah, al, bh, bl, kp, grid); break;
-      case kEpiGeluBwd: launch_tc<kEpiGeluBwd, 256>(ah, al, bh, bl, kp, grid); break;
-      default: launch_tc<kEpiSoftmaxBwd, 256>(ah, al, bh, bl, kp, grid); break;
-    }
-  } else if (BN == 192) {
-    switch (pr.epi) {
-      case kEpiStore: launch_tc<kEpiStore, 192>(ah, al, bh, bl, kp, grid); break;
-      case kEpiResid: launch_tc<kEpiResid, 192>(ah, al, bh, bl, kp, grid); break;
-      case kEpiGelu: launch_tc<kEpiGelu, 192>(ah, al, bh, bl, kp, grid); break;
-      case kEpiGeluBwd: launch_tc<kEpiGeluBwd, 192>(ah, al, bh, bl, kp, grid); break;
-      default: launch_tc<kEpiSoftmaxBwd, 192>(ah, al, bh, bl, kp, grid); break;
-    }
-  } else {
-    switch (pr.epi) {
-      case kEpiStore: launch_tc<kEpiStore, 128>(ah, al, bh, bl, kp, grid); break;
-      case kEpiResid: launch_tc<kEpiResid, 128>(ah, al, bh, bl, kp, grid); break;
-      case kEpiGelu: launch_tc<kEpiGelu, 128>(ah, al, bh, bl, kp, grid); break;
-      case kEpiGeluBwd: launch_tc<kEpiGeluBwd, 128>(ah, al, bh, bl, kp, grid); break;
-      default: launch_tc<kEpiSoftmaxBwd, 128>(ah, al, bh, bl, kp, grid); break;
-    }
+#define MALUS_TC_EPI_SWITCH(BN_, BK_)                                               \
+  switch (pr.epi) {                                                                \
+    case kEpiStore: launch_tc<kEpiStore, BN_, BK_>(ah, al, bh, bl, kp, grid); break; \
+    case kEpiResid: launch_tc<kEpiResid, BN_, BK_>(ah, al, bh, bl, kp, grid); break; \
+    case kEpiGelu: launch_tc<kEpiGelu, BN_, BK_>(ah, al, bh, bl, kp, grid); break;   \
+    case kEpiGeluBwd: launch_tc<kEpiGeluBwd, BN_, BK_>(ah, al, bh, bl, kp, grid); break; \
+    default: launch_tc<kEpiSoftmaxBwd, BN_, BK_>(ah, al, bh, bl, kp, grid); break;   \
   }
+  if (BN == 192 && BK == 16) { MALUS_TC_EPI_SWITCH(192, 16) }
+  else if (BN == 192) { MALUS_TC_EPI_SWITCH(192, 32) }
+  else if (BK == 16) { MALUS_TC_EPI_SWITCH(128, 16) }
+  else { MALUS_TC_EPI_SWITCH(128, 32) }
+#undef MALUS_TC_EPI_SWITCH
   count_launch(kp.splits > 1 ? 2 : 1);
   after_launch("k_gemm_tc");
   prof_end(pid);
