@@ -151,7 +151,7 @@ struct TileCfg {
   static constexpr int kFixed = 1024 /*align*/ + 256 /*barriers*/ + 8 * kEpiWarpFloats * 4 /*staging*/;
   static constexpr int STAGES = (232448 - kFixed) / kStageBytes > 6 ? 6 : (232448 - kFixed) / kStageBytes;
   static constexpr int kSmemBytes = STAGES * kStageBytes + kFixed;
-  static constexpr uint32_t kTmemCols = BN <= 128 ? 256 : 512;   // two accumulators, power of 2
+  static constexpr uint32_t kTmemCols = BN <= 64 ? 128 : (BN <= 128 ? 256 : 512);   // two accumulators, power of 2
   static constexpr int kChunkBytes = BK * 128;   // one 32-wide MN chunk (or 32-row K-major box)
   static_assert(STAGES >= 2 && kSmemBytes <= 232448, "shared memory");
 };
@@ -823,6 +823,8 @@ TileShape tile_shape_for(const TcProblem& pr) {
   int bn = 128;
   if (forced_bn == 128 || forced_bn == 192) {
     bn = forced_bn;
+  } else if (pr.N <= 64) {
+    bn = 64;                       // attention outputs (N = head size): no idle half tile
   } else if (!pr.causal && pr.N % 192 == 0) {
     long tiles = (long)((pr.M + BM - 1) / BM) * (pr.N / 192) * pr.batch;
     if (tiles >= kNumSMs || splitk_for((int)tiles, (pr.K + 15) / 16) > 1) bn = 192;
@@ -965,7 +967,8 @@ void gemm_tc_planes(const TcProblem& pr) {
     case kEpiGeluBwd: launch_tc<kEpiGeluBwd, BN_, BK_>(ah, al, bh, bl, kp, grid); break; \
     default: launch_tc<kEpiSoftmaxBwd, BN_, BK_>(ah, al, bh, bl, kp, grid); break;   \
   }
-  if (BN == 192 && BK == 16) { MALUS_TC_EPI_SWITCH(192, 16) }
+  if (BN == 64) { MALUS_TC_EPI_SWITCH(64, 32) }
+  else if (BN == 192 && BK == 16) { MALUS_TC_EPI_SWITCH(192, 16) }
   else if (BN == 192) { MALUS_TC_EPI_SWITCH(192, 32) }
   else if (BK == 16) { MALUS_TC_EPI_SWITCH(128, 16) }
   else { MALUS_TC_EPI_SWITCH(128, 32) }
