@@ -33,6 +33,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 C4 = dict(vocab=65, n_layer=6, n_head=6, n_embd=384, block_size=256, batch=64)
+# GPT-2-small shape (a parity config of the survey; measured on request, not the contract line)
+C5 = dict(vocab=50304, n_layer=12, n_head=12, n_embd=768, block_size=1024, batch=8, tied=True)
+WORKLOADS = {"c4": (C4, "C4 Karpathy char-nanoGPT: V65 L6 H6 C384 T256, batch 64/GPU"),
+             "c5": (C5, "C5 GPT-2-small shape: V50304 L12 H12 C768 T1024, batch 8/GPU, tied head")}
 OPT = dict(lr=1e-3, beta1=0.9, beta2=0.99, eps=1e-8, wd=0.01)
 METRIC = "nanoGPT f32 train tokens/s"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
@@ -260,6 +264,8 @@ def main():
     ap.add_argument("--mode", type=int, default=int(os.environ.get("MALUS_BENCH_MODE", "1")))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ops", action="store_true", help="C2 op microbench (GPU and CPU oracle)")
+    ap.add_argument("--workload", default="c4", choices=sorted(WORKLOADS),
+                    help="c4 (the contract line) or c5 (GPT-2-small shape, on request)")
     ap.add_argument("--graph", type=int, default=int(os.environ.get("MALUS_BENCH_GRAPH", "1")),
                     help="replay the fused step as one CUDA graph (mode 1)")
     args = ap.parse_args()
@@ -291,7 +297,8 @@ def main():
         from malus_b200.dist import init_data_parallel
         init_data_parallel(lib, rank, world, timeout_ms=120000)
 
-    cfg = dict(C4)
+    cfg, workload_name = WORKLOADS[args.workload]
+    cfg = dict(cfg)
     model = M.GPT(**cfg, **OPT, mode=args.mode, use_graph=args.graph if args.mode == 1 else 0, seed=0)
     m = cfg["batch"] * cfg["block_size"]
     rng = np.random.default_rng(1000 + rank)
@@ -394,7 +401,7 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt_ms / args.steps, 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic: uniform token ids in [0,65) from a seed; N(0,0.02) Philox init",
-                "config": {"workload": "C4 Karpathy char-nanoGPT: V65 L6 H6 C384 T256, batch 64/GPU",
+                "config": {"workload": workload_name,
                            "model": "char-nanoGPT", "global_batch": cfg["batch"] * world,
                            "seq_len": cfg["block_size"], "parallelism": f"dp{world}",
                            "mode": "fused" if args.mode == 1 else "tape",

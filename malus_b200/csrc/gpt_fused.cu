@@ -389,6 +389,53 @@ __global__ void k_xent_fused(const float* __restrict__ logits, const int32_t* __
   }
 }
 
+// The same cross-entropy for wide rows (vocab > 1024): one 512-thread block
+// per row, three passes over the row (max, sum of exp, probabilities and
+// dlogits planes); block reductions in a fixed order.
+__device__ __forceinline__ float block_reduce(float v, float* sh, bool is_max) {
+  v = is_max ? wmax(v) : wsum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  float t = l < nw ? sh[l] : (is_max ? -INFINITY : 0.0f);
+  t = is_max ? wmax(t) : wsum(t);
+  return t;   // every thread of warp 0..nw-1 holds the result
+}
+
+__global__ void k_xent_fused_wide(const float* __restrict__ logits, const int32_t* __restrict__ tgt,
+                                  float* __restrict__ nll, float* __restrict__ d_hi,
+                                  float* __restrict__ d_lo, int M, int V, int ldp, int32_t* err) {
+  __shared__ float sh[32];
+  __shared__ float pt_sh;
+  const float scale = 1.0f / (float)M;
+  for (int r = blockIdx.x; r < M; r += gridDim.x) {
+    const float* xr = logits + (size_t)r * V;
+    float m = -INFINITY;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) m = fmaxf(m, xr[j]);
+    m = block_reduce(m, sh, true);
+    float s = 0.0f;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) s += expf(xr[j] - m);
+    s = block_reduce(s, sh, false);
+    const int t = tgt[r];
+    const bool bad = t < 0 || t >= V;
+    if (threadIdx.x == 0) pt_sh = 0.0f;
+    __syncthreads();
+    for (int j = threadIdx.x; j < ldp; j += blockDim.x) {
+      const float p = j < V ? expf(xr[j] - m) / s : 0.0f;
+      if (j == t) pt_sh = p;
+      const float gr = j < V ? (j == t ? p - 1.0f : p) * scale : 0.0f;
+      split_store(d_hi, d_lo, (size_t)r * ldp + j, gr);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      if (bad) { atomicExch(err, 3); nll[r] = 0.0f; }
+      else nll[r] = -logf(pt_sh);
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void k_mean_nll(const float* __restrict__ v, float* __restrict__ out, int n) {
   __shared__ float sh[32];
   float s = 0.0f;
@@ -604,9 +651,9 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
   f->M = f->B * f->T; f->hs = f->C / f->H; f->C4 = 4 * f->C; f->BH = f->B * f->H;
   f->Vp = (f->V + 3) & ~3;
   f->scale = 1.0f / sqrtf((float)f->hs);
-  if (f->C % 32 || f->hs % 4 || f->T % 4 || f->T > 1024 || f->C > 1024 || f->Vp > 1024)
-    panic("fused step needs n_embd %% 32 == 0, head size %% 4 == 0, T, C, vocab <= 1024 "
-          "(got C=%d hs=%d T=%d V=%d)", f->C, f->hs, f->T, f->V);
+  if (f->C % 32 || f->hs % 4 || f->T % 4 || f->T > 1024 || f->C > 1024)
+    panic("fused step needs n_embd %% 32 == 0, head size %% 4 == 0, T %% 4 == 0, T, C <= 1024 "
+          "(got C=%d hs=%d T=%d)", f->C, f->hs, f->T);
   f->params = params;
   f->sizes = sizes;
   f->gbuf = gbuf;
@@ -732,8 +779,13 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
   else
     gemm(M, V, C, 1, op(f->xf, M, C, C, false), op(f->lmpl, C, V, Vp, true), kEpiStore, none,
          L(0, 0, 0, 0, V), unit, f->logits, Planes{}, nullptr);
-  PER_DISPATCH(Vp, (k_xent_fused<P_><<<rows_grid(M), 256, 0, stream()>>>(
-                       f->logits, yt, f->nll, f->dlog.hi, f->dlog.lo, M, V, Vp, device_error_word())));
+  if (Vp <= 1024) {
+    PER_DISPATCH(Vp, (k_xent_fused<P_><<<rows_grid(M), 256, 0, stream()>>>(
+                         f->logits, yt, f->nll, f->dlog.hi, f->dlog.lo, M, V, Vp, device_error_word())));
+  } else {
+    k_xent_fused_wide<<<std::min(M, kNumSMs * 4), 512, 0, stream()>>>(f->logits, yt, f->nll, f->dlog.hi,
+                                                                      f->dlog.lo, M, V, Vp, device_error_word());
+  }
   k_mean_nll<<<1, 1024, 0, stream()>>>(f->nll, loss_dev, M);
   count_launch(2);
   after_launch("k_xent_fused");

@@ -155,3 +155,14 @@ def test_graph_step_matches_oracle(M, orc):
     assert np.all(np.abs(lg - lo) / lo < 5e-3), (lg, lo)
     assert abs(lg[0] - lo[0]) / lo[0] < 1e-5
     check_params(pg, po, lr=1e-3)
+
+
+def test_fused_wide_vocab_tied_matches_oracle(M, orc):
+    """C5's vocabulary (50304, tied head) through the fused step: the block-per-row
+    cross-entropy, the 50304-row LM head GEMMs and the large-vocab embedding VJP;
+    other dimensions small so the oracle keeps up."""
+    cfg = dict(vocab=50304, n_layer=1, n_head=2, n_embd=128, block_size=128, batch=2)
+    lg, lo, pg, po = run_pair(M, orc, cfg, 3, mode=1, lr=1e-3, tied=True, use_graph=1)
+    assert abs(lg[0] - lo[0]) / lo[0] < 1e-5, (lg, lo)
+    assert np.max(np.abs(lg - lo) / lo) < 5e-3, (lg, lo)
+    check_params(pg, po, lr=1e-3)
