@@ -115,11 +115,12 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def traffic_from_profiles(kernel: str):
+def traffic_from_profiles(kernel: str, workload: str, mode: int):
     """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
-    capture of this bench command (profiles/roofline_traffic.json)."""
+    capture of this bench command (profiles/roofline_traffic.json).  The capture
+    is of the default workload's fused step; other workloads get None."""
     p = ROOT / "profiles" / "roofline_traffic.json"
-    if p.exists():
+    if p.exists() and workload == "c4" and mode == 1:
         d = json.loads(p.read_text())
         e = d.get(kernel)
         return e.get("bytes_per_launch") if isinstance(e, dict) else e
@@ -258,7 +259,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="malus", choices=["malus", "reference"])
     ap.add_argument("--mode", type=int, default=int(os.environ.get("MALUS_BENCH_MODE", "1")))
@@ -367,7 +368,7 @@ def main():
         roofline = {"bound": "tensor", "kernel": "k_gemm_tc (3xTF32 tcgen05)",
                     "achieved": round(algo, 2), "peak": round(f32_peak, 2), "unit": "TFLOP/s",
                     "frac": round(algo / f32_peak, 4),
-                    "traffic": traffic_from_profiles("k_gemm_tc"),
+                    "traffic": traffic_from_profiles("k_gemm_tc", args.workload, args.mode),
                     "algorithmic_bytes_per_launch": round(by_k.value / cnt.value),
                     "launches_per_step": cnt.value / args.steps,
                     "gemm_share_of_step": round(ms_k.value / dt_prof_ms, 4) if world == 1 else None,
@@ -400,9 +401,10 @@ def main():
         line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt_ms / args.steps, 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic: uniform token ids in [0,65) from a seed; N(0,0.02) Philox init",
+                "data": f"synthetic: uniform token ids in [0,{cfg['vocab']}) from a seed; N(0,0.02) Philox init",
                 "config": {"workload": workload_name,
-                           "model": "char-nanoGPT", "global_batch": cfg["batch"] * world,
+                           "model": "char-nanoGPT" if args.workload == "c4" else "nanoGPT (GPT-2-small shape)",
+                           "global_batch": cfg["batch"] * world,
                            "seq_len": cfg["block_size"], "parallelism": f"dp{world}",
                            "mode": "fused" if args.mode == 1 else "tape",
                            "cuda_graph": bool(args.graph and args.mode == 1),

@@ -6,18 +6,20 @@
 // diagonal), P = softmax(scores, axis -1), O = P V.  Masked scores underflow to
 // exactly 0 after the exponential, so keys past the diagonal are skipped.
 //
-// One CTA = one head (z = b*H + h) x 128 query rows; 192 threads:
+// One CTA = one head (z = b*H + h) x 128 query rows; 320 threads:
 //   warp 0     TMA producer: Q once (tf32 hi/lo planes), then key blocks of 64
-//              keys through two K/V stages (K only in pass 1, K and V in pass 2);
+//              keys: K through two stages (both passes), V into one buffer
+//              (pass 2, after the previous block's P V);
 //   warp 1     TMEM owner and MMA issuer: S_b = Q K^T into two 64-column TMEM
-//              buffers, O += P V into a third region;
-//   warps 2-5  softmax: one thread per query row (its TMEM lane).
-//              Pass 1: row max m and sum l over the key blocks (online).
-//              Pass 2: S recomputed, p = exp(s*scale - m) * (1/l) written in 32-key
-//              halves into a swizzled shared stage that is both the A operand of
-//              the P V MMA and the source of a TMA store of the P planes (the
-//              backward reads them); finally O is read from TMEM and written as
-//              head-unfolded tf32 planes [B*T][H*hs].
+//              buffers (one block ahead), O += P V into a third region;
+//   warps 2-9  softmax, two groups of four warps: group g owns keys 32g..32g+31
+//              of every block, one thread per query row (its TMEM lane).
+//              Pass 1: each group's row max and sum (online), combined once.
+//              Pass 2: S recomputed, p = exp(s*scale - m) * (1/l) written into
+//              the group's own swizzled shared stage, which is both the A
+//              operand of that half's P V MMA and the source of a TMA store of
+//              the P planes (the backward reads them); finally O is read from
+//              TMEM and written as head-unfolded tf32 planes [B*T][H*hs].
 // Every mbarrier wait is bounded; on timeout the CTA records an error, drains
 // its MMAs and returns.
 #include "common.cuh"
@@ -27,31 +29,53 @@ namespace malus {
 namespace {
 using namespace malus::tc;
 
-// OR of `v` over the 128 softmax threads (named barrier 1): every exit
+// OR of `v` over the 256 softmax threads (named barrier 1): every exit
 // decision in those warps is collective, so no thread is left at a barrier.
-__device__ __forceinline__ bool any128(bool v) {
+__device__ __forceinline__ bool any256(bool v) {
   uint32_t r;
   asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 128, p;\n"
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n"
       " selp.u32 %0, 1, 0, q;\n}\n"
       : "=r"(r)
       : "r"((uint32_t)v)
       : "memory");
   return r != 0;
 }
+// barrier among the 128 threads of softmax group g (named barriers 2 and 3)
+__device__ __forceinline__ void group_sync(int g) {
+  asm volatile("bar.sync %0, 128;" ::"r"(2 + g) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 
 constexpr int AQ = 128;  // query rows per CTA
 constexpr int AK = 64;   // keys per block
+constexpr int kAttnThreads = 64 + 256;   // producer, MMA, 8 softmax warps
 
 template <int HS>
 struct AttnCfg {
   static constexpr int kQBytes = AQ * HS * 4;              // one plane of the Q tile
   static constexpr int kKBytes = AK * HS * 4;              // one plane of a K (or V) block
-  static constexpr int kStageBytes = 4 * kKBytes;          // K hi, K lo, V hi, V lo
   static constexpr int kPBytes = AQ * 32 * 4;              // one plane of a 32-key P half
-  static constexpr int kOffStage = 2 * kQBytes;
-  static constexpr int kOffP = kOffStage + 2 * kStageBytes;
-  static constexpr int kOffBar = kOffP + 2 * kPBytes;
+  static constexpr int kOffK = 2 * kQBytes;                // two K stages (hi, lo)
+  static constexpr int kOffV = kOffK + 2 * 2 * kKBytes;    // one V buffer (hi, lo)
+  static constexpr int kOffP = kOffV + 2 * kKBytes;        // two P stages (hi, lo), one per half
+  // [2 groups][128 rows] (m, l) at the end of pass 1.  Aliases P stage 0: every
+  // thread reads the other group's statistics before the first collective
+  // any256() of pass 2, and no P stage is written before that.
+  static constexpr int kOffStats = kOffP;
+  static constexpr int kOffBar = kOffP + 2 * 2 * kPBytes;
   static constexpr int kSmem = kOffBar + 256 + 1024;
   static_assert(kSmem <= 232448, "shared memory");
 };
@@ -65,7 +89,7 @@ struct AttnArgs {
 };
 
 template <int HS>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kAttnThreads, 1)
 k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUtensorMap mQKl,
            const __grid_constant__ CUtensorMap mVh, const __grid_constant__ CUtensorMap mVl,
            const __grid_constant__ CUtensorMap mPh, const __grid_constant__ CUtensorMap mPl,
@@ -75,16 +99,19 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bar = (uint64_t*)(smem + CF::kOffBar);
   uint64_t* q_full = bar;
-  uint64_t* kv_full = bar + 1;   // [2]
-  uint64_t* kv_empty = bar + 3;  // [2]
+  uint64_t* k_full = bar + 1;    // [2]
+  uint64_t* k_empty = bar + 3;   // [2]
   uint64_t* s_full = bar + 5;    // [2]
   uint64_t* s_empty = bar + 7;   // [2]
-  uint64_t* p_full = bar + 9;
-  uint64_t* p_empty = bar + 10;
-  uint64_t* o_full = bar + 11;
-  uint64_t* drain = bar + 12;
-  uint32_t* tmem_slot = (uint32_t*)(bar + 13);
+  uint64_t* p_full = bar + 9;    // [2] one per P half
+  uint64_t* p_empty = bar + 11;  // [2]
+  uint64_t* v_full = bar + 13;
+  uint64_t* v_empty = bar + 14;
+  uint64_t* o_full = bar + 15;
+  uint64_t* drain = bar + 16;
+  uint32_t* tmem_slot = (uint32_t*)(bar + 17);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  float2* stats = (float2*)(smem + CF::kOffStats);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = a.T / AQ;
@@ -98,13 +125,15 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&kv_full[i]), 1);
-      mbar_init(smem_u32(&kv_empty[i]), 1);
+      mbar_init(smem_u32(&k_full[i]), 1);
+      mbar_init(smem_u32(&k_empty[i]), 1);
       mbar_init(smem_u32(&s_full[i]), 1);
-      mbar_init(smem_u32(&s_empty[i]), 4);
+      mbar_init(smem_u32(&s_empty[i]), 8);
+      mbar_init(smem_u32(&p_full[i]), 1);
+      mbar_init(smem_u32(&p_empty[i]), 1);
     }
-    mbar_init(smem_u32(p_full), 1);
-    mbar_init(smem_u32(p_empty), 1);
+    mbar_init(smem_u32(v_full), 1);
+    mbar_init(smem_u32(v_empty), 1);
     mbar_init(smem_u32(o_full), 1);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -122,8 +151,8 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
 
   uint8_t* q_h = smem;
   uint8_t* q_l = smem + CF::kQBytes;
-  uint8_t* p_h = smem + CF::kOffP;
-  uint8_t* p_l = p_h + CF::kPBytes;
+  uint8_t* v_h = smem + CF::kOffV;
+  uint8_t* v_l = v_h + CF::kKBytes;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -135,26 +164,36 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
           tma_load_3d(smem_u32(q_h + off), &mQKh, smem_u32(q_full), sl * 32, row_base + q0 + rh * 64, 0);
           tma_load_3d(smem_u32(q_l + off), &mQKl, smem_u32(q_full), sl * 32, row_base + q0 + rh * 64, 0);
         }
-      int it = 0;
-      for (; it < iters; ++it) {
+      int it = 0, vcount = 0;
+      bool ok = true;
+      for (; it < iters && ok; ++it) {
         const int s = it & 1;
         const uint32_t ph = (it >> 1) & 1;
-        if (it >= 2 && !mbar_wait(smem_u32(&kv_empty[s]), ph ^ 1, abort_flag, a.err, 31)) break;
+        if (it >= 2 && !mbar_wait(smem_u32(&k_empty[s]), ph ^ 1, abort_flag, a.err, 31)) { ok = false; break; }
         const bool pass2 = it >= nkb;
         const int kb = pass2 ? it - nkb : it;
-        uint8_t* st = smem + CF::kOffStage + s * CF::kStageBytes;
-        const uint32_t fb = smem_u32(&kv_full[s]);
-        mbar_expect_tx(fb, pass2 ? CF::kStageBytes : 2 * CF::kKBytes);
+        uint8_t* kst = smem + CF::kOffK + s * 2 * CF::kKBytes;
+        const uint32_t fb = smem_u32(&k_full[s]);
+        mbar_expect_tx(fb, 2 * CF::kKBytes);
         for (int sl = 0; sl < HS / 32; ++sl) {
-          tma_load_3d(smem_u32(st + sl * (AK * 128)), &mQKh, fb, sl * 32, row_base + kb * AK, 1);
-          tma_load_3d(smem_u32(st + CF::kKBytes + sl * (AK * 128)), &mQKl, fb, sl * 32, row_base + kb * AK, 1);
+          tma_load_3d(smem_u32(kst + sl * (AK * 128)), &mQKh, fb, sl * 32, row_base + kb * AK, 1);
+          tma_load_3d(smem_u32(kst + CF::kKBytes + sl * (AK * 128)), &mQKl, fb, sl * 32, row_base + kb * AK, 1);
         }
         if (pass2) {
-          for (int half = 0; half < 2; ++half) {
-            const uint32_t voff = 2 * CF::kKBytes + half * (HS / 32) * 4096;
-            tma_load_4d(smem_u32(st + voff), &mVh, fb, 0, row_base + kb * AK + 32 * half, 0, 2);
-            tma_load_4d(smem_u32(st + CF::kKBytes + voff), &mVl, fb, 0, row_base + kb * AK + 32 * half, 0, 2);
+          // the V buffer is free once the previous block's P V MMAs are done
+          if (vcount > 0 && !mbar_wait(smem_u32(v_empty), (vcount - 1) & 1, abort_flag, a.err, 39)) {
+            ok = false;
+            ++it;   // K of this block is in flight and must be drained
+            break;
           }
+          const uint32_t vb = smem_u32(v_full);
+          mbar_expect_tx(vb, 2 * CF::kKBytes);
+          for (int half = 0; half < 2; ++half) {
+            const uint32_t voff = half * (HS / 32) * 4096;
+            tma_load_4d(smem_u32(v_h + voff), &mVh, vb, 0, row_base + kb * AK + 32 * half, 0, 2);
+            tma_load_4d(smem_u32(v_l + voff), &mVl, vb, 0, row_base + kb * AK + 32 * half, 0, 2);
+          }
+          ++vcount;
         }
       }
       if (*abort_flag) {
@@ -163,7 +202,11 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
         while (!mbar_try(smem_u32(q_full), 0) && gtimer() - t0 < kWaitNs) {}
         for (int qi = it > 2 ? it - 2 : 0; qi < it; ++qi) {
           t0 = gtimer();
-          while (!mbar_try(smem_u32(&kv_full[qi & 1]), (qi >> 1) & 1) && gtimer() - t0 < kWaitNs) {}
+          while (!mbar_try(smem_u32(&k_full[qi & 1]), (qi >> 1) & 1) && gtimer() - t0 < kWaitNs) {}
+        }
+        if (vcount > 0) {
+          t0 = gtimer();
+          while (!mbar_try(smem_u32(v_full), (vcount - 1) & 1) && gtimer() - t0 < kWaitNs) {}
         }
       }
     }
@@ -174,16 +217,15 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
       const uint32_t id_o = idesc_tf32(false, true, HS);
       bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, a.err, 32);
       bool issued = false;
-      int pcount = 0;
       const uint32_t qh = smem_u32(q_h), ql = smem_u32(q_l);
       // S_it = Q K_it^T into TMEM buffer it & 1
       auto issue_s = [&](int it) -> bool {
         const int s = it & 1;
         const uint32_t ph = (it >> 1) & 1;
-        if (!mbar_wait(smem_u32(&kv_full[s]), ph, abort_flag, a.err, 33)) return false;
+        if (!mbar_wait(smem_u32(&k_full[s]), ph, abort_flag, a.err, 33)) return false;
         if (it >= 2 && !mbar_wait(smem_u32(&s_empty[s]), ph ^ 1, abort_flag, a.err, 34)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t kh = smem_u32(smem + CF::kOffStage + s * CF::kStageBytes), kl = kh + CF::kKBytes;
+        const uint32_t kh = smem_u32(smem + CF::kOffK + s * 2 * CF::kKBytes), kl = kh + CF::kKBytes;
         const uint32_t dS = tmem + s * AK;
 #pragma unroll
         for (int kk = 0; kk < HS / 8; ++kk) {
@@ -196,35 +238,37 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
         }
         issued = true;
         mma_commit(smem_u32(&s_full[s]));
+        mma_commit(smem_u32(&k_empty[s]));   // K of this stage is consumed once these finish
         return true;
       };
       ok = ok && issue_s(0);
+      int vcount = 0;
       for (int it = 0; it < iters && ok; ++it) {
         // the next block's scores first, so the softmax warps never wait for them
         if (it + 1 < iters && !issue_s(it + 1)) { ok = false; break; }
-        const int s = it & 1;
-        if (it >= nkb) {
-          // O += P V for the two 32-key halves of this block
-          const uint32_t vh = smem_u32(smem + CF::kOffStage + s * CF::kStageBytes) + 2 * CF::kKBytes;
-          const uint32_t vl = vh + CF::kKBytes;
-          for (int half = 0; half < 2; ++half, ++pcount) {
-            if (!mbar_wait(smem_u32(p_full), pcount & 1, abort_flag, a.err, 35)) { ok = false; break; }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t pvh = vh + half * (HS / 32) * 4096, pvl = vl + half * (HS / 32) * 4096;
+        if (it < nkb) continue;
+        // O += P V, half g from P stage g
+        if (!mbar_wait(smem_u32(v_full), vcount & 1, abort_flag, a.err, 40)) { ok = false; break; }
+        for (int g = 0; g < 2; ++g) {
+          const int pc = vcount;   // uses of each P stage so far
+          if (!mbar_wait(smem_u32(&p_full[g]), pc & 1, abort_flag, a.err, 35)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t ph_ = smem_u32(smem + CF::kOffP + g * 2 * CF::kPBytes), pl_ = ph_ + CF::kPBytes;
+          const uint32_t pvh = smem_u32(v_h) + g * (HS / 32) * 4096, pvl = smem_u32(v_l) + g * (HS / 32) * 4096;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t dph = desc_kmajor(smem_u32(p_h), kk), dpl = desc_kmajor(smem_u32(p_l), kk);
-              const uint64_t dvh = desc_mnmajor(pvh, kk), dvl = desc_mnmajor(pvl, kk);
-              const uint32_t acc0 = (pcount > 0 || kk > 0) ? 1u : 0u;
-              mma_tf32(tmem + 128, dpl, dvh, id_o, acc0);
-              mma_tf32(tmem + 128, dph, dvl, id_o, 1u);
-              mma_tf32(tmem + 128, dph, dvh, id_o, 1u);
-            }
-            mma_commit(smem_u32(p_empty));
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t dph = desc_kmajor(ph_, kk), dpl = desc_kmajor(pl_, kk);
+            const uint64_t dvh = desc_mnmajor(pvh, kk), dvl = desc_mnmajor(pvl, kk);
+            const uint32_t acc0 = (vcount > 0 || g > 0 || kk > 0) ? 1u : 0u;
+            mma_tf32(tmem + 128, dpl, dvh, id_o, acc0);
+            mma_tf32(tmem + 128, dph, dvl, id_o, 1u);
+            mma_tf32(tmem + 128, dph, dvh, id_o, 1u);
           }
-          if (!ok) break;
+          mma_commit(smem_u32(&p_empty[g]));
         }
-        mma_commit(smem_u32(&kv_empty[s]));   // K (and V) of this stage are consumed
+        if (!ok) break;
+        mma_commit(smem_u32(v_empty));
+        ++vcount;
       }
       if (ok) mma_commit(smem_u32(o_full));
       if (!ok && issued) {
@@ -235,106 +279,90 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
       if (!ok) *abort_flag = 1;
     }
   } else {
-    // ---------------- softmax warps ----------------
+    // ---------------- softmax warps: group g owns keys 32g..32g+31 of each block ----------------
     const int quarter = warp & 3;
+    const int g = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;      // TMEM lane == tile row
     const int q = q0 + row;                   // query index in the head
-    const bool issuer = (warp == 2 && lane == 0);
-    float m = -INFINITY, l = 0.0f;
+    const bool issuer = (warp == 2 + 4 * g) && lane == 0;
+    uint8_t* p_h = smem + CF::kOffP + g * 2 * CF::kPBytes;
+    uint8_t* p_l = p_h + CF::kPBytes;
+    float m = -INFINITY, l = 0.0f, inv_l = 0.0f;
     int pcount = 0;
     bool ok = true;
     for (int it = 0; it < iters && ok; ++it) {
       const int s = it & 1;
       const uint32_t ph = (it >> 1) & 1;
       const bool failed = !mbar_wait(smem_u32(&s_full[s]), ph, abort_flag, a.err, 36);
-      if (any128(failed)) { ok = false; break; }
+      if (any256(failed)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const bool pass2 = it >= nkb;
       const int kb = pass2 ? it - nkb : it;
-      uint32_t r[64];
-      const uint32_t taddr = tmem + s * AK + ((uint32_t)(quarter * 32) << 16);
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-            "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-            "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-            "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-            "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-          : "r"(taddr));
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-          : "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]),
-            "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]),
-            "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]),
-            "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]),
-            "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-          : "r"(taddr + 32));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      // scores of this block; keys past the query are masked (exp -> 0)
-      float sv[64];
+      if (it == nkb) {
+        // end of pass 1: combine the two groups' row statistics
+        stats[g * AQ + row] = make_float2(m, l);
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        const float2 o = stats[(1 - g) * AQ + row];
+        const float mm = fmaxf(m, o.x);
+        l = (m == -INFINITY ? 0.0f : l * expf(m - mm)) + (o.x == -INFINITY ? 0.0f : o.y * expf(o.x - mm));
+        m = mm;
+        inv_l = 1.0f / l;
+      }
+      uint32_t r[32];
+      tmem_ld32(tmem + s * AK + 32 * g + ((uint32_t)(quarter * 32) << 16), r);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&s_empty[s]));   // S is in registers
+      float sv[32];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const int key = kb * AK + c;
+      for (int c = 0; c < 32; ++c) {
+        const int key = kb * AK + 32 * g + c;   // keys past the query are masked (exp -> 0)
         sv[c] = key <= q ? __uint_as_float(r[c]) * a.scale : -INFINITY;
       }
       if (!pass2) {
         float bm = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) bm = fmaxf(bm, sv[c]);
+        for (int c = 0; c < 32; ++c) bm = fmaxf(bm, sv[c]);
         const float mn = fmaxf(m, bm);
-        float sum = 0.0f;
+        if (mn != -INFINITY) {
+          float sum = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) sum += expf(sv[c] - mn);
-        l = (m == -INFINITY ? 0.0f : l * expf(m - mn)) + sum;
-        m = mn;
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&s_empty[s]));
+          for (int c = 0; c < 32; ++c) sum += expf(sv[c] - mn);
+          l = (m == -INFINITY ? 0.0f : l * expf(m - mn)) + sum;
+          m = mn;
+        }
         continue;
       }
-      // pass 2: S has been read into registers: release the TMEM buffer, then
-      // p = exp(s - m) / l for the whole block before touching the stage
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&s_empty[s]));
-      const float inv_l = 1.0f / l;
+      // pass 2: p = exp(s - m) / l for this group's 32 keys, then the P stage
 #pragma unroll
-      for (int c = 0; c < 64; ++c) sv[c] = expf(sv[c] - m) * inv_l;
-#pragma unroll
-      for (int half = 0; half < 2; ++half, ++pcount) {
-        // the stage is free once the previous P V MMAs and the previous TMA
-        // store have finished reading it
-        bool failed2 = false;
-        if (issuer) {
-          if (pcount > 0) failed2 = !mbar_wait(smem_u32(p_empty), (pcount - 1) & 1, abort_flag, a.err, 37);
-          bulk_wait_read<0>();
-        }
-        if (any128(failed2)) { ok = false; break; }   // also the barrier before the stage is rewritten
-        float4* rh = reinterpret_cast<float4*>(p_h + row * 128);
-        float4* rl = reinterpret_cast<float4*>(p_l + row * 128);
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          float pv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) pv[e] = sv[32 * half + 4 * g + e];
-          const float4 h4 = make_float4(tf32_rn(pv[0]), tf32_rn(pv[1]), tf32_rn(pv[2]), tf32_rn(pv[3]));
-          rh[g ^ (row & 7)] = h4;
-          rl[g ^ (row & 7)] = make_float4(tf32_rn(pv[0] - h4.x), tf32_rn(pv[1] - h4.y),
-                                          tf32_rn(pv[2] - h4.z), tf32_rn(pv[3] - h4.w));
-        }
-        fence_async_smem();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (issuer) {
-          mbar_arrive(smem_u32(p_full));
-          tma_store_2d(&mPh, smem_u32(p_h), kb * AK + 32 * half, row_base + q0);
-          tma_store_2d(&mPl, smem_u32(p_l), kb * AK + 32 * half, row_base + q0);
-          bulk_commit();
-        }
+      for (int c = 0; c < 32; ++c) sv[c] = expf(sv[c] - m) * inv_l;
+      bool failed2 = false;
+      if (issuer) {
+        if (pcount > 0) failed2 = !mbar_wait(smem_u32(&p_empty[g]), (pcount - 1) & 1, abort_flag, a.err, 37);
+        bulk_wait_read<0>();
       }
+      if (any256(failed2)) { ok = false; break; }   // also: the stage is free for the whole group
+      float4* rh = reinterpret_cast<float4*>(p_h + row * 128);
+      float4* rl = reinterpret_cast<float4*>(p_l + row * 128);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 v = make_float4(sv[4 * j], sv[4 * j + 1], sv[4 * j + 2], sv[4 * j + 3]);
+        const float4 h4 = make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
+        rh[j ^ (row & 7)] = h4;
+        rl[j ^ (row & 7)] = make_float4(tf32_rn(v.x - h4.x), tf32_rn(v.y - h4.y), tf32_rn(v.z - h4.z),
+                                        tf32_rn(v.w - h4.w));
+      }
+      fence_async_smem();
+      group_sync(g);
+      if (issuer) {
+        mbar_arrive(smem_u32(&p_full[g]));
+        tma_store_2d(&mPh, smem_u32(p_h), kb * AK + 32 * g, row_base + q0);
+        tma_store_2d(&mPl, smem_u32(p_l), kb * AK + 32 * g, row_base + q0);
+        bulk_commit();
+      }
+      ++pcount;
     }
-    // O = P V: read the accumulator and write head-unfolded tf32 planes
+    // O = P V: group g reads and writes columns [g*HS/2, (g+1)*HS/2) as head-unfolded tf32 planes
     if (ok && mbar_wait(smem_u32(o_full), 0, abort_flag, a.err, 38)) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int b = z / a.H, h = z % a.H;
@@ -342,18 +370,9 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
       float* oh = a.o_hi + ((size_t)b * a.T + q) * C + (size_t)h * HS;
       float* ol = a.o_lo + ((size_t)b * a.T + q) * C + (size_t)h * HS;
 #pragma unroll
-      for (int c0 = 0; c0 < HS; c0 += 32) {
+      for (int c0 = g * 32; c0 < HS; c0 += 64) {
         uint32_t o[32];
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3]), "=r"(o[4]), "=r"(o[5]), "=r"(o[6]),
-              "=r"(o[7]), "=r"(o[8]), "=r"(o[9]), "=r"(o[10]), "=r"(o[11]), "=r"(o[12]), "=r"(o[13]),
-              "=r"(o[14]), "=r"(o[15]), "=r"(o[16]), "=r"(o[17]), "=r"(o[18]), "=r"(o[19]),
-              "=r"(o[20]), "=r"(o[21]), "=r"(o[22]), "=r"(o[23]), "=r"(o[24]), "=r"(o[25]),
-              "=r"(o[26]), "=r"(o[27]), "=r"(o[28]), "=r"(o[29]), "=r"(o[30]), "=r"(o[31])
-            : "r"(tmem + 128 + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        tmem_ld32(tmem + 128 + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, o);
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const float4 v = make_float4(__uint_as_float(o[j]), __uint_as_float(o[j + 1]),
@@ -403,7 +422,7 @@ void launch_attn(const float* qkv_hi, const float* qkv_lo, int B, int H, int T, 
     attr = true;
   }
   const unsigned grid = (unsigned)(B * H * (T / AQ));
-  k_attn_fwd<HS><<<grid, 192, CF::kSmem, stream()>>>(qh, ql, vh, vl, ph, pl, args);
+  k_attn_fwd<HS><<<grid, kAttnThreads, CF::kSmem, stream()>>>(qh, ql, vh, vl, ph, pl, args);
   count_launch();
   after_launch("k_attn_fwd");
 }
