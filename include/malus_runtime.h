@@ -278,13 +278,30 @@ int32_t malus_dp_destroy(void);
 int32_t malus_jit_translate(const char* msl, char* out, size_t cap);
 int32_t malus_jit_compile_check(const char* msl, char* log, size_t cap);
 /* Fused causal attention forward (tcgen05, 3xTF32): from the tf32 planes of
- * q|k|v laid out [3][B][H][T][hs], writes P = causal_softmax(q k^T * scale) as
- * planes [B*H][T][T] (keys up to each query's 128-wide tile) and O = P v as
- * head-unfolded planes [B*T][H*hs].  Needs T % 128 == 0 and hs in {32, 64}
- * (returns -1 otherwise).  New in this build; replaces the reference's
- * bmm + scale + mask + softmax + bmm sequence of the attention block. */
+ * q|k|v laid out [3][B][H][T][hs], writes O = causal_softmax(q k^T * scale) v
+ * as head-unfolded planes [B*T][H*hs]; optionally the planes of P
+ * [B*H][T][T] (keys up to each query's 128-wide tile; p_hi = p_lo = NULL
+ * skips them) and the per-row statistics `stats` [B*H*T][2] = (row max of the
+ * scaled scores times log2 e, 1 / row sum) that malus_attn_bwd recomputes P
+ * from as 2^(s*scale*log2 e - max) / sum (NULL
+ * skips them).  Needs T % 128 == 0 and hs in {32, 64} (returns -1 otherwise).
+ * New in this build; replaces the reference's bmm + scale + mask + softmax +
+ * bmm sequence of the attention block. */
 int32_t malus_attn_fwd(const float* qkv_hi, const float* qkv_lo, int32_t B, int32_t H, int32_t T,
-                       int32_t hs, float scale, float* p_hi, float* p_lo, float* o_hi, float* o_lo);
+                       int32_t hs, float scale, float* p_hi, float* p_lo, float* o_hi, float* o_lo,
+                       float* stats);
+/* Fused causal attention backward (tcgen05, 3xTF32), the VJP of
+ * malus_attn_fwd: from the q|k|v planes, the planes of dO (head-folded
+ * [B][H][T][hs]) and of O (head-unfolded, as the forward wrote them) and the
+ * forward's `stats`, writes the planes of dq | dk | dv head-unfolded into
+ * dqkv [3][B*T][H*hs].  `D` is a workspace of B*H*T floats (rowsum(dO * O)).
+ * P is recomputed; no [T][T] tensor is touched.  Same shape limits as the
+ * forward (returns -1 otherwise).  New in this build; replaces the reference's
+ * VJPs of that sequence (tape.rs matmul VJP, softmax.ml softmax VJP). */
+int32_t malus_attn_bwd(const float* qkv_hi, const float* qkv_lo, const float* do_hi,
+                       const float* do_lo, const float* o_hi, const float* o_lo, const float* stats,
+                       float* D, int32_t B, int32_t H, int32_t T, int32_t hs, float scale,
+                       float* dqkv_hi, float* dqkv_lo);
 /* Abort the communicator without contacting peers (after one is known lost). */
 int32_t malus_dp_abort(void);
 int32_t malus_dp_world(void);

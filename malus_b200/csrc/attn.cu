@@ -15,7 +15,7 @@
 //   warps 2-9  softmax, two groups of four warps: group g owns keys 32g..32g+31
 //              of every block, one thread per query row (its TMEM lane).
 //              Pass 1: each group's row max and sum (online), combined once.
-//              Pass 2: S recomputed, p = exp(s*scale - m) * (1/l) written into
+//              Pass 2: S recomputed, p = 2^(s*scale*log2 e - m2) * (1/l) written into
 //              the group's own swizzled shared stage, which is both the A
 //              operand of that half's P V MMA and the source of a TMA store of
 //              the P planes (the backward reads them); finally O is read from
@@ -32,6 +32,7 @@ using namespace malus::tc;
 // OR of `v` over the 256 softmax threads (named barrier 1): every exit
 // decision in those warps is collective, so no thread is left at a barrier.
 __device__ __forceinline__ bool any256(bool v) {
+  __syncwarp();   // the barrier needs the warp converged (lane 0 may have waited alone)
   uint32_t r;
   asm volatile(
       "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n"
@@ -43,20 +44,8 @@ __device__ __forceinline__ bool any256(bool v) {
 }
 // barrier among the 128 threads of softmax group g (named barriers 2 and 3)
 __device__ __forceinline__ void group_sync(int g) {
+  __syncwarp();
   asm volatile("bar.sync %0, 128;" ::"r"(2 + g) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 constexpr int AQ = 128;  // query rows per CTA
@@ -85,6 +74,8 @@ struct AttnArgs {
   float scale;
   float* o_hi;
   float* o_lo;
+  float2* stats;   // optional [B*H*T] (row max of the scores in base-2 units, 1 / row sum)
+  int store_p;     // write the P planes
   int32_t* err;
 };
 
@@ -145,6 +136,7 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();   // lane 0 of the producer / MMA warps may arrive alone: reconverge first
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;   // S buffers at columns 0 and 64, O at 128
@@ -217,7 +209,12 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
       const uint32_t id_o = idesc_tf32(false, true, HS);
       bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, a.err, 32);
       bool issued = false;
-      const uint32_t qh = smem_u32(q_h), ql = smem_u32(q_l);
+      // descriptors built once; a stage or k-step adds (byte offset / 16) (the
+      // address field is the low 14 bits, every address is below 256 KB)
+      const uint64_t dqh = desc_kmajor(smem_u32(q_h), 0), dql = desc_kmajor(smem_u32(q_l), 0);
+      const uint64_t dk0 = desc_kmajor(smem_u32(smem + CF::kOffK), 0);
+      const uint64_t dp0 = desc_kmajor(smem_u32(smem + CF::kOffP), 0);
+      const uint64_t dv0 = desc_mnmajor(smem_u32(v_h), 0);
       // S_it = Q K_it^T into TMEM buffer it & 1
       auto issue_s = [&](int it) -> bool {
         const int s = it & 1;
@@ -225,16 +222,15 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
         if (!mbar_wait(smem_u32(&k_full[s]), ph, abort_flag, a.err, 33)) return false;
         if (it >= 2 && !mbar_wait(smem_u32(&s_empty[s]), ph ^ 1, abort_flag, a.err, 34)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t kh = smem_u32(smem + CF::kOffK + s * 2 * CF::kKBytes), kl = kh + CF::kKBytes;
+        const uint64_t kh = dk0 + (uint64_t)(s * (2 * CF::kKBytes / 16)), kl = kh + CF::kKBytes / 16;
         const uint32_t dS = tmem + s * AK;
 #pragma unroll
         for (int kk = 0; kk < HS / 8; ++kk) {
-          const int sl = kk >> 2, sub = kk & 3;
-          const uint64_t dqh = desc_kmajor(qh + sl * (AQ * 128), sub), dql = desc_kmajor(ql + sl * (AQ * 128), sub);
-          const uint64_t dkh = desc_kmajor(kh + sl * (AK * 128), sub), dkl = desc_kmajor(kl + sl * (AK * 128), sub);
-          mma_tf32(dS, dql, dkh, id_s, kk > 0 ? 1u : 0u);
-          mma_tf32(dS, dqh, dkl, id_s, 1u);
-          mma_tf32(dS, dqh, dkh, id_s, 1u);
+          const uint64_t oa = (uint64_t)((kk >> 2) * (AQ * 128 / 16) + (kk & 3) * 2);
+          const uint64_t ob = (uint64_t)((kk >> 2) * (AK * 128 / 16) + (kk & 3) * 2);
+          mma_tf32(dS, dql + oa, kh + ob, id_s, kk > 0 ? 1u : 0u);
+          mma_tf32(dS, dqh + oa, kl + ob, id_s, 1u);
+          mma_tf32(dS, dqh + oa, kh + ob, id_s, 1u);
         }
         issued = true;
         mma_commit(smem_u32(&s_full[s]));
@@ -253,12 +249,12 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
           const int pc = vcount;   // uses of each P stage so far
           if (!mbar_wait(smem_u32(&p_full[g]), pc & 1, abort_flag, a.err, 35)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t ph_ = smem_u32(smem + CF::kOffP + g * 2 * CF::kPBytes), pl_ = ph_ + CF::kPBytes;
-          const uint32_t pvh = smem_u32(v_h) + g * (HS / 32) * 4096, pvl = smem_u32(v_l) + g * (HS / 32) * 4096;
+          const uint64_t ph0 = dp0 + (uint64_t)(g * (2 * CF::kPBytes / 16)), pl0 = ph0 + CF::kPBytes / 16;
+          const uint64_t vh0 = dv0 + (uint64_t)(g * (HS / 32) * (4096 / 16)), vl0 = vh0 + CF::kKBytes / 16;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t dph = desc_kmajor(ph_, kk), dpl = desc_kmajor(pl_, kk);
-            const uint64_t dvh = desc_mnmajor(pvh, kk), dvl = desc_mnmajor(pvl, kk);
+            const uint64_t dph = ph0 + (uint64_t)(kk * 2), dpl = pl0 + (uint64_t)(kk * 2);
+            const uint64_t dvh = vh0 + (uint64_t)(kk * 64), dvl = vl0 + (uint64_t)(kk * 64);
             const uint32_t acc0 = (vcount > 0 || g > 0 || kk > 0) ? 1u : 0u;
             mma_tf32(tmem + 128, dpl, dvh, id_o, acc0);
             mma_tf32(tmem + 128, dph, dvl, id_o, 1u);
@@ -287,7 +283,8 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
     const bool issuer = (warp == 2 + 4 * g) && lane == 0;
     uint8_t* p_h = smem + CF::kOffP + g * 2 * CF::kPBytes;
     uint8_t* p_l = p_h + CF::kPBytes;
-    float m = -INFINITY, l = 0.0f, inv_l = 0.0f;
+    float m = -INFINITY, l = 0.0f, inv_l = 0.0f;   // row max (base-2 units) and sum
+    const float sl2e = a.scale * kLog2e;
     int pcount = 0;
     bool ok = true;
     for (int it = 0; it < iters && ok; ++it) {
@@ -304,38 +301,39 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
         asm volatile("bar.sync 1, 256;" ::: "memory");
         const float2 o = stats[(1 - g) * AQ + row];
         const float mm = fmaxf(m, o.x);
-        l = (m == -INFINITY ? 0.0f : l * expf(m - mm)) + (o.x == -INFINITY ? 0.0f : o.y * expf(o.x - mm));
+        l = (m == -INFINITY ? 0.0f : l * exp2_hw(m - mm)) + (o.x == -INFINITY ? 0.0f : o.y * exp2_hw(o.x - mm));
         m = mm;
         inv_l = 1.0f / l;
+        if (g == 0 && a.stats) a.stats[row_base + q] = make_float2(m, inv_l);
       }
       uint32_t r[32];
       tmem_ld32(tmem + s * AK + 32 * g + ((uint32_t)(quarter * 32) << 16), r);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&s_empty[s]));   // S is in registers
+      // scores in base-2 units: exp(s*scale - m) = 2^(s*scale*log2 e - m2)
+      const int key0 = kb * AK + 32 * g;   // keys past the query are masked (P = 0)
       float sv[32];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int key = kb * AK + 32 * g + c;   // keys past the query are masked (exp -> 0)
-        sv[c] = key <= q ? __uint_as_float(r[c]) * a.scale : -INFINITY;
-      }
       if (!pass2) {
         float bm = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) bm = fmaxf(bm, sv[c]);
+        for (int c = 0; c < 32; ++c)
+          if (key0 + c <= q) bm = fmaxf(bm, __uint_as_float(r[c]) * sl2e);
         const float mn = fmaxf(m, bm);
         if (mn != -INFINITY) {
           float sum = 0.0f;
 #pragma unroll
-          for (int c = 0; c < 32; ++c) sum += expf(sv[c] - mn);
-          l = (m == -INFINITY ? 0.0f : l * expf(m - mn)) + sum;
+          for (int c = 0; c < 32; ++c)
+            sum += key0 + c <= q ? exp2_hw(fmaf(__uint_as_float(r[c]), sl2e, -mn)) : 0.0f;
+          l = (m == -INFINITY ? 0.0f : l * exp2_hw(m - mn)) + sum;
           m = mn;
         }
         continue;
       }
-      // pass 2: p = exp(s - m) / l for this group's 32 keys, then the P stage
+      // pass 2: p = 2^(s2 - m2) / l for this group's 32 keys, then the P stage
 #pragma unroll
-      for (int c = 0; c < 32; ++c) sv[c] = expf(sv[c] - m) * inv_l;
+      for (int c = 0; c < 32; ++c)
+        sv[c] = key0 + c <= q ? exp2_hw(fmaf(__uint_as_float(r[c]), sl2e, -m)) * inv_l : 0.0f;
       bool failed2 = false;
       if (issuer) {
         if (pcount > 0) failed2 = !mbar_wait(smem_u32(&p_empty[g]), (pcount - 1) & 1, abort_flag, a.err, 37);
@@ -356,9 +354,11 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
       group_sync(g);
       if (issuer) {
         mbar_arrive(smem_u32(&p_full[g]));
-        tma_store_2d(&mPh, smem_u32(p_h), kb * AK + 32 * g, row_base + q0);
-        tma_store_2d(&mPl, smem_u32(p_l), kb * AK + 32 * g, row_base + q0);
-        bulk_commit();
+        if (a.store_p) {
+          tma_store_2d(&mPh, smem_u32(p_h), kb * AK + 32 * g, row_base + q0);
+          tma_store_2d(&mPl, smem_u32(p_l), kb * AK + 32 * g, row_base + q0);
+          bulk_commit();
+        }
       }
       ++pcount;
     }
@@ -387,6 +387,7 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
     if (issuer) bulk_wait<0>();   // the P stores have landed before the CTA exits
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();   // lane 0 of the producer / MMA warps may arrive alone: reconverge first
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -396,7 +397,7 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
 
 template <int HS>
 void launch_attn(const float* qkv_hi, const float* qkv_lo, int B, int H, int T, float scale,
-                 float* p_hi, float* p_lo, float* o_hi, float* o_lo) {
+                 float* p_hi, float* p_lo, float* o_hi, float* o_lo, float* stats) {
   using CF = AttnCfg<HS>;
   const uint64_t BHT = (uint64_t)B * H * T;
   const uint64_t plane = BHT * HS * 4;           // bytes of one of q, k, v
@@ -413,9 +414,12 @@ void launch_attn(const float* qkv_hi, const float* qkv_lo, int B, int H, int T, 
   CUtensorMap ql = encode_f32_map(3, qkv_lo, d3, s3, b3, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap vh = encode_f32_map(4, qkv_hi, d4, s4, b4, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   CUtensorMap vl = encode_f32_map(4, qkv_lo, d4, s4, b4, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-  CUtensorMap ph = encode_f32_map(2, p_hi, d2, s2, b2, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap pl = encode_f32_map(2, p_lo, d2, s2, b2, CU_TENSOR_MAP_SWIZZLE_128B);
-  AttnArgs args{H, T, HS, scale, o_hi, o_lo, device_error_word()};
+  // without P planes the P maps are never used; they describe a valid range anyway
+  const bool store_p = p_hi != nullptr;
+  CUtensorMap ph = store_p ? encode_f32_map(2, p_hi, d2, s2, b2, CU_TENSOR_MAP_SWIZZLE_128B) : qh;
+  CUtensorMap pl = store_p ? encode_f32_map(2, p_lo, d2, s2, b2, CU_TENSOR_MAP_SWIZZLE_128B) : ql;
+  AttnArgs args{H, T, HS, scale, o_hi, o_lo, reinterpret_cast<float2*>(stats), store_p ? 1 : 0,
+                device_error_word()};
   static bool attr = false;
   if (!attr) {
     MALUS_CUDA(cudaFuncSetAttribute(k_attn_fwd<HS>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem));
@@ -432,23 +436,27 @@ void launch_attn(const float* qkv_hi, const float* qkv_lo, int B, int H, int T, 
 bool attn_fwd_supported(int T, int hs) { return T % AQ == 0 && (hs == 32 || hs == 64); }
 
 // qkv planes: [3][B][H][T][hs] (q, k, v); P planes [B*H][T][T] (keys up to each
-// query's 128-wide tile written); O planes [B*T][H*hs].
+// query's 128-wide tile written; optional: null skips them); O planes
+// [B*T][H*hs]; stats (optional) [B*H*T] pairs (row max of the scaled scores
+// in base-2 units, i.e. times log2 e; 1 / row sum), which the fused backward
+// recomputes P from.
 void attn_fwd(const float* qkv_hi, const float* qkv_lo, int B, int H, int T, int hs, float scale,
-              float* p_hi, float* p_lo, float* o_hi, float* o_lo) {
+              float* p_hi, float* p_lo, float* o_hi, float* o_lo, float* stats) {
   if (!attn_fwd_supported(T, hs)) panic("attn_fwd: needs T %% 128 == 0 and hs in {32, 64} (T=%d hs=%d)", T, hs);
+  if ((p_hi == nullptr) != (p_lo == nullptr)) panic("attn_fwd: P planes come in pairs");
   for (const void* p : {(const void*)qkv_hi, (const void*)qkv_lo, (const void*)p_hi, (const void*)p_lo,
-                        (const void*)o_hi, (const void*)o_lo})
+                        (const void*)o_hi, (const void*)o_lo, (const void*)stats})
     if ((uintptr_t)p & 15) panic("attn_fwd: buffers must be 16-byte aligned");
-  if (hs == 64) launch_attn<64>(qkv_hi, qkv_lo, B, H, T, scale, p_hi, p_lo, o_hi, o_lo);
-  else launch_attn<32>(qkv_hi, qkv_lo, B, H, T, scale, p_hi, p_lo, o_hi, o_lo);
+  if (hs == 64) launch_attn<64>(qkv_hi, qkv_lo, B, H, T, scale, p_hi, p_lo, o_hi, o_lo, stats);
+  else launch_attn<32>(qkv_hi, qkv_lo, B, H, T, scale, p_hi, p_lo, o_hi, o_lo, stats);
 }
 
 }  // namespace malus
 
 extern "C" int32_t malus_attn_fwd(const float* qkv_hi, const float* qkv_lo, int32_t B, int32_t H,
                                   int32_t T, int32_t hs, float scale, float* p_hi, float* p_lo,
-                                  float* o_hi, float* o_lo) {
+                                  float* o_hi, float* o_lo, float* stats) {
   if (!malus::attn_fwd_supported(T, hs)) return -1;
-  malus::attn_fwd(qkv_hi, qkv_lo, B, H, T, hs, scale, p_hi, p_lo, o_hi, o_lo);
+  malus::attn_fwd(qkv_hi, qkv_lo, B, H, T, hs, scale, p_hi, p_lo, o_hi, o_lo, stats);
   return 0;
 }

@@ -368,6 +368,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();   // a CTA barrier needs converged warps (thread 0 initialised the barriers)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
@@ -443,6 +444,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32(p.a.mn_major, p.b.mn_major, BN);
+      // Descriptors of stage 0's tiles, built once.  A descriptor's address
+      // field is (byte address / 16) in its low 14 bits and every shared
+      // address here is below 256 KB, so a stage or k-step is a plain add of
+      // (byte offset / 16): the issue loop spends no instructions on building
+      // descriptors, and one thread keeps the tensor pipe fed.
+      const uint32_t s0 = smem_u32(smem);
+      const uint64_t da0 = p.a.mn_major ? desc_mn<BK>(s0, 0) : desc_k<BK>(s0, 0);
+      const uint64_t db0 = p.b.mn_major ? desc_mn<BK>(s0 + 2 * kTileBytesA, 0)
+                                        : desc_k<BK>(s0 + 2 * kTileBytesA, 0);
+      const uint32_t ka = p.a.mn_major ? 1024 / 16 : 32 / 16;   // k-step of 8: 8 rows (MN) or 32 B (K)
+      const uint32_t kbs = p.b.mn_major ? 1024 / 16 : 32 / 16;
+      constexpr uint32_t kLoA = kTileBytesA / 16, kLoB = kTileBytesB / 16, kStage16 = kStageBytes / 16;
       uint32_t it = 0, local = 0;
       bool ok = true, issued = false;
       for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
@@ -458,23 +471,21 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
         const uint32_t dacc = tmem + b * BN;
         const int kb_lo = un.kb_lo, kb_hi = un.kb_hi;
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
-          int s = it % STAGES;
-          uint32_t ph = (it / STAGES) & 1;
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, kp.err, 12)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          uint8_t* st = smem + s * kStageBytes;
-          uint32_t ah = smem_u32(st), al = smem_u32(st + kTileBytesA);
-          uint32_t bh = smem_u32(st + 2 * kTileBytesA), bl = bh + kTileBytesB;
+          const uint64_t dah = da0 + (uint64_t)(s * kStage16), dal = dah + kLoA;
+          const uint64_t dbh = db0 + (uint64_t)(s * kStage16), dbl = dbh + kLoB;
+          mma_tf32(dacc, dal, dbh, idesc, kb > kb_lo ? 1u : 0u);   // small terms first
+          mma_tf32(dacc, dah, dbl, idesc, 1u);
+          mma_tf32(dacc, dah, dbh, idesc, 1u);
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            uint64_t dah = p.a.mn_major ? desc_mn<BK>(ah, kk) : desc_k<BK>(ah, kk);
-            uint64_t dal = p.a.mn_major ? desc_mn<BK>(al, kk) : desc_k<BK>(al, kk);
-            uint64_t dbh = p.b.mn_major ? desc_mn<BK>(bh, kk) : desc_k<BK>(bh, kk);
-            uint64_t dbl = p.b.mn_major ? desc_mn<BK>(bl, kk) : desc_k<BK>(bl, kk);
-            uint32_t acc0 = (kb > kb_lo || kk > 0) ? 1u : 0u;
-            mma_tf32(dacc, dal, dbh, idesc, acc0);   // small terms first
-            mma_tf32(dacc, dah, dbl, idesc, 1u);
-            mma_tf32(dacc, dah, dbh, idesc, 1u);
+          for (int kk = 1; kk < BK / 8; ++kk) {
+            const uint64_t oa = (uint64_t)(kk * ka), ob = (uint64_t)(kk * kbs);
+            mma_tf32(dacc, dal + oa, dbh + ob, idesc, 1u);
+            mma_tf32(dacc, dah + oa, dbl + ob, idesc, 1u);
+            mma_tf32(dacc, dah + oa, dbh + ob, idesc, 1u);
           }
           issued = true;
           mma_commit(smem_u32(&empty[s]));   // frees the stage when these MMAs finish
@@ -626,6 +637,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  // lane 0 of the producer and MMA warps ran the role loops alone: the warps
+  // reconverge before the CTA barrier, so no warp counts as arrived early and
+  // TMEM is freed only after every epilogue read
+  __syncwarp();
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");

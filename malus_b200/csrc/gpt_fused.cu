@@ -25,7 +25,10 @@ namespace malus {
 int dp_allreduce_async(float* ptr, size_t count);
 bool attn_fwd_supported(int T, int hs);
 void attn_fwd(const float* qkv_hi, const float* qkv_lo, int B, int H, int T, int hs, float scale,
-              float* p_hi, float* p_lo, float* o_hi, float* o_lo);
+              float* p_hi, float* p_lo, float* o_hi, float* o_lo, float* stats);
+void attn_bwd(const float* qkv_hi, const float* qkv_lo, const float* do_hi, const float* do_lo,
+              const float* o_hi, const float* o_lo, const float* stats, float* D, int B, int H, int T, int hs,
+              float scale, float* dqkv_hi, float* dqkv_lo);
 void dp_join();
 int dp_world();
 
@@ -498,6 +501,10 @@ struct FusedStep {
   std::vector<float*> x;      // L+1 residual stream tensors [M][C]
   std::vector<float*> mean1, var1, mean2, var2, x2, h;  // per layer
   std::vector<Planes> xn1, qkv, P, O, xn2, gel;
+  bool fused_attn = false;     // attention forward by attn_fwd
+  bool fused_attn_bwd = false; // ... and backward by attn_bwd (no [T][T] tensor at all)
+  std::vector<float*> astats;  // per layer [B*H*T][2] row statistics of the fused forward
+  float* arow = nullptr;       // [B*H*T] rowsum(dO * O) workspace of the fused backward
   Planes xf;
   float *meanf, *varf, *logits, *nll;
   Planes dlog;
@@ -651,6 +658,13 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
   f->M = f->B * f->T; f->hs = f->C / f->H; f->C4 = 4 * f->C; f->BH = f->B * f->H;
   f->Vp = (f->V + 3) & ~3;
   f->scale = 1.0f / sqrtf((float)f->hs);
+  // MALUS_ATTN_FUSED=0 keeps the GEMM + softmax attention where the fused kernels
+  // apply; MALUS_ATTN_BWD=1 also takes the backward through the fused kernels
+  // (otherwise the forward keeps P planes for the GEMM backward)
+  const char* fa = getenv("MALUS_ATTN_FUSED");
+  const char* fb = getenv("MALUS_ATTN_BWD");
+  f->fused_attn = attn_fwd_supported(f->T, f->hs) && !(fa && fa[0] == '0');
+  f->fused_attn_bwd = f->fused_attn && fb && fb[0] == '1';
   if (f->C % 32 || f->hs % 4 || f->T % 4 || f->T > 1024 || f->C > 1024)
     panic("fused step needs n_embd %% 32 == 0, head size %% 4 == 0, T %% 4 == 0, T, C <= 1024 "
           "(got C=%d hs=%d T=%d)", f->C, f->hs, f->T);
@@ -674,7 +688,8 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
     f->h.push_back(dalloc(f, M * C4));
     f->xn1.push_back(palloc(f, M * C));
     f->qkv.push_back(palloc(f, 3 * M * C));
-    f->P.push_back(palloc(f, TT));
+    if (f->fused_attn_bwd) f->astats.push_back(dalloc(f, 2 * (size_t)f->BH * f->T));
+    else f->P.push_back(palloc(f, TT));
     f->O.push_back(palloc(f, M * C));
     f->xn2.push_back(palloc(f, M * C));
     f->gel.push_back(palloc(f, M * C4));
@@ -685,8 +700,13 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
   f->logits = dalloc(f, M * f->V);
   f->nll = dalloc(f, M);
   f->dlog = palloc(f, M * f->Vp);
-  f->S = dalloc(f, TT);
-  f->dP = dalloc(f, TT);
+  if (!f->fused_attn) f->S = dalloc(f, TT);
+  if (f->fused_attn_bwd) {
+    f->arow = dalloc(f, (size_t)f->BH * f->T);
+  } else {
+    f->dP = dalloc(f, TT);
+    f->dS = palloc(f, TT);
+  }
   f->dxf = dalloc(f, M * C);
   f->dxn = dalloc(f, M * C);
   f->g_a = dalloc(f, M * C);
@@ -696,7 +716,6 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
   f->dh = palloc(f, M * C4);
   f->dO = palloc(f, M * C);
   f->dqkv = palloc(f, 3 * M * C);
-  f->dS = palloc(f, TT);
   f->part_blocks = kNumSMs * 2;
   f->part = dalloc(f, (size_t)f->part_blocks * C);
   f->emb_tmp = dalloc(f, (size_t)f->V * C);
@@ -742,10 +761,15 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
          op(W(b + 1), C, C, C, true, 3, (int64_t)C * C, kZMNSeg, C), kEpiStore, none,
          L(T, (int64_t)H * T * hs, 0, 0, hs), L(C, (int64_t)B * H * T * hs, hs, (int64_t)T * hs, 1),
          nullptr, f->qkv[l], nullptr);
-    if (attn_fwd_supported(T, hs)) {
-      // S, causal softmax and O = P V in one kernel (P planes kept for the backward)
+    if (f->fused_attn_bwd) {
+      // S, causal softmax and O = P V in one kernel; the row statistics let the
+      // backward recompute P
+      attn_fwd(f->qkv[l].hi, f->qkv[l].lo, B, H, T, hs, f->scale, nullptr, nullptr, f->O[l].hi, f->O[l].lo,
+               f->astats[l]);
+    } else if (f->fused_attn) {
+      // the same kernel, keeping the P planes for the GEMM backward
       attn_fwd(f->qkv[l].hi, f->qkv[l].lo, B, H, T, hs, f->scale, f->P[l].hi, f->P[l].lo, f->O[l].hi,
-               f->O[l].lo);
+               f->O[l].lo, nullptr);
     } else {
     // S = Q K^T * scale
     gemm(T, T, hs, BH, op(f->qkv[l], T, hs, hs, false, BH, (int64_t)T * hs, kZBatch),
@@ -826,6 +850,11 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
          L(T, (int64_t)H * T * hs, 0, 0, hs), L(hs, (int64_t)T * hs, 0, 0, 1), nullptr, f->dO, nullptr);
     gemm(C, C, M, 1, op(f->O[l], M, C, C, true), op(g2p, M, C, C, true), kEpiStore, none, rowC, unit,
          G(b + 4), Planes{}, nullptr);
+    if (f->fused_attn_bwd) {
+      // dq | dk | dv planes (head-unfolded into dqkv) with P recomputed
+      attn_bwd(f->qkv[l].hi, f->qkv[l].lo, f->dO.hi, f->dO.lo, f->O[l].hi, f->O[l].lo, f->astats[l], f->arow,
+               B, H, T, hs, f->scale, f->dqkv.hi, f->dqkv.lo);
+    } else {
     // dP = dO V^T ; dV = P^T dO
     gemm(T, T, hs, BH, op(f->dO, T, hs, hs, false, BH, (int64_t)T * hs, kZBatch),
          op(f->qkv[l], T, hs, hs, false, BH, (int64_t)T * hs, kZBatch, 0, 2 * MC), kEpiStore,
@@ -846,6 +875,7 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     gemm(T, hs, T, BH, op(f->dS, T, T, T, true, BH, (int64_t)TT, kZBatch),
          op(f->qkv[l], T, hs, hs, true, BH, (int64_t)T * hs, kZBatch), kEpiStore,
          L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, dqkv1, nullptr, 1.0f, kCausalAUpper);
+    }
     // dxn1 = sum_j dqkv_j W_j^T (K segments) ; dW_j = xn1^T dqkv_j (N segments)
     gemm(M, C, 3 * C, 1, op(f->dqkv, M, C, C, false, 3, (int64_t)MC, kZKSeg, C),
          op(W(b + 1), C, C, C, false, 3, (int64_t)C * C, kZKSeg, C), kEpiStore, none, rowC, unit,

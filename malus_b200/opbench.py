@@ -212,18 +212,32 @@ def plane_cases(b: Bench, rng):
     ]
     for name, q, (Mm, N, K, batch, nout, aux) in cases_:
         yield name, (lambda q=q: run(q)), nbytes(q, Mm, N, K, batch, nout, aux), 2.0 * Mm * N * K * batch
-    # fused causal attention forward at the C4 shape: q|k|v planes in, P and O planes out
+    # fused causal attention at the C4 shape: q|k|v planes in, O planes and row
+    # statistics out (the step's form; P planes are not written)
     qh, ql = buf(3, Bz, H, T, hs), buf(3, Bz, H, T, hs)
-    ph, pl = buf(Bz * H, T, T, rand=False), buf(Bz * H, T, T, rand=False)
     oh, ol = buf(Mt, Cc, rand=False), buf(Mt, Cc, rand=False)
+    st = buf(Bz * H * T, 2, rand=False)
 
     def attn():
-        lib.malus_attn_fwd(qh, ql, Bz, H, T, hs, C.c_float(0.125), ph, pl, oh, ol)
+        lib.malus_attn_fwd(qh, ql, Bz, H, T, hs, C.c_float(0.125), None, None, oh, ol, st)
         return 0
-    causal = 0.75   # key blocks up to the diagonal (T = 256, 128-row query blocks)
+    causal = 0.5 * (1 + 128 / T)   # score entries up to each query's 128-wide tile
     yield ("attn fwd fused (causal, C4)", attn,
-           8 * 3 * Mt * Cc + 8 * Bz * H * T * T * causal + 8 * Mt * Cc,
-           2.0 * 2 * Bz * H * T * T * hs * causal)
+           8 * 3 * Mt * Cc + 8 * Mt * Cc + 8 * Bz * H * T,
+           2.0 * 2 * Bz * H * T * T * hs * 0.5)
+    # backward: dq | dk | dv planes from q|k|v, dO and O planes and the statistics
+    dh, dl = buf(Bz * H, T, hs), buf(Bz * H, T, hs)
+    dw = buf(Bz * H * T, rand=False)
+    gh, gl = buf(3, Mt, Cc, rand=False), buf(3, Mt, Cc, rand=False)
+    attn()
+    lib.gpu_barrier()
+
+    def attn_bwd():
+        lib.malus_attn_bwd(qh, ql, dh, dl, oh, ol, st, dw, Bz, H, T, hs, C.c_float(0.125), gh, gl)
+        return 0
+    yield ("attn bwd fused (causal, C4)", attn_bwd,
+           8 * 3 * Mt * Cc + 8 * 2 * Mt * Cc + 8 * 3 * Mt * Cc + 12 * Bz * H * T,
+           2.0 * 5 * Bz * H * T * T * hs * 0.5)
 
 
 def run(only: str | None = None, reps: int = 20, verbose: bool = True) -> tuple[list[dict], dict]:

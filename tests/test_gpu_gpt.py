@@ -10,6 +10,9 @@ pytestmark = pytest.mark.gpu
 
 TOY = dict(vocab=65, n_layer=2, n_head=4, n_embd=64, block_size=32, batch=4)
 C3 = dict(vocab=65, n_layer=4, n_head=4, n_embd=128, block_size=64, batch=16)
+# shapes the fused attention kernels take (T % 128 == 0; hs 64 and 32)
+A128 = dict(vocab=65, n_layer=2, n_head=2, n_embd=128, block_size=128, batch=2)
+A256 = dict(vocab=65, n_layer=1, n_head=4, n_embd=128, block_size=256, batch=2)
 
 
 def batches(cfg, n, seed=7):
@@ -117,7 +120,7 @@ def test_fused_and_tape_modes_agree(M):
 
 @pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("tied", [False, True])
-@pytest.mark.parametrize("cfg", [TOY, C3], ids=["toy", "c3"])
+@pytest.mark.parametrize("cfg", [TOY, C3, A128, A256], ids=["toy", "c3", "attn128", "attn256"])
 def test_gradients_match_oracle(M, orc, cfg, tied, mode):
     """Every parameter's first-step gradient against the oracle's, normwise per tensor."""
     orc.set_threads(os.cpu_count())
@@ -133,12 +136,14 @@ def test_gradients_match_oracle(M, orc, cfg, tied, mode):
     o.close()
 
 
+@pytest.mark.parametrize("T", [64, 128])
 @pytest.mark.parametrize("tied", [False, True])
-def test_graph_replay_matches_eager_bitwise(M, tied):
+def test_graph_replay_matches_eager_bitwise(M, tied, T):
     """The fused step captured once as a CUDA graph and replayed gives the same
     bits as launching it eagerly (same kernels, same arguments; the AdamW bias
-    corrections come from a device step counter)."""
-    cfg = dict(vocab=65, n_layer=2, n_head=4, n_embd=128, block_size=64, batch=4)
+    corrections come from a device step counter).  T = 128 runs the fused
+    attention kernels, which are deterministic (no atomics)."""
+    cfg = dict(vocab=65, n_layer=2, n_head=4, n_embd=128, block_size=T, batch=4)
     a = M.GPT(**cfg, lr=1e-3, mode=1, use_graph=0, tied=tied)
     b = M.GPT(**cfg, lr=1e-3, mode=1, use_graph=1, tied=tied)
     for x, y in batches(cfg, 6, seed=5):
@@ -166,3 +171,45 @@ def test_fused_wide_vocab_tied_matches_oracle(M, orc):
     assert abs(lg[0] - lo[0]) / lo[0] < 1e-5, (lg, lo)
     assert np.max(np.abs(lg - lo) / lo) < 5e-3, (lg, lo)
     check_params(pg, po, lr=1e-3)
+
+
+@pytest.mark.parametrize("tied", [False, True])
+@pytest.mark.parametrize("cfg", [A128, A256], ids=["attn128", "attn256"])
+def test_fused_attention_backward_gradients_match_oracle(M, orc, cfg, tied, monkeypatch):
+    """The step with the fused attention backward (P recomputed from the
+    forward's row statistics, MALUS_ATTN_BWD=1): first-step gradients against
+    the oracle's, as for the GEMM backward."""
+    monkeypatch.setenv("MALUS_ATTN_BWD", "1")
+    orc.set_threads(os.cpu_count())
+    g = M.GPT(**cfg, tied=tied, lr=1e-3, mode=1)
+    o = orc.Gpt(**cfg, tied=tied, lr=1e-3)
+    x, y = batches(cfg, 1)[0]
+    g.step(x, y)
+    o.step(x, y)
+    for i, (a, b) in enumerate(zip(g.grads(), o.grads())):
+        e = np.max(np.abs(a.ravel().astype(np.float64) - b)) / np.max(np.abs(b))
+        assert e < 3e-5, (i, e)
+    g.close()
+    o.close()
+
+
+def test_fused_attention_backward_graph_c4_architecture(M, orc, monkeypatch):
+    """C4's architecture with the fused attention backward, replayed as a graph:
+    losses and parameters track the oracle; graph replay is bitwise equal to
+    eager launches."""
+    monkeypatch.setenv("MALUS_ATTN_BWD", "1")
+    cfg = dict(vocab=65, n_layer=6, n_head=6, n_embd=384, block_size=256, batch=2)
+    lg, lo, pg, po = run_pair(M, orc, cfg, 4, mode=1, lr=1e-3, use_graph=1, wd=0.01, beta2=0.99)
+    assert abs(lg[0] - lo[0]) / lo[0] < 1e-5, (lg, lo)
+    assert np.max(np.abs(lg - lo) / lo) < 5e-3, (lg, lo)
+    check_params(pg, po, lr=1e-3)
+    small = dict(vocab=65, n_layer=2, n_head=4, n_embd=128, block_size=128, batch=4)
+    a = M.GPT(**small, lr=1e-3, mode=1, use_graph=0)
+    b = M.GPT(**small, lr=1e-3, mode=1, use_graph=1)
+    for x, y in batches(small, 5, seed=5):
+        la, lb = a.step(x, y), b.step(x, y)
+        assert la == lb, (la, lb)
+    for pa, pb in zip(a.params(), b.params()):
+        assert np.array_equal(pa, pb)
+    a.close()
+    b.close()
