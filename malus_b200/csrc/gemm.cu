@@ -136,7 +136,7 @@ using namespace malus::tc;
 
 constexpr int BM = 128;
 constexpr int kEpiWarpFloats = 32 * 32;   // per-warp 32x32 staging block (XOR-swizzled granules)
-// Tile shape: width BN (128 or 192) and k-block depth BK (32 or 16).  A wider
+// Tile shape: width BN (64, 128, 192 or 256) and k-block depth BK (32 or 16).  A wider
 // tile reads each A k-block once for more columns (less shared-memory and L2
 // traffic per FLOP); a shallower k-block makes stages smaller, so more of them
 // fit and the TMA latency is covered further ahead.  K-major tiles use the
@@ -825,26 +825,34 @@ int splitk_for(int tiles, int nk) {
   return std::max(1, std::min({kNumSMs / tiles, nk / 8, 64}));
 }
 
-// Tile shape (measured on the C4 GEMMs): width 192 when N is a whole number of
-// 192-wide tiles and the grid is either full or split along K (every C4 layer
-// GEMM: N = 384, 1152, 1536), else 128.  k-block depth 16 with the 192-wide
-// tile (four stages instead of two) except for stores of tf32 planes, which
-// measured faster at 32; 32 with the 128-wide tile.  MALUS_GEMM_BN / _BK
-// override for tuning.
+// Tile shape (measured on the C4 GEMMs): width 256 when N is a whole number of
+// 256-wide tiles and the problem splits along K (the N = 1536 weight gradient;
+// for full grids such as MLP up it measured no faster and the GELU backward
+// slower), else 192 when N is a whole number of 192-wide tiles and the grid is
+// either full or split along K (N = 384, 1152, 1536), else 128.  k-block depth 16 with the 192- and 256-wide tiles
+// (four stages instead of two) except for stores of tf32 planes, which measured
+// faster at 32; 32 with the 128-wide tile.  MALUS_GEMM_BN / _BK override for
+// tuning (192 also keeps N % 256 == 0 problems at 192).
 struct TileShape { int bn, bk; };
 TileShape tile_shape_for(const TcProblem& pr) {
   static int forced_bn = [] { const char* e = getenv("MALUS_GEMM_BN"); return e ? atoi(e) : 0; }();
   static int forced_bk = [] { const char* e = getenv("MALUS_GEMM_BK"); return e ? atoi(e) : 0; }();
   int bn = 128;
+  auto fills = [&](int w) {   // w-wide tiles fill the SMs, or the problem splits along K
+    long tiles = (long)((pr.M + BM - 1) / BM) * (pr.N / w) * pr.batch;
+    return tiles >= kNumSMs || splitk_for((int)tiles, (pr.K + 15) / 16) > 1;
+  };
   if (forced_bn == 128 || forced_bn == 192) {
     bn = forced_bn;
   } else if (pr.N <= 64) {
     bn = 64;                       // attention outputs (N = head size): no idle half tile
-  } else if (!pr.causal && pr.N % 192 == 0) {
-    long tiles = (long)((pr.M + BM - 1) / BM) * (pr.N / 192) * pr.batch;
-    if (tiles >= kNumSMs || splitk_for((int)tiles, (pr.K + 15) / 16) > 1) bn = 192;
+  } else if (!pr.causal && pr.N % 256 == 0 && forced_bn != 192 &&
+             splitk_for((int)((pr.M + BM - 1) / BM * (pr.N / 256) * pr.batch), (pr.K + 15) / 16) > 1) {
+    bn = 256;   // split-K (weight gradients): measured 11 % faster than 192 at C4's dW1
+  } else if (!pr.causal && pr.N % 192 == 0 && fills(192)) {
+    bn = 192;
   }
-  int bk = (bn == 192 && !(pr.epi == kEpiStore && pr.out_hi)) ? 16 : 32;
+  int bk = (bn >= 192 && !(pr.epi == kEpiStore && pr.out_hi)) ? 16 : 32;
   if (forced_bk == 16 || forced_bk == 32) bk = forced_bk;
   return {bn, bk};
 }
@@ -983,6 +991,8 @@ void gemm_tc_planes(const TcProblem& pr) {
     default: launch_tc<kEpiSoftmaxBwd, BN_, BK_>(ah, al, bh, bl, kp, grid); break;   \
   }
   if (BN == 64) { MALUS_TC_EPI_SWITCH(64, 32) }
+  else if (BN == 256 && BK == 16) { MALUS_TC_EPI_SWITCH(256, 16) }
+  else if (BN == 256) { MALUS_TC_EPI_SWITCH(256, 32) }
   else if (BN == 192 && BK == 16) { MALUS_TC_EPI_SWITCH(192, 16) }
   else if (BN == 192) { MALUS_TC_EPI_SWITCH(192, 32) }
   else if (BK == 16) { MALUS_TC_EPI_SWITCH(128, 16) }

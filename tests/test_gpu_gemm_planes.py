@@ -78,7 +78,8 @@ def err(got, ref, a, b):
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
 @pytest.mark.parametrize("Mm,N,K", [(300, 200, 130), (512, 384, 384), (1024, 65, 384), (129, 1536, 64),
-                                    (32, 16, 16), (32, 32, 16), (64, 16, 32), (40, 24, 20)])
+                                    (32, 16, 16), (32, 32, 16), (64, 16, 32), (40, 24, 20),
+                                    (3200, 1536, 96)])   # a full grid of 192-wide tiles
 def test_majors(M, rt, rng, a_mn, b_mn, Mm, N, K):
     A = rng.standard_normal((Mm, K)).astype(np.float32)
     B = rng.standard_normal((K, N)).astype(np.float32)
@@ -117,8 +118,8 @@ def test_planes_only_output(M, rt, rng):
     assert err(got, A.astype(np.float64) @ B, A, B) < 1e-4
 
 
-def test_residual_gelu_gelubwd(M, rt, rng):
-    Mm, N, K = 384, 512, 128
+@pytest.mark.parametrize("Mm,N,K", [(384, 512, 128), (3200, 1536, 96)])   # 128- and 192-wide tiles
+def test_residual_gelu_gelubwd(M, rt, rng, Mm, N, K):
     A = rng.standard_normal((Mm, K)).astype(np.float32) * 0.5
     B = rng.standard_normal((K, N)).astype(np.float32) * 0.5
     ref = A.astype(np.float64) @ B
@@ -361,3 +362,31 @@ def test_softmax_backward_epilogue(M, rt, rng):
     bound = scale * P * (np.einsum("ztd,zkd->ztk", np.abs(dO).astype(np.float64), np.abs(V)) + np.abs(D)[..., None])
     low = np.tril(np.ones((T, T), bool))
     assert np.max((np.abs(got - ref) / np.maximum(bound, 1e-30))[:, low]) < 1e-5
+
+
+def test_splitk_256_wide_tiles_epilogues(M, rt, rng):
+    """Split-K problem with N % 256 == 0 (the 256-wide tile): plain store,
+    residual, GELU (f32 + planes) and GELU-backward epilogues after the
+    deterministic reduction."""
+    Mm, N, K = 256, 512, 8192
+    A = rng.standard_normal((K, Mm)).astype(np.float32) * 0.1
+    B = rng.standard_normal((K, N)).astype(np.float32) * 0.1
+    ao, bo = operand(M, rt, A, True), operand(M, rt, B, True)
+    ref = A.T.astype(np.float64) @ B
+    out = dev(M, np.zeros((Mm, N)))
+    run(M, rt, Mm, N, K, 1, ao, bo, out=out)
+    assert err(out.numpy(), ref, A.T, B) < 1e-4
+    R = rng.standard_normal((Mm, N)).astype(np.float32)
+    rs = dev(M, R)
+    run(M, rt, Mm, N, K, 1, ao, bo, epi=1, out=out, aux=rs)
+    assert err(out.numpy() - R, ref, A.T, B) < 2e-4
+    hi, lo = dev(M, np.zeros((Mm, N))), dev(M, np.zeros((Mm, N)))
+    run(M, rt, Mm, N, K, 1, ao, bo, epi=2, out=out, out_hi=hi, out_lo=lo)
+    g = 0.5 * ref * (1 + np.tanh(0.7978845608028654 * (ref + 0.044715 * ref ** 3)))
+    assert np.max(np.abs(hi.numpy().astype(np.float64) + lo.numpy() - g)) < 1e-4 * np.max(np.abs(ref))
+    run(M, rt, Mm, N, K, 1, ao, bo, epi=3, out=out, out_hi=hi, out_lo=lo, aux=rs)
+    x = R.astype(np.float64)
+    t = np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3))
+    gp = 0.7978845608028654 * (1 + 3 * 0.044715 * x * x)
+    dref = ref * (0.5 * (1 + t) + 0.5 * x * (1 - t * t) * gp)
+    assert np.max(np.abs(out.numpy() - dref) / (np.abs(A.T) @ np.abs(B) + 1e-9)) < 2e-4
