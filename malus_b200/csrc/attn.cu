@@ -100,7 +100,8 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
   uint64_t* v_empty = bar + 14;
   uint64_t* o_full = bar + 15;
   uint64_t* drain = bar + 16;
-  uint32_t* tmem_slot = (uint32_t*)(bar + 17);
+  uint64_t* done = bar + 17;   // the eight softmax warps finished reading TMEM
+  uint32_t* tmem_slot = (uint32_t*)(bar + 18);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   float2* stats = (float2*)(smem + CF::kOffStats);
 
@@ -127,6 +128,7 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
     mbar_init(smem_u32(v_empty), 1);
     mbar_init(smem_u32(o_full), 1);
     mbar_init(smem_u32(drain), 1);
+    mbar_init(smem_u32(done), 8);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -385,11 +387,16 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
       }
     }
     if (issuer) bulk_wait<0>();   // the P stores have landed before the CTA exits
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(done));
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncwarp();   // lane 0 of the producer / MMA warps may arrive alone: reconverge first
   __syncthreads();
   if (warp == 1) {
+    // TMEM is freed only after every softmax warp said it finished reading it
+    mbar_wait_bounded(smem_u32(done), 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
   }

@@ -339,7 +339,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
   uint64_t* accf = empty + STAGES;
   uint64_t* acce = accf + 2;
   uint64_t* drain = acce + 2;
-  uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+  uint64_t* done = drain + 1;   // every epilogue warp finished reading TMEM
+  uint32_t* tmem_slot = (uint32_t*)(done + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -358,6 +359,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       mbar_init(smem_u32(&acce[b]), epi_warps(EPI));
     }
     mbar_init(smem_u32(drain), 1);
+    mbar_init(smem_u32(done), epi_warps(EPI));
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -635,14 +637,19 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acce[b]));
     }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(done));
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   // lane 0 of the producer and MMA warps ran the role loops alone: the warps
-  // reconverge before the CTA barrier, so no warp counts as arrived early and
-  // TMEM is freed only after every epilogue read
+  // reconverge before the CTA barrier
   __syncwarp();
   __syncthreads();
   if (warp == 1) {
+    // TMEM is freed only after every epilogue warp said it finished reading it
+    // (an explicit barrier: the CTA barrier alone was seen to release early)
+    mbar_wait_bounded(smem_u32(done), 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols));

@@ -48,6 +48,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile 
     }
   }
 }
+// Bounded wait without error reporting (exit paths: draining copies and MMAs,
+// waiting for the TMEM readers before freeing TMEM).
+__device__ __forceinline__ void mbar_wait_bounded(uint32_t a, uint32_t parity) {
+  const uint64_t t0 = gtimer();
+  while (!mbar_try(a, parity) && gtimer() - t0 < kWaitNs) {}
+}
 __device__ __forceinline__ void mbar_arrive(uint32_t a) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
 }
