@@ -300,7 +300,7 @@ def main():
 
     cfg, workload_name = WORKLOADS[args.workload]
     cfg = dict(cfg)
-    model = M.GPT(**cfg, **OPT, mode=args.mode, use_graph=args.graph if args.mode == 1 else 0, seed=0)
+    model = M.GPT(**cfg, **OPT, mode=args.mode, use_graph=args.graph, seed=0)
     m = cfg["batch"] * cfg["block_size"]
     rng = np.random.default_rng(1000 + rank)
     nb = args.steps + args.warmup

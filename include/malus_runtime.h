@@ -302,6 +302,21 @@ int32_t malus_attn_bwd(const float* qkv_hi, const float* qkv_lo, const float* do
                        const float* do_lo, const float* o_hi, const float* o_lo, const float* stats,
                        float* D, int32_t B, int32_t H, int32_t T, int32_t hs, float scale,
                        float* dqkv_hi, float* dqkv_lo);
+/* Graph capture of the runtime stream (the caller side of the boundary: one
+ * launch per training step).  Between malus_graph_begin and malus_graph_end
+ * every runtime call is recorded instead of executed; malus_graph_replay
+ * launches the recording on the runtime stream.  Replays run on the buffers
+ * of the capture: the pool keeps every buffer the graph touches out of reuse
+ * until malus_graph_destroy, a replayed step must update its state in place
+ * and read its inputs from tensors that stay alive (write new inputs with
+ * malus_tensor_write between replays), and host reads inside the capture
+ * abort with a message.  Run the sequence once before capturing it so that
+ * grow-on-demand workspaces are sized.  New in this build (no reference
+ * counterpart: Metal command buffers are re-encoded every step). */
+int32_t malus_graph_begin(void);
+int64_t malus_graph_end(void);            /* graph id (> 0) */
+int32_t malus_graph_replay(int64_t graph);   /* -1 for an unknown id */
+int32_t malus_graph_destroy(int64_t graph);
 /* Abort the communicator without contacting peers (after one is known lost). */
 int32_t malus_dp_abort(void);
 int32_t malus_dp_world(void);

@@ -183,6 +183,10 @@ SIGNATURES: dict[str, tuple] = {
     "malus_jit_compile_check": (i32, [C.c_char_p, C.c_char_p, sz]),
     "malus_attn_fwd": (i32, [vp, vp, i32, i32, i32, i32, f32, vp, vp, vp, vp, vp]),
     "malus_attn_bwd": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, vp, vp]),
+    "malus_graph_begin": (i32, []),
+    "malus_graph_end": (i64, []),
+    "malus_graph_replay": (i32, [i64]),
+    "malus_graph_destroy": (i32, [i64]),
     "malus_dp_abort": (i32, []),
     "malus_dp_world": (i32, []),
     "malus_gpt_create": (i64, [C.POINTER(GptConfig)]),

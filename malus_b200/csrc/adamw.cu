@@ -13,6 +13,8 @@
 // applied to the raw gradient first (exact when world is a power of two).
 #include "common.cuh"
 
+#include <vector>
+
 namespace malus {
 namespace {
 
@@ -117,6 +119,29 @@ void adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float l
       p, g, m, v, n / 4, lr, b1, b2, eps, wd, c1, c2, grad_scale, bc_tab, step_dev, hi, lo);
   count_launch();
   after_launch("k_adamw_flat");
+}
+
+namespace {
+__global__ void k_step_advance(int64_t* step) { *step += 1; }
+}  // namespace
+
+// One more optimizer step on the device counter the table-driven AdamW reads
+// (a captured step replays it, so every replay is a new step).
+void step_advance(int64_t* step_dev) {
+  k_step_advance<<<1, 1, 0, stream()>>>(step_dev);
+  count_launch();
+  after_launch("k_step_advance");
+}
+
+// Bias corrections 1 - beta**t for t = 1..cap, as the host path computes them
+// (f32 powf), laid out [2*(t-1)] = bc1, [2*(t-1)+1] = bc2.
+std::vector<float> adam_bc_table(float b1, float b2, int64_t cap) {
+  std::vector<float> h((size_t)cap * 2);
+  for (int64_t t = 1; t <= cap; ++t) {
+    h[2 * (t - 1)] = 1.0f - powf(b1, (float)t);
+    h[2 * (t - 1) + 1] = 1.0f - powf(b2, (float)t);
+  }
+  return h;
 }
 
 void adamw_multi(const AdamSeg* segs, int nseg, float lr, float b1, float b2, float eps, float wd,

@@ -209,6 +209,8 @@ void gemm_force_backend(int b);            // -1 = auto (tests)
 
 // ---- optimizer (adamw.cu) ----
 struct AdamSeg { float* p; const float* g; float* m; float* v; int64_t n; };
+void step_advance(int64_t* step_dev);
+std::vector<float> adam_bc_table(float b1, float b2, int64_t cap);
 void adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1,
                 float b2, float eps, float wd, float grad_scale, const float* bc_tab,
                 const int64_t* step_dev, float* hi, float* lo);

@@ -872,6 +872,10 @@ float* splitk_workspace(size_t floats) {
   MALUS_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 16) panic("split-K workspace: device index %d out of range", dev);
   if (floats > cap[dev]) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    MALUS_CUDA(cudaStreamIsCapturing(stream(), &cs));
+    if (cs != cudaStreamCaptureStatusNone)
+      panic("split-K workspace must grow during graph capture: run the sequence once before capturing it");
     MALUS_CUDA(cudaStreamSynchronize(stream()));   // the old buffer may still be in use
     if (buf[dev]) MALUS_CUDA(cudaFree(buf[dev]));
     MALUS_CUDA(cudaMalloc(&buf[dev], floats * sizeof(float)));

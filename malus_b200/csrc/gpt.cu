@@ -56,6 +56,12 @@ struct Model {
   float* loss_pin = nullptr;
   int64_t step = 0;
   FusedStep* fused = nullptr;
+  // tape mode: AdamW's step counter on the device and the bias-correction
+  // table it indexes (so a captured step replays as a new step); the graph
+  int64_t* step_dev = nullptr;
+  float* bc_tab = nullptr;
+  int64_t bc_cap = 0;
+  int64_t graph = 0;
 };
 
 int64_t wrap(float* p, std::initializer_list<size_t> shape) {
@@ -211,10 +217,26 @@ void tape_step(Model& m) {
     dp_join();
     gscale = 1.0f / (float)dp_world();
   }
-  m.step++;
-  malus_adamw_multi(m.params.data(), grads.data(), m.ms.data(), m.vs.data(), nparam, m.cfg.lr,
-                    m.cfg.beta1, m.cfg.beta2, m.cfg.eps, m.cfg.wd, m.step, gscale);
+  // the fused multi-tensor AdamW (malus_adamw_multi's kernel) with the bias
+  // corrections read from the table at the device step counter
+  std::vector<AdamSeg> segs(nparam);
+  for (size_t i = 0; i < nparam; ++i)
+    segs[i] = AdamSeg{fptr(m.params[i]), fptr(grads[i]), fptr(m.ms[i]), fptr(m.vs[i]), (int64_t)m.sizes[i]};
+  step_advance(m.step_dev);
+  adamw_multi_tab(segs.data(), (int)nparam, m.cfg.lr, m.cfg.beta1, m.cfg.beta2, m.cfg.eps, m.cfg.wd, 0.0f,
+                  0.0f, gscale, m.bc_tab, m.step_dev);
   for (int64_t g : grads) tensor_release(g);
+}
+
+void tape_bc_table(Model& m, int64_t cap) {
+  const std::vector<float> h = adam_bc_table(m.cfg.beta1, m.cfg.beta2, cap);
+  if (m.bc_tab) {
+    MALUS_CUDA(cudaStreamSynchronize(stream()));
+    MALUS_CUDA(cudaFree(m.bc_tab));
+  }
+  MALUS_CUDA(cudaMalloc(&m.bc_tab, h.size() * sizeof(float)));
+  MALUS_CUDA(cudaMemcpy(m.bc_tab, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+  m.bc_cap = cap;
 }
 
 // Under data parallelism, wait (bounded) for this step's collectives before a
@@ -368,6 +390,9 @@ int64_t malus_gpt_create(const malus_gpt_config* cfgp) {
   std::vector<int32_t> pos(m->M);
   for (size_t i = 0; i < m->M; ++i) pos[i] = (int32_t)(i % m->T);
   m->pos_h = tensor_alloc_gpu(MALUS_I32, sm, 1, reinterpret_cast<const float*>(pos.data()));
+  MALUS_CUDA(cudaMalloc(&m->step_dev, sizeof(int64_t)));
+  MALUS_CUDA(cudaMemsetAsync(m->step_dev, 0, sizeof(int64_t), stream()));
+  tape_bc_table(*m, 1 << 16);
   if (c.mode == 1) {
     std::vector<float*> ps;
     for (size_t i = 0; i < m->params.size(); ++i) ps.push_back(m->pbuf + m->offs[i]);
@@ -380,6 +405,9 @@ int64_t malus_gpt_create(const malus_gpt_config* cfgp) {
 void malus_gpt_destroy(int64_t h) {
   auto* m = reinterpret_cast<Model*>(h);
   gpu_barrier();
+  if (m->graph) malus_graph_destroy(m->graph);
+  cudaFree(m->step_dev);
+  cudaFree(m->bc_tab);
   if (m->fused) fused_destroy(m->fused);
   for (int64_t p : m->params) tensor_release(p);
   for (int64_t p : m->ms) tensor_release(p);
@@ -404,7 +432,25 @@ void malus_gpt_step_device(int64_t h, const int32_t* x_dev, const int32_t* y_dev
     m->step++;
     fused_train_step(m->fused, m->x_dev, m->y_dev, m->loss_dev);
   } else {
-    tape_step(*m);
+    m->step++;
+    if (m->step > m->bc_cap) {   // a new table (new address): the captured step is stale
+      if (m->graph) malus_graph_destroy(m->graph);
+      m->graph = 0;
+      tape_bc_table(*m, m->bc_cap * 4);
+    }
+    // The reference's call sequence captured once (after one eager step sized
+    // every workspace) as a CUDA graph through the runtime's graph API and
+    // replayed: the caller side of the boundary, one launch per step.
+    if (m->cfg.use_graph && !prof_on() && !sync_dispatch() && m->step > 1) {
+      if (!m->graph) {
+        malus_graph_begin();
+        tape_step(*m);
+        m->graph = malus_graph_end();
+      }
+      malus_graph_replay(m->graph);
+    } else {
+      tape_step(*m);
+    }
   }
 }
 

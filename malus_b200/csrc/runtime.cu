@@ -18,6 +18,7 @@
 #include <string>
 #include <thread>
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 namespace malus {
@@ -126,6 +127,28 @@ bool capturing() {
   return st != cudaStreamCaptureStatusNone;
 }
 
+// Graph capture (malus_graph_begin .. malus_graph_end).  While the runtime
+// stream is being captured, buffers freed go to the session's own free lists
+// (reusable by later allocations of the same capture: one stream, so the
+// graph runs them in capture order) instead of the pool, and every buffer
+// handed out is recorded.  At the end the graph keeps all of them: a buffer
+// the graph touches is never given to another tensor while the graph exists
+// (a release of such a buffer is deferred to malus_graph_destroy).
+struct GraphRec;
+struct CaptureSession {
+  bool active = false;
+  std::unordered_map<size_t, std::vector<void*>> free_lists;
+  std::vector<std::pair<void*, size_t>> touched;
+};
+CaptureSession g_cap;                           // guarded by g_pool.mu
+std::unordered_map<void*, GraphRec*> g_pinned;  // buffer -> graph that uses it (g_pool.mu)
+
+struct GraphRec {
+  cudaGraphExec_t exec = nullptr;
+  std::vector<std::pair<void*, size_t>> held;   // buffers returned to the pool at destroy
+  std::vector<void*> pinned;
+};
+
 void trim_pool_locked() {
   if (capturing()) return;
   MALUS_CUDA(cudaStreamSynchronize(g_ctx.stream));
@@ -142,6 +165,16 @@ void* pool_get(size_t bytes, size_t* bucket_out) {
   size_t b = bucket_of(bytes);
   *bucket_out = b;
   std::lock_guard<std::mutex> lk(g_pool.mu);
+  if (g_cap.active) {
+    auto ct = g_cap.free_lists.find(b);
+    if (ct != g_cap.free_lists.end() && !ct->second.empty()) {
+      void* p = ct->second.back();
+      ct->second.pop_back();
+      g_pool.hits++;
+      g_pool.live += (int64_t)b;
+      return p;
+    }
+  }
   auto it = g_pool.free_lists.find(b);
   if (it != g_pool.free_lists.end() && !it->second.empty()) {
     void* p = it->second.back();
@@ -149,6 +182,7 @@ void* pool_get(size_t bytes, size_t* bucket_out) {
     g_pool.hits++;
     g_pool.pooled -= (int64_t)b;
     g_pool.live += (int64_t)b;
+    if (g_cap.active) g_cap.touched.emplace_back(p, b);
     return p;
   }
   g_pool.misses++;
@@ -164,11 +198,24 @@ void* pool_get(size_t bytes, size_t* bucket_out) {
   }
   g_pool.live += (int64_t)b;
   if (g_pool.live + g_pool.pooled > g_pool.peak) g_pool.peak = g_pool.live + g_pool.pooled;
+  if (g_cap.active) g_cap.touched.emplace_back(p, b);
   return p;
 }
 
 void pool_put(void* p, size_t bucket) {
   std::lock_guard<std::mutex> lk(g_pool.mu);
+  auto pin = g_pinned.find(p);
+  if (pin != g_pinned.end()) {          // a captured graph still uses it
+    pin->second->held.emplace_back(p, bucket);
+    g_pinned.erase(pin);
+    g_pool.live -= (int64_t)bucket;
+    return;
+  }
+  if (g_cap.active) {                   // reusable within the capture only
+    g_cap.free_lists[bucket].push_back(p);
+    g_pool.live -= (int64_t)bucket;
+    return;
+  }
   g_pool.free_lists[bucket].push_back(p);
   g_pool.live -= (int64_t)bucket;
   g_pool.pooled += (int64_t)bucket;
@@ -280,6 +327,9 @@ using namespace malus;
 extern "C" {
 
 int64_t tensor_alloc_gpu(int32_t dtype, const size_t* shape, size_t ndims, const float* data) {
+  if (data && capturing())
+    panic("tensor_alloc_gpu with host data during graph capture: upload into an existing tensor "
+          "(malus_tensor_write) before malus_graph_replay instead");
   int64_t h = alloc(dtype, shape, (int)ndims);
   auto* t = tb(h);
   if (data && t->len > 0) {
@@ -367,6 +417,9 @@ void tensor_print(int64_t h) {
 }
 
 void gpu_barrier(void) {
+  if (capturing())
+    panic("host read or synchronisation during graph capture (between malus_graph_begin and "
+          "malus_graph_end): read results after malus_graph_replay instead");
   cudaError_t e = cudaStreamSynchronize(stream());
   if (e != cudaSuccess)
     panic("GPU stream failed: %s (set MALUS_SYNC_DISPATCH=1 to attribute the failing op)",
@@ -396,14 +449,24 @@ int64_t tensor_reshape(int64_t h, const size_t* dims, size_t ndims) {
   return make_handle(t->dtype, dims, (int)ndims, t->st, t->len);
 }
 
+// metal.rs:1601-1612 fills the [T,T] additive mask on the host (0 on and
+// below the diagonal, -1e9 above); the same values are written by a kernel
+// here, so the mask costs no host work or synchronisation (and can be
+// captured in a graph).
+__global__ void k_causal_mask(float* d, size_t T) {
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < T * T) d[i] = (i % T) > (i / T) ? -1e9f : 0.0f;
+}
+
 int64_t tensor_causal_mask(int64_t tsz) {
   size_t T = (size_t)tsz;
-  std::vector<float> d(T * T, 0.0f);
-  for (size_t i = 0; i < T; ++i)
-    for (size_t j = i + 1; j < T; ++j) d[i * T + j] = -1e9f;
   size_t shape[2] = {T, T};
-  int64_t h = tensor_alloc_gpu(MALUS_F32, shape, 2, d.data());
-  gpu_barrier();  // d is a stack vector; make sure the copy has consumed it
+  int64_t h = alloc(MALUS_F32, shape, 2);
+  if (T) {
+    k_causal_mask<<<(unsigned)((T * T + 255) / 256), 256, 0, stream()>>>(fptr(h), T);
+    count_launch();
+    after_launch("k_causal_mask");
+  }
   return h;
 }
 
@@ -633,6 +696,94 @@ int32_t malus_device_error(void) {
   gpu_barrier();
   if (v) MALUS_CUDA(cudaMemsetAsync(device_error_word(), 0, 4, stream()));
   return v;
+}
+
+// ------------------------------------------------------------ graph capture
+// Capture a sequence of runtime calls on the runtime stream into a CUDA graph
+// and replay it (the caller side of the boundary: one training step becomes one
+// launch).  Replays run on the same buffers as the capture, so a replayed
+// step must update its state in place (malus_adamw_multi, malus_tensor_write
+// of the next inputs) and its inputs must stay alive while the graph exists;
+// host reads are not allowed inside the capture.  Run the sequence once
+// before capturing it so that grow-on-demand workspaces are sized.
+namespace {
+std::unordered_map<int64_t, GraphRec*> g_graphs;
+int64_t g_graph_next = 1;
+}  // namespace
+
+int32_t malus_graph_begin(void) {
+  ensure_init();
+  {
+    std::lock_guard<std::mutex> lk(g_pool.mu);
+    if (g_cap.active) panic("malus_graph_begin: a capture is already open");
+    g_cap.active = true;
+  }
+  MALUS_CUDA(cudaStreamBeginCapture(stream(), cudaStreamCaptureModeRelaxed));
+  return 0;
+}
+
+int64_t malus_graph_end(void) {
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(stream(), &graph);
+  auto* rec = new GraphRec();
+  {
+    std::lock_guard<std::mutex> lk(g_pool.mu);
+    if (!g_cap.active) panic("malus_graph_end without malus_graph_begin");
+    std::unordered_set<void*> freed;
+    for (auto& kv : g_cap.free_lists)
+      for (void* p : kv.second) {
+        rec->held.emplace_back(p, kv.first);
+        freed.insert(p);
+      }
+    for (auto& pb : g_cap.touched) {
+      if (!freed.count(pb.first)) {      // still live in a tensor: pinned until destroy
+        g_pinned[pb.first] = rec;
+        rec->pinned.push_back(pb.first);
+      }
+    }
+    g_cap = CaptureSession();
+  }
+  if (e != cudaSuccess || graph == nullptr)
+    panic("graph capture failed: %s (an operation in the captured sequence cannot be captured)",
+          cudaGetErrorString(e));
+  MALUS_CUDA(cudaGraphInstantiate(&rec->exec, graph, 0));
+  MALUS_CUDA(cudaGraphDestroy(graph));
+  const int64_t id = g_graph_next++;
+  g_graphs[id] = rec;
+  return id;
+}
+
+int32_t malus_graph_replay(int64_t id) {
+  auto it = g_graphs.find(id);
+  if (it == g_graphs.end()) return -1;
+  MALUS_CUDA(cudaGraphLaunch(it->second->exec, stream()));
+  count_launch(1);
+  return 0;
+}
+
+int32_t malus_graph_destroy(int64_t id) {
+  auto it = g_graphs.find(id);
+  if (it == g_graphs.end()) return -1;
+  GraphRec* rec = it->second;
+  g_graphs.erase(it);
+  MALUS_CUDA(cudaStreamSynchronize(stream()));   // replays in flight still use the buffers
+  MALUS_CUDA(cudaGraphExecDestroy(rec->exec));
+  std::vector<std::pair<void*, size_t>> back;
+  {
+    std::lock_guard<std::mutex> lk(g_pool.mu);
+    for (void* p : rec->pinned) {
+      auto pin = g_pinned.find(p);
+      if (pin != g_pinned.end() && pin->second == rec) g_pinned.erase(pin);
+    }
+    back.swap(rec->held);
+  }
+  for (auto& pb : back) {   // the pool takes back what the graph held
+    std::lock_guard<std::mutex> lk(g_pool.mu);
+    g_pool.free_lists[pb.second].push_back(pb.first);
+    g_pool.pooled += (int64_t)pb.second;
+  }
+  delete rec;
+  return 0;
 }
 
 // ------------------------------------------------------------- bench timer
