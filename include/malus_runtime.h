@@ -267,6 +267,17 @@ int32_t malus_dp_init(int32_t rank, int32_t world, const uint8_t* nccl_id, int32
 /* In-place sum-allreduce of a contiguous f32 device buffer on the DP stream. */
 int32_t malus_dp_allreduce_f32(void* dev_ptr, size_t count);
 int32_t malus_dp_finish(void);   /* wait for outstanding collectives */
+/* Per-leaf gradient readiness (overlaps the gradient all-reduce with the
+ * backward pass).  Register the leaves (parameters) once, in order; they are
+ * grouped into buckets of at least bucket_bytes (returns the bucket count,
+ * -1 if a leaf is listed twice).  After that the tape's backward reports each
+ * registered leaf as soon as its gradient is final and averages every
+ * completed bucket in place across ranks (one grouped all-reduce on the DP
+ * stream); callers that build gradients outside the tape report them with
+ * malus_dp_grad_ready(leaf, grad) (grad 0: no gradient this round).  All
+ * ranks must report the same leaves in the same order. */
+int32_t malus_dp_register_leaves(const int64_t* leaves, size_t n, size_t bucket_bytes);
+int32_t malus_dp_grad_ready(int64_t leaf, int64_t grad);
 int32_t malus_dp_destroy(void);
 /* User kernel bodies.  malus_runtime_init accepts, for any id, either a native
  * kernel name or the MSL text that malus-codegen-gpu emits for a `kernel`

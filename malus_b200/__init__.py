@@ -188,6 +188,8 @@ SIGNATURES: dict[str, tuple] = {
     "malus_graph_replay": (i32, [i64]),
     "malus_graph_destroy": (i32, [i64]),
     "malus_dp_abort": (i32, []),
+    "malus_dp_register_leaves": (i32, [P_i64, sz, sz]),
+    "malus_dp_grad_ready": (i32, [i64, i64]),
     "malus_dp_world": (i32, []),
     "malus_gpt_create": (i64, [C.POINTER(GptConfig)]),
     "malus_gpt_destroy": (None, [i64]),

@@ -210,6 +210,11 @@ void gemm_force_backend(int b);            // -1 = auto (tests)
 // ---- optimizer (adamw.cu) ----
 struct AdamSeg { float* p; const float* g; float* m; float* v; int64_t n; };
 void step_advance(int64_t* step_dev);
+// data parallelism: per-leaf gradient readiness (dp.cu)
+bool dp_leaves_registered();
+bool dp_is_leaf(int64_t h);
+int dp_leaf_ready(int64_t leaf, int64_t grad);
+int dp_leaves_join();
 std::vector<float> adam_bc_table(float b1, float b2, int64_t cap);
 void adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1,
                 float b2, float eps, float wd, float grad_scale, const float* bc_tab,

@@ -14,6 +14,8 @@
 #include <nccl.h>
 #include <chrono>
 #include <thread>
+#include <unordered_map>
+#include <vector>
 
 namespace malus {
 namespace {
@@ -75,6 +77,80 @@ void dp_join() {
   if (g_world <= 1 || !g_comm) return;
   MALUS_CUDA(cudaEventRecord(g_ev_done, g_dp_stream));
   MALUS_CUDA(cudaStreamWaitEvent(stream(), g_ev_done, 0));
+}
+
+// ---- per-leaf readiness (malus_dp_register_leaves / malus_dp_grad_ready) ----
+// Registered leaves are grouped, in registration order, into buckets of at
+// least `bucket_bytes`.  A leaf becomes ready when its gradient is final; when
+// the last leaf of a bucket is ready, the bucket's gradients are averaged in
+// place across ranks by one grouped NCCL all-reduce on the DP stream, after
+// everything already queued on the main stream (the gradients' producers).
+// Every rank reports the same leaves in the same order (the tape walk is
+// deterministic), so every rank launches the same buckets in the same order.
+namespace {
+struct DpLeafReg {
+  std::unordered_map<int64_t, int> bucket_of;      // leaf -> bucket
+  std::vector<int> need;                           // leaves per bucket
+  std::vector<int> have;                           // reported this round
+  std::vector<std::vector<std::pair<float*, size_t>>> pending;   // gradients per bucket
+  std::vector<int64_t> held;                       // gradient handles retained until dp_leaves_join
+  std::vector<int64_t> first_leaf;                 // one leaf of each bucket
+};
+DpLeafReg g_reg;
+}  // namespace
+
+bool dp_leaves_registered() { return g_world > 1 && g_comm && !g_reg.bucket_of.empty(); }
+bool dp_is_leaf(int64_t h) { return g_reg.bucket_of.count(h) > 0; }
+
+int dp_leaf_ready(int64_t leaf, int64_t grad) {
+  if (g_world <= 1 || !g_comm) return 0;
+  auto it = g_reg.bucket_of.find(leaf);
+  if (it == g_reg.bucket_of.end()) return -7;
+  const int b = it->second;
+  if (grad) {
+    tensor_retain(grad);
+    g_reg.held.push_back(grad);
+    g_reg.pending[(size_t)b].emplace_back(fptr(grad), tb(grad)->len);
+  }
+  if (++g_reg.have[(size_t)b] < g_reg.need[(size_t)b]) return 0;
+  // the bucket is complete: one grouped all-reduce of its gradients
+  auto& items = g_reg.pending[(size_t)b];
+  g_reg.have[(size_t)b] = 0;
+  if (items.empty()) return 0;
+  MALUS_CUDA(cudaEventRecord(g_ev_ready, stream()));
+  MALUS_CUDA(cudaStreamWaitEvent(g_dp_stream, g_ev_ready, 0));
+  ncclResult_t r = ncclGroupStart();
+  for (auto& pc : items)
+    if (r == ncclSuccess || r == ncclInProgress)
+      r = ncclAllReduce(pc.first, pc.first, pc.second, ncclFloat, ncclAvg, g_comm, g_dp_stream);
+  ncclResult_t e = ncclGroupEnd();
+  items.clear();
+  if ((r != ncclSuccess && r != ncclInProgress) || (e != ncclSuccess && e != ncclInProgress)) {
+    fprintf(stderr, "malus: bucket all-reduce failed: %s\n", ncclGetErrorString(r != ncclSuccess ? r : e));
+    return -5;
+  }
+  if ((r == ncclInProgress || e == ncclInProgress) && wait_comm(g_timeout_ms) != 0) {
+    abort_comm();
+    return -4;
+  }
+  return 0;
+}
+
+// Launch every bucket that was only partly reported this round (its other
+// leaves received no gradient), make the main stream wait for all the
+// bucket reductions, and drop the gradients' extra references.
+int dp_leaves_join() {
+  if (!dp_leaves_registered()) return 0;
+  int rc = 0;
+  for (size_t b = 0; b < g_reg.need.size() && rc == 0; ++b)
+    if (g_reg.have[b] != 0) {
+      g_reg.have[b] = g_reg.need[b] - 1;
+      rc = dp_leaf_ready(g_reg.first_leaf[b], 0);
+    }
+  dp_join();
+  for (int64_t h : g_reg.held) tensor_release(h);
+  g_reg.held.clear();
+  return rc;
 }
 
 }  // namespace malus
@@ -174,6 +250,31 @@ int32_t malus_dp_destroy(void) {
 }
 
 int32_t malus_dp_world(void) { return g_world; }
+
+int32_t malus_dp_register_leaves(const int64_t* leaves, size_t n, size_t bucket_bytes) {
+  g_reg = DpLeafReg();
+  size_t acc = 0;
+  int b = -1;
+  for (size_t i = 0; i < n; ++i) {
+    if (b < 0 || acc >= bucket_bytes) {
+      ++b;
+      acc = 0;
+      g_reg.need.push_back(0);
+      g_reg.have.push_back(0);
+      g_reg.pending.emplace_back();
+      g_reg.first_leaf.push_back(leaves[i]);
+    }
+    if (!g_reg.bucket_of.emplace(leaves[i], b).second) {
+      g_reg = DpLeafReg();
+      return -1;   // a leaf listed twice
+    }
+    g_reg.need[(size_t)b]++;
+    acc += tb(leaves[i])->len * 4;
+  }
+  return b + 1;   // number of buckets
+}
+
+int32_t malus_dp_grad_ready(int64_t leaf, int64_t grad) { return dp_leaf_ready(leaf, grad); }
 
 // Local teardown after a peer is known to be gone: ncclCommAbort needs no peer.
 int32_t malus_dp_abort(void) {

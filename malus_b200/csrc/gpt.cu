@@ -62,6 +62,7 @@ struct Model {
   float* bc_tab = nullptr;
   int64_t bc_cap = 0;
   int64_t graph = 0;
+  bool dp_registered = false;
 };
 
 int64_t wrap(float* p, std::initializer_list<size_t> shape) {
@@ -164,6 +165,14 @@ int64_t block_forward(Model& m, int l, int64_t x) {
 
 void tape_step(Model& m) {
   size_t nparam = m.params.size();
+  // Under data parallelism the parameters are the tape's registered leaves:
+  // backward averages each bucket of their gradients across ranks as soon as
+  // the walk has finished them (buckets of about one layer).
+  if (dp_world() > 1 && !m.dp_registered) {
+    if (malus_dp_register_leaves(m.params.data(), nparam, (size_t)4 << 20) <= 0)
+      panic("data parallelism: registering the parameters failed");
+    m.dp_registered = true;
+  }
   tape_zero_grad(m.params.data(), nparam);
   const int64_t* top = &m.params[(size_t)m.L * 8];
   int64_t wte = top[0], wpe = top[1], lnf = top[2];
@@ -211,12 +220,7 @@ void tape_step(Model& m) {
     tensor_release(grads[i]);
     grads[i] = wrap(m.gbuf + m.offs[i], {m.sizes[i]});
   }
-  float gscale = 1.0f;
-  if (dp_world() > 1) {
-    if (dp_allreduce_async(m.gbuf, m.total) != 0) panic("data-parallel all-reduce failed");
-    dp_join();
-    gscale = 1.0f / (float)dp_world();
-  }
+  const float gscale = 1.0f;   // gradients are already averaged across ranks
   // the fused multi-tensor AdamW (malus_adamw_multi's kernel) with the bias
   // corrections read from the table at the device step counter
   std::vector<AdamSeg> segs(nparam);

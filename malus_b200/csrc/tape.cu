@@ -250,6 +250,23 @@ void backward(int64_t loss) {
   }
   auto need = [&](int64_t h) { return live.count(h) > 0; };
 
+  // Data parallelism (malus_dp_register_leaves): a registered leaf's gradient
+  // is final once the earliest node (in forward order) that reads it has been
+  // processed by this reverse walk; it is reported then, so its bucket's
+  // all-reduce overlaps the rest of the backward pass.
+  const bool dp = dp_leaves_registered();
+  std::unordered_map<size_t, std::vector<int64_t>> final_after;
+  if (dp) {
+    std::unordered_set<int64_t> seen;
+    for (size_t i = 0; i < nodes.size(); ++i) {
+      const Node& n = nodes[i];
+      size_t nin = n.saved.size();
+      if (n.op == kLayernorm || n.op == kCrossEntropy || n.op == kEmbedding) nin = 1;
+      for (size_t k = 0; k < nin; ++k)
+        if (dp_is_leaf(n.saved[k]) && seen.insert(n.saved[k]).second) final_after[i].push_back(n.saved[k]);
+    }
+  }
+
   std::unordered_map<int64_t, int64_t> grads;
   {
     auto* t = tb(loss);
@@ -258,6 +275,17 @@ void backward(int64_t loss) {
 
   for (auto it = nodes.rbegin(); it != nodes.rend(); ++it) {
     const Node& n = *it;
+    if (dp) {
+      // leaves whose earliest reader is the node after this one are final now
+      const size_t after = nodes.size() - (size_t)(it - nodes.rbegin());
+      auto fa = final_after.find(after);
+      if (fa != final_after.end())
+        for (int64_t leaf : fa->second) {
+          auto g = grads.find(leaf);
+          if (dp_leaf_ready(leaf, g == grads.end() ? 0 : g->second) != 0)
+            panic("data-parallel gradient all-reduce failed (peer lost or timed out)");
+        }
+    }
     auto gi = grads.find(n.output);
     if (gi == grads.end()) continue;
     int64_t dout = gi->second;
@@ -357,6 +385,17 @@ void backward(int64_t loss) {
       }
       default: panic("backward: unhandled op tag %d", n.op);
     }
+  }
+
+  if (dp) {
+    auto fa = final_after.find(0);   // leaves first read by node 0
+    if (fa != final_after.end())
+      for (int64_t leaf : fa->second) {
+        auto g = grads.find(leaf);
+        if (dp_leaf_ready(leaf, g == grads.end() ? 0 : g->second) != 0)
+          panic("data-parallel gradient all-reduce failed (peer lost or timed out)");
+      }
+    if (dp_leaves_join() != 0) panic("data-parallel gradient all-reduce failed (peer lost or timed out)");
   }
 
   // Fold leaf grads into the persistent registry (accumulate semantics).

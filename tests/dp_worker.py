@@ -1,7 +1,9 @@
 """One data-parallel rank for tests/test_gpu_dp.py (run under torchrun).
 
-  parity: a few fused steps on this rank's token shard; writes its losses and
-          (rank 0) the final parameters.
+  parity: a few training steps (fused, or the tape replay whose backward
+          averages each bucket of parameter gradients as soon as it is final)
+          on this rank's token shard; writes its losses and (rank 0) the final
+          parameters.
   leave:  rank 1 finishes step 0 and leaves between steps (nothing in flight);
           rank 0 must learn of it on the host (Liveness) before launching any
           collective of step 1, abort its communicator locally and report.
@@ -26,6 +28,7 @@ def main():
     ap.add_argument("--out", required=True)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--graph", type=int, default=0)
+    ap.add_argument("--model-mode", type=int, default=1)   # 0: tape (per-leaf bucketed all-reduce), 1: fused
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -42,7 +45,7 @@ def main():
                     prefix="dpw")
     m = CFG["batch"] * CFG["block_size"]
     xs, ys = shard_tokens(11, rank, CFG["vocab"], m, args.steps)
-    g = M.GPT(**CFG, lr=1e-3, mode=1, use_graph=args.graph)
+    g = M.GPT(**CFG, lr=1e-3, mode=args.model_mode, use_graph=args.graph)
     out = Path(args.out)
     if args.mode == "parity":
         losses = []
