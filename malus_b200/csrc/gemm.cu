@@ -195,6 +195,8 @@ struct TcKernelParams {
   int bn;          // tile width (the kernel's BN)
   int bk;          // k-block depth (the kernel's BK)
   int a_chunked, b_chunked;   // MN-major operand loaded as one {32, 32 K, 4 chunks} box per plane
+  int a_pair, b_pair;         // both planes of a stage's tile in one box (a plane dimension)
+  int a_swap, b_swap;         // ... whose plane 0 is the lo plane (it is the lower address)
   int staged;                 // epilogue through the smem transpose (see epi_warps)
   int32_t* err;
 };
@@ -404,8 +406,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
             tma_load_4d(smem_u32(st + kTileBytesA), &mAl, fb, 0, kc, mnc >> 5, zc);
           } else if (!p.a.mn_major && p.a.zmode != kZMNSeg) {
             operand_coords(p.a.zmode, p.a.seg, z, k0, m0, &kc, &mnc, &zc);
-            tma_load_3d(smem_u32(st), &mAh, fb, kc, mnc, zc);
-            tma_load_3d(smem_u32(st + kTileBytesA), &mAl, fb, kc, mnc, zc);
+            if (kp.a_pair) {
+              tma_load_3d(smem_u32(st), &mAh, fb, kc, mnc, 0);   // unbatched: the third coordinate is the plane
+            } else {
+              tma_load_3d(smem_u32(st), &mAh, fb, kc, mnc, zc);
+              tma_load_3d(smem_u32(st + kTileBytesA), &mAl, fb, kc, mnc, zc);
+            }
           } else {
             for (int j = 0; j < BM / 32; ++j) {
               operand_coords(p.a.zmode, p.a.seg, z, k0, m0 + 32 * j, &kc, &mnc, &zc);
@@ -419,6 +425,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
             operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
             tma_load_4d(smem_u32(sb), &mBh, fb, 0, kc, mnc >> 5, zc);
             tma_load_4d(smem_u32(sb + kTileBytesB), &mBl, fb, 0, kc, mnc >> 5, zc);
+          } else if (!p.b.mn_major && p.b.zmode != kZMNSeg && kp.b_pair) {
+            operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
+            tma_load_3d(smem_u32(sb), &mBh, fb, kc, mnc, 0);   // unbatched: the third coordinate is the plane
           } else if (!p.b.mn_major && p.b.zmode != kZMNSeg) {
             operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
             tma_load_3d(smem_u32(sb), &mBh, fb, kc, mnc, zc);
@@ -458,6 +467,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       const uint32_t ka = p.a.mn_major ? 1024 / 16 : 32 / 16;   // k-step of 8: 8 rows (MN) or 32 B (K)
       const uint32_t kbs = p.b.mn_major ? 1024 / 16 : 32 / 16;
       constexpr uint32_t kLoA = kTileBytesA / 16, kLoB = kTileBytesB / 16, kStage16 = kStageBytes / 16;
+      // which tile of a stage holds which plane (a paired box puts the lower
+      // address first, which may be the lo plane)
+      const uint64_t a_hi = kp.a_swap ? kLoA : 0, a_lo = kp.a_swap ? 0 : kLoA;
+      const uint64_t b_hi = kp.b_swap ? kLoB : 0, b_lo = kp.b_swap ? 0 : kLoB;
       uint32_t it = 0, local = 0;
       bool ok = true, issued = false;
       for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
@@ -477,8 +490,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, kp.err, 12)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint64_t dah = da0 + (uint64_t)(s * kStage16), dal = dah + kLoA;
-          const uint64_t dbh = db0 + (uint64_t)(s * kStage16), dbl = dbh + kLoB;
+          const uint64_t sa = da0 + (uint64_t)(s * kStage16), sbb = db0 + (uint64_t)(s * kStage16);
+          const uint64_t dah = sa + a_hi, dal = sa + a_lo, dbh = sbb + b_hi, dbl = sbb + b_lo;
           mma_tf32(dacc, dal, dbh, idesc, kb > kb_lo ? 1u : 0u);   // small terms first
           mma_tf32(dacc, dah, dbl, idesc, 1u);
           mma_tf32(dacc, dah, dbh, idesc, 1u);
@@ -804,6 +817,40 @@ CUtensorMap chunked_map(const TcOperand& o, const float* plane, uint64_t pitch_b
   return m;
 }
 
+// Both planes of an operand in one tensor map: one more (outermost) dimension,
+// the plane, whose stride is the distance between the planes and whose base
+// is the lower one; a stage's hi and lo tiles then arrive in one box (half the
+// TMA requests: each box carries a fixed issue cost on top of its bytes).
+// Used only for K-major, unsegmented operands whose every box lies inside the
+// tensor (rows a multiple of the tile, K a multiple of the k-block), with the
+// distance a multiple of 16 bytes below 2^40.  The MN-major chunked view is
+// never paired: a paired 5-D box reaching past a batched operand's columns
+// made an illegal memory access.
+bool pair_planes(const TcOperand& o, int tile_mn, int bk, bool* swap, uint64_t* delta) {
+  const bool whole = !o.mn_major && o.zmode == kZNone && o.rows % tile_mn == 0 && o.cols % bk == 0;
+  const uint64_t h = (uint64_t)(uintptr_t)o.hi, l = (uint64_t)(uintptr_t)o.lo;
+  const uint64_t d = h > l ? h - l : l - h;
+  if (!whole || d == 0 || d % 16 || d >= (1ull << 40)) return false;
+  *swap = l < h;
+  *delta = d;
+  return true;
+}
+
+CUtensorMap paired_map(const TcOperand& o, int tile_mn, int bk, uint64_t delta) {
+  const uint64_t pb = (uint64_t)o.pitch * 4;
+  const void* base = std::min(o.hi, o.lo);
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)o.cols, (cuuint64_t)o.rows, 2};
+  cuuint64_t strides[2] = {pb, delta};
+  cuuint32_t box[3] = {(cuuint32_t)bk, (cuuint32_t)tile_mn, 2};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, bk == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) panic("cuTensorMapEncodeTiled (paired planes) failed (%d)", (int)r);
+  return m;
+}
+
 // tile_mn: the operand's tile extent along M (A: BM) or N (B: the tile width);
 // bk: the k-block depth.
 CUtensorMap operand_map(const TcOperand& o, const float* plane, int tile_mn, int bk) {
@@ -949,9 +996,20 @@ void gemm_tc_planes(const TcProblem& pr) {
   load_encoder();
   const TileShape ts = tile_shape_for(pr);
   const int BN = ts.bn, BK = ts.bk;
-  CUtensorMap ah = operand_map(pr.a, pr.a.hi, BM, BK), al = operand_map(pr.a, pr.a.lo, BM, BK);
-  CUtensorMap bh = operand_map(pr.b, pr.b.hi, BN, BK), bl = operand_map(pr.b, pr.b.lo, BN, BK);
+  static const bool no_pair = [] { const char* e = getenv("MALUS_GEMM_PAIR"); return e && e[0] == '0'; }();
+  bool a_swap = false, b_swap = false;
+  uint64_t a_d = 0, b_d = 0;
+  const bool a_pair = !no_pair && pair_planes(pr.a, BM, BK, &a_swap, &a_d);
+  const bool b_pair = !no_pair && pair_planes(pr.b, BN, BK, &b_swap, &b_d);
+  CUtensorMap ah = a_pair ? paired_map(pr.a, BM, BK, a_d) : operand_map(pr.a, pr.a.hi, BM, BK);
+  CUtensorMap al = a_pair ? ah : operand_map(pr.a, pr.a.lo, BM, BK);
+  CUtensorMap bh = b_pair ? paired_map(pr.b, BN, BK, b_d) : operand_map(pr.b, pr.b.hi, BN, BK);
+  CUtensorMap bl = b_pair ? bh : operand_map(pr.b, pr.b.lo, BN, BK);
   TcKernelParams kp;
+  kp.a_pair = a_pair ? 1 : 0;
+  kp.b_pair = b_pair ? 1 : 0;
+  kp.a_swap = a_swap ? 1 : 0;
+  kp.b_swap = b_swap ? 1 : 0;
   kp.pr = pr;
   kp.bn = BN;
   kp.bk = BK;

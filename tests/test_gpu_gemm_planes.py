@@ -390,3 +390,30 @@ def test_splitk_256_wide_tiles_epilogues(M, rt, rng):
     gp = 0.7978845608028654 * (1 + 3 * 0.044715 * x * x)
     dref = ref * (0.5 * (1 + t) + 0.5 * x * (1 - t * t) * gp)
     assert np.max(np.abs(out.numpy() - dref) / (np.abs(A.T) @ np.abs(B) + 1e-9)) < 2e-4
+
+
+@pytest.mark.parametrize("lo_first", [False, True])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, False), (False, False)])
+def test_paired_plane_loads_either_order(M, rt, rng, lo_first, a_mn, b_mn):
+    """Both planes of an operand in one buffer, hi then lo or lo then hi: the
+    paired-plane load (one box per stage for both planes, based at the lower
+    address) must put each plane where the MMA reads it."""
+    Mm, N, K = 1024, 1536, 96
+
+    def op_in_one_buffer(x, mn):
+        rows, cols = x.shape
+        both = dev(M, np.zeros((2, rows, cols)))
+        src = dev(M, x)
+        base = ptr(rt, both)
+        first, second = base, base + rows * cols * 4
+        hi, lo = (second, first) if lo_first else (first, second)
+        rt.malus_tf32_split(ptr(rt, src), rows, cols, cols, 1, rows * cols, hi, lo, cols)
+        return M.TcOperand(hi, lo, rows, cols, cols, 1, rows * cols, int(mn), 0, 0)
+
+    A = rng.standard_normal((Mm, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    ao = op_in_one_buffer(np.ascontiguousarray(A.T) if a_mn else A, a_mn)
+    bo = op_in_one_buffer(B if b_mn else np.ascontiguousarray(B.T), b_mn)
+    out = dev(M, np.zeros((Mm, N)))
+    run(M, rt, Mm, N, K, 1, ao, bo, out=out)
+    assert err(out.numpy(), A.astype(np.float64) @ B, A, B) < 1e-4
