@@ -659,12 +659,15 @@ FusedStep* fused_create(const malus_gpt_config& cfg, const std::vector<float*>& 
   f->Vp = (f->V + 3) & ~3;
   f->scale = 1.0f / sqrtf((float)f->hs);
   // MALUS_ATTN_FUSED=0 keeps the GEMM + softmax attention where the fused kernels
-  // apply; MALUS_ATTN_BWD=1 also takes the backward through the fused kernels
-  // (otherwise the forward keeps P planes for the GEMM backward)
+  // apply.  The backward goes through the fused kernels (no [B*H][T][T]
+  // tensor) from T = 512 on, where those tensors dominate (C5, T = 1024:
+  // 47.5 vs 49.0 ms per step, 9.7 GB of P planes saved), and through the
+  // GEMMs below (C4, T = 256: the GEMM backward is faster);
+  // MALUS_ATTN_BWD=1 / 0 forces either
   const char* fa = getenv("MALUS_ATTN_FUSED");
   const char* fb = getenv("MALUS_ATTN_BWD");
   f->fused_attn = attn_fwd_supported(f->T, f->hs) && !(fa && fa[0] == '0');
-  f->fused_attn_bwd = f->fused_attn && fb && fb[0] == '1';
+  f->fused_attn_bwd = f->fused_attn && (fb ? fb[0] == '1' : f->T >= 512);
   if (f->C % 32 || f->hs % 4 || f->T % 4 || f->T > 1024 || f->C > 1024)
     panic("fused step needs n_embd %% 32 == 0, head size %% 4 == 0, T %% 4 == 0, T, C <= 1024 "
           "(got C=%d hs=%d T=%d)", f->C, f->hs, f->T);
