@@ -411,6 +411,16 @@ typedef struct malus_tc_problem {
   const float* rowv;
 } malus_tc_problem;
 void malus_tc_gemm(const malus_tc_problem* p);
+/* CTA pairs the tcgen05 GEMM keeps resident when it runs a problem as 2-CTA
+ * clusters (256-row tiles; problems with M a multiple of 256, unsplit and
+ * non-causal); 0 when pairs are off or cannot be placed.  A diagnostic with
+ * no counterpart in the reference. */
+int32_t malus_gemm_pair_clusters(void);
+/* Which eligible problems run as CTA pairs: -1 the measured rule (plain-store
+ * and GELU epilogues with K >= 256), 0 none, 1 all.  Starts from the
+ * environment variable MALUS_GEMM_CTA2 (unset: -1).  Returns the previous
+ * mode.  A tuning and test hook with no counterpart in the reference. */
+int32_t malus_gemm_pair_mode(int32_t mode);
 void malus_tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t batch,
                       int64_t sstride, float* hi, float* lo, int64_t pitch);
 

@@ -204,6 +204,8 @@ SIGNATURES: dict[str, tuple] = {
     "malus_gpt_dp_buckets": (i32, [C.POINTER(GptConfig), P_i64, P_i64, i32]),
     "malus_device_error": (i32, []),
     "malus_tc_gemm": (None, [C.POINTER(TcProblem)]),
+    "malus_gemm_pair_clusters": (i32, []),
+    "malus_gemm_pair_mode": (i32, [i32]),
     "malus_tf32_split": (None, [vp, i64, i64, i64, i64, i64, vp, vp, i64]),
     "malus_prof_enable": (None, [i32]),
     "malus_embedding_bwd_noalloc": (i32, [vp, vp, i32, sz, sz, sz, vp, vp]),

@@ -142,14 +142,19 @@ constexpr int kEpiWarpFloats = 32 * 32;   // per-warp 32x32 staging block (XOR-s
 // fit and the TMA latency is covered further ahead.  K-major tiles use the
 // 128-byte swizzle (BK 32) or the 64-byte swizzle (BK 16); MN-major tiles the
 // 32-byte-granule 128-byte swizzle with BK rows per 32-column chunk.
-template <int BN_, int BK_>
+// With PAIR_ the tile is one of a CTA pair's (256 rows): this CTA loads its
+// 128 rows of A and BN / 2 rows of B (see the pair notes at k_gemm_tc).
+template <int BN_, int BK_, bool PAIR_ = false>
 struct TileCfg {
   static constexpr int BN = BN_, BK = BK_;
+  static constexpr int BNL = PAIR_ ? BN_ / 2 : BN_;   // B rows (tile columns) loaded by this CTA
   static constexpr int kTileBytesA = BM * BK * 4;
-  static constexpr int kTileBytesB = BN * BK * 4;
+  static constexpr int kTileBytesB = BNL * BK * 4;
   static constexpr int kStageBytes = 2 * kTileBytesA + 2 * kTileBytesB;
   static constexpr int kFixed = 1024 /*align*/ + 256 /*barriers*/ + 8 * kEpiWarpFloats * 4 /*staging*/;
-  static constexpr int STAGES = (232448 - kFixed) / kStageBytes > 6 ? 6 : (232448 - kFixed) / kStageBytes;
+  static constexpr int kMaxStages = 6;   // barrier area: 2 x 6 stage barriers + 6 more + 2 words
+  static constexpr int STAGES = (232448 - kFixed) / kStageBytes > kMaxStages ? kMaxStages
+                                                                             : (232448 - kFixed) / kStageBytes;
   static constexpr int kSmemBytes = STAGES * kStageBytes + kFixed;
   static constexpr uint32_t kTmemCols = BN <= 64 ? 128 : (BN <= 128 ? 256 : 512);   // two accumulators, power of 2
   static constexpr int kChunkBytes = BK * 128;   // one 32-wide MN chunk (or 32-row K-major box)
@@ -194,6 +199,7 @@ struct TcKernelParams {
   float* ws;       // [tile][split][BM][bn] partial accumulators when splits > 1
   int bn;          // tile width (the kernel's BN)
   int bk;          // k-block depth (the kernel's BK)
+  int bm;          // tile height: 128, or 256 for a CTA pair
   int a_chunked, b_chunked;   // MN-major operand loaded as one {32, 32 K, 4 chunks} box per plane
   int a_pair, b_pair;         // both planes of a stage's tile in one box (a plane dimension)
   int a_swap, b_swap;         // ... whose plane 0 is the lo plane (it is the lower address)
@@ -212,7 +218,7 @@ __device__ __forceinline__ bool unit_of(const TcKernelParams& kp, int unit, Unit
   const int tile = unit / kp.splits, sl = unit % kp.splits;
   u.z = tile / per_batch;
   const int rem = tile % per_batch;
-  u.m0 = (rem / kp.tiles_n) * BM;
+  u.m0 = (rem / kp.tiles_n) * kp.bm;
   u.n0 = (rem % kp.tiles_n) * kp.bn;
   if (p.causal == kCausalOut && u.n0 > u.m0 + BM - 1) return false;
   int lo = 0, hi = kp.nk;
@@ -323,13 +329,24 @@ __device__ __forceinline__ void epi_store4(const TcProblem& p, int64_t o, float4
   }
 }
 
-template <int EPI, int BNT, int BKT>
+// PAIR: the kernel runs as 2-CTA clusters and each work unit is a 256 x BN
+// tile computed by one M = 256 tcgen05.mma (cta_group::2) per k-step.  Both
+// CTAs load their own 128 rows of A and BN / 2 rows of B into their own ring;
+// the transaction bytes of both count on rank 0's full barrier (rank 0 expects
+// the pair's bytes), rank 0 issues the MMAs, and its commits arrive on the
+// empty and accumulator-full barriers of both CTAs.  Each CTA's epilogue
+// drains its own 128 accumulator rows and arrives on rank 0's
+// accumulator-empty barrier.  Per SM a k-step then moves A (128 rows) and half
+// of B instead of all of B, which bounded the single-CTA mainloop (its TMA
+// traffic per MMA).
+template <int EPI, int BNT, int BKT, bool PAIR>
 __global__ void __launch_bounds__(threads_tc(EPI), 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
           const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
           const TcKernelParams kp) {
-  using CF = TileCfg<BNT, BKT>;
+  using CF = TileCfg<BNT, BKT, PAIR>;
   constexpr int BN = CF::BN, BK = CF::BK, STAGES = CF::STAGES, kStageBytes = CF::kStageBytes;
+  constexpr int BNL = CF::BNL;
   constexpr int kTileBytesA = CF::kTileBytesA, kTileBytesB = CF::kTileBytesB, kChunk = CF::kChunkBytes;
   constexpr uint32_t kTmemCols = CF::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
@@ -344,12 +361,17 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
   uint64_t* done = drain + 1;   // every epilogue warp finished reading TMEM
   uint32_t* tmem_slot = (uint32_t*)(done + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  static_assert(CF::kMaxStages * 2 * 8 + 6 * 8 + 8 <= 256, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per_batch = kp.tiles_m * kp.tiles_n;
   const int splits = kp.splits;
   const int total = per_batch * p.batch * splits;   // work units: (tile, K slice)
   const int nk = kp.nk;
+  // A pair walks the unit list as one: position = cluster index.
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int grp = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ngrp = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -358,7 +380,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&accf[b]), 1);
-      mbar_init(smem_u32(&acce[b]), epi_warps(EPI));
+      mbar_init(smem_u32(&acce[b]), epi_warps(EPI) * (PAIR ? 2 : 1));   // a pair: both CTAs' epilogues
     }
     mbar_init(smem_u32(drain), 1);
     mbar_init(smem_u32(done), epi_warps(EPI));
@@ -366,26 +388,44 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (PAIR) {   // the same columns in both CTAs' tensor memory
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncwarp();   // a CTA barrier needs converged warps (thread 0 initialised the barriers)
   __syncthreads();
+  if (PAIR) cluster_sync_all();   // both CTAs' barriers exist before either signals the other
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      // a pair's loads count on rank 0's full barrier
+      auto ld3 = [&](uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2) {
+        if constexpr (PAIR) tma_load_3d_pair(dst, m, bar, c0, c1, c2);
+        else tma_load_3d(dst, m, bar, c0, c1, c2);
+      };
+      auto ld4 = [&](uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2, int c3) {
+        if constexpr (PAIR) tma_load_4d_pair(dst, m, bar, c0, c1, c2, c3);
+        else tma_load_4d(dst, m, bar, c0, c1, c2, c3);
+      };
       uint32_t it = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
+      for (int unit = grp; unit < total && ok; unit += ngrp) {
         Unit un;
         if (!unit_of(kp, unit, un)) continue;
-        const int z = un.z, m0 = un.m0, n0 = un.n0;
+        // this CTA's rows of A and of B (a pair: rank 1 takes the second halves)
+        const int z = un.z, m0 = un.m0 + (int)rank * BM, n0 = un.n0 + (int)rank * BNL;
         for (int kb = un.kb_lo; kb < un.kb_hi; ++kb, ++it) {
           int s = it % STAGES;
           uint32_t ph = (it / STAGES) & 1;
@@ -395,66 +435,78 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
           }
           uint8_t* st = smem + s * kStageBytes;
           uint32_t fb = smem_u32(&full[s]);
-          mbar_expect_tx(fb, kStageBytes);
+          if (PAIR) {
+            if (rank == 0) mbar_expect_tx(fb, 2 * kStageBytes);   // this CTA's and rank 1's copies
+            fb = cluster_addr(fb, 0);
+          } else {
+            mbar_expect_tx(fb, kStageBytes);
+          }
           int k0 = kb * BK, kc, mnc, zc;
           // A 128-wide M/N tile may straddle segments (segment width a multiple
           // of 32): MN-major tiles and K-major tiles of an MN-segmented operand
           // are loaded as four 32-wide boxes, each with its own segment.
           if (kp.a_chunked) {
             operand_coords(p.a.zmode, p.a.seg, z, k0, m0, &kc, &mnc, &zc);
-            tma_load_4d(smem_u32(st), &mAh, fb, 0, kc, mnc >> 5, zc);
-            tma_load_4d(smem_u32(st + kTileBytesA), &mAl, fb, 0, kc, mnc >> 5, zc);
+            ld4(smem_u32(st), &mAh, fb, 0, kc, mnc >> 5, zc);
+            ld4(smem_u32(st + kTileBytesA), &mAl, fb, 0, kc, mnc >> 5, zc);
           } else if (!p.a.mn_major && p.a.zmode != kZMNSeg) {
             operand_coords(p.a.zmode, p.a.seg, z, k0, m0, &kc, &mnc, &zc);
             if (kp.a_pair) {
-              tma_load_3d(smem_u32(st), &mAh, fb, kc, mnc, 0);   // unbatched: the third coordinate is the plane
+              ld3(smem_u32(st), &mAh, fb, kc, mnc, 0);   // unbatched: the third coordinate is the plane
             } else {
-              tma_load_3d(smem_u32(st), &mAh, fb, kc, mnc, zc);
-              tma_load_3d(smem_u32(st + kTileBytesA), &mAl, fb, kc, mnc, zc);
+              ld3(smem_u32(st), &mAh, fb, kc, mnc, zc);
+              ld3(smem_u32(st + kTileBytesA), &mAl, fb, kc, mnc, zc);
             }
           } else {
             for (int j = 0; j < BM / 32; ++j) {
               operand_coords(p.a.zmode, p.a.seg, z, k0, m0 + 32 * j, &kc, &mnc, &zc);
               int x = p.a.mn_major ? mnc : kc, y = p.a.mn_major ? kc : mnc;
-              tma_load_3d(smem_u32(st + j * kChunk), &mAh, fb, x, y, zc);
-              tma_load_3d(smem_u32(st + kTileBytesA + j * kChunk), &mAl, fb, x, y, zc);
+              ld3(smem_u32(st + j * kChunk), &mAh, fb, x, y, zc);
+              ld3(smem_u32(st + kTileBytesA + j * kChunk), &mAl, fb, x, y, zc);
             }
           }
           uint8_t* sb = st + 2 * kTileBytesA;
           if (kp.b_chunked) {
             operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
-            tma_load_4d(smem_u32(sb), &mBh, fb, 0, kc, mnc >> 5, zc);
-            tma_load_4d(smem_u32(sb + kTileBytesB), &mBl, fb, 0, kc, mnc >> 5, zc);
+            ld4(smem_u32(sb), &mBh, fb, 0, kc, mnc >> 5, zc);
+            ld4(smem_u32(sb + kTileBytesB), &mBl, fb, 0, kc, mnc >> 5, zc);
           } else if (!p.b.mn_major && p.b.zmode != kZMNSeg && kp.b_pair) {
             operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
-            tma_load_3d(smem_u32(sb), &mBh, fb, kc, mnc, 0);   // unbatched: the third coordinate is the plane
+            ld3(smem_u32(sb), &mBh, fb, kc, mnc, 0);   // unbatched: the third coordinate is the plane
           } else if (!p.b.mn_major && p.b.zmode != kZMNSeg) {
             operand_coords(p.b.zmode, p.b.seg, z, k0, n0, &kc, &mnc, &zc);
-            tma_load_3d(smem_u32(sb), &mBh, fb, kc, mnc, zc);
-            tma_load_3d(smem_u32(sb + kTileBytesB), &mBl, fb, kc, mnc, zc);
+            ld3(smem_u32(sb), &mBh, fb, kc, mnc, zc);
+            ld3(smem_u32(sb + kTileBytesB), &mBl, fb, kc, mnc, zc);
           } else {
-            for (int j = 0; j < BN / 32; ++j) {
+            for (int j = 0; j < BNL / 32; ++j) {
               operand_coords(p.b.zmode, p.b.seg, z, k0, n0 + 32 * j, &kc, &mnc, &zc);
               int x = p.b.mn_major ? mnc : kc, y = p.b.mn_major ? kc : mnc;
-              tma_load_3d(smem_u32(sb + j * kChunk), &mBh, fb, x, y, zc);
-              tma_load_3d(smem_u32(sb + kTileBytesB + j * kChunk), &mBl, fb, x, y, zc);
+              ld3(smem_u32(sb + j * kChunk), &mBh, fb, x, y, zc);
+              ld3(smem_u32(sb + kTileBytesB + j * kChunk), &mBl, fb, x, y, zc);
             }
           }
         }
       }
       if (*abort_flag) {
-        // every issued stage must land before the CTA exits
+        // every issued stage must land before the CTA exits.  A pair's copies
+        // count on rank 0's barrier only: rank 0 waits for its stages (both
+        // CTAs' bytes, bounded as a whole), rank 1, which cannot observe its
+        // own copies, waits a fixed 200 us (a copy takes microseconds).
         uint32_t lo = it > (uint32_t)STAGES ? it - STAGES : 0;
-        for (uint32_t q = lo; q < it; ++q) {
-          uint64_t t0 = gtimer();
-          while (!mbar_try(smem_u32(&full[q % STAGES]), (q / STAGES) & 1) && gtimer() - t0 < kWaitNs) {}
+        if (PAIR && rank != 0) {
+          const uint64_t t0 = gtimer();
+          while (gtimer() - t0 < 200000ull) {}
+        } else {
+          const uint64_t t0 = gtimer();
+          for (uint32_t q = lo; q < it; ++q)
+            while (!mbar_try(smem_u32(&full[q % STAGES]), (q / STAGES) & 1) && gtimer() - t0 < kWaitNs) {}
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(p.a.mn_major, p.b.mn_major, BN);
+    // ---------------- MMA issuer (a pair: rank 0) ----------------
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = idesc_tf32(p.a.mn_major, p.b.mn_major, BN, PAIR ? 2 * BM : BM);
       // Descriptors of stage 0's tiles, built once.  A descriptor's address
       // field is (byte address / 16) in its low 14 bits and every shared
       // address here is below 256 KB, so a stage or k-step is a plain add of
@@ -473,12 +525,13 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       const uint64_t b_hi = kp.b_swap ? kLoB : 0, b_lo = kp.b_swap ? 0 : kLoB;
       uint32_t it = 0, local = 0;
       bool ok = true, issued = false;
-      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
+      for (int unit = grp; unit < total && ok; unit += ngrp) {
         Unit un;
         if (!unit_of(kp, unit, un)) continue;
         uint32_t b = local & 1, u = local >> 1;
         ++local;
-        if (u >= 1 && !mbar_wait(smem_u32(&acce[b]), (u - 1) & 1, abort_flag, kp.err, 14)) {
+        if (u >= 1 && !(PAIR ? mbar_wait_cluster(smem_u32(&acce[b]), (u - 1) & 1, abort_flag, kp.err, 14)
+                             : mbar_wait(smem_u32(&acce[b]), (u - 1) & 1, abort_flag, kp.err, 14))) {
           ok = false;
           break;
         }
@@ -492,24 +545,35 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint64_t sa = da0 + (uint64_t)(s * kStage16), sbb = db0 + (uint64_t)(s * kStage16);
           const uint64_t dah = sa + a_hi, dal = sa + a_lo, dbh = sbb + b_hi, dbl = sbb + b_lo;
-          mma_tf32(dacc, dal, dbh, idesc, kb > kb_lo ? 1u : 0u);   // small terms first
-          mma_tf32(dacc, dah, dbl, idesc, 1u);
-          mma_tf32(dacc, dah, dbh, idesc, 1u);
+          auto mma = [&](uint64_t da, uint64_t db, uint32_t acc) {
+            if constexpr (PAIR) mma_tf32_pair(dacc, da, db, idesc, acc);
+            else mma_tf32(dacc, da, db, idesc, acc);
+          };
+          mma(dal, dbh, kb > kb_lo ? 1u : 0u);   // small terms first
+          mma(dah, dbl, 1u);
+          mma(dah, dbh, 1u);
 #pragma unroll
           for (int kk = 1; kk < BK / 8; ++kk) {
             const uint64_t oa = (uint64_t)(kk * ka), ob = (uint64_t)(kk * kbs);
-            mma_tf32(dacc, dal + oa, dbh + ob, idesc, 1u);
-            mma_tf32(dacc, dah + oa, dbl + ob, idesc, 1u);
-            mma_tf32(dacc, dah + oa, dbh + ob, idesc, 1u);
+            mma(dal + oa, dbh + ob, 1u);
+            mma(dah + oa, dbl + ob, 1u);
+            mma(dah + oa, dbh + ob, 1u);
           }
           issued = true;
-          mma_commit(smem_u32(&empty[s]));   // frees the stage when these MMAs finish
+          // frees the stage (in both CTAs of a pair) when these MMAs finish
+          if constexpr (PAIR) mma_commit_pair_both(smem_u32(&empty[s]));
+          else mma_commit(smem_u32(&empty[s]));
         }
-        if (ok) mma_commit(smem_u32(&accf[b]));
+        if (ok) {
+          if constexpr (PAIR) mma_commit_pair_both(smem_u32(&accf[b]));
+          else mma_commit(smem_u32(&accf[b]));
+        }
       }
-      if (!ok && issued) {
-        // no MMA may be in flight when TMEM is freed
-        mma_commit(smem_u32(drain));
+      if ((PAIR || !ok) && issued) {
+        // no MMA may be in flight when TMEM is freed; a pair always drains, so
+        // that no MMA or commit touches rank 1 after the closing cluster barrier
+        if constexpr (PAIR) mma_commit_pair(smem_u32(drain));
+        else mma_commit(smem_u32(drain));
         uint64_t t0 = gtimer();
         while (!mbar_try(smem_u32(drain), 0) && gtimer() - t0 < kWaitNs) {}
       }
@@ -527,14 +591,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
     const bool contig = (p.on.d1 % 32 == 0) && (p.on.d2 % 32 == 0) && p.on.s3 == 1;
     const int rsub = lane >> 3, cgr = lane & 7, csub = cgr * 4;   // staged layout: lane's row group / columns
     uint32_t local = 0;
-    for (int unit = blockIdx.x; unit < total; unit += gridDim.x) {
+    for (int unit = grp; unit < total; unit += ngrp) {
       Unit un;
       if (!unit_of(kp, unit, un)) continue;
       uint32_t b = local & 1, u = local >> 1;
       ++local;
       if (!mbar_wait(smem_u32(&accf[b]), u & 1, abort_flag, kp.err, 13)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int z = un.z, m0 = un.m0, n0 = un.n0;
+      const int z = un.z, m0 = un.m0 + (int)rank * BM, n0 = un.n0;   // this CTA's 128 rows
       const int m = m0 + row;
       const int64_t zm_z = lay(p.oz, z);
       const int64_t zm_off = zm_z + lay(p.om, m);
@@ -648,7 +712,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&acce[b]));
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(cluster_addr(smem_u32(&acce[b]), 0));   // rank 0 reuses the columns
+        else mbar_arrive(smem_u32(&acce[b]));
+      }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncwarp();
@@ -659,13 +726,19 @@ k_gemm_tc(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUten
   // reconverge before the CTA barrier
   __syncwarp();
   __syncthreads();
+  // a pair: rank 0 has drained its MMAs and both CTAs' epilogues and copies
+  // are done before either CTA frees its tensor memory or exits
+  if (PAIR) cluster_sync_all();
   if (warp == 1) {
     // TMEM is freed only after every epilogue warp said it finished reading it
     // (an explicit barrier: the CTA barrier alone was seen to release early)
     mbar_wait_bounded(smem_u32(done), 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(kTmemCols));
+    if constexpr (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"(kTmemCols));
   }
 }
 
@@ -931,17 +1004,68 @@ float* splitk_workspace(size_t floats) {
   return buf[dev];
 }
 
-template <int EPI, int BNT, int BKT>
-void launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
-               const CUtensorMap& bl, const TcKernelParams& kp, int grid) {
-  constexpr int smem = TileCfg<BNT, BKT>::kSmemBytes;
+template <int EPI, int BNT, int BKT, bool PAIR>
+void tc_smem_attr() {
   static bool attr = false;
   if (!attr) {
-    MALUS_CUDA(cudaFuncSetAttribute(k_gemm_tc<EPI, BNT, BKT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    smem));
+    MALUS_CUDA(cudaFuncSetAttribute(k_gemm_tc<EPI, BNT, BKT, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    TileCfg<BNT, BKT, PAIR>::kSmemBytes));
     attr = true;
   }
-  k_gemm_tc<EPI, BNT, BKT><<<grid, threads_tc(EPI), smem, stream()>>>(ah, al, bh, bl, kp);
+}
+
+cudaLaunchConfig_t pair_config(dim3 grid, int threads, int smem, cudaLaunchAttribute* at) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream();
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+std::atomic<int> g_pair_mode{[] {
+  const char* e = getenv("MALUS_GEMM_CTA2");
+  return e ? (atoi(e) == 0 ? 0 : (atoi(e) == 1 ? 1 : -1)) : -1;
+}()};
+
+// CTA pairs that can be resident at once (one CTA per SM, both SMs of a TPC).
+// Every pair instantiation has the same footprint class (one CTA per SM), so
+// one query stands for all; 0 disables pairs.
+int pair_clusters() {
+  static int n = -1;
+  if (n < 0) {
+    using CF = TileCfg<192, 16, true>;
+    tc_smem_attr<kEpiStore, 192, 16, true>();
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = pair_config(dim3(2 * (kNumSMs / 2)), threads_tc(kEpiStore), CF::kSmemBytes, at);
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, k_gemm_tc<kEpiStore, 192, 16, true>, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      c = 0;
+    }
+    n = std::min(c, kNumSMs / 2);
+  }
+  return n;
+}
+
+template <int EPI, int BNT, int BKT, bool PAIR>
+void launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh,
+               const CUtensorMap& bl, const TcKernelParams& kp, int grid) {
+  constexpr int smem = TileCfg<BNT, BKT, PAIR>::kSmemBytes;
+  tc_smem_attr<EPI, BNT, BKT, PAIR>();
+  if (PAIR) {   // grid = 2 x pairs, launched as 2-CTA clusters
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = pair_config(dim3(grid), threads_tc(EPI), smem, at);
+    MALUS_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI, BNT, BKT, PAIR>, ah, al, bh, bl, kp));
+  } else {
+    k_gemm_tc<EPI, BNT, BKT, PAIR><<<grid, threads_tc(EPI), smem, stream()>>>(ah, al, bh, bl, kp);
+  }
   if (kp.splits > 1) {
     int64_t chunks = (int64_t)kp.tiles_m * kp.tiles_n * kp.pr.batch * (BM * kp.bn / 4);
     unsigned g = (unsigned)std::min<int64_t>((chunks + 255) / 256, (int64_t)kNumSMs * 8);
@@ -999,12 +1123,28 @@ void gemm_tc_planes(const TcProblem& pr) {
   static const bool no_pair = [] { const char* e = getenv("MALUS_GEMM_PAIR"); return e && e[0] == '0'; }();
   bool a_swap = false, b_swap = false;
   uint64_t a_d = 0, b_d = 0;
+  // CTA pairs (256 x BN tiles, one M = 256 MMA per k-step): unsplit,
+  // non-causal problems whose M is whole 256-row tiles, with the 192-wide
+  // tiles or the 128-wide ones of depth 32, K >= 256 and an epilogue without
+  // an auxiliary input (plain store, GELU).  Measured on the C4 GEMMs: Q|K|V
+  // 14 % and MLP up + GELU 7 % faster as pairs; the residual and
+  // GELU-derivative epilogues (whose aux reads make the two coupled CTAs wait
+  // on the slower one) 5-9 % slower, a K = 64 batched product 26 % slower.
+  // Mode (malus_gemm_pair_mode, initially MALUS_GEMM_CTA2): -1 this rule,
+  // 0 no pairs, 1 pairs for every problem of an eligible shape.
+  const int mode = g_pair_mode.load(std::memory_order_relaxed);
+  const int tiles128 = ((pr.M + BM - 1) / BM) * ((pr.N + BN - 1) / BN) * pr.batch;
+  const bool measured_ok = (pr.epi == kEpiStore || pr.epi == kEpiGelu) && pr.K >= 256;
+  const bool cta2 = mode != 0 && (mode == 1 || measured_ok) && !pr.causal && pr.M % (2 * BM) == 0 &&
+                    (BN == 192 || (BN == 128 && BK == 32)) && splitk_for(tiles128, (pr.K + BK - 1) / BK) == 1 &&
+                    pair_clusters() > 0;
+  const int BNL = cta2 ? BN / 2 : BN;   // B rows each CTA loads
   const bool a_pair = !no_pair && pair_planes(pr.a, BM, BK, &a_swap, &a_d);
-  const bool b_pair = !no_pair && pair_planes(pr.b, BN, BK, &b_swap, &b_d);
+  const bool b_pair = !no_pair && pair_planes(pr.b, BNL, BK, &b_swap, &b_d);
   CUtensorMap ah = a_pair ? paired_map(pr.a, BM, BK, a_d) : operand_map(pr.a, pr.a.hi, BM, BK);
   CUtensorMap al = a_pair ? ah : operand_map(pr.a, pr.a.lo, BM, BK);
-  CUtensorMap bh = b_pair ? paired_map(pr.b, BN, BK, b_d) : operand_map(pr.b, pr.b.hi, BN, BK);
-  CUtensorMap bl = b_pair ? bh : operand_map(pr.b, pr.b.lo, BN, BK);
+  CUtensorMap bh = b_pair ? paired_map(pr.b, BNL, BK, b_d) : operand_map(pr.b, pr.b.hi, BNL, BK);
+  CUtensorMap bl = b_pair ? bh : operand_map(pr.b, pr.b.lo, BNL, BK);
   TcKernelParams kp;
   kp.a_pair = a_pair ? 1 : 0;
   kp.b_pair = b_pair ? 1 : 0;
@@ -1013,24 +1153,25 @@ void gemm_tc_planes(const TcProblem& pr) {
   kp.pr = pr;
   kp.bn = BN;
   kp.bk = BK;
-  kp.tiles_m = (pr.M + BM - 1) / BM;
+  kp.bm = cta2 ? 2 * BM : BM;
+  kp.tiles_m = (pr.M + kp.bm - 1) / kp.bm;
   kp.tiles_n = (pr.N + BN - 1) / BN;
   kp.nk = (pr.K + BK - 1) / BK;
   kp.err = device_error_word();
   int tiles = kp.tiles_m * kp.tiles_n * pr.batch;
-  kp.splits = pr.causal ? 1 : splitk_for(tiles, kp.nk);
+  kp.splits = pr.causal || cta2 ? 1 : splitk_for(tiles, kp.nk);
   {
     const bool contig = (pr.on.d1 % 32 == 0) && (pr.on.d2 % 32 == 0) && pr.on.s3 == 1;
     kp.staged = contig && (pr.epi != kEpiStore || pr.out_hi != nullptr) ? 1 : 0;
   }
   kp.a_chunked = mn_chunked(pr.a, BM) ? 1 : 0;
-  kp.b_chunked = mn_chunked(pr.b, BN) ? 1 : 0;
+  kp.b_chunked = mn_chunked(pr.b, BNL) ? 1 : 0;
   kp.ws = kp.splits > 1 ? splitk_workspace((size_t)tiles * kp.splits * BM * BN) : nullptr;
   int total = tiles * kp.splits;
   // Static round-robin over units: for causal problems the per-batch pattern of
   // skipped tiles / short K ranges has period 2 or 4, so an odd grid (147)
   // spreads the light and heavy units evenly over the CTAs.
-  int grid = std::min(total, pr.causal ? kNumSMs - 1 : kNumSMs);
+  int grid = cta2 ? 2 * std::min(total, pair_clusters()) : std::min(total, pr.causal ? kNumSMs - 1 : kNumSMs);
   double flops = 2.0 * pr.M * (double)pr.N * pr.K * pr.batch;
   if (pr.causal) {   // the work actually done: tiles and K ranges the mask leaves
     double f = 0.0;
@@ -1051,21 +1192,26 @@ void gemm_tc_planes(const TcProblem& pr) {
   const int arrays = (pr.out ? 1 : 0) + (pr.out_hi ? 2 : 0) + (pr.aux ? 1 : 0);
   int pid = prof_begin(0, flops, 8.0 * ((double)pr.M * pr.K + (double)pr.N * pr.K) * pr.batch +
                                      4.0 * mn * arrays);
-#define MALUS_TC_EPI_SWITCH(BN_, BK_)                                               \
-  switch (pr.epi) {                                                                \
-    case kEpiStore: launch_tc<kEpiStore, BN_, BK_>(ah, al, bh, bl, kp, grid); break; \
-    case kEpiResid: launch_tc<kEpiResid, BN_, BK_>(ah, al, bh, bl, kp, grid); break; \
-    case kEpiGelu: launch_tc<kEpiGelu, BN_, BK_>(ah, al, bh, bl, kp, grid); break;   \
-    case kEpiGeluBwd: launch_tc<kEpiGeluBwd, BN_, BK_>(ah, al, bh, bl, kp, grid); break; \
-    default: launch_tc<kEpiSoftmaxBwd, BN_, BK_>(ah, al, bh, bl, kp, grid); break;   \
+#define MALUS_TC_EPI_SWITCH(BN_, BK_, P_)                                                 \
+  switch (pr.epi) {                                                                      \
+    case kEpiStore: launch_tc<kEpiStore, BN_, BK_, P_>(ah, al, bh, bl, kp, grid); break;     \
+    case kEpiResid: launch_tc<kEpiResid, BN_, BK_, P_>(ah, al, bh, bl, kp, grid); break;     \
+    case kEpiGelu: launch_tc<kEpiGelu, BN_, BK_, P_>(ah, al, bh, bl, kp, grid); break;       \
+    case kEpiGeluBwd: launch_tc<kEpiGeluBwd, BN_, BK_, P_>(ah, al, bh, bl, kp, grid); break; \
+    default: launch_tc<kEpiSoftmaxBwd, BN_, BK_, P_>(ah, al, bh, bl, kp, grid); break;       \
   }
-  if (BN == 64) { MALUS_TC_EPI_SWITCH(64, 32) }
-  else if (BN == 256 && BK == 16) { MALUS_TC_EPI_SWITCH(256, 16) }
-  else if (BN == 256) { MALUS_TC_EPI_SWITCH(256, 32) }
-  else if (BN == 192 && BK == 16) { MALUS_TC_EPI_SWITCH(192, 16) }
-  else if (BN == 192) { MALUS_TC_EPI_SWITCH(192, 32) }
-  else if (BK == 16) { MALUS_TC_EPI_SWITCH(128, 16) }
-  else { MALUS_TC_EPI_SWITCH(128, 32) }
+  if (cta2) {
+    if (BN == 192 && BK == 16) { MALUS_TC_EPI_SWITCH(192, 16, true) }
+    else if (BN == 192) { MALUS_TC_EPI_SWITCH(192, 32, true) }
+    else { MALUS_TC_EPI_SWITCH(128, 32, true) }
+  }
+  else if (BN == 64) { MALUS_TC_EPI_SWITCH(64, 32, false) }
+  else if (BN == 256 && BK == 16) { MALUS_TC_EPI_SWITCH(256, 16, false) }
+  else if (BN == 256) { MALUS_TC_EPI_SWITCH(256, 32, false) }
+  else if (BN == 192 && BK == 16) { MALUS_TC_EPI_SWITCH(192, 16, false) }
+  else if (BN == 192) { MALUS_TC_EPI_SWITCH(192, 32, false) }
+  else if (BK == 16) { MALUS_TC_EPI_SWITCH(128, 16, false) }
+  else { MALUS_TC_EPI_SWITCH(128, 32, false) }
 #undef MALUS_TC_EPI_SWITCH
   count_launch(kp.splits > 1 ? 2 : 1);
   after_launch("k_gemm_tc");
@@ -1132,6 +1278,16 @@ extern "C" void malus_tc_gemm(const malus_tc_problem* q) {
   p.aux_lo = q->aux_lo;
   p.rowv = q->rowv;
   gemm_tc_planes(p);
+}
+
+extern "C" int32_t malus_gemm_pair_clusters(void) {
+  if (malus::g_pair_mode.load() == 0) return 0;
+  return malus::pair_clusters();
+}
+
+extern "C" int32_t malus_gemm_pair_mode(int32_t mode) {
+  const int m = mode == 0 ? 0 : (mode == 1 ? 1 : -1);
+  return malus::g_pair_mode.exchange(m);
 }
 
 extern "C" void malus_tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld,

@@ -210,6 +210,99 @@ __device__ __forceinline__ void mma_commit(uint32_t mbar) {
       : "memory");
 }
 
+// ---- CTA pairs (cta_group::2) ----
+// The two CTAs of a 2-CTA cluster (one TPC) share one M = 256 MMA: each holds
+// its 128 rows of A and half of B's columns at the same shared-memory offsets,
+// and its 128 accumulator rows in its own tensor memory at the same column.
+// Rank 0 issues the MMAs; a pair kernel uses cta_group::2 for every tcgen05
+// instruction that takes the qualifier.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of both CTAs, converged: writes before it (barrier
+// initialisation included) are visible to the whole cluster after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier anywhere in the cluster (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_address) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_address)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t a, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait for a barrier that the other CTA of the pair arrives on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t a, uint32_t parity, volatile int* abort_flag,
+                                                  int32_t* err, int code) {
+  if (mbar_try_cluster(a, parity)) return true;
+  uint64_t t0 = gtimer();
+  while (true) {
+    if (mbar_try_cluster(a, parity)) return true;
+    if (*abort_flag) return false;
+    if (gtimer() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      atomicExch(err, code);
+      return false;
+    }
+  }
+}
+// TMA loads of one CTA of a pair: the data lands in this CTA's shared memory
+// and the transaction bytes count on `mbar`, which may be the other CTA's
+// barrier (a shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t mbar,
+                                                 int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(dst), "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap* map, uint32_t mbar,
+                                                 int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(dst), "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+// Arrive on the barrier at this shared-memory offset in both CTAs of the pair
+// once the issuing thread's MMAs so far have completed.
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t mbar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(mbar), "h"((uint16_t)3)
+      : "memory");
+}
+// ... on this CTA's barrier only.
+__device__ __forceinline__ void mma_commit_pair(uint32_t mbar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
                ::"l"((uint64_t)map), "r"(src), "r"(c0), "r"(c1)

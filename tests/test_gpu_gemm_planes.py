@@ -417,3 +417,111 @@ def test_paired_plane_loads_either_order(M, rt, rng, lo_first, a_mn, b_mn):
     out = dev(M, np.zeros((Mm, N)))
     run(M, rt, Mm, N, K, 1, ao, bo, out=out)
     assert err(out.numpy(), A.astype(np.float64) @ B, A, B) < 1e-4
+
+
+# ---- CTA pairs: problems whose M is whole 256-row tiles, unsplit and
+# non-causal, run as 2-CTA clusters (one M = 256 MMA per k-step, each CTA
+# loading its 128 rows of A and half of the tile's B columns).  These tests
+# put the GEMM in pair mode 1 (every eligible shape as pairs, whatever the
+# epilogue and K) and pick shapes that are eligible: 192-wide tiles (full
+# grid), 128-wide tiles with depth 32, ragged N and K edges, batching, segments.
+@pytest.fixture
+def pairs_all(rt):
+    assert rt.malus_gemm_pair_clusters() > 0
+    prev = rt.malus_gemm_pair_mode(1)
+    yield
+    rt.malus_gemm_pair_mode(prev)
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("Mm,N,K", [(4096, 1152, 384), (1024, 1536, 96), (512, 200, 72)])
+def test_pair_majors(M, rt, rng, pairs_all, a_mn, b_mn, Mm, N, K):
+    A = rng.standard_normal((Mm, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    ao = operand(M, rt, A.T if a_mn else A, a_mn)
+    bo = operand(M, rt, B if b_mn else B.T, b_mn)
+    out = dev(M, np.zeros((Mm, N)))
+    run(M, rt, Mm, N, K, 1, ao, bo, out=out)
+    assert err(out.numpy(), A.astype(np.float64) @ B, A, B) < 1e-4
+
+
+def test_pair_epilogues(M, rt, rng, pairs_all):
+    """Residual add (192 x 16 tiles) and GELU / GELU backward with tf32 output
+    planes (192 x 32 tiles) on 256-row pair tiles."""
+    test_residual_gelu_gelubwd(M, rt, rng, 4096, 1536, 96)
+
+
+def test_pair_batched(M, rt, rng, pairs_all):
+    Z, Mm, N, K = 6, 256, 128, 256
+    A = rng.standard_normal((Z, Mm, K)).astype(np.float32)
+    B = rng.standard_normal((Z, K, N)).astype(np.float32)
+    ao = operand(M, rt, A, False, zmode=1)
+    bo = operand(M, rt, B, True, zmode=1)              # [K][N] per batch: MN-major
+    out = dev(M, np.zeros((Z, Mm, N)))
+    run(M, rt, Mm, N, K, Z, ao, bo, out=out, oz=lay(s3=Mm * N))
+    ref = np.einsum("zmk,zkn->zmn", A.astype(np.float64), B)
+    scale = np.einsum("zmk,zkn->zmn", np.abs(A).astype(np.float64), np.abs(B))
+    assert np.max(np.abs(out.numpy() - ref) / scale) < 1e-4
+
+
+@pytest.mark.parametrize("side", ["a", "b"])
+@pytest.mark.parametrize("mn", [False, True])
+def test_pair_mnseg(M, rt, rng, pairs_all, side, mn):
+    """Segmented operands on pair tiles: B's 96-wide segments straddle the two
+    CTAs' 64-column halves; A's 96-row segments straddle the 128-row halves."""
+    K, seg = 80, 96
+    nseg = 8 if side == "a" else 3
+    other = 200 if side == "a" else 512
+    S = rng.standard_normal((nseg, seg, K)).astype(np.float32)
+    full = np.concatenate(list(S), axis=0)
+    X = rng.standard_normal((other, K)).astype(np.float32)
+    stored = np.ascontiguousarray(S.transpose(0, 2, 1)) if mn else S
+    so = operand(M, rt, stored, mn, zmode=3, seg=seg)
+    if side == "a":
+        xo = operand(M, rt, X.T, True)
+        Mm, N, A, B = nseg * seg, other, full, X.T
+        out = dev(M, np.zeros((Mm, N)))
+        run(M, rt, Mm, N, K, 1, so, xo, out=out)
+    else:
+        xo = operand(M, rt, X, False)
+        Mm, N, A, B = other, nseg * seg, X, full.T
+        out = dev(M, np.zeros((Mm, N)))
+        run(M, rt, Mm, N, K, 1, xo, so, out=out)
+    assert err(out.numpy(), A.astype(np.float64) @ B, A, B) < 1e-4
+
+
+def test_pair_clusters_resident(M, rt):
+    """On a B200 every TPC can hold one CTA pair of the GEMM: 74 pairs (148 SMs)."""
+    n = rt.malus_gemm_pair_clusters()
+    assert 1 <= n <= 74
+
+
+def test_pair_mode_hook(M, rt):
+    prev = rt.malus_gemm_pair_mode(0)
+    try:
+        assert rt.malus_gemm_pair_clusters() == 0
+        assert rt.malus_gemm_pair_mode(7) == 0        # any other value selects the measured rule
+        assert rt.malus_gemm_pair_mode(-1) == -1
+    finally:
+        rt.malus_gemm_pair_mode(prev)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_pair_mode_same_result(M, rt, rng, mode):
+    """The same product as pairs and as single CTAs agrees to the tf32x3 error
+    (the per-element arithmetic is the same; only the CTA that computes a row
+    changes)."""
+    A = rng.standard_normal((2048, 384)).astype(np.float32)
+    B = rng.standard_normal((384, 1152)).astype(np.float32)
+    ao, bo = operand(M, rt, A, False), operand(M, rt, B, True)
+    outs = []
+    prev = rt.malus_gemm_pair_mode(mode)
+    try:
+        for m in (mode, 1 - mode):
+            rt.malus_gemm_pair_mode(m)
+            out = dev(M, np.zeros((2048, 1152)))
+            run(M, rt, 2048, 1152, 384, 1, ao, bo, out=out)
+            outs.append(out.numpy())
+    finally:
+        rt.malus_gemm_pair_mode(prev)
+    assert np.array_equal(outs[0], outs[1])
