@@ -225,23 +225,28 @@ __global__ void k_ln_bwd_fused(const float* __restrict__ x, const float* __restr
   }
 }
 
-// out[c] = sum_b part[b][c] in a fixed order: 8 row groups per column, then
-// the 8 group sums in order.  Block = 32 columns x 8 row groups.
-__global__ void k_colsum(const float* __restrict__ part, float* __restrict__ out, int nblk, int C) {
-  __shared__ float sh[8][33];
+// out[c] = sum_b part[b][c] in a fixed order: 32 row groups per column (group
+// g sums rows g, g + 32, ...), then the 32 group sums in order.  Block = 32
+// columns x 32 row groups: the column count is small (C / 32 blocks), so the
+// rows are spread over as many warps as a block holds to keep the serial
+// chains short (the kernel is latency-bound).
+constexpr int kColGroups = 32;
+__global__ void __launch_bounds__(32 * kColGroups)
+k_colsum(const float* __restrict__ part, float* __restrict__ out, int nblk, int C) {
+  __shared__ float sh[kColGroups][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + tx;
   float s = 0.0f;
   if (c < C) {
 #pragma unroll 4
-    for (int b = ty; b < nblk; b += 8) s += part[(size_t)b * C + c];
+    for (int b = ty; b < nblk; b += kColGroups) s += part[(size_t)b * C + c];
   }
   sh[ty][tx] = s;
   __syncthreads();
   if (ty == 0 && c < C) {
     float t = sh[0][tx];
 #pragma unroll
-    for (int q = 1; q < 8; ++q) t += sh[q][tx];
+    for (int q = 1; q < kColGroups; ++q) t += sh[q][tx];
     out[c] = t;
   }
 }
@@ -595,7 +600,7 @@ void ln_bwd(FusedStep* f, const float* x, const float* mean, const float* var, c
   size_t smem = (size_t)(threads / 32) * f->C * sizeof(float);
   P4_DISPATCH(f->C, (k_ln_bwd_fused<P_><<<f->part_blocks, threads, smem, stream()>>>(
                           x, mean, var, g, dz, resid, gout, gpl.hi, gpl.lo, f->part, f->M, f->C)));
-  k_colsum<<<(f->C + 31) / 32, 256, 0, stream()>>>(f->part, dgain, f->part_blocks, f->C);
+  k_colsum<<<(f->C + 31) / 32, 32 * kColGroups, 0, stream()>>>(f->part, dgain, f->part_blocks, f->C);
   count_launch(2);
   after_launch("k_ln_bwd_fused");
 }
