@@ -980,7 +980,9 @@ TileShape tile_shape_for(const TcProblem& pr) {
     bn = 192;
   }
   int bk = (bn >= 192 && !(pr.epi == kEpiStore && pr.out_hi)) ? 16 : 32;
-  if (forced_bk == 16 || forced_bk == 32) bk = forced_bk;
+  // the 64-wide tile exists with depth 32 only: an override must not give it
+  // tensor maps of another depth than the kernel's stages expect
+  if ((forced_bk == 16 || forced_bk == 32) && bn != 64) bk = forced_bk;
   return {bn, bk};
 }
 
@@ -1192,6 +1194,9 @@ void gemm_tc_planes(const TcProblem& pr) {
   const int arrays = (pr.out ? 1 : 0) + (pr.out_hi ? 2 : 0) + (pr.aux ? 1 : 0);
   int pid = prof_begin(0, flops, 8.0 * ((double)pr.M * pr.K + (double)pr.N * pr.K) * pr.batch +
                                      4.0 * mn * arrays);
+  // the maps above were built for (BN, BK): the kernel launched must have the same stages
+  if ((BN == 64 && BK != 32) || (cta2 && BN == 128 && BK != 32) || (BK != 16 && BK != 32))
+    panic("gemm_tc_planes: no kernel for tile width %d with k-block depth %d%s", BN, BK, cta2 ? " (pairs)" : "");
 #define MALUS_TC_EPI_SWITCH(BN_, BK_, P_)                                                 \
   switch (pr.epi) {                                                                      \
     case kEpiStore: launch_tc<kEpiStore, BN_, BK_, P_>(ah, al, bh, bl, kp, grid); break;     \
