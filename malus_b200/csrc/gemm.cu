@@ -117,11 +117,13 @@ void gemm_simt(const GemmArgs& g) {
 
 // =============================================================== tcgen05
 //
-// Persistent 3xTF32 GEMM.  One CTA per SM walks a static list of 128x128
-// output tiles.  Warp 0 streams operand tiles with TMA into a 3-stage
-// shared-memory ring, warp 1 issues tcgen05.mma into one of two TMEM
-// accumulators (2 x 128 columns), and warps 2-5 drain the other accumulator
-// (tcgen05.ld -> registers -> global) while the next tile is being computed.
+// Persistent 3xTF32 GEMM.  One CTA per SM walks a static list of 128 x BN
+// output tiles (BN 64-256), or one 2-CTA cluster per TPC walks 256 x BN tiles
+// (CTA pairs, cta_group::2).  Warp 0 streams operand tiles with TMA into a
+// shared-memory ring of up to six stages, warp 1 issues tcgen05.mma into one of
+// two TMEM accumulators (2 x BN columns), and the epilogue warps (4 or 8) drain
+// the other accumulator (tcgen05.ld -> registers -> global) while the next
+// tile is being computed.
 // Each f32 operand arrives as two tf32 planes (hi = rn(x), lo = rn(x - hi));
 // the accumulator receives lo*hi + hi*lo + hi*hi per k-step.
 //
