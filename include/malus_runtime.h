@@ -274,7 +274,7 @@ int32_t malus_dp_finish(void);   /* wait for outstanding collectives */
  * registered leaf as soon as its gradient is final and averages every
  * completed bucket in place across ranks (one grouped all-reduce on the DP
  * stream); callers that build gradients outside the tape report them with
- * malus_dp_grad_ready(leaf, grad) (grad 0: no gradient this round).  All
+ * malus_dp_grad_ready(leaf, grad) (grad 0: no gradient in this backward pass).  All
  * ranks must report the same leaves in the same order. */
 int32_t malus_dp_register_leaves(const int64_t* leaves, size_t n, size_t bucket_bytes);
 int32_t malus_dp_grad_ready(int64_t leaf, int64_t grad);

@@ -91,7 +91,7 @@ namespace {
 struct DpLeafReg {
   std::unordered_map<int64_t, int> bucket_of;      // leaf -> bucket
   std::vector<int> need;                           // leaves per bucket
-  std::vector<int> have;                           // reported this round
+  std::vector<int> have;                           // reported in this backward pass
   std::vector<std::vector<std::pair<float*, size_t>>> pending;   // gradients per bucket
   std::vector<int64_t> held;                       // gradient handles retained until dp_leaves_join
   std::vector<int64_t> first_leaf;                 // one leaf of each bucket
@@ -136,7 +136,7 @@ int dp_leaf_ready(int64_t leaf, int64_t grad) {
   return 0;
 }
 
-// Launch every bucket that was only partly reported this round (its other
+// Launch every bucket that was only partly reported in this backward pass (its other
 // leaves received no gradient), make the main stream wait for all the
 // bucket reductions, and drop the gradients' extra references.
 int dp_leaves_join() {
