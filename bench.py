@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """nanoGPT f32 training throughput (tokens/s) on B200 through the malus C ABI.
 
-Workload: BASELINE.json configs[3], the Karpathy char-nanoGPT shape (V=65,
+Workload: benchmark config C4, the Karpathy char-nanoGPT shape (V=65,
 L=6, H=6, C=384, T=256, batch 64 per GPU, f32, AdamW lr=1e-3 b2=0.99),
 random-init N(0,0.02) weights (seeded Philox, as the reference) and uniform
 random token ids from a seed (synthetic; no dataset).  One step = forward +
@@ -9,6 +9,12 @@ backward + (N>1: all-reduce of the fused gradient buffer) + AdamW.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl malus|reference]
 
+The headline `value` is the compiled step (mode 1, one CUDA graph per step).
+At N=1 the same line also carries
+  * `tape`: the reference's own call sequence (examples/nanogpt_modular.ml
+    through RuntimeSymbols, the stdlib host functions and the tape, mode 0),
+    captured once as a CUDA graph and replayed, on the same C4 workload;
+  * `c5`: the GPT-2-small shape (config C5) through the compiled step.
 N>1 runs under torchrun, one process per GPU; per-GPU batch is fixed (weak
 scaling); value = all ranks' tokens / max-over-ranks device time.
 `--impl reference` times the CPU restatement of the reference's step (the
@@ -33,13 +39,17 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 C4 = dict(vocab=65, n_layer=6, n_head=6, n_embd=384, block_size=256, batch=64)
-# GPT-2-small shape (a parity config of the survey; measured on request, not the contract line)
+# GPT-2-small shape (a parity config of the survey; measured as the line's `c5` object)
 C5 = dict(vocab=50304, n_layer=12, n_head=12, n_embd=768, block_size=1024, batch=8, tied=True)
 WORKLOADS = {"c4": (C4, "C4 Karpathy char-nanoGPT: V65 L6 H6 C384 T256, batch 64/GPU"),
              "c5": (C5, "C5 GPT-2-small shape: V50304 L12 H12 C768 T1024, batch 8/GPU, tied head")}
 OPT = dict(lr=1e-3, beta1=0.9, beta2=0.99, eps=1e-8, wd=0.01)
 METRIC = "nanoGPT f32 train tokens/s"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
+# sequences per CPU step (both CPU legs): 2048 of the 16384 tokens of a C4 step
+# (MALUS_BENCH_CPU_BATCH shrinks it for the CPU test suite)
+CPU_SAMPLE_BATCH = int(os.environ.get("MALUS_BENCH_CPU_BATCH", "8"))
+L2_NOTE = "working set (activations, several GB) exceeds the 126 MB L2"
 
 
 def peaks():
@@ -58,13 +68,22 @@ def step_flops(cfg) -> float:
     return 3.0 * fwd
 
 
+def workload_config(workload: str, world: int) -> dict:
+    """The `config` object of both arms' lines (same keys and values)."""
+    cfg, name = WORKLOADS[workload]
+    return {"workload": name,
+            "model": "char-nanoGPT" if workload == "c4" else "nanoGPT (GPT-2-small shape)",
+            "global_batch": cfg["batch"] * world, "seq_len": cfg["block_size"],
+            "parallelism": f"dp{world}", "l2": L2_NOTE}
+
+
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks/throttle reasons sampled every 50 ms while under load."""
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
-        self.out = None
+        self.lines = []
 
     def __enter__(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -72,9 +91,8 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.lines = []
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except FileNotFoundError:
@@ -112,7 +130,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "period_ms": 50}
 
 
 def traffic_from_profiles(kernel: str, workload: str, mode: int):
@@ -127,25 +145,40 @@ def traffic_from_profiles(kernel: str, workload: str, mode: int):
     return None
 
 
-def cpu_baseline_port(cfg, steps=2, sample_batch=8):
-    """The oracle (CPU restatement of the reference step) on all host cores."""
+def _oracle_tokens_per_s(cfg, threads: int, steps: int, warmup: int, seed: int):
+    """Time `steps` oracle training steps (batch CPU_SAMPLE_BATCH of the C4
+    model) on `threads` host threads; returns (tokens/s, seconds, threads used)."""
     from oracle import pyoracle as O
-    threads = O.set_threads(os.cpu_count())
-    c = dict(cfg, batch=sample_batch)
+    used = O.set_threads(threads)
+    c = dict(cfg, batch=CPU_SAMPLE_BATCH)
     g = O.Gpt(**c, **OPT)
-    rng = np.random.default_rng(99)
-    m = sample_batch * cfg["block_size"]
-    x = rng.integers(0, cfg["vocab"], m).astype(np.int32)
-    y = rng.integers(0, cfg["vocab"], m).astype(np.int32)
-    g.step(x, y)  # warm-up (allocation, first touch)
+    rng = np.random.default_rng(seed)
+    m = CPU_SAMPLE_BATCH * cfg["block_size"]
+
+    def ids():
+        return rng.integers(0, cfg["vocab"], m).astype(np.int32)
+
+    for _ in range(warmup):
+        g.step(ids(), ids())
     t0 = time.perf_counter()
     for _ in range(steps):
-        g.step(x, y)
+        g.step(ids(), ids())
     dt = time.perf_counter() - t0
     g.close()
-    return {"value": steps * m / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} steps of the C4 model with batch {sample_batch} x {cfg['block_size']} "
-                      f"tokens ({m} tokens/step) on the oracle's OpenMP loops"}
+    return steps * m / dt, dt, used
+
+
+def cpu_baseline_port(cfg, steps=2):
+    """The oracle (CPU restatement of the reference step) on all host cores, and
+    one step on a single thread beside it."""
+    v, _, threads = _oracle_tokens_per_s(cfg, os.cpu_count() or 1, steps, 1, 99)
+    v1, dt1, _ = _oracle_tokens_per_s(cfg, 1, 1, 0, 98)
+    m = CPU_SAMPLE_BATCH * cfg["block_size"]
+    return {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} steps of the C4 model with batch {CPU_SAMPLE_BATCH} x {cfg['block_size']} "
+                      f"tokens ({m} tokens/step) on the oracle's OpenMP loops",
+            "single_thread": {"value": v1, "unit": "tokens/s", "cores": 1,
+                              "sample": f"1 step of batch {CPU_SAMPLE_BATCH} on one thread ({dt1:.1f} s)"}}
 
 
 def c2_cpu_ops(threads: int):
@@ -205,7 +238,7 @@ def run_ops(args):
     the oracle's CPU path on 1 thread and on all host threads; GB/s = algorithmic
     bytes / time."""
     from malus_b200 import opbench
-    rows, peaks = opbench.run(reps=20, verbose=False)
+    rows, peaks_ = opbench.run(reps=20, verbose=False)
     ncpu = os.cpu_count() or 1
     cpu1 = c2_cpu_ops(1)
     cpun = c2_cpu_ops(ncpu)
@@ -213,7 +246,7 @@ def run_ops(args):
         if r["op"] in cpu1:
             r["cpu1_gbs"] = round(r["bytes"] / cpu1[r["op"]] / 1e9, 2)
             r["cpun_gbs"] = round(r["bytes"] / cpun[r["op"]] / 1e9, 2)
-    print(json.dumps({"metric": "C2 op microbench", "unit": "GB/s", "peaks": peaks, "cpu_threads": ncpu,
+    print(json.dumps({"metric": "C2 op microbench", "unit": "GB/s", "peaks": peaks_, "cpu_threads": ncpu,
                       "ops": rows}))
     print(f"| op | GPU ms | GPU GB/s | of HBM | f32 TF/s (tf32 pipe) | CPU 1-thread GB/s | CPU {ncpu}-thread GB/s |")
     print("|---|---:|---:|---:|---:|---:|---:|")
@@ -224,36 +257,148 @@ def run_ops(args):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the oracle step (the reference's CPU path restated) on
+    all host threads, on rank 0 only; each step is a batch-8 sample of the C4
+    step.  A single-thread step is timed beside it."""
     if rank != 0:
         return
-    from oracle import pyoracle as O
-    threads = O.set_threads(os.cpu_count())
-    sample_batch = 4
-    c = dict(C4, batch=sample_batch)
-    g = O.Gpt(**c, **OPT)
-    rng = np.random.default_rng(5)
-    m = sample_batch * C4["block_size"]
-    for _ in range(args.warmup):
-        g.step(rng.integers(0, 65, m).astype(np.int32), rng.integers(0, 65, m).astype(np.int32))
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        g.step(rng.integers(0, 65, m).astype(np.int32), rng.integers(0, 65, m).astype(np.int32))
-    dt = time.perf_counter() - t0
-    g.close()
-    v = args.steps * m / dt
+    v, dt, threads = _oracle_tokens_per_s(C4, os.cpu_count() or 1, args.steps, args.warmup, 5)
+    v1, dt1, _ = _oracle_tokens_per_s(C4, 1, 1, 0, 6)
+    m = CPU_SAMPLE_BATCH * C4["block_size"]
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic uniform token ids from a seed; N(0,0.02) Philox init",
-            "config": {"workload": "C4 Karpathy char-nanoGPT (V65 L6 H6 C384 T256), CPU sample of "
-                                   f"batch {sample_batch} per step", "global_batch": sample_batch,
-                       "seq_len": 256, "parallelism": "cpu"},
+            "config": workload_config("c4", world),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": f"batch {sample_batch} x 256 tokens per step on the oracle "
-                                       "(CPU restatement of the reference step; the Rust/Metal "
-                                       "reference cannot build or run on this box)"},
+                             "sample": f"each step: batch {CPU_SAMPLE_BATCH} x 256 tokens ({m} of the C4 step's "
+                                       "16384) on the oracle (CPU restatement of the reference step; the "
+                                       "Rust/Metal reference cannot build or run on this box)",
+                             "single_thread": {"value": v1, "unit": "tokens/s", "cores": 1,
+                                               "sample": f"1 step of batch {CPU_SAMPLE_BATCH} on one thread "
+                                                         f"({dt1:.1f} s)"}},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+class Runner:
+    """Times one (workload, mode) on this rank's GPU: the device-timed pass with
+    inputs resident, an optional profiled pass for the GEMM roofline, and the
+    end-to-end pass through malus_gpt_step with host ids."""
+
+    def __init__(self, lib, torch, dist, world, rank):
+        self.lib, self.torch, self.dist, self.world, self.rank = lib, torch, dist, world, rank
+        self.mstream = torch.cuda.ExternalStream(lib.malus_stream())
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def measure(self, workload, mode, graph, steps, warmup, roofline=True, clocks=None):
+        import malus_b200 as M
+        torch, lib = self.torch, self.lib
+        cfg = dict(WORKLOADS[workload][0])
+        model = M.GPT(**cfg, **OPT, mode=mode, use_graph=graph, seed=0)
+        m = cfg["batch"] * cfg["block_size"]
+        rng = np.random.default_rng(1000 + self.rank)
+        nb = steps + warmup
+        xs = rng.integers(0, cfg["vocab"], (nb, m)).astype(np.int32)
+        ys = rng.integers(0, cfg["vocab"], (nb, m)).astype(np.int32)
+        xd = torch.from_numpy(xs).cuda()
+        yd = torch.from_numpy(ys).cuda()
+        for i in range(warmup):
+            lib.malus_gpt_step_device(model.h, xd[i].data_ptr(), yd[i].data_ptr())
+        lib.gpu_barrier()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+
+        def timed_steps():
+            self.barrier()
+            torch.cuda.synchronize()
+            lib.gpu_barrier()
+            ev0.record(self.mstream)
+            for i in range(steps):
+                j = warmup + i
+                lib.malus_gpt_step_device(model.h, xd[j].data_ptr(), yd[j].data_ptr())
+            ev1.record(self.mstream)
+            lib.gpu_barrier()
+            torch.cuda.synchronize()
+            return self.max_over_ranks(ev0.elapsed_time(ev1))
+
+        launches0 = lib.malus_launch_count()
+        if clocks is not None:
+            clocks.__enter__()
+        dt_ms = timed_steps()
+        launches = lib.malus_launch_count() - launches0
+        self.barrier()
+        loss_last = lib.malus_gpt_last_loss(model.h)
+        out = {"value": round(self.world * steps * m / (dt_ms / 1e3), 1),
+               "ms_per_step": round(dt_ms / steps, 4), "gpu_launches": int(launches),
+               "loss_last": loss_last}
+
+        # roofline: the same K steps again, every GEMM bracketed by CUDA events on
+        # the runtime stream (the events cost a few percent, so `value` is taken
+        # without them)
+        if roofline:
+            lib.malus_prof_enable(1)
+            dt_prof_ms = timed_steps()
+            cnt, ms_k, fl_k, by_k = C.c_int64(), C.c_double(), C.c_double(), C.c_double()
+            lib.malus_prof_report(0, C.byref(cnt), C.byref(ms_k), C.byref(fl_k), C.byref(by_k))
+            lib.malus_prof_enable(0)
+            out["roofline"] = self._gemm_roofline(cnt.value, ms_k.value, fl_k.value, by_k.value, dt_prof_ms,
+                                                  steps, workload, mode)
+
+        # end to end through the public API (host ids in, host loss out)
+        self.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(steps):
+            j = (warmup + i) % nb
+            model.step(xs[j], ys[j])        # H2D ids, step, D2H loss (synchronous)
+        e2e_s = self.max_over_ranks(time.perf_counter() - t0)
+        if clocks is not None:
+            clocks.__exit__(None, None, None)
+        out["e2e"] = {"value": self.world * steps * m / e2e_s, "unit": "tokens/s",
+                      "h2d_bytes_per_step": 2 * m * 4, "d2h_bytes_per_step": 4}
+        model.close()
+        del xd, yd
+        torch.cuda.empty_cache()
+        return out
+
+    def _gemm_roofline(self, cnt, ms_k, fl_k, by_k, dt_prof_ms, steps, workload, mode):
+        if not cnt:
+            return None
+        _, bf16, bf16_sus, peak_src = peaks()
+        per_launch_ms = ms_k / cnt
+        algo = fl_k / cnt / (per_launch_ms / 1e3) / 1e12   # 2MNK f32 flops per launch / time
+        # tf32 runs at half the bf16 rate on tcgen05; 3xTF32 issues three tf32
+        # products per f32 product.  `peak` uses the burst bf16 figure (the
+        # GEMMs run at full clock in the short timed region); the sustained
+        # (power-capped, seconds-long) figure is reported beside it.
+        f32_burst = 0.5 * bf16 / 3.0
+        f32_sus = 0.5 * (bf16_sus or bf16) / 3.0
+        return {"bound": "tensor", "kernel": "k_gemm_tc (3xTF32 tcgen05)",
+                "achieved": round(algo, 2), "peak": round(f32_burst, 2), "unit": "TFLOP/s",
+                "frac": round(algo / f32_burst, 4), "frac_sustained": round(algo / f32_sus, 4),
+                "peak_sustained": round(f32_sus, 2),
+                "traffic": traffic_from_profiles("k_gemm_tc", workload, mode),
+                "algorithmic_bytes_per_launch": round(by_k / cnt),
+                "launches_per_step": cnt / steps,
+                "gemm_share_of_step": round(ms_k / dt_prof_ms, 4) if self.world == 1 else None,
+                "executed_tf32_tflops": round(3.0 * algo, 2),
+                "profiled_pass_ms_per_step": round(dt_prof_ms / steps, 4),
+                "note": f"achieved = algorithmic f32 2MNK per launch / mean launch time (CUDA events on the "
+                        f"runtime stream around every GEMM, over a second pass of the same K steps); "
+                        f"peak = {peak_src} burst bf16 dense ({bf16}) x 1/2 (tf32 rate) / 3 (3xTF32 "
+                        f"products per f32 product); peak_sustained the same from the sustained figure "
+                        f"({bf16_sus})"}
 
 
 def main():
@@ -262,13 +407,15 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="malus", choices=["malus", "reference"])
-    ap.add_argument("--mode", type=int, default=int(os.environ.get("MALUS_BENCH_MODE", "1")))
+    ap.add_argument("--mode", type=int, default=int(os.environ.get("MALUS_BENCH_MODE", "1")),
+                    help="headline path: 1 compiled step, 0 the reference's call sequence (tape)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the `tape` and `c5` objects")
     ap.add_argument("--ops", action="store_true", help="C2 op microbench (GPU and CPU oracle)")
     ap.add_argument("--workload", default="c4", choices=sorted(WORKLOADS),
-                    help="c4 (the contract line) or c5 (GPT-2-small shape, on request)")
+                    help="headline workload: c4 (the contract line) or c5")
     ap.add_argument("--graph", type=int, default=int(os.environ.get("MALUS_BENCH_GRAPH", "1")),
-                    help="replay the fused step as one CUDA graph (mode 1)")
+                    help="replay each step as one CUDA graph")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -298,120 +445,39 @@ def main():
         from malus_b200.dist import init_data_parallel
         init_data_parallel(lib, rank, world, timeout_ms=120000)
 
-    cfg, workload_name = WORKLOADS[args.workload]
-    cfg = dict(cfg)
-    model = M.GPT(**cfg, **OPT, mode=args.mode, use_graph=args.graph, seed=0)
-    m = cfg["batch"] * cfg["block_size"]
-    rng = np.random.default_rng(1000 + rank)
-    nb = args.steps + args.warmup
-    xs = rng.integers(0, cfg["vocab"], (nb, m)).astype(np.int32)
-    ys = rng.integers(0, cfg["vocab"], (nb, m)).astype(np.int32)
-    xd = torch.from_numpy(xs).cuda()
-    yd = torch.from_numpy(ys).cuda()
-    mstream = torch.cuda.ExternalStream(lib.malus_stream())
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    for i in range(args.warmup):
-        lib.malus_gpt_step_device(model.h, xd[i].data_ptr(), yd[i].data_ptr())
-    lib.gpu_barrier()
-
-    # ---------------- device-timed throughput (inputs resident in HBM) ----------------
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-
-    def timed_steps():
-        barrier()
-        torch.cuda.synchronize()
-        lib.gpu_barrier()
-        ev0.record(mstream)
-        for i in range(args.steps):
-            j = args.warmup + i
-            lib.malus_gpt_step_device(model.h, xd[j].data_ptr(), yd[j].data_ptr())
-        ev1.record(mstream)
-        lib.gpu_barrier()
-        torch.cuda.synchronize()
-        return max_over_ranks(ev0.elapsed_time(ev1))
-
-    launches0 = lib.malus_launch_count()
-    with ClockSampler(local) as clk:
-        dt_ms = timed_steps()
-    launches = lib.malus_launch_count() - launches0
-    barrier()
-    loss_last = lib.malus_gpt_last_loss(model.h)
-    value = world * args.steps * m / (dt_ms / 1e3)
-
-    # ---------------- roofline: the same K steps again, every GEMM bracketed by
-    # CUDA events on the runtime stream (the events cost a few percent, so the
-    # throughput above is taken without them)
-    lib.malus_prof_enable(1)
-    dt_prof_ms = timed_steps()
-    cnt, ms_k, fl_k, by_k = C.c_int64(), C.c_double(), C.c_double(), C.c_double()
-    lib.malus_prof_report(0, C.byref(cnt), C.byref(ms_k), C.byref(fl_k), C.byref(by_k))
-    lib.malus_prof_enable(0)
-    hbm, bf16, bf16_sus, peak_src = peaks()
-    roofline = None
-    if cnt.value:
-        per_launch_ms = ms_k.value / cnt.value
-        algo = fl_k.value / cnt.value / (per_launch_ms / 1e3) / 1e12   # 2MNK f32 flops per launch / time
-        tf32_peak = 0.5 * (bf16_sus or bf16)            # tf32 runs at half the bf16 rate on tcgen05
-        f32_peak = tf32_peak / 3.0                      # 3xTF32: three tf32 products per f32 product
-        roofline = {"bound": "tensor", "kernel": "k_gemm_tc (3xTF32 tcgen05)",
-                    "achieved": round(algo, 2), "peak": round(f32_peak, 2), "unit": "TFLOP/s",
-                    "frac": round(algo / f32_peak, 4),
-                    "traffic": traffic_from_profiles("k_gemm_tc", args.workload, args.mode),
-                    "algorithmic_bytes_per_launch": round(by_k.value / cnt.value),
-                    "launches_per_step": cnt.value / args.steps,
-                    "gemm_share_of_step": round(ms_k.value / dt_prof_ms, 4) if world == 1 else None,
-                    "executed_tf32_tflops": round(3.0 * algo, 2),
-                    "profiled_pass_ms_per_step": round(dt_prof_ms / args.steps, 4),
-                    "note": f"achieved = algorithmic f32 2MNK per launch / mean launch time (CUDA events on the "
-                            f"runtime stream around every GEMM, over a second pass of the same K steps); "
-                            f"peak = {peak_src} sustained bf16 dense ({bf16_sus or bf16}) "
-                            "x 1/2 (tf32 rate) / 3 (3xTF32 products per f32 product)"}
-
-    # ---------------- end to end through the public API (host buffers) ----------------
-    barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        j = (args.warmup + i) % nb
-        model.step(xs[j], ys[j])        # H2D ids, step, D2H loss (synchronous)
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    e2e = {"value": world * args.steps * m / e2e_s, "unit": "tokens/s",
-           "h2d_bytes_per_step": 2 * m * 4, "d2h_bytes_per_step": 4}
+    run = Runner(lib, torch, dist, world, rank)
+    clk = ClockSampler(local)
+    head = run.measure(args.workload, args.mode, args.graph, args.steps, args.warmup, roofline=True, clocks=clk)
+    extras = {}
+    if world == 1 and not args.no_extras:
+        if not (args.workload == "c4" and args.mode == 0):
+            t = run.measure("c4", 0, 1, args.steps, args.warmup, roofline=False)
+            t["path"] = ("the reference's call sequence (nanogpt_modular.ml through RuntimeSymbols, stdlib "
+                         "host functions, tape backward, AdamW), captured once as a CUDA graph and replayed")
+            t["of_headline"] = round(t["value"] / head["value"], 4) if args.workload == "c4" else None
+            extras["tape"] = t
+        if args.workload != "c5":
+            c5 = run.measure("c5", 1, 1, max(3, min(args.steps, 20)), 3, roofline=True)
+            c5["config"] = workload_config("c5", world)
+            extras["c5"] = c5
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_port(cfg)
+        cpu = cpu_baseline_port(C4 if args.workload == "c4" else C5)
 
-    model.close()
     if world > 1:
         lib.malus_dp_destroy()
     if rank == 0:
-        line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt_ms / args.steps, 4),
+        cfg = WORKLOADS[args.workload][0]
+        line = {"metric": METRIC, "value": head["value"], "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": f"synthetic: uniform token ids in [0,{cfg['vocab']}) from a seed; N(0,0.02) Philox init",
-                "config": {"workload": workload_name,
-                           "model": "char-nanoGPT" if args.workload == "c4" else "nanoGPT (GPT-2-small shape)",
-                           "global_batch": cfg["batch"] * world,
-                           "seq_len": cfg["block_size"], "parallelism": f"dp{world}",
-                           "mode": "fused" if args.mode == 1 else "tape",
-                           "cuda_graph": bool(args.graph and args.mode == 1),
-                           "l2": "working set (activations, several GB) exceeds the 126 MB L2"},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
-                "clocks": clk.summary(), "loss_last": loss_last,
-                "algorithmic_tflops_per_step": round(step_flops(cfg) / 1e12, 4)}
+                "config": workload_config(args.workload, world),
+                "path": {"mode": "fused" if args.mode == 1 else "tape", "cuda_graph": bool(args.graph)},
+                "roofline": head.get("roofline"), "cpu_baseline": cpu, "e2e": head["e2e"],
+                "gpu_launches": head["gpu_launches"], "clocks": clk.summary(), "loss_last": head["loss_last"],
+                "algorithmic_tflops_per_step": round(step_flops(cfg) / 1e12, 4), **extras}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

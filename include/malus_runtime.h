@@ -115,8 +115,8 @@ void malus_record_diff(float v);
 void bench_step_begin(void);
 void bench_step_end(void);
 
-/* strio.rs (out of scope for the training hot path: BASELINE uses synthetic
- * token ids).  Provided so a JIT link table resolves: strings are host byte
+/* strio.rs (out of scope for the training hot path, whose workloads use
+ * synthetic token ids).  Provided so a JIT link table resolves: strings are host byte
  * boxes, read_file reads a whole file. */
 int64_t malus_str_box(const uint8_t* bytes, size_t len);
 int64_t malus_read_file(int64_t path_box);
@@ -449,7 +449,10 @@ void malus_prof_report(int32_t cls, int64_t* count, double* ms, double* flops, d
  * device looks up that array's device address (cudaGetSymbolAddress); make
  * that first call before any stream capture.  All calls share the array, so
  * calls that overlap on the GPU race; ordered calls (one stream) are safe.
- * Returns 0 on success. */
+ * An id outside [0, vocab) is skipped without a report (its dout row adds to
+ * no gradient row; the call still returns 0), because this entry point does
+ * not touch the runtime's error word; validate ids first where that matters.
+ * n = 0 writes zeros to dweight.  Returns 0 on success. */
 int32_t malus_embedding_bwd_noalloc(const float* dout, const void* indices, int32_t index_dtype,
                                     size_t n, size_t vocab, size_t dim, float* dweight,
                                     void* stream);

@@ -144,8 +144,10 @@ void embedding_bwd(const float* dout, const void* idx, int idx_dtype, float* dw,
                    size_t vocab, size_t dim);
 void permute_nd(const float* x, float* out, const Shape& in_shape, const int* perm);
 size_t embedding_bwd_ws_bytes(size_t n, size_t vocab);
+// err: device word set to 4 when an id lies outside [0, vocab) (nullptr: a
+// word in the workspace, cleared per call and never read)
 int embedding_bwd_ws(const float* dout, const void* idx, int idx_dtype, float* dw, size_t n,
-                     size_t vocab, size_t dim, void* workspace, cudaStream_t st);
+                     size_t vocab, size_t dim, void* workspace, cudaStream_t st, int32_t* err);
 
 // ---- GEMM (gemm.cu) ----
 // C[b] (MxN) = alpha * op(A[b]) * op(B[b]) + beta * C[b], f32 semantics via

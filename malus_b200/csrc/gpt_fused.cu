@@ -901,7 +901,9 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
   }
   // embeddings: x0 = wte[tok] + wpe[pos]
   float* dwte = f->cfg.tied ? f->emb_tmp : G(top);
-  int er = embedding_bwd_ws(g3, xt, MALUS_I32, dwte, M, V, C, f->emb_ws, stream());
+  // a token id outside [0, V) is reported through the runtime's error word,
+  // as in __embedding_bwd
+  int er = embedding_bwd_ws(g3, xt, MALUS_I32, dwte, M, V, C, f->emb_ws, stream(), device_error_word());
   if (er != 0) panic("fused step: embedding backward failed (%d)", er);
   if (f->cfg.tied) {
     k_add_inplace<<<grid_for((size_t)V * C, 256), 256, 0, stream()>>>(G(top), f->emb_tmp, (size_t)V * C);

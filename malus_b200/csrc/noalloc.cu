@@ -10,6 +10,10 @@
 // array of fixed size; the caller passes the inputs, the output and the
 // stream.  It calls no cudaMalloc/cudaFree and no allocating library routine,
 // and it does not touch the runtime's own context (pool, error word, stream).
+// Because of that, an id outside [0, vocab) is skipped without a report: its
+// row of dout contributes to no gradient row, and the call still returns 0
+// (the allocating __embedding_bwd reports such ids through the runtime's
+// error word).
 //
 // The array exists on every GPU that loads this library, for the life of the
 // process.  All calls share it: two calls that overlap on the GPU (different
@@ -40,7 +44,14 @@ void* g_addr[64] = {nullptr};  // device address of the array, per device ordina
 // __device__ array is not a device address, so fetch the real one.
 int scratch_address(void** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -7;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    fprintf(stderr, "malus: embedding_bwd_noalloc: cudaGetDevice failed\n");
+    return -7;
+  }
+  if (dev < 0 || dev >= 64) {
+    fprintf(stderr, "malus: embedding_bwd_noalloc: device ordinal %d is outside 0..63\n", dev);
+    return -7;
+  }
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_addr[dev]) {
     void* p = nullptr;
@@ -85,5 +96,5 @@ extern "C" int32_t malus_embedding_bwd_noalloc(const float* dout, const void* in
   int r = scratch_address(&ws);
   if (r) return r;
   return embedding_bwd_ws(dout, indices, index_dtype, dweight, n, vocab, dim, ws,
-                          (cudaStream_t)stream);
+                          (cudaStream_t)stream, nullptr);
 }

@@ -957,9 +957,12 @@ void permute_nd(const float* x, float* out, const Shape& s, const int* perm) {
 }  // namespace malus
 
 // ---------------------------------------------------------------------------
-// Embedding VJP on caller-provided workspace and stream (used by the entry
-// point that allocates nothing).  Same kernels and order as embedding_bwd, so
-// results are bit-identical; errors are returned instead of raised.
+// Embedding VJP on caller-provided workspace and stream (used by the fused
+// step and by the entry point that allocates nothing).  Same kernels and order
+// as embedding_bwd, so results are bit-identical; errors are returned instead
+// of raised.  An id outside [0, V) contributes nothing and sets *err to 4
+// (err = nullptr: a word at the head of the workspace, cleared by every call
+// and never read, so such ids are skipped without a report).
 namespace malus {
 
 static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
@@ -974,7 +977,7 @@ size_t embedding_bwd_ws_bytes(size_t n, size_t V) {
 }
 
 int embedding_bwd_ws(const float* dout, const void* idx, int idt, float* dw, size_t n, size_t V,
-                     size_t D, void* ws, cudaStream_t st) {
+                     size_t D, void* ws, cudaStream_t st, int32_t* err) {
   if (!V || !D) return 0;
   if (!n) return cudaMemsetAsync(dw, 0, V * D * sizeof(float), st) == cudaSuccess ? 0 : -5;
   int nch = (int)((n + kEmbChunk - 1) / kEmbChunk);
@@ -982,23 +985,37 @@ int embedding_bwd_ws(const float* dout, const void* idx, int idt, float* dw, siz
   int nt = (int)((m + kScanTile - 1) / kScanTile);
   if (nt == 0) nt = 1;
   char* p = (char*)ws;
-  int32_t* err = (int32_t*)p;                 p += 256;
+  int32_t* own_err = (int32_t*)p;             p += 256;
   auto* keys = (unsigned long long*)p;        p += align256((size_t)nch * kEmbChunk * 8);
   int* counts = (int*)p;                      p += align256(m * 4);
   int* offs = (int*)p;                        p += align256((m + 1) * 4);
   int* order = (int*)p;                       p += align256(n * 4);
   int* sums = (int*)p;
+  if (!err) {
+    err = own_err;
+    if (cudaMemsetAsync(err, 0, sizeof(int32_t), st) != cudaSuccess) return -5;
+  }
   if (cudaMemsetAsync(counts, 0, m * sizeof(int), st) != cudaSuccess) return -5;
+  // each launch is checked right after it (cudaGetLastError), so an error
+  // left by some earlier, unrelated launch is not reported as this call's
+  int bad = 0;
+  auto check = [&] { if (cudaGetLastError() != cudaSuccess) bad = 1; };
   k_emb_chunk_sort<<<nch, 512, 0, st>>>(idx, idt, n, V, nch, keys, counts, err);
+  check();
   k_scan_tile_sums<<<nt, 1024, 0, st>>>(counts, m, sums);
+  check();
   k_scan_sums_serial<<<1, 32, 0, st>>>(sums, nt, offs + m);
+  check();
   k_scan_tile_apply<<<nt, 1024, 0, st>>>(counts, m, sums, offs);
+  check();
   k_emb_scatter<<<nch, 512, 0, st>>>(keys, n, nch, offs, order);
+  check();
   unsigned threads = (unsigned)std::min<size_t>(256, std::max<size_t>(32, ((D + 3) / 4 + 31) / 32 * 32));
   dim3 grid((unsigned)V, (unsigned)(((D + 3) / 4 + threads - 1) / threads));
   k_emb_segsum<<<grid, threads, 0, st>>>(dout, order, offs, nch, V, D, dw);
+  check();
   count_launch(6);
-  return cudaPeekAtLastError() == cudaSuccess ? 0 : -6;
+  return bad ? -6 : 0;
 }
 
 }  // namespace malus

@@ -1,4 +1,4 @@
-"""Per-op microbenchmark through the C ABI.
+"""Per-op microbenchmark (the C2 op shapes of the benchmark configs) through the C ABI.
 
 Each op runs on seeded N(0,1) inputs of the configured shape; the timing is
 the median of `--reps` launches bracketed by CUDA events on the runtime's own

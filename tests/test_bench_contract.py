@@ -14,7 +14,7 @@ ROOT = Path(__file__).resolve().parent.parent
 
 
 def _run(env_extra):
-    env = dict(os.environ, **env_extra)
+    env = dict(os.environ, MALUS_BENCH_CPU_BATCH="1", **env_extra)
     return subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
                            "--warmup", "3"], cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
 
@@ -31,6 +31,14 @@ def test_reference_arm_line():
     assert d["steps"] == 1 and d["warmup"] == 3
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    st = cb["single_thread"]
+    assert st["cores"] == 1 and st["value"] > 0 and st["unit"] == "tokens/s"
+    sys.path.insert(0, str(ROOT))
+    try:
+        import bench
+    finally:
+        sys.path.pop(0)
+    assert d["config"] == bench.workload_config("c4", 1)   # the same config object as the GPU arm
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
 

@@ -1,6 +1,6 @@
 """GPU: the nanoGPT training step (malus_gpt_*) against the CPU oracle's
 restatement of the same step, from identical seeded initial weights and
-token ids.  Bar (BASELINE.json): loss curves within 0.5% per step."""
+token ids.  Bar: loss curves within 0.5% per step."""
 import os
 
 import numpy as np
