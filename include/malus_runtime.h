@@ -142,10 +142,13 @@ void malus_pool_stats(int64_t* hits, int64_t* misses, int64_t* pooled_bytes, int
 void malus_pool_reset(void);                    /* metal.rs:175 */
 void malus_set_mem_budget(int64_t bytes);       /* metal.rs:148 */
 void bench_enable(void);                        /* bench.rs:18 */
-/* bench.rs:51-70: warm median over steps after 3 warm-up steps, in ms; -1 if
- * fewer than 4 steps were recorded.  n_steps receives the timed count. */
+/* bench.rs:51-70: warm median (host clock, ms) over the steps after 3 warm-up
+ * steps; -1 if fewer than 4 steps were recorded.  n_steps receives the timed
+ * count.  bench_report_range gives the same steps' min and max (BenchReport's
+ * min / max; -1 when there are none). */
 double bench_report(int64_t* n_steps);
-void bench_reset(void);                         /* bench.rs:72 */
+void bench_report_range(double* min_ms, double* max_ms);
+void bench_reset(void);                         /* bench.rs:72: disables and clears */
 /* Test helper mirroring tape.rs:733-750 tape_reset: drops leaves, grads, tape. */
 void malus_tape_reset(void);
 /* Number of live leaves / leaf grads (tape.rs:791-797 registry_lens). */
@@ -163,9 +166,14 @@ int64_t malus_tensor_wrap(int32_t dtype, void* dev_ptr, const size_t* shape, siz
 /* Reset the Philox call counter (metal.rs:1713-1715 is thread-local; the
  * reference resets it only per thread start). */
 void malus_rng_reset(uint64_t counter);
+/* Host-only: the Philox4x32-10 block function of metal.rs:1692-1711 (Salmon
+ * et al., SC'11) applied in place to a 4-word counter under a 2-word key, for
+ * known-answer tests of the generator behind tensor_randn / malus_rand_*. */
+void malus_philox4x32_10(uint32_t ctr[4], const uint32_t key[2]);
 /* Select the CUDA device for this process (default: LOCAL_RANK or 0). */
 void malus_set_device(int32_t dev);
-/* Device kernel launches issued by this runtime since the last reset. */
+/* Device kernel launches issued by this runtime since the last reset; the
+ * kernels of a captured graph count at each malus_graph_replay, not at capture. */
 int64_t malus_launch_count(void);
 void malus_launch_count_reset(void);
 /* Current stream as a cudaStream_t (for callers that share the stream). */
@@ -360,6 +368,9 @@ int64_t malus_gpt_param(int64_t model, int32_t i);
 /* Gradient of parameter i from the last step (before the update; summed over
  * data-parallel ranks), same shape; a borrowed handle like malus_gpt_param. */
 int64_t malus_gpt_grad(int64_t model, int32_t i);
+/* AdamW state of parameter i (which = 0: first moment m, 1: second moment v),
+ * a borrowed handle like malus_gpt_param. */
+int64_t malus_gpt_moment(int64_t model, int32_t i, int32_t which);
 int64_t malus_gpt_num_elements(int64_t model);
 /* Host-only (no device work): the fused parameter/gradient buffer layout for a
  * config.  Writes offsets[i] and sizes[i] (elements) for the first n tensors,

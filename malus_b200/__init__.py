@@ -111,6 +111,7 @@ SIGNATURES: dict[str, tuple] = {
     "malus_set_mem_budget": (None, [i64]),
     "bench_enable": (None, []),
     "bench_report": (C.c_double, [P_i64]),
+    "bench_report_range": (None, [C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "bench_reset": (None, []),
     "malus_tape_reset": (None, []),
     "malus_tape_registry_lens": (None, [P_i64, P_i64]),
@@ -120,6 +121,7 @@ SIGNATURES: dict[str, tuple] = {
     "malus_tensor_write": (None, [i64, vp, sz]),
     "malus_tensor_wrap": (i64, [i32, vp, P_sz, sz]),
     "malus_rng_reset": (None, [u64]),
+    "malus_philox4x32_10": (None, [C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
     "malus_set_device": (None, [i32]),
     "malus_launch_count": (i64, []),
     "malus_launch_count_reset": (None, []),
@@ -199,6 +201,7 @@ SIGNATURES: dict[str, tuple] = {
     "malus_gpt_num_params": (i32, [i64]),
     "malus_gpt_param": (i64, [i64, i32]),
     "malus_gpt_grad": (i64, [i64, i32]),
+    "malus_gpt_moment": (i64, [i64, i32, i32]),
     "malus_gpt_num_elements": (i64, [i64]),
     "malus_gpt_layout": (i32, [C.POINTER(GptConfig), P_i64, P_i64, i32, P_i64]),
     "malus_gpt_dp_buckets": (i32, [C.POINTER(GptConfig), P_i64, P_i64, i32]),
@@ -324,6 +327,13 @@ class GPT:
         lib = load()
         return [Tensor(lib.malus_gpt_grad(self.h, i), owned=False).numpy()
                 for i in range(lib.malus_gpt_num_params(self.h))]
+
+    def moments(self) -> tuple[list[np.ndarray], list[np.ndarray]]:
+        """AdamW first and second moments, in parameter order."""
+        lib = load()
+        n = lib.malus_gpt_num_params(self.h)
+        return ([Tensor(lib.malus_gpt_moment(self.h, i, 0), owned=False).numpy() for i in range(n)],
+                [Tensor(lib.malus_gpt_moment(self.h, i, 1), owned=False).numpy() for i in range(n)])
 
     def close(self):
         if self.h:

@@ -136,6 +136,9 @@ void xent_fwd(const float* logits, const void* targets, int tgt_dtype, float* pr
               size_t n, size_t v);
 void xent_bwd(const float* probs, const void* targets, int tgt_dtype, const float* dout_dev,
               float* dx, size_t n, size_t v);
+// the same with a host scale in place of dout[0] / n
+void xent_bwd_scaled(const float* probs, const void* targets, int tgt_dtype, float scale, float* dx,
+                     size_t n, size_t v);
 void xent_nll_gather(const float* probs, const void* targets, int tgt_dtype, float* out, size_t n,
                      size_t v);
 void embedding_fwd(const float* w, const void* idx, int idx_dtype, float* out, size_t n,

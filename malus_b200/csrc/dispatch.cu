@@ -247,17 +247,12 @@ int64_t kernel_dispatch_v2(uint64_t kernel_id, const int64_t* h, size_t hc, cons
       break;
     }
     case K_XENT_BWD: {
+      // (p - onehot) * scale with the host-computed scale uniform
+      // (transformer_bwd.ml:56-75)
       need(2);
       int32_t vocab = ui(u, ub, 0);
       float scale = uf(u, ub, 1);
-      // (p - onehot) * scale with a host-supplied scale: express it through
-      // the device-scalar CE backward with dout = scale * N.
-      size_t n = on / (size_t)vocab;
-      float dval = scale * (float)n;
-      float* d = (float*)scratch_alloc(16);
-      scalar_op_imm(kSFill, nullptr, dval, d, 1);
-      xent_bwd(fptr(h[0]), vptr(h[1]), tb(h[1])->dtype, d, o, n, (size_t)vocab);
-      scratch_free(d);
+      xent_bwd_scaled(fptr(h[0]), vptr(h[1]), tb(h[1])->dtype, scale, o, on / (size_t)vocab, (size_t)vocab);
       break;
     }
     case K_EMBED: {

@@ -483,6 +483,10 @@ float malus_gpt_last_loss(int64_t h) {
 int32_t malus_gpt_num_params(int64_t h) { return (int32_t)reinterpret_cast<Model*>(h)->params.size(); }
 int64_t malus_gpt_param(int64_t h, int32_t i) { return reinterpret_cast<Model*>(h)->params.at((size_t)i); }
 int64_t malus_gpt_grad(int64_t h, int32_t i) { return reinterpret_cast<Model*>(h)->gradv.at((size_t)i); }
+int64_t malus_gpt_moment(int64_t h, int32_t i, int32_t which) {
+  auto* m = reinterpret_cast<Model*>(h);
+  return (which ? m->vs : m->ms).at((size_t)i);
+}
 int64_t malus_gpt_num_elements(int64_t h) {
   auto* m = reinterpret_cast<Model*>(h);
   int64_t n = 0;

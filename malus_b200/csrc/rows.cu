@@ -439,13 +439,43 @@ __global__ void k_xent_nll_gather(const float* __restrict__ probs, const void* _
   out[i] = -logf(probs[i * V + (size_t)t]);
 }
 
+// dx = (p - onehot(t)) * scale, scale = dout[0] / rows (the tape's VJP) or a
+// host value (the stdlib kernel's uniform, transformer_bwd.ml:56-75).  With
+// 32-bit flat indices and aligned buffers each thread handles four
+// consecutive elements (one float4), walking row boundaries incrementally
+// instead of dividing per element.
 __global__ void k_xent_bwd(const float* __restrict__ probs, const void* __restrict__ tgt, int tdt,
-                           const float* __restrict__ dout, float* __restrict__ dx, size_t rows,
-                           size_t V) {
-  float scale = dout[0] / (float)rows;
-  size_t n = rows * V;
-  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
+                           const float* __restrict__ dout, float hscale, float* __restrict__ dx,
+                           size_t rows, size_t V, bool vec) {
+  const float scale = dout ? dout[0] / (float)rows : hscale;
+  const size_t n = rows * V;
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  if (vec) {
+    const uint32_t n4 = (uint32_t)(n / 4), V32 = (uint32_t)V;
+    for (uint32_t q = (uint32_t)tid; q < n4; q += (uint32_t)stride) {
+      const float4 p = reinterpret_cast<const float4*>(probs)[q];
+      float r[4] = {p.x, p.y, p.z, p.w};
+      uint32_t i = (q * 4) / V32, j = q * 4 - i * V32;
+      int64_t t = load_index(tgt, tdt, i);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (j == V32) { ++i; j = 0; t = load_index(tgt, tdt, i); }
+        float g = r[u];
+        if ((int64_t)j == t) g = g - 1.0f;
+        r[u] = g * scale;
+        ++j;
+      }
+      reinterpret_cast<float4*>(dx)[q] = make_float4(r[0], r[1], r[2], r[3]);
+    }
+    for (size_t f = (size_t)n4 * 4 + tid; f < n; f += stride) {
+      size_t i = f / V, j = f - i * V;
+      float g = probs[f];
+      if ((int64_t)j == load_index(tgt, tdt, i)) g = g - 1.0f;
+      dx[f] = g * scale;
+    }
+    return;
+  }
   for (size_t f = tid; f < n; f += stride) {
     size_t i = f / V, j = f - i * V;
     float g = probs[f];
@@ -846,13 +876,25 @@ void xent_nll_gather(const float* probs, const void* tgt, int tdt, float* out, s
   after_launch("k_xent_nll_gather");
 }
 
-void xent_bwd(const float* probs, const void* tgt, int tdt, const float* dout_dev, float* dx,
-              size_t n, size_t v) {
+static void xent_bwd_launch(const float* probs, const void* tgt, int tdt, const float* dout_dev,
+                            float hscale, float* dx, size_t n, size_t v) {
   size_t total = n * v;
   if (!total) return;
-  k_xent_bwd<<<grid_for(total, 256), 256, 0, stream()>>>(probs, tgt, tdt, dout_dev, dx, n, v);
+  const bool vec = total < (1ull << 32) && ((((uintptr_t)probs) | ((uintptr_t)dx)) & 15) == 0;
+  k_xent_bwd<<<grid_for(vec ? (total + 3) / 4 : total, 256), 256, 0, stream()>>>(probs, tgt, tdt, dout_dev,
+                                                                                  hscale, dx, n, v, vec);
   count_launch();
   after_launch("k_xent_bwd");
+}
+
+void xent_bwd(const float* probs, const void* tgt, int tdt, const float* dout_dev, float* dx,
+              size_t n, size_t v) {
+  xent_bwd_launch(probs, tgt, tdt, dout_dev, 0.0f, dx, n, v);
+}
+
+void xent_bwd_scaled(const float* probs, const void* tgt, int tdt, float scale, float* dx, size_t n,
+                     size_t v) {
+  xent_bwd_launch(probs, tgt, tdt, nullptr, scale, dx, n, v);
 }
 
 void embedding_fwd(const float* w, const void* idx, int idt, float* out, size_t n, size_t vocab,

@@ -12,6 +12,8 @@
 //  - host reads synchronise the stream (replaces flush_if_pending).
 #include "common.cuh"
 
+#include <chrono>
+
 #include <cmath>
 #include <cstdarg>
 #include <mutex>
@@ -137,6 +139,7 @@ bool capturing() {
 struct GraphRec;
 struct CaptureSession {
   bool active = false;
+  int64_t launches_at_begin = 0;   // launch counter when the capture opened
   std::unordered_map<size_t, std::vector<void*>> free_lists;
   std::vector<std::pair<void*, size_t>> touched;
 };
@@ -145,6 +148,7 @@ std::unordered_map<void*, GraphRec*> g_pinned;  // buffer -> graph that uses it 
 
 struct GraphRec {
   cudaGraphExec_t exec = nullptr;
+  int64_t launches = 0;    // kernels the graph holds (counted per replay)
   std::vector<std::pair<void*, size_t>> held;   // buffers returned to the pool at destroy
   std::vector<void*> pinned;
 };
@@ -553,6 +557,8 @@ int64_t malus_rand_int(int64_t n) {
 
 void malus_rng_reset(uint64_t counter) { t_rng_counter = counter; }
 
+void malus_philox4x32_10(uint32_t ctr[4], const uint32_t key[2]) { Philox::run(ctr, key[0], key[1]); }
+
 // ------------------------------------------------------ host i32 buffers
 // buffer.rs:11-50: a host Vec<i32>; freeze copies it into an i32 tensor.
 struct HostBuf { std::vector<int32_t> v; };
@@ -717,6 +723,7 @@ int32_t malus_graph_begin(void) {
     std::lock_guard<std::mutex> lk(g_pool.mu);
     if (g_cap.active) panic("malus_graph_begin: a capture is already open");
     g_cap.active = true;
+    g_cap.launches_at_begin = g_launches.load();
   }
   MALUS_CUDA(cudaStreamBeginCapture(stream(), cudaStreamCaptureModeRelaxed));
   return 0;
@@ -729,6 +736,7 @@ int64_t malus_graph_end(void) {
   {
     std::lock_guard<std::mutex> lk(g_pool.mu);
     if (!g_cap.active) panic("malus_graph_end without malus_graph_begin");
+    rec->launches = g_launches.load() - g_cap.launches_at_begin;
     std::unordered_set<void*> freed;
     for (auto& kv : g_cap.free_lists)
       for (void* p : kv.second) {
@@ -748,6 +756,7 @@ int64_t malus_graph_end(void) {
           cudaGetErrorString(e));
   MALUS_CUDA(cudaGraphInstantiate(&rec->exec, graph, 0));
   MALUS_CUDA(cudaGraphDestroy(graph));
+  count_launch(-(int)rec->launches);   // captured, not launched: counted at each replay
   const int64_t id = g_graph_next++;
   g_graphs[id] = rec;
   return id;
@@ -757,7 +766,7 @@ int32_t malus_graph_replay(int64_t id) {
   auto it = g_graphs.find(id);
   if (it == g_graphs.end()) return -1;
   MALUS_CUDA(cudaGraphLaunch(it->second->exec, stream()));
-  count_launch(1);
+  count_launch((int)it->second->launches);
   return 0;
 }
 
@@ -787,40 +796,53 @@ int32_t malus_graph_destroy(int64_t id) {
 }
 
 // ------------------------------------------------------------- bench timer
-// bench.rs:12-70: dormant unless enabled; each step's end waits for the GPU
-// inside the timed region; report = median of the steps after 3 warm-ups.
+// bench.rs:12-70: dormant unless enabled; a step is timed on the host clock
+// from bench_step_begin to bench_step_end, whose wait for the GPU (gpu_barrier)
+// lies inside the timed region; an end without a begin records nothing; the
+// report is the median of the steps after the first 3 (warm-up); reset
+// disables the timer and forgets the steps.
 static bool g_bench_on = false;
+static bool g_bench_started = false;
+static std::chrono::steady_clock::time_point g_bench_t0;
 static std::vector<double> g_bench_ms;
-static cudaEvent_t g_bench_ev0 = nullptr, g_bench_ev1 = nullptr;
-void bench_enable(void) {
-  g_bench_on = true;
-  if (!g_bench_ev0) {
-    MALUS_CUDA(cudaEventCreate(&g_bench_ev0));
-    MALUS_CUDA(cudaEventCreate(&g_bench_ev1));
-  }
-}
+void bench_enable(void) { g_bench_on = true; }
 void bench_step_begin(void) {
   if (!g_bench_on) return;
-  MALUS_CUDA(cudaEventRecord(g_bench_ev0, stream()));
+  g_bench_t0 = std::chrono::steady_clock::now();
+  g_bench_started = true;
 }
 void bench_step_end(void) {
   if (!g_bench_on) return;
-  MALUS_CUDA(cudaEventRecord(g_bench_ev1, stream()));
   gpu_barrier();
-  float ms = 0;
-  MALUS_CUDA(cudaEventElapsedTime(&ms, g_bench_ev0, g_bench_ev1));
-  g_bench_ms.push_back(ms);
+  if (!g_bench_started) return;
+  g_bench_started = false;
+  g_bench_ms.push_back(
+      std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - g_bench_t0).count());
 }
-double bench_report(int64_t* n_steps) {
+static std::vector<double> bench_warm_sorted() {
   const size_t warm = 3;
-  if (g_bench_ms.size() <= warm) { if (n_steps) *n_steps = 0; return -1.0; }
+  if (g_bench_ms.size() <= warm) return {};
   std::vector<double> v(g_bench_ms.begin() + warm, g_bench_ms.end());
   std::sort(v.begin(), v.end());
+  return v;
+}
+double bench_report(int64_t* n_steps) {
+  std::vector<double> v = bench_warm_sorted();
   if (n_steps) *n_steps = (int64_t)v.size();
+  if (v.empty()) return -1.0;
   size_t n = v.size();
   return n % 2 ? v[n / 2] : 0.5 * (v[n / 2 - 1] + v[n / 2]);
 }
-void bench_reset(void) { g_bench_ms.clear(); }
+void bench_report_range(double* min_ms, double* max_ms) {
+  std::vector<double> v = bench_warm_sorted();
+  if (min_ms) *min_ms = v.empty() ? -1.0 : v.front();
+  if (max_ms) *max_ms = v.empty() ? -1.0 : v.back();
+}
+void bench_reset(void) {
+  g_bench_on = false;
+  g_bench_started = false;
+  g_bench_ms.clear();
+}
 
 }  // extern "C"
 

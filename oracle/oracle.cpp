@@ -358,6 +358,7 @@ static void philox(uint32_t c[4], uint32_t k0, uint32_t k1) {
     k1 += 0xBB67AE85u;
   }
 }
+void or_philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) { philox(c, k0, k1); }
 void or_randn(float* out, int64_t n, uint64_t call_idx) {
   uint32_t k0 = (uint32_t)call_idx, k1 = (uint32_t)(call_idx >> 32);
   for (int64_t k = 0; k < (n + 1) / 2; ++k) {

@@ -43,6 +43,7 @@ _SIG = {
     "or_embedding": (None, [vp, vp, i64, i64, i64, vp]),
     "or_embedding_bwd": (None, [vp, vp, i64, i64, i64, vp]),
     "or_permute": (None, [vp, vp, C.c_int, vp, vp]),
+    "or_philox4x32_10": (None, [vp, C.c_uint32, C.c_uint32]),
     "or_randn": (None, [vp, i64, u64]),
     "or_rand_int": (i64, [i64, u64]),
     "or_rand_uniform": (f32, [u64]),
@@ -241,6 +242,13 @@ def randn(shape, call_idx):
     out = np.empty(n, np.float32)
     load().or_randn(_p(out), n, call_idx)
     return out.reshape(shape)
+
+
+def philox4x32_10(ctr, key):
+    """The Philox4x32-10 block function on a 4-word counter and a 2-word key."""
+    c = np.ascontiguousarray(ctr, np.uint32).copy()
+    load().or_philox4x32_10(c.ctypes.data_as(C.c_void_p), int(key[0]), int(key[1]))
+    return c
 
 
 def rand_int(n, call_idx):
