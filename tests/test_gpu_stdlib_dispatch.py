@@ -85,7 +85,8 @@ def test_layernorm_kernels(M, rt, kid, orc, rng, shape, axis):
     var = v2(M, rt, kid, "__layernorm_var_kernel", [x], [outer * inner, 1, 1], [a, 1, 1], None,
              (a, inner, 1e-5))
     ry, rv = orc.layernorm(x, axis)
-    assert rel_err(y, ry, np.abs(ry) + 1e-3) < 1e-5
+    # x - mean cancels near the group mean: relative to max(|y|, 1) (y is O(1) by construction)
+    assert rel_err(y, ry, np.maximum(np.abs(ry), 1.0)) < 1e-5
     # layernorm.ml:35-57: the per-group variance written at every element of the group
     assert rel_err(var, np.broadcast_to(rv, shape), np.broadcast_to(rv, shape)) < 1e-5
 
