@@ -152,6 +152,7 @@ void adamw_multi(const AdamSeg* segs, int nseg, float lr, float b1, float b2, fl
 void adamw_multi_tab(const AdamSeg* segs, int nseg, float lr, float b1, float b2, float eps,
                      float wd, float bc1, float bc2, float grad_scale, const float* bc_tab,
                      const int64_t* step_dev) {
+  plane_cache_clear();   // parameters and moments change in place
   float c1 = 1.0f - b1, c2 = 1.0f - b2;  // the host-side (1.0 - beta) literals
   for (int base = 0; base < nseg; base += 64) {
     int n = std::min(64, nseg - base);

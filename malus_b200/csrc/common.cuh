@@ -40,8 +40,23 @@ struct Storage {
   size_t bytes;      // allocated (pool bucket) size
   int aliases;       // number of TensorBuffers sharing this storage
   bool owned;        // false for malus_tensor_wrap'd memory
+  uint64_t id;       // unique per storage for the process (never reused)
 };
 
+// One logical dimension of a strided view: index i lies at element offset
+// (i / div) * hi + (i % div) * lo from the storage base (div == 0: i * lo).
+// Two radices let a reshape merge two dimensions that are not adjacent in
+// memory (the attention head fold [B, T, H, hs] -> [B*H, T, hs] after a permute).
+struct ViewDim {
+  int64_t div = 0, hi = 0, lo = 0;
+  __host__ __device__ int64_t at(int64_t i) const { return div ? (i / div) * hi + (i % div) * lo : i * lo; }
+};
+struct View { ViewDim d[kMaxRank]; };
+
+// A tensor is either contiguous row-major over its storage (view == nullptr)
+// or a strided view of a storage shared with the tensor it was made from
+// (permute, and reshapes of such views).  Raw pointers (fptr / vptr) always
+// see contiguous row-major data: they materialise a view first.
 struct TensorBuffer {
   Storage* st;
   int32_t dtype;
@@ -49,14 +64,31 @@ struct TensorBuffer {
   size_t len;
   size_t shape[kMaxRank];
   std::atomic<int64_t> rc;
+  View* view = nullptr;
 };
 
 inline TensorBuffer* tb(int64_t h) {
   if (h == 0) panic("null tensor handle");
   return reinterpret_cast<TensorBuffer*>(h);
 }
-inline float* fptr(int64_t h) { return static_cast<float*>(tb(h)->st->ptr); }
-inline void* vptr(int64_t h) { return tb(h)->st->ptr; }
+void materialize(int64_t h);   // a view becomes a contiguous tensor with storage of its own
+inline float* fptr(int64_t h) {
+  auto* t = tb(h);
+  if (t->view) materialize(h);
+  return static_cast<float*>(t->st->ptr);
+}
+inline void* vptr(int64_t h) {
+  auto* t = tb(h);
+  if (t->view) materialize(h);
+  return t->st->ptr;
+}
+// The view of tensor h's dims (row-major strides when it is contiguous).
+View view_of(int64_t h);
+// h's data read as the shape `dims` (same element count) through one view of
+// its storage, when its memory allows that (false: it does not).
+bool view_as(int64_t h, const size_t* dims, size_t nd, View* out);
+// A new handle over h's storage with the given shape and view (no copy).
+int64_t make_view(int64_t h, const size_t* shape, int ndim, const View& v);
 size_t dtype_size(int32_t dtype);
 
 // ---- runtime core (runtime.cu) ----
@@ -155,15 +187,40 @@ int embedding_bwd_ws(const float* dout, const void* idx, int idx_dtype, float* d
 // ---- GEMM (gemm.cu) ----
 // C[b] (MxN) = alpha * op(A[b]) * op(B[b]) + beta * C[b], f32 semantics via
 // 3xTF32 on tcgen05 (large shapes) or exact-f32 SIMT (small shapes).
-// A is MxK: a_trans=false -> A stored row-major [M][lda] ; true -> stored [K][lda] (A^T)
-// B is KxN: b_trans=false -> B stored row-major [K][ldb] ; true -> stored [N][ldb] (B^T)
+// Each operand is the stored matrix as the call sees it, a [nz][rows][cols]
+// stack read through a strided view of a tensor's storage (element (z, r, c)
+// at base + z.at(z) + r.at(r) + c.at(c)); nz is 1 (shared by every batch
+// entry) or the batch.  A is MxK: a_trans = false -> stored {rows M, cols K};
+// true -> stored {rows K, cols M} (A^T).  B is KxN: b_trans = false -> stored
+// {rows K, cols N}; true -> {rows N, cols K}.  scale_dev (optional): the
+// values are those of the view times *scale_dev (one f32 multiply).
+// key: the storage's id for the operand-plane cache (0: not cached).
+struct GemmOperand {
+  const float* base = nullptr;
+  int64_t nz = 1, rows = 0, cols = 0;
+  ViewDim z, r, c;
+  const float* scale_dev = nullptr;
+  uint64_t key = 0;
+};
+// A contiguous row-major stack: nz slices of rows x cols, row pitch ld, slice stride sstride.
+GemmOperand plain_operand(const float* p, int64_t nz, int64_t rows, int64_t cols, int64_t ld,
+                          int64_t sstride);
 struct GemmArgs {
   int M, N, K, batch;
-  const float* A; int64_t lda; int64_t strideA; bool a_trans;
-  const float* B; int64_t ldb; int64_t strideB; bool b_trans;
+  GemmOperand A; bool a_trans;
+  GemmOperand B; bool b_trans;
   float* C; int64_t ldc; int64_t strideC;
   float alpha = 1.f, beta = 0.f;
 };
+// Operand planes split from tensors during a step are kept per storage and
+// view and reused by later GEMMs that read the same data (a weight in the
+// forward and in both backward products, an activation saved for backward).
+// The cache is dropped whenever tensor data may change in place (step
+// boundaries: tape_zero_grad, the end of backward; AdamW; host writes;
+// user-kernel dispatch; graph capture and replay) and entry by entry when a
+// storage is freed.  MALUS_PLANE_CACHE=0 disables it.
+void plane_cache_clear();
+void plane_cache_drop(uint64_t storage_id);
 void gemm(const GemmArgs& g);
 
 // Low-level tcgen05 GEMM on pre-split tf32 planes (hi/lo), for callers that
@@ -208,7 +265,7 @@ void gemm_tc_planes(const TcProblem& p);
 // hi/lo planes of a stack of `batch` row-major slices (rows x cols, ld, sstride)
 void tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t batch,
                 int64_t sstride, float* hi, float* lo, int64_t pitch);
-void gemm_simt(const GemmArgs& g);
+void gemm_simt(const GemmArgs& g);        // contiguous (plain) operands only
 int gemm_backend_for(const GemmArgs& g);   // 0 = SIMT, 1 = tcgen05
 void gemm_force_backend(int b);            // -1 = auto (tests)
 

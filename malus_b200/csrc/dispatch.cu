@@ -138,6 +138,7 @@ void malus_runtime_init(const uint64_t* ids, const char* const* nm, size_t n) {
 int64_t kernel_dispatch(uint64_t kernel_id, const int64_t* h, size_t count) {
   if (count == 0) panic("kernel_dispatch: no inputs");
   if (JitKernel* jk = jit_of(kernel_id)) {
+    plane_cache_clear();   // a user kernel may write any buffer it is given
     int64_t o = alloc_like(h[0]);
     jit_dispatch_implicit(jk, h, count, o);
     return o;
@@ -188,6 +189,7 @@ int64_t kernel_dispatch_v2(uint64_t kernel_id, const int64_t* h, size_t hc, cons
     out = alloc(out_dtype, out_shape, (int)out_ndim);
   }
   if (jk) {
+    plane_cache_clear();   // a user kernel may write any buffer it is given
     jit_dispatch_explicit(jk, h, hc, grid, tg, out, u, ub);
     return out;
   }

@@ -23,6 +23,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <mutex>
+#include <unordered_map>
+#include <vector>
 
 namespace malus {
 
@@ -107,9 +109,9 @@ void gemm_simt(const GemmArgs& g) {
   }
   dim3 grid((g.N + ST - 1) / ST, (g.M + ST - 1) / ST, g.batch);
   int pid = prof_begin(2, 2.0 * g.M * (double)g.N * g.K * g.batch, 0.0);
-  k_gemm_simt<<<grid, 256, 0, stream()>>>(g.M, g.N, g.K, g.A, g.lda, g.strideA, g.a_trans, g.B,
-                                          g.ldb, g.strideB, g.b_trans, g.C, g.ldc, g.strideC,
-                                          g.alpha, g.beta);
+  k_gemm_simt<<<grid, 256, 0, stream()>>>(g.M, g.N, g.K, g.A.base, g.A.r.lo, g.A.nz > 1 ? g.A.z.lo : 0,
+                                          g.a_trans, g.B.base, g.B.r.lo, g.B.nz > 1 ? g.B.z.lo : 0,
+                                          g.b_trans, g.C, g.ldc, g.strideC, g.alpha, g.beta);
   count_launch();
   after_launch("k_gemm_simt");
   prof_end(pid);
@@ -812,6 +814,59 @@ __global__ void k_split_tf32(const float* __restrict__ src, int64_t rows, int64_
   *reinterpret_cast<float4*>(lo + row * pitch + c) = make_float4(l[0], l[1], l[2], l[3]);
 }
 
+// ---- operand split through a strided view: planes [nz][n_outer][pitch],
+// element (z, o, i) read at base + z.at(z) + outer.at(o) + inner.at(i) and
+// multiplied by *scale when given (one f32 multiply, as the materialised
+// product would be); pitch padding is zero-filled.  One block row per plane
+// row, 1024 inner elements per block (four per thread).
+struct SplitGeom {
+  const float* base;
+  const float* scale;
+  int64_t n_outer, n_inner, pitch;
+  ViewDim z, outer, inner;
+  bool vec;   // inner runs of 4 are contiguous and 16-byte aligned
+};
+
+__global__ void k_split_view(SplitGeom g, float* __restrict__ hi, float* __restrict__ lo) {
+  const int64_t row = blockIdx.x;
+  const int64_t c = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * 4;
+  if (c >= g.pitch) return;
+  const int64_t zi = row / g.n_outer, o = row - zi * g.n_outer;
+  const float* s = g.base + g.z.at(zi) + g.outer.at(o);
+  float x[4];
+  if (g.vec && c + 4 <= g.n_inner) {
+    const float4 v = *reinterpret_cast<const float4*>(s + g.inner.at(c));
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) x[q] = c + q < g.n_inner ? s[g.inner.at(c + q)] : 0.0f;
+  }
+  if (g.scale) {
+    const float sc = *g.scale;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) x[q] = __fmul_rn(x[q], sc);
+  }
+  float h[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    h[q] = tf32_rn(x[q]);
+    l[q] = tf32_rn(x[q] - h[q]);
+  }
+  *reinterpret_cast<float4*>(hi + row * g.pitch + c) = make_float4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<float4*>(lo + row * g.pitch + c) = make_float4(l[0], l[1], l[2], l[3]);
+}
+
+// ---- operand gather into a contiguous [nz][rows][cols] stack (the SIMT path
+// reads plain row-major operands), scaled like k_split_view
+__global__ void k_operand_gather(GemmOperand o, float* __restrict__ out, int64_t n) {
+  for (int64_t f = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; f < n; f += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = f % o.cols, rz = f / o.cols, r = rz % o.rows, zi = rz / o.rows;
+    float x = o.base[o.z.at(zi) + o.r.at(r) + o.c.at(c)];
+    if (o.scale_dev) x = __fmul_rn(x, *o.scale_dev);
+    out[f] = x;
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 void load_encoder() {
@@ -1225,26 +1280,119 @@ void gemm_tc_planes(const TcProblem& pr) {
   prof_end(pid);
 }
 
-// tensor_matmul / VJP path: split both operands into workspace planes, then one
-// persistent GEMM with a plain row-major (batched) output.
-static void gemm_tc(const GemmArgs& g) {
-  int64_t ar = g.a_trans ? g.K : g.M, ac = g.a_trans ? g.M : g.K;
-  int64_t br = g.b_trans ? g.N : g.K, bc = g.b_trans ? g.K : g.N;
-  int64_t ap = (ac + 3) & ~int64_t(3), bp = (bc + 3) & ~int64_t(3);
-  int64_t abatch = g.strideA ? g.batch : 1, bbatch = g.strideB ? g.batch : 1;
-  int64_t an = abatch * ar * ap, bn = bbatch * br * bp;
-  float* ws = (float*)scratch_alloc((size_t)(2 * an + 2 * bn) * sizeof(float) + 256);
-  float *ahp = ws, *alp = ws + an, *bhp = ws + 2 * an, *blp = bhp + bn;
-  int pid = prof_begin(1, 0.0, 12.0 * (double)(an + bn));
-  tf32_split(g.A, ar, ac, g.lda, abatch, g.strideA, ahp, alp, ap);
-  tf32_split(g.B, br, bc, g.ldb, bbatch, g.strideB, bhp, blp, bp);
+GemmOperand plain_operand(const float* p, int64_t nz, int64_t rows, int64_t cols, int64_t ld,
+                          int64_t sstride) {
+  GemmOperand o;
+  o.base = p;
+  o.nz = nz;
+  o.rows = rows;
+  o.cols = cols;
+  o.z = ViewDim{0, 0, nz > 1 ? sstride : 0};
+  o.r = ViewDim{0, 0, ld};
+  o.c = ViewDim{0, 0, 1};
+  return o;
+}
+
+namespace {
+
+bool is_plain(const GemmOperand& o) {
+  return !o.scale_dev && o.z.div == 0 && o.r.div == 0 && o.c.div == 0 && o.c.lo == 1;
+}
+
+// ---------------------------------------------------------- plane cache
+struct PlaneEntry {
+  int64_t nz, rows, cols;
+  ViewDim z, r, c;
+  const float* scale;
+  float* mem;          // hi then lo, each nz * n_outer * pitch floats
+  int64_t pitch;
+  bool transposed;     // planes hold the operand's columns as rows
+};
+std::mutex g_pc_mu;
+std::unordered_map<uint64_t, std::vector<PlaneEntry>> g_pc;
+
+bool plane_cache_on() {
+  static const bool on = [] { const char* e = getenv("MALUS_PLANE_CACHE"); return !(e && e[0] == '0'); }();
+  return on;
+}
+
+bool same_dim(const ViewDim& a, const ViewDim& b) { return a.div == b.div && a.hi == b.hi && a.lo == b.lo; }
+
+const PlaneEntry* pc_find(const GemmOperand& o) {
+  auto it = g_pc.find(o.key);
+  if (it == g_pc.end()) return nullptr;
+  for (const PlaneEntry& e : it->second)
+    if (e.nz == o.nz && e.rows == o.rows && e.cols == o.cols && same_dim(e.z, o.z) && same_dim(e.r, o.r) &&
+        same_dim(e.c, o.c) && e.scale == o.scale_dev)
+      return &e;
+  return nullptr;
+}
+
+// The tf32 planes of one operand.  They hold the operand's inner dimension
+// contiguously: its columns, or its rows when only those are contiguous in
+// memory (then *trans flips: the GEMM reads them with the other major-ness).
+struct Planes {
+  const float* hi;
+  const float* lo;
+  int64_t rows, cols, pitch;   // as stored in the planes
+  void* tmp;                   // scratch to free after the GEMM (null: cached)
+};
+
+Planes operand_planes(const GemmOperand& o, bool* trans) {
+  const bool flip = o.c.lo != 1 && o.r.lo == 1;
+  const int64_t n_outer = flip ? o.cols : o.rows, n_inner = flip ? o.rows : o.cols;
+  const ViewDim outer = flip ? o.c : o.r, inner = flip ? o.r : o.c;
+  const int64_t pitch = (n_inner + 3) & ~int64_t(3);
+  if (flip) *trans = !*trans;
+  std::lock_guard<std::mutex> lk(g_pc_mu);
+  const bool cache = o.key != 0 && plane_cache_on();
+  if (cache)
+    if (const PlaneEntry* e = pc_find(o)) {
+      const int64_t n = o.nz * n_outer * e->pitch;
+      return Planes{e->mem, e->mem + n, n_outer, n_inner, e->pitch, nullptr};
+    }
+  const int64_t n = o.nz * n_outer * pitch;
+  float* mem = (float*)scratch_alloc((size_t)(2 * n) * sizeof(float) + 256);
+  SplitGeom g;
+  g.base = o.base;
+  g.scale = o.scale_dev;
+  g.n_outer = n_outer;
+  g.n_inner = n_inner;
+  g.pitch = pitch;
+  g.z = o.z;
+  g.outer = outer;
+  g.inner = inner;
+  auto m4 = [](int64_t v) { return v % 4 == 0; };
+  g.vec = inner.lo == 1 && (inner.div == 0 || (m4(inner.div) && m4(inner.hi))) && m4(outer.lo) &&
+          (outer.div == 0 || m4(outer.hi)) && m4(o.z.lo) && (o.z.div == 0 || m4(o.z.hi)) &&
+          ((uintptr_t)o.base & 15) == 0;
+  if (o.nz * n_outer > 0 && pitch > 0) {
+    dim3 grid((unsigned)(o.nz * n_outer), (unsigned)((pitch + 1023) / 1024));
+    k_split_view<<<grid, 256, 0, stream()>>>(g, mem, mem + n);
+    count_launch();
+    after_launch("k_split_view");
+  }
+  if (cache) {
+    g_pc[o.key].push_back(PlaneEntry{o.nz, o.rows, o.cols, o.z, o.r, o.c, o.scale_dev, mem, pitch, flip});
+    return Planes{mem, mem + n, n_outer, n_inner, pitch, nullptr};
+  }
+  return Planes{mem, mem + n, n_outer, n_inner, pitch, mem};
+}
+
+// tensor_matmul / VJP path: the operands' planes (cached, or split now from
+// their views), then one persistent GEMM with a plain row-major (batched) output.
+void gemm_tc(const GemmArgs& g) {
+  bool at = g.a_trans, bt = g.b_trans;
+  int pid = prof_begin(1, 0.0, 12.0 * (double)(g.A.nz * g.A.rows * g.A.cols + g.B.nz * g.B.rows * g.B.cols));
+  const Planes pa = operand_planes(g.A, &at);
+  const Planes pb = operand_planes(g.B, &bt);
   prof_end(pid);
   TcProblem pr{};
   pr.M = g.M; pr.N = g.N; pr.K = g.K; pr.batch = g.batch;
-  pr.a = TcOperand{ahp, alp, ar, ac, ap, (int)abatch, ar * ap, g.a_trans,
-                   g.strideA ? kZBatch : kZNone, 0};
-  pr.b = TcOperand{bhp, blp, br, bc, bp, (int)bbatch, br * bp, !g.b_trans,
-                   g.strideB ? kZBatch : kZNone, 0};
+  pr.a = TcOperand{pa.hi, pa.lo, pa.rows, pa.cols, pa.pitch, (int)g.A.nz, pa.rows * pa.pitch, at,
+                   g.A.nz > 1 ? kZBatch : kZNone, 0};
+  pr.b = TcOperand{pb.hi, pb.lo, pb.rows, pb.cols, pb.pitch, (int)g.B.nz, pb.rows * pb.pitch, !bt,
+                   g.B.nz > 1 ? kZBatch : kZNone, 0};
   pr.epi = kEpiStore;
   pr.oz = TcLayout{0, 0, 0, 0, g.batch > 1 ? g.strideC : 0};
   pr.om = TcLayout{0, 0, 0, 0, g.ldc};
@@ -1253,13 +1401,61 @@ static void gemm_tc(const GemmArgs& g) {
   pr.alpha = g.alpha;
   pr.beta = g.beta;
   gemm_tc_planes(pr);
-  scratch_free(ws);
+  if (pa.tmp) scratch_free(pa.tmp);
+  if (pb.tmp) scratch_free(pb.tmp);
+}
+
+// A contiguous copy of a non-plain operand for the SIMT path.
+GemmOperand gathered(const GemmOperand& o, void** tmp) {
+  const int64_t n = o.nz * o.rows * o.cols;
+  float* buf = (float*)scratch_alloc((size_t)std::max<int64_t>(n, 1) * sizeof(float));
+  if (n) {
+    k_operand_gather<<<grid_for((size_t)n, 256), 256, 0, stream()>>>(o, buf, n);
+    count_launch();
+    after_launch("k_operand_gather");
+  }
+  *tmp = buf;
+  return plain_operand(buf, o.nz, o.rows, o.cols, o.cols, o.rows * o.cols);
+}
+
+}  // namespace
+
+void plane_cache_clear() {
+  std::vector<float*> mem;
+  {
+    std::lock_guard<std::mutex> lk(g_pc_mu);
+    for (auto& kv : g_pc)
+      for (auto& e : kv.second) mem.push_back(e.mem);
+    g_pc.clear();
+  }
+  for (float* m : mem) scratch_free(m);
+}
+
+void plane_cache_drop(uint64_t sid) {
+  std::vector<float*> mem;
+  {
+    std::lock_guard<std::mutex> lk(g_pc_mu);
+    auto it = g_pc.find(sid);
+    if (it == g_pc.end()) return;
+    for (auto& e : it->second) mem.push_back(e.mem);
+    g_pc.erase(it);
+  }
+  for (float* m : mem) scratch_free(m);
 }
 
 void gemm(const GemmArgs& g) {
   if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return;
-  if (gemm_backend_for(g) == 1 && g.K > 0) gemm_tc(g);
-  else gemm_simt(g);
+  if (gemm_backend_for(g) == 1 && g.K > 0) {
+    gemm_tc(g);
+    return;
+  }
+  GemmArgs s = g;
+  void *ta = nullptr, *tb_ = nullptr;
+  if (!is_plain(s.A)) s.A = gathered(s.A, &ta);
+  if (!is_plain(s.B)) s.B = gathered(s.B, &tb_);
+  gemm_simt(s);
+  if (ta) scratch_free(ta);
+  if (tb_) scratch_free(tb_);
 }
 
 }  // namespace malus

@@ -428,6 +428,7 @@ void malus_gpt_destroy(int64_t h) {
 
 void malus_gpt_step_device(int64_t h, const int32_t* x_dev, const int32_t* y_dev) {
   auto* m = reinterpret_cast<Model*>(h);
+  plane_cache_clear();   // the step rewrites its parameters in place
   if (x_dev != m->x_dev)
     MALUS_CUDA(cudaMemcpyAsync(m->x_dev, x_dev, m->M * 4, cudaMemcpyDeviceToDevice, stream()));
   if (y_dev != m->y_dev)

@@ -156,14 +156,41 @@ std::vector<int> normalize_perm(const size_t* raw, size_t n, int rank) {
   panic("permute/transpose got %zu dim args for rank-%d tensor; expected 0, 2, or %d", n, rank, rank);
 }
 
+// A permute is a view of the input's storage with its dims reordered (no
+// copy): a GEMM reads it through its strides when it splits its operands, and
+// any other consumer's raw-pointer access materialises it once.
 int64_t permute_impl(int64_t x, const std::vector<int>& perm) {
   Shape s = shape_of(x);
-  Shape o;
-  o.ndim = s.ndim;
-  for (int d = 0; d < s.ndim; ++d) o.d[d] = s.d[perm[d]];
-  int64_t out = alloc_shape(o);
-  permute_nd(fptr(x), fptr(out), s, perm.data());
-  return out;
+  const View in = view_of(x);
+  View v;
+  size_t shape[kMaxRank];
+  for (int d = 0; d < s.ndim; ++d) {
+    shape[d] = s.d[perm[d]];
+    v.d[d] = in.d[perm[d]];
+  }
+  return make_view(x, shape, s.ndim, v);
+}
+
+// Tensor h read as a GEMM operand [nz][rows][cols] (a view of its storage;
+// a tensor whose memory cannot be read so is materialised first).
+GemmOperand operand_of(int64_t h, size_t nz, size_t rows, size_t cols) {
+  auto* t = tb(h);
+  const size_t dims[3] = {nz, rows, cols};
+  View v;
+  if (!view_as(h, dims, 3, &v)) {
+    materialize(h);
+    if (!view_as(h, dims, 3, &v)) panic("matmul operand of %zu elements read as [%zu][%zu][%zu]", t->len, nz, rows, cols);
+  }
+  GemmOperand o;
+  o.base = static_cast<const float*>(t->st->ptr);
+  o.nz = (int64_t)nz;
+  o.rows = (int64_t)rows;
+  o.cols = (int64_t)cols;
+  o.z = v.d[0];
+  o.r = v.d[1];
+  o.c = v.d[2];
+  o.key = t->st->id;
+  return o;
 }
 
 void check_f32(int64_t h, const char* what) {
@@ -180,8 +207,6 @@ int64_t tensor_matmul(int64_t ha, int64_t hb) {
   check_f32(ha, "matmul");
   check_f32(hb, "matmul");
   GemmArgs g{};
-  g.A = fptr(ha);
-  g.B = fptr(hb);
   g.a_trans = false;
   g.b_trans = false;
   Shape o;
@@ -196,29 +221,26 @@ int64_t tensor_matmul(int64_t ha, int64_t hb) {
     if (a.d[2] != b.d[1]) panic("batched matmul inner dims must match: %zu vs %zu", a.d[2], b.d[1]);
     g.batch = (int)a.d[0]; g.M = (int)a.d[1]; g.K = (int)a.d[2]; g.N = (int)b.d[2];
     o.ndim = 3; o.d[0] = a.d[0]; o.d[1] = a.d[1]; o.d[2] = b.d[2];
-    g.strideA = (int64_t)g.M * g.K;
-    g.strideB = (int64_t)g.K * g.N;
   } else if (a.ndim == 3 && b.ndim == 2) {
     if (a.d[2] != b.d[0]) panic("matmul shape mismatch: inner dims %zu != %zu", a.d[2], b.d[0]);
-    // (B, M, K) @ (K, N) is one (B*M, K) @ (K, N) GEMM on contiguous data
+    // (B, M, K) @ (K, N) is one (B*M, K) @ (K, N) GEMM
     g.batch = 1; g.M = (int)(a.d[0] * a.d[1]); g.K = (int)a.d[2]; g.N = (int)b.d[1];
     o.ndim = 3; o.d[0] = a.d[0]; o.d[1] = a.d[1]; o.d[2] = b.d[1];
   } else {
     panic("tensor_matmul requires both inputs to be 2-D, both 3-D, or (3-D, 2-D); got rank %d and %d",
           a.ndim, b.ndim);
   }
-  g.lda = g.K;
-  g.ldb = g.N;
   int64_t out = alloc_shape(o);
   g.C = fptr(out);
   g.ldc = g.N;
-  g.strideC = (int64_t)g.M * g.N;
-  if (g.batch == 1) g.strideC = 0;
+  g.strideC = g.batch > 1 ? (int64_t)g.M * g.N : 0;
   if (o.numel() == 0) return out;
   if (g.K == 0) {
     MALUS_CUDA(cudaMemsetAsync(g.C, 0, o.numel() * 4, stream()));
     return out;
   }
+  g.A = operand_of(ha, (size_t)g.batch, (size_t)g.M, (size_t)g.K);
+  g.B = operand_of(hb, b.ndim == 3 ? (size_t)g.batch : 1, (size_t)g.K, (size_t)g.N);
   gemm(g);
   return out;
 }
@@ -477,52 +499,63 @@ int64_t __embedding_bwd(int64_t weight, int64_t indices, int64_t dout) {
 }
 
 int64_t __matmul_bwd_a(int64_t a, int64_t b, int64_t dout) {
-  Shape sa = shape_of(a), sb = shape_of(b), sd = shape_of(dout);
+  Shape sa = shape_of(a), sb = shape_of(b);
   int64_t da = alloc_shape(sa);
   GemmArgs g{};
   if (sb.ndim == 3) {
     // dA[b] = dC[b] @ B[b]^T : (M=m, N=k, K=n)
-    g.batch = (int)sb.d[0]; g.M = (int)sd.d[1]; g.N = (int)sb.d[1]; g.K = (int)sb.d[2];
-    g.A = fptr(dout); g.lda = g.K; g.strideA = (int64_t)g.M * g.K; g.a_trans = false;
-    g.B = fptr(b); g.ldb = g.K; g.strideB = (int64_t)g.N * g.K; g.b_trans = true;
-    g.C = fptr(da); g.ldc = g.N; g.strideC = (int64_t)g.M * g.N;
+    g.batch = (int)sb.d[0]; g.M = (int)(tb(dout)->len / (sb.d[0] * sb.d[2])); g.N = (int)sb.d[1];
+    g.K = (int)sb.d[2];
+    g.a_trans = false;
+    g.b_trans = true;
+    g.strideC = (int64_t)g.M * g.N;
   } else {
     // (2,2) and (3,2): dA = dC @ B^T over all leading rows
-    size_t rows = tb(dout)->len / sb.d[1];
-    g.batch = 1; g.M = (int)rows; g.N = (int)sb.d[0]; g.K = (int)sb.d[1];
-    g.A = fptr(dout); g.lda = g.K; g.a_trans = false;
-    g.B = fptr(b); g.ldb = g.K; g.b_trans = true;
-    g.C = fptr(da); g.ldc = g.N;
+    g.batch = 1; g.M = (int)(tb(dout)->len / sb.d[1]); g.N = (int)sb.d[0]; g.K = (int)sb.d[1];
+    g.a_trans = false;
+    g.b_trans = true;
+    g.strideC = 0;
   }
+  g.C = fptr(da);
+  g.ldc = g.N;
   if (sa.numel()) {
-    if (g.K == 0) MALUS_CUDA(cudaMemsetAsync(fptr(da), 0, sa.numel() * 4, stream()));
-    else gemm(g);
+    if (g.K == 0) {
+      MALUS_CUDA(cudaMemsetAsync(fptr(da), 0, sa.numel() * 4, stream()));
+    } else {
+      g.A = operand_of(dout, (size_t)g.batch, (size_t)g.M, (size_t)g.K);
+      g.B = operand_of(b, (size_t)g.batch, (size_t)g.N, (size_t)g.K);   // stored [N][K]
+      gemm(g);
+    }
   }
   return da;
 }
 
 int64_t __matmul_bwd_b(int64_t a, int64_t b, int64_t dout) {
-  Shape sa = shape_of(a), sb = shape_of(b), sd = shape_of(dout);
+  Shape sa = shape_of(a), sb = shape_of(b);
   int64_t db = alloc_shape(sb);
   GemmArgs g{};
   if (sa.ndim == 3 && sb.ndim == 3) {
     // dB[b] = A[b]^T @ dC[b] : (M=k, N=n, K=m)
-    g.batch = (int)sa.d[0]; g.M = (int)sa.d[2]; g.N = (int)sd.d[2]; g.K = (int)sa.d[1];
-    g.A = fptr(a); g.lda = g.M; g.strideA = (int64_t)g.K * g.M; g.a_trans = true;
-    g.B = fptr(dout); g.ldb = g.N; g.strideB = (int64_t)g.K * g.N; g.b_trans = false;
-    g.C = fptr(db); g.ldc = g.N; g.strideC = (int64_t)g.M * g.N;
+    g.batch = (int)sa.d[0]; g.M = (int)sa.d[2]; g.N = (int)sb.d[2]; g.K = (int)sa.d[1];
+    g.strideC = (int64_t)g.M * g.N;
   } else {
     // (2,2): A^T @ dC ; (3,2): sum_b A[b]^T @ dC[b] == A'^T @ dC' with K = B*m
     size_t kdim = sa.d[sa.ndim - 1];
-    size_t rows = tb(a)->len / kdim;
-    g.batch = 1; g.M = (int)kdim; g.N = (int)sb.d[1]; g.K = (int)rows;
-    g.A = fptr(a); g.lda = g.M; g.a_trans = true;
-    g.B = fptr(dout); g.ldb = g.N; g.b_trans = false;
-    g.C = fptr(db); g.ldc = g.N;
+    g.batch = 1; g.M = (int)kdim; g.N = (int)sb.d[1]; g.K = (int)(tb(a)->len / kdim);
+    g.strideC = 0;
   }
+  g.a_trans = true;
+  g.b_trans = false;
+  g.C = fptr(db);
+  g.ldc = g.N;
   if (sb.numel()) {
-    if (g.K == 0) MALUS_CUDA(cudaMemsetAsync(fptr(db), 0, sb.numel() * 4, stream()));
-    else gemm(g);
+    if (g.K == 0) {
+      MALUS_CUDA(cudaMemsetAsync(fptr(db), 0, sb.numel() * 4, stream()));
+    } else {
+      g.A = operand_of(a, (size_t)g.batch, (size_t)g.K, (size_t)g.M);      // stored [K][M]
+      g.B = operand_of(dout, (size_t)g.batch, (size_t)g.K, (size_t)g.N);
+      gemm(g);
+    }
   }
   return db;
 }

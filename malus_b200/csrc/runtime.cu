@@ -267,6 +267,8 @@ static int64_t make_handle(int32_t dtype, const size_t* shape, int ndim, Storage
   return reinterpret_cast<int64_t>(t);
 }
 
+static std::atomic<uint64_t> g_storage_ids{1};
+
 int64_t alloc(int32_t dtype, const size_t* shape, int ndim) {
   if (dtype != MALUS_F32 && dtype != MALUS_I32 && dtype != MALUS_I64)
     panic("unsupported dtype tag %d; supported: f32, i32, i64", dtype);
@@ -278,6 +280,7 @@ int64_t alloc(int32_t dtype, const size_t* shape, int ndim) {
   st->ptr = pool_get(bytes, &st->bytes);
   st->aliases = 1;
   st->owned = true;
+  st->id = g_storage_ids.fetch_add(1, std::memory_order_relaxed);
   return make_handle(dtype, shape, ndim, st, n);
 }
 
@@ -319,8 +322,159 @@ void split_axis(const Shape& s, int axis, size_t* outer, size_t* axis_sz, size_t
 
 static void release_storage(Storage* st) {
   if (--st->aliases > 0) return;
+  plane_cache_drop(st->id);
   if (st->owned) pool_put(st->ptr, st->bytes);
   delete st;
+}
+
+// ------------------------------------------------------------------- views
+static bool reshape_view(const size_t* shape, int ndim, const View& view, const size_t* dims, size_t nd,
+                         View* out);
+
+bool view_as(int64_t h, const size_t* dims, size_t nd, View* out) {
+  auto* t = tb(h);
+  return t->len && reshape_view(t->shape, t->ndim, view_of(h), dims, nd, out);
+}
+
+View view_of(int64_t h) {
+  auto* t = tb(h);
+  if (t->view) return *t->view;
+  View v;
+  int64_t stride = 1;
+  for (int d = t->ndim - 1; d >= 0; --d) {
+    v.d[d] = ViewDim{0, 0, stride};
+    stride *= (int64_t)t->shape[d];
+  }
+  return v;
+}
+
+static bool is_row_major(const size_t* shape, int ndim, const View& v) {
+  int64_t stride = 1;
+  for (int d = ndim - 1; d >= 0; --d) {
+    if (shape[d] != 1 && (v.d[d].div != 0 || v.d[d].lo != stride)) return false;
+    stride *= (int64_t)shape[d];
+  }
+  return true;
+}
+
+int64_t make_view(int64_t h, const size_t* shape, int ndim, const View& v) {
+  auto* t = tb(h);
+  t->st->aliases++;
+  int64_t out = make_handle(t->dtype, shape, ndim, t->st, t->len);
+  if (!is_row_major(shape, ndim, v)) tb(out)->view = new View(v);
+  return out;
+}
+
+struct ViewMeta {
+  int ndim;
+  int64_t size[kMaxRank];
+  ViewDim d[kMaxRank];
+};
+
+// out[f] = src[offset of logical element f] (row-major over the logical shape)
+template <typename T>
+__global__ void k_view_gather(const T* __restrict__ src, T* __restrict__ out, size_t n, ViewMeta m) {
+  for (size_t f = blockIdx.x * (size_t)blockDim.x + threadIdx.x; f < n; f += (size_t)gridDim.x * blockDim.x) {
+    int64_t rem = (int64_t)f, off = 0;
+    for (int d = m.ndim - 1; d >= 0; --d) {
+      int64_t i = rem % m.size[d];
+      rem /= m.size[d];
+      off += m.d[d].at(i);
+    }
+    out[f] = src[off];
+  }
+}
+
+void materialize(int64_t h) {
+  auto* t = tb(h);
+  if (!t->view) return;
+  ViewMeta m;
+  m.ndim = t->ndim;
+  for (int d = 0; d < t->ndim; ++d) {
+    m.size[d] = (int64_t)t->shape[d];
+    m.d[d] = t->view->d[d];
+  }
+  const size_t es = dtype_size(t->dtype);
+  auto* st = new Storage();
+  st->ptr = pool_get(t->len * es, &st->bytes);
+  st->aliases = 1;
+  st->owned = true;
+  st->id = g_storage_ids.fetch_add(1, std::memory_order_relaxed);
+  if (t->len) {
+    if (es == 8)
+      k_view_gather<int64_t><<<grid_for(t->len, 256), 256, 0, stream()>>>(
+          (const int64_t*)t->st->ptr, (int64_t*)st->ptr, t->len, m);
+    else
+      k_view_gather<int32_t><<<grid_for(t->len, 256), 256, 0, stream()>>>(
+          (const int32_t*)t->st->ptr, (int32_t*)st->ptr, t->len, m);
+    count_launch();
+    after_launch("k_view_gather");
+  }
+  release_storage(t->st);
+  t->st = st;
+  delete t->view;
+  t->view = nullptr;
+}
+
+// The view of a reshape of a strided view, when the new shape can be read
+// from the same memory.  The view's dims are flattened into atoms (extent,
+// stride) in row-major order (a two-radix dim gives two), size-1 atoms are
+// dropped and adjacent atoms that are contiguous with each other merged; each
+// new dim must then be made of at most two consecutive atoms (an atom may be
+// split: its leading part strides over the trailing one).  False: not
+// expressible (the caller materialises).
+static bool reshape_view(const size_t* shape, int ndim, const View& view, const size_t* dims, size_t nd,
+                         View* out) {
+  std::vector<std::pair<int64_t, int64_t>> at;   // (extent, stride)
+  for (int d = 0; d < ndim; ++d) {
+    const int64_t n = (int64_t)shape[d];
+    if (n == 0) return false;
+    const ViewDim vd = view.d[d];
+    if (vd.div) {
+      if (n % vd.div) return false;
+      at.push_back({n / vd.div, vd.hi});
+      at.push_back({vd.div, vd.lo});
+    } else {
+      at.push_back({n, vd.lo});
+    }
+  }
+  std::vector<std::pair<int64_t, int64_t>> a;
+  for (auto& x : at) {
+    if (x.first == 1) continue;
+    if (!a.empty() && a.back().second == x.first * x.second) {
+      a.back().first *= x.first;
+      a.back().second = x.second;
+    } else {
+      a.push_back(x);
+    }
+  }
+  size_t ai = 0;
+  int64_t rem = a.empty() ? 1 : a[0].first;
+  for (size_t k = 0; k < nd; ++k) {
+    int64_t need = (int64_t)dims[k];
+    if (need == 1) { out->d[k] = ViewDim{0, 0, 0}; continue; }
+    int np = 0;
+    int64_t pn[2] = {0, 0}, ps[2] = {0, 0};
+    while (need > 1) {
+      if (ai >= a.size() || np == 2) return false;
+      const int64_t st = a[ai].second;
+      if (rem <= need) {
+        if (need % rem) return false;
+        pn[np] = rem; ps[np] = st; ++np;
+        need /= rem;
+        ++ai;
+        rem = ai < a.size() ? a[ai].first : 1;
+      } else {
+        if (rem % need) return false;
+        pn[np] = need; ps[np] = st * (rem / need); ++np;
+        rem /= need;
+        need = 1;
+      }
+    }
+    if (np == 1 || ps[0] == pn[1] * ps[1]) out->d[k] = ViewDim{0, 0, np == 1 ? ps[0] : ps[1]};
+    else out->d[k] = ViewDim{pn[1], ps[0], ps[1]};
+  }
+  return ai >= a.size();
 }
 
 }  // namespace malus
@@ -377,6 +531,7 @@ void tensor_release(int64_t h) {
   if (prev == 1) {
     tape_on_release(h);
     release_storage(t->st);
+    delete t->view;
     delete t;
   }
 }
@@ -435,8 +590,7 @@ float malus_tensor_get_f32(int64_t h, int64_t idx) {
   if (idx < 0 || (size_t)idx >= t->len)
     panic("tensor_get_f32 index %lld out of range for length %zu", (long long)idx, t->len);
   float v;
-  MALUS_CUDA(cudaMemcpyAsync(&v, (const float*)t->st->ptr + idx, 4, cudaMemcpyDeviceToHost,
-                             stream()));
+  MALUS_CUDA(cudaMemcpyAsync(&v, fptr(h) + idx, 4, cudaMemcpyDeviceToHost, stream()));
   gpu_barrier();
   return v;
 }
@@ -449,6 +603,11 @@ int64_t tensor_reshape(int64_t h, const size_t* dims, size_t ndims) {
     panic("reshape element count mismatch: input has %zu elements, target would have %zu",
           t->len, n);
   if (ndims > (size_t)kMaxRank) panic("reshape rank %zu exceeds %d", ndims, kMaxRank);
+  if (t->view) {   // a strided view: a view again where the memory allows, else copied once
+    View v;
+    if (t->len && reshape_view(t->shape, t->ndim, *t->view, dims, ndims, &v)) return make_view(h, dims, (int)ndims, v);
+    materialize(h);
+  }
   t->st->aliases++;
   return make_handle(t->dtype, dims, (int)ndims, t->st, t->len);
 }
@@ -662,14 +821,15 @@ void malus_tensor_read(int64_t h, void* dst, size_t bytes) {
   auto* t = tb(h);
   size_t have = t->len * dtype_size(t->dtype);
   if (bytes > have) panic("tensor_read of %zu bytes from a %zu-byte tensor", bytes, have);
-  if (bytes) MALUS_CUDA(cudaMemcpyAsync(dst, t->st->ptr, bytes, cudaMemcpyDeviceToHost, stream()));
+  if (bytes) MALUS_CUDA(cudaMemcpyAsync(dst, vptr(h), bytes, cudaMemcpyDeviceToHost, stream()));
   gpu_barrier();
 }
 void malus_tensor_write(int64_t h, const void* src, size_t bytes) {
   auto* t = tb(h);
   size_t have = t->len * dtype_size(t->dtype);
   if (bytes > have) panic("tensor_write of %zu bytes into a %zu-byte tensor", bytes, have);
-  if (bytes) MALUS_CUDA(cudaMemcpyAsync(t->st->ptr, src, bytes, cudaMemcpyHostToDevice, stream()));
+  plane_cache_clear();   // the data changes in place
+  if (bytes) MALUS_CUDA(cudaMemcpyAsync(vptr(h), src, bytes, cudaMemcpyHostToDevice, stream()));
   gpu_barrier();
 }
 int64_t malus_tensor_wrap(int32_t dtype, void* dev_ptr, const size_t* shape, size_t ndims) {
@@ -678,6 +838,7 @@ int64_t malus_tensor_wrap(int32_t dtype, void* dev_ptr, const size_t* shape, siz
   st->bytes = 0;
   st->aliases = 1;
   st->owned = false;
+  st->id = g_storage_ids.fetch_add(1, std::memory_order_relaxed);
   size_t n = 1;
   for (size_t i = 0; i < ndims; ++i) n *= shape[i];
   return make_handle(dtype, shape, (int)ndims, st, n);
@@ -719,6 +880,7 @@ int64_t g_graph_next = 1;
 
 int32_t malus_graph_begin(void) {
   ensure_init();
+  plane_cache_clear();
   {
     std::lock_guard<std::mutex> lk(g_pool.mu);
     if (g_cap.active) panic("malus_graph_begin: a capture is already open");
@@ -730,6 +892,7 @@ int32_t malus_graph_begin(void) {
 }
 
 int64_t malus_graph_end(void) {
+  plane_cache_clear();
   cudaGraph_t graph = nullptr;
   cudaError_t e = cudaStreamEndCapture(stream(), &graph);
   auto* rec = new GraphRec();
@@ -765,6 +928,7 @@ int64_t malus_graph_end(void) {
 int32_t malus_graph_replay(int64_t id) {
   auto it = g_graphs.find(id);
   if (it == g_graphs.end()) return -1;
+  plane_cache_clear();   // the replay rewrites tensors in place
   MALUS_CUDA(cudaGraphLaunch(it->second->exec, stream()));
   count_launch((int)it->second->launches);
   return 0;

@@ -418,9 +418,11 @@ void backward(int64_t loss) {
   for (int64_t h : to_release) tensor_release(h);
   for (auto& kv : grads) tensor_release(kv.second);
   tape_clear();
+  plane_cache_clear();   // a step boundary: parameters are about to change in place
 }
 
 void tape_zero_grad(const int64_t* handles, size_t count) {
+  plane_cache_clear();   // a step boundary (the optimizer has written the parameters)
   if (!handles || !count) return;
   std::vector<int64_t> rel;
   for (size_t i = 0; i < count; ++i) {
