@@ -53,6 +53,15 @@ struct ViewDim {
 };
 struct View { ViewDim d[kMaxRank]; };
 
+// A deferred elementwise result: value = src * scale[0] (+ addend, broadcast
+// over src's leading dims: its shape is src's trailing dims), with the two f32
+// roundings of the eager multiply and add.  A multiply by a one-element tensor
+// makes one (the attention score scaling, and its VJP), an add of such a
+// product and a tensor of its trailing shape extends it (the causal mask).
+// The softmax and the GEMM operand split read it fused; any raw access
+// materialises it.  It holds references to its operands and no storage.
+struct Lazy { int64_t src, scale, addend; };
+
 // A tensor is either contiguous row-major over its storage (view == nullptr)
 // or a strided view of a storage shared with the tensor it was made from
 // (permute, and reshapes of such views).  Raw pointers (fptr / vptr) always
@@ -65,23 +74,29 @@ struct TensorBuffer {
   size_t shape[kMaxRank];
   std::atomic<int64_t> rc;
   View* view = nullptr;
+  Lazy* lazy = nullptr;    // st == nullptr while set
 };
 
 inline TensorBuffer* tb(int64_t h) {
   if (h == 0) panic("null tensor handle");
   return reinterpret_cast<TensorBuffer*>(h);
 }
-void materialize(int64_t h);   // a view becomes a contiguous tensor with storage of its own
+// A view or a deferred result becomes a contiguous tensor with storage of its own.
+void materialize(int64_t h);
 inline float* fptr(int64_t h) {
   auto* t = tb(h);
-  if (t->view) materialize(h);
+  if (t->view || t->lazy) materialize(h);
   return static_cast<float*>(t->st->ptr);
 }
 inline void* vptr(int64_t h) {
   auto* t = tb(h);
-  if (t->view) materialize(h);
+  if (t->view || t->lazy) materialize(h);
   return t->st->ptr;
 }
+// A deferred src * scale (+ addend) of the given shape (src's); retains the operands.
+int64_t make_lazy(const size_t* shape, int ndim, int64_t src, int64_t scale, int64_t addend);
+// A new handle for the same values (same storage, view or deferred result).
+int64_t alias_of(int64_t h);
 // The view of tensor h's dims (row-major strides when it is contiguous).
 View view_of(int64_t h);
 // h's data read as the shape `dims` (same element count) through one view of
@@ -156,7 +171,10 @@ enum RedOp : int { kRSum = 0, kRMean = 1, kRMax = 2, kRVar = 3 };
 void reduce_axis(int op, const float* x, float* out, size_t outer, size_t axis_sz, size_t inner);
 
 // ---- row kernels (rows.cu) ----
-void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner);
+// x (optionally): each element times scale[0], plus addend[(row % add_rows) * axis + i]
+// (same roundings as the eager multiply and add; rows along the last axis only)
+void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner,
+                 const float* scale = nullptr, const float* addend = nullptr, size_t add_rows = 1);
 void softmax_bwd(const float* s, const float* dout, float* dx, size_t outer, size_t axis_sz,
                  size_t inner);
 void layernorm_fwd(const float* x, float* y, float* var, size_t outer, size_t axis_sz,

@@ -111,6 +111,42 @@ int64_t sum_to_shape(int64_t g, const Shape& target) {
   return cur;
 }
 
+// Deferred products are made only for large tensors (where the pass they
+// save matters) whose consumers can read them fused.
+constexpr size_t kLazyMin = (size_t)1 << 16;
+
+bool one_element_f32(int64_t h) { return tb(h)->len == 1 && tb(h)->dtype == MALUS_F32; }
+
+// a * b for a one-element b, deferred (the result has a's shape when b's rank
+// does not exceed a's); 0 when not applicable.
+int64_t lazy_scale(int64_t a, int64_t b) {
+  auto *ta = tb(a), *tb_ = tb(b);
+  if (ta->dtype != MALUS_F32 || ta->len < kLazyMin || !one_element_f32(b) || tb_->ndim > ta->ndim) return 0;
+  return make_lazy(ta->shape, ta->ndim, a, b, 0);
+}
+
+// (x * s) + m for a deferred x * s and an m of its trailing shape, deferred; 0
+// when not applicable.
+int64_t lazy_add(int64_t a, int64_t b) {
+  auto *ta = tb(a), *tm = tb(b);
+  if (!ta->lazy || !ta->lazy->scale || ta->lazy->addend || tm->dtype != MALUS_F32 || tm->ndim > ta->ndim ||
+      tm->len == 0)
+    return 0;
+  for (int i = 0; i < tm->ndim; ++i)
+    if (tm->shape[i] != ta->shape[ta->ndim - tm->ndim + i]) return 0;
+  return make_lazy(ta->shape, ta->ndim, ta->lazy->src, ta->lazy->scale, b);
+}
+
+// The gradient of a same-shape operand is the incoming gradient itself: a new
+// handle on the same data (gradients are never written in place); otherwise
+// summed down to the target shape.
+int64_t sum_to_shape_alias(int64_t g, const Shape& target) {
+  Shape s = shape_of(g);
+  bool same = s.ndim == target.ndim;
+  for (int i = 0; same && i < s.ndim; ++i) same = s.d[i] == target.d[i];
+  return same ? alias_of(g) : sum_to_shape(g, target);
+}
+
 int64_t scaled_copy(int64_t x, float c) {
   int64_t out = alloc_like(x);
   scalar_op_imm(kSMul, fptr(x), c, fptr(out), tb(x)->len);
@@ -175,6 +211,12 @@ int64_t permute_impl(int64_t x, const std::vector<int>& perm) {
 // a tensor whose memory cannot be read so is materialised first).
 GemmOperand operand_of(int64_t h, size_t nz, size_t rows, size_t cols) {
   auto* t = tb(h);
+  if (t->lazy && t->lazy->scale && !t->lazy->addend && !tb(t->lazy->src)->lazy) {
+    // x * s read straight from x: the split applies the multiply
+    GemmOperand o = operand_of(t->lazy->src, nz, rows, cols);
+    o.scale_dev = fptr(t->lazy->scale);
+    return o;
+  }
   const size_t dims[3] = {nz, rows, cols};
   View v;
   if (!view_as(h, dims, 3, &v)) {
@@ -251,9 +293,15 @@ int64_t tensor_permute(int64_t h, const size_t* perm, size_t ndims) {
 }
 
 // ------------------------------------------------------------ forward fns
-int64_t __broadcast_add_fwd(int64_t a, int64_t b) { return binary_broadcast(kAdd, a, b); }
+int64_t __broadcast_add_fwd(int64_t a, int64_t b) {
+  if (int64_t z = lazy_add(a, b)) return z;
+  return binary_broadcast(kAdd, a, b);
+}
 int64_t __broadcast_sub_fwd(int64_t a, int64_t b) { return binary_broadcast(kSub, a, b); }
-int64_t __broadcast_mul_fwd(int64_t a, int64_t b) { return binary_broadcast(kMul, a, b); }
+int64_t __broadcast_mul_fwd(int64_t a, int64_t b) {
+  if (int64_t z = lazy_scale(a, b)) return z;
+  return binary_broadcast(kMul, a, b);
+}
 int64_t __broadcast_div_fwd(int64_t a, int64_t b) { return binary_broadcast(kDiv, a, b); }
 
 int64_t __softmax_fwd(int64_t x, int64_t axis) {
@@ -263,6 +311,14 @@ int64_t __softmax_fwd(int64_t x, int64_t axis) {
   size_t outer, asz, inner;
   split_axis(s, ax, &outer, &asz, &inner);
   int64_t out = alloc_shape(s);
+  const Lazy* z = tb(x)->lazy;
+  if (z && inner == 1 && !tb(z->src)->lazy && (!z->addend || tb(z->addend)->len % asz == 0)) {
+    // softmax(src * s + m): one pass over src (the scaled and masked scores
+    // are never written)
+    softmax_fwd(fptr(z->src), fptr(out), outer, asz, inner, z->scale ? fptr(z->scale) : nullptr,
+                z->addend ? fptr(z->addend) : nullptr, z->addend ? tb(z->addend)->len / asz : 1);
+    return out;
+  }
   softmax_fwd(fptr(x), fptr(out), outer, asz, inner);
   return out;
 }
@@ -365,17 +421,26 @@ int64_t __rsqrt_eps_fwd(int64_t v, float eps) {
 }
 
 // ------------------------------------------------------------ BwdSlot fns
-int64_t __add_bwd_a(int64_t dout, int64_t a) { return sum_to_shape(dout, shape_of(a)); }
-int64_t __add_bwd_b(int64_t dout, int64_t b) { return sum_to_shape(dout, shape_of(b)); }
-int64_t __sub_bwd_a(int64_t dout, int64_t a) { return sum_to_shape(dout, shape_of(a)); }
+int64_t __add_bwd_a(int64_t dout, int64_t a) { return sum_to_shape_alias(dout, shape_of(a)); }
+int64_t __add_bwd_b(int64_t dout, int64_t b) { return sum_to_shape_alias(dout, shape_of(b)); }
+int64_t __sub_bwd_a(int64_t dout, int64_t a) { return sum_to_shape_alias(dout, shape_of(a)); }
 int64_t __sub_bwd_b(int64_t dout, int64_t b) {
-  int64_t r = sum_to_shape(dout, shape_of(b));
+  Shape sb = shape_of(b), sd = shape_of(dout);
+  bool same = sb.ndim == sd.ndim;
+  for (int i = 0; same && i < sb.ndim; ++i) same = sb.d[i] == sd.d[i];
+  if (same) {   // -g in one pass
+    int64_t r = alloc_shape(sb);
+    unary_op(kNeg, fptr(dout), fptr(r), tb(r)->len);
+    return r;
+  }
+  int64_t r = sum_to_shape(dout, sb);
   unary_op(kNeg, fptr(r), fptr(r), tb(r)->len);  // -(sum g) == sum(-g) exactly
   return r;
 }
 int64_t __mul_bwd_a(int64_t dout, int64_t a, int64_t b) {
-  int64_t full = binary_broadcast(kMul, dout, b);
-  int64_t r = sum_to_shape(full, shape_of(a));
+  int64_t full = lazy_scale(dout, b);   // dout * s for a one-element b: deferred
+  if (!full) full = binary_broadcast(kMul, dout, b);
+  int64_t r = sum_to_shape_alias(full, shape_of(a));
   tensor_release(full);
   return r;
 }

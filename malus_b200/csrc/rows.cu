@@ -56,21 +56,35 @@ __device__ float bmax(float v, float* sh) {
 }
 
 // ------------------------------------------------------------------ softmax
+// The row values a softmax reads: x, or the deferred x * scale[0] + addend
+// (addend rows repeat every add_rows rows), rounded like the eager ops.
+struct RowSrc {
+  const float* x;
+  const float* scale;
+  const float* add;
+  size_t add_rows;
+  __device__ __forceinline__ float at(size_t r, size_t i, size_t len, float sc) const {
+    float v = x[r * len + i];
+    if (scale) v = __fmul_rn(v, sc);
+    if (add) v = __fadd_rn(v, add[(r % add_rows) * len + i]);
+    return v;
+  }
+};
+
 // One warp per contiguous row; the row is kept in registers (<= 32*PER).
 template <int PER>
-__global__ void k_softmax_warp(const float* __restrict__ x, float* __restrict__ y, size_t rows,
-                               int len) {
+__global__ void k_softmax_warp(RowSrc x, float* __restrict__ y, size_t rows, int len) {
   int lane = threadIdx.x & 31;
   size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
   size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  const float sc = x.scale ? *x.scale : 1.0f;
   for (size_t r = warp; r < rows; r += nw) {
-    const float* xr = x + r * (size_t)len;
     float v[PER];
     float m = -INFINITY;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int i = lane + 32 * k;
-      v[k] = i < len ? xr[i] : -INFINITY;
+      v[k] = i < len ? x.at(r, i, len, sc) : -INFINITY;
       m = fmaxf(m, v[k]);
     }
     m = wmax(m);
@@ -92,19 +106,18 @@ __global__ void k_softmax_warp(const float* __restrict__ x, float* __restrict__ 
 }
 
 // Long rows: one block per row, three passes (max, sum, write).
-__global__ void k_softmax_block(const float* __restrict__ x, float* __restrict__ y, size_t rows,
-                                size_t len) {
+__global__ void k_softmax_block(RowSrc x, float* __restrict__ y, size_t rows, size_t len) {
   __shared__ float sh[32];
+  const float sc = x.scale ? *x.scale : 1.0f;
   for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const float* xr = x + r * len;
     float m = -INFINITY;
-    for (size_t i = threadIdx.x; i < len; i += blockDim.x) m = fmaxf(m, xr[i]);
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) m = fmaxf(m, x.at(r, i, len, sc));
     m = bmax(m, sh);
     float s = 0.0f;
-    for (size_t i = threadIdx.x; i < len; i += blockDim.x) s += expf(xr[i] - m);
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) s += expf(x.at(r, i, len, sc) - m);
     s = bsum(s, sh);
     float* yr = y + r * len;
-    for (size_t i = threadIdx.x; i < len; i += blockDim.x) yr[i] = expf(xr[i] - m) / s;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) yr[i] = expf(x.at(r, i, len, sc) - m) / s;
     __syncthreads();
   }
 }
@@ -776,12 +789,15 @@ static unsigned row_blocks(size_t rows) {
   return (unsigned)std::max<size_t>(1, std::min<size_t>(rows, (size_t)kNumSMs * 8));
 }
 
-void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner) {
+void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner,
+                 const float* scale, const float* addend, size_t add_rows) {
   if (!outer || !axis_sz || !inner) return;
+  if ((scale || addend) && inner != 1) panic("softmax_fwd: a deferred input needs the last axis");
+  const RowSrc src{x, scale, addend, std::max<size_t>(add_rows, 1)};
   if (inner == 1 && axis_sz <= 1024) {
-    LAUNCH_ROWS_WARP(k_softmax_warp, axis_sz, outer, x, y, outer, (int)axis_sz);
+    LAUNCH_ROWS_WARP(k_softmax_warp, axis_sz, outer, src, y, outer, (int)axis_sz);
   } else if (inner == 1) {
-    k_softmax_block<<<row_blocks(outer), 512, 0, stream()>>>(x, y, outer, axis_sz);
+    k_softmax_block<<<row_blocks(outer), 512, 0, stream()>>>(src, y, outer, axis_sz);
     count_launch();
     after_launch("k_softmax_block");
   } else {

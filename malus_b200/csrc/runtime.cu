@@ -333,6 +333,7 @@ static bool reshape_view(const size_t* shape, int ndim, const View& view, const 
 
 bool view_as(int64_t h, const size_t* dims, size_t nd, View* out) {
   auto* t = tb(h);
+  if (t->lazy) materialize(h);
   return t->len && reshape_view(t->shape, t->ndim, view_of(h), dims, nd, out);
 }
 
@@ -359,6 +360,7 @@ static bool is_row_major(const size_t* shape, int ndim, const View& v) {
 
 int64_t make_view(int64_t h, const size_t* shape, int ndim, const View& v) {
   auto* t = tb(h);
+  if (t->lazy) materialize(h);
   t->st->aliases++;
   int64_t out = make_handle(t->dtype, shape, ndim, t->st, t->len);
   if (!is_row_major(shape, ndim, v)) tb(out)->view = new View(v);
@@ -385,8 +387,68 @@ __global__ void k_view_gather(const T* __restrict__ src, T* __restrict__ out, si
   }
 }
 
+// out = src * scale[0] (+ addend[f % add_len]), the eager ops' two roundings
+__global__ void k_lazy_eval(const float* __restrict__ src, const float* __restrict__ scale,
+                            const float* __restrict__ add, size_t add_len, float* __restrict__ out,
+                            size_t n) {
+  const float sc = scale ? *scale : 1.0f;
+  for (size_t f = blockIdx.x * (size_t)blockDim.x + threadIdx.x; f < n; f += (size_t)gridDim.x * blockDim.x) {
+    float v = src[f];
+    if (scale) v = __fmul_rn(v, sc);
+    if (add) v = __fadd_rn(v, add[f % add_len]);
+    out[f] = v;
+  }
+}
+
+int64_t make_lazy(const size_t* shape, int ndim, int64_t src, int64_t scale, int64_t addend) {
+  size_t n = 1;
+  for (int i = 0; i < ndim; ++i) n *= shape[i];
+  if (n != tb(src)->len) panic("make_lazy: %zu elements over a %zu-element source", n, tb(src)->len);
+  int64_t h = make_handle(MALUS_F32, shape, ndim, nullptr, n);
+  tensor_retain(src);
+  if (scale) tensor_retain(scale);
+  if (addend) tensor_retain(addend);
+  tb(h)->lazy = new Lazy{src, scale, addend};
+  return h;
+}
+
+int64_t alias_of(int64_t h) {
+  auto* t = tb(h);
+  if (t->lazy) return make_lazy(t->shape, t->ndim, t->lazy->src, t->lazy->scale, t->lazy->addend);
+  if (t->view) return make_view(h, t->shape, t->ndim, *t->view);
+  t->st->aliases++;
+  return make_handle(t->dtype, t->shape, t->ndim, t->st, t->len);
+}
+
+static void release_lazy(Lazy* z) {
+  tensor_release(z->src);
+  if (z->scale) tensor_release(z->scale);
+  if (z->addend) tensor_release(z->addend);
+  delete z;
+}
+
 void materialize(int64_t h) {
   auto* t = tb(h);
+  if (t->lazy) {
+    Lazy* z = t->lazy;
+    auto* st = new Storage();
+    st->ptr = pool_get(t->len * 4, &st->bytes);
+    st->aliases = 1;
+    st->owned = true;
+    st->id = g_storage_ids.fetch_add(1, std::memory_order_relaxed);
+    if (t->len) {
+      const float* add = z->addend ? fptr(z->addend) : nullptr;
+      k_lazy_eval<<<grid_for(t->len, 256), 256, 0, stream()>>>(
+          fptr(z->src), z->scale ? fptr(z->scale) : nullptr, add, add ? tb(z->addend)->len : 1,
+          (float*)st->ptr, t->len);
+      count_launch();
+      after_launch("k_lazy_eval");
+    }
+    t->st = st;
+    t->lazy = nullptr;
+    release_lazy(z);
+    return;
+  }
   if (!t->view) return;
   ViewMeta m;
   m.ndim = t->ndim;
@@ -530,7 +592,8 @@ void tensor_release(int64_t h) {
           "borrow-inference or tape-retain bug", (unsigned long long)h);
   if (prev == 1) {
     tape_on_release(h);
-    release_storage(t->st);
+    if (t->lazy) release_lazy(t->lazy);
+    else release_storage(t->st);
     delete t->view;
     delete t;
   }
@@ -603,6 +666,9 @@ int64_t tensor_reshape(int64_t h, const size_t* dims, size_t ndims) {
     panic("reshape element count mismatch: input has %zu elements, target would have %zu",
           t->len, n);
   if (ndims > (size_t)kMaxRank) panic("reshape rank %zu exceeds %d", ndims, kMaxRank);
+  if (t->lazy) {   // same element order: a deferred result of the new shape
+    return make_lazy(dims, (int)ndims, t->lazy->src, t->lazy->scale, t->lazy->addend);
+  }
   if (t->view) {   // a strided view: a view again where the memory allows, else copied once
     View v;
     if (t->len && reshape_view(t->shape, t->ndim, *t->view, dims, ndims, &v)) return make_view(h, dims, (int)ndims, v);

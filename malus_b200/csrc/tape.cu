@@ -3,10 +3,16 @@
 // persistent accumulate-until-zero_grad leaf gradients, a 30-entry BwdSlot
 // table of VJP function pointers, and the same retain/release rules.
 //
-// One addition that changes no observable value: before the reverse walk the
+// Two additions that change no observable value: before the reverse walk the
 // tape marks which handles can reach a registered leaf, and skips VJPs whose
 // result could only flow into gradients that are dropped at the end of
-// backward() (the reference computes and then releases them, tape.rs:714-717).
+// backward() (the reference computes and then releases them, tape.rs:714-717);
+// and the gradient of a registered leaf that only a multiply or an add reads
+// (the attention scale and mask leaves of nanogpt_modular.ml:52-56) is
+// deferred to the end of backward(), where it is evaluated, with the same
+// VJP and arguments, only if the leaf outlives the tape (a leaf released
+// with the tape has its gradient dropped unevaluated, as the reference drops
+// the one it computed).
 #include "common.cuh"
 
 #include <unordered_map>
@@ -37,8 +43,16 @@ struct Node {
   std::vector<int64_t> meta;
 };
 
+// A leaf gradient not yet evaluated: VJP slot `slot` applied to (dout, a, b),
+// all three retained.
+struct Thunk {
+  int slot;
+  int64_t dout, a, b;
+};
+
 struct TapeState {
   bool recording = true;
+  std::unordered_map<int64_t, Thunk> pending;   // leaf -> deferred gradient (during backward)
   std::vector<Node> nodes;
   std::unordered_set<int64_t> leaves;
   std::unordered_map<int64_t, int64_t> leaf_grad;
@@ -100,6 +114,17 @@ void check_op(int32_t tag) {
 }
 
 int64_t grad_acc(int64_t old, int64_t nw) { return ((F2)slot(sGradAcc))(old, nw); }
+
+int64_t run_thunk(const Thunk& k) {
+  if (k.slot == sMulB || k.slot == sDivB) return ((F3)slot(k.slot))(k.dout, k.a, k.b);
+  return ((F2)slot(k.slot))(k.dout, k.b);   // sAddB, sSubB
+}
+
+void drop_thunk(const Thunk& k) {
+  tensor_release(k.dout);
+  tensor_release(k.a);
+  tensor_release(k.b);
+}
 
 void accumulate(std::unordered_map<int64_t, int64_t>& grads, int64_t input, int64_t g) {
   auto it = grads.find(input);
@@ -273,6 +298,27 @@ void backward(int64_t loss) {
     grads.emplace(loss, tensor_alloc_ones_gpu(t->shape, t->ndim));
   }
 
+  // A leaf read by exactly one node (and in no data-parallel bucket) gets its
+  // gradient as a thunk, which holds the leaf; after the tape is cleared the
+  // thunk is evaluated only if something besides it still holds the leaf.
+  std::unordered_map<int64_t, int> reads;
+  for (auto& n : nodes) {
+    size_t nin = n.saved.size();
+    if (n.op == kLayernorm || n.op == kCrossEntropy || n.op == kEmbedding) nin = 1;
+    for (size_t i = 0; i < nin; ++i)
+      if (T.leaves.count(n.saved[i])) reads[n.saved[i]]++;
+  }
+  auto defer = [&](int64_t leaf, int slot_id, int64_t dout, int64_t a) -> bool {
+    if (!T.leaves.count(leaf) || reads[leaf] != 1 || (dp && dp_is_leaf(leaf)) || grads.count(leaf) ||
+        T.pending.count(leaf))
+      return false;
+    tensor_retain(dout);
+    tensor_retain(a);
+    tensor_retain(leaf);
+    T.pending.emplace(leaf, Thunk{slot_id, dout, a, leaf});
+    return true;
+  };
+
   for (auto it = nodes.rbegin(); it != nodes.rend(); ++it) {
     const Node& n = *it;
     if (dp) {
@@ -300,14 +346,14 @@ void backward(int64_t loss) {
         int64_t a = n.saved[0], b = n.saved[1];
         int sa = n.op == kTAdd ? sAddA : sSubA, sb = n.op == kTAdd ? sAddB : sSubB;
         if (need(a)) accumulate(grads, a, ((F2)slot(sa))(dout, a));
-        if (need(b)) accumulate(grads, b, ((F2)slot(sb))(dout, b));
+        if (need(b) && !defer(b, sb, dout, a)) accumulate(grads, b, ((F2)slot(sb))(dout, b));
         break;
       }
       case kTMul: case kTDiv: {
         int64_t a = n.saved[0], b = n.saved[1];
         int sa = n.op == kTMul ? sMulA : sDivA, sb = n.op == kTMul ? sMulB : sDivB;
         if (need(a)) accumulate(grads, a, ((F3)slot(sa))(dout, a, b));
-        if (need(b)) accumulate(grads, b, ((F3)slot(sb))(dout, a, b));
+        if (need(b) && !defer(b, sb, dout, a)) accumulate(grads, b, ((F3)slot(sb))(dout, a, b));
         break;
       }
       case kTSigmoid: if (need(n.saved[0])) accumulate(grads, n.saved[0], ((F2)slot(sSigmoid))(n.output, dout)); break;
@@ -417,7 +463,29 @@ void backward(int64_t loss) {
   }
   for (int64_t h : to_release) tensor_release(h);
   for (auto& kv : grads) tensor_release(kv.second);
+  // The thunks hold their leaves, so every pending leaf is alive here.  The
+  // tape's references go first; a leaf then held by its thunk alone needs no
+  // gradient (dropping the thunk releases it and its registry entry).
   tape_clear();
+  std::vector<std::pair<int64_t, Thunk>> due(T.pending.begin(), T.pending.end());
+  T.pending.clear();
+  for (auto& kv : due) {
+    const int64_t leaf = kv.first;
+    const Thunk& k = kv.second;
+    if (tb(leaf)->rc.load() > 1) {   // held by someone besides the thunk: evaluate now
+      int64_t ng = run_thunk(k);
+      auto li = T.leaf_grad.find(leaf);
+      if (li == T.leaf_grad.end()) {
+        T.leaf_grad.emplace(leaf, ng);
+      } else {
+        int64_t old = li->second;
+        li->second = grad_acc(old, ng);
+        tensor_release(old);
+        tensor_release(ng);
+      }
+    }
+    drop_thunk(k);
+  }
   plane_cache_clear();   // a step boundary: parameters are about to change in place
 }
 
