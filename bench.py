@@ -351,6 +351,8 @@ class Runner:
             dt_prof_ms = timed_steps()
             cnt, ms_k, fl_k, by_k = C.c_int64(), C.c_double(), C.c_double(), C.c_double()
             lib.malus_prof_report(0, C.byref(cnt), C.byref(ms_k), C.byref(fl_k), C.byref(by_k))
+            if self.world > 1:
+                out["dp"] = self._dp_report(lib, steps, dt_prof_ms)
             lib.malus_prof_enable(0)
             out["roofline"] = self._gemm_roofline(cnt.value, ms_k.value, fl_k.value, by_k.value, dt_prof_ms,
                                                   steps, workload, mode)
@@ -371,6 +373,24 @@ class Runner:
         del xd, yd
         torch.cuda.empty_cache()
         return out
+
+    def _dp_report(self, lib, steps, dt_prof_ms):
+        """The gradient all-reduces of the profiled pass (this rank): their time on
+        the collective stream, the part the main stream waited for at the join
+        (not hidden by the backward pass), and the bus bandwidth NCCL reached."""
+        n, ms, _, by = C.c_int64(), C.c_double(), C.c_double(), C.c_double()
+        lib.malus_prof_report(3, C.byref(n), C.byref(ms), None, C.byref(by))
+        nj, msj = C.c_int64(), C.c_double()
+        lib.malus_prof_report(4, C.byref(nj), C.byref(msj), None, None)
+        w = self.world
+        bus = 2.0 * (w - 1) / w * by.value / (ms.value / 1e3) / 1e9 if ms.value else None
+        return {"allreduce_calls_per_step": n.value / steps,
+                "allreduce_ms_per_step": round(ms.value / steps, 4),
+                "exposed_ms_per_step": round(msj.value / steps, 4),
+                "payload_mb_per_step": round(by.value / steps / 1e6, 2),
+                "bus_gbs": round(bus, 1) if bus else None,
+                "profiled_step_ms": round(dt_prof_ms / steps, 4),
+                "note": "rank 0's profiled pass (eager, CUDA events on the collective stream and at the join)"}
 
     def _gemm_roofline(self, cnt, ms_k, fl_k, by_k, dt_prof_ms, steps, workload, mode):
         if not cnt:
@@ -477,6 +497,7 @@ def main():
                 "path": {"mode": "fused" if args.mode == 1 else "tape", "cuda_graph": bool(args.graph)},
                 "roofline": head.get("roofline"), "cpu_baseline": cpu, "e2e": head["e2e"],
                 "gpu_launches": head["gpu_launches"], "clocks": clk.summary(), "loss_last": head["loss_last"],
+                **({"dp": head["dp"]} if "dp" in head else {}),
                 "algorithmic_tflops_per_step": round(step_flops(cfg) / 1e12, 4), **extras}
         print(json.dumps(line), flush=True)
     if world > 1:

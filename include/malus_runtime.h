@@ -439,9 +439,12 @@ void malus_tf32_split(const float* src, int64_t rows, int64_t cols, int64_t ld, 
  * bounded wait ran out (0 = none); cleared by reading. */
 int32_t malus_device_error(void);
 
-/* Live per-kernel-class timing with CUDA events on the runtime stream (for
- * roofline figures).  Classes: 0 tcgen05 GEMM, 1 GEMM operand split,
- * 2 SIMT GEMM.  Enabling resets the records. */
+/* Live per-kernel-class timing with CUDA events (for roofline figures).
+ * Classes: 0 tcgen05 GEMM, 1 GEMM operand split, 2 SIMT GEMM (on the runtime
+ * stream); 3 data-parallel all-reduce (on the collective stream, bytes =
+ * payload); 4 the runtime stream's wait for the all-reduces (the part the
+ * backward pass does not hide).  Enabling resets the records; while enabled
+ * the model step runs without its CUDA graph. */
 void malus_prof_enable(int32_t on);
 void malus_prof_report(int32_t cls, int64_t* count, double* ms, double* flops, double* bytes);
 

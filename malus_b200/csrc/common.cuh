@@ -120,6 +120,8 @@ int32_t* device_error_word();
 bool prof_on();
 int prof_begin(int cls, double flops, double bytes);
 void prof_end(int id);
+int prof_begin_on(int cls, double flops, double bytes, cudaStream_t s);   // on another stream
+void prof_end_on(int id, cudaStream_t s);
 
 // Shape helpers
 struct Shape {

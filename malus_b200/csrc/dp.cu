@@ -60,7 +60,9 @@ int dp_allreduce_async(float* ptr, size_t count) {
   if (g_world <= 1 || !g_comm) return 0;
   MALUS_CUDA(cudaEventRecord(g_ev_ready, stream()));
   MALUS_CUDA(cudaStreamWaitEvent(g_dp_stream, g_ev_ready, 0));
+  const int pid = prof_begin_on(3, 0.0, 4.0 * (double)count, g_dp_stream);
   ncclResult_t r = ncclAllReduce(ptr, ptr, count, ncclFloat, ncclSum, g_comm, g_dp_stream);
+  prof_end_on(pid, g_dp_stream);
   if (r != ncclSuccess && r != ncclInProgress) {
     fprintf(stderr, "malus: ncclAllReduce failed: %s\n", ncclGetErrorString(r));
     return -5;
@@ -76,7 +78,9 @@ int dp_allreduce_async(float* ptr, size_t count) {
 void dp_join() {
   if (g_world <= 1 || !g_comm) return;
   MALUS_CUDA(cudaEventRecord(g_ev_done, g_dp_stream));
+  const int pid = prof_begin(4, 0.0, 0.0);   // from here to the end of the wait: exposed communication
   MALUS_CUDA(cudaStreamWaitEvent(stream(), g_ev_done, 0));
+  prof_end(pid);
 }
 
 // ---- per-leaf readiness (malus_dp_register_leaves / malus_dp_grad_ready) ----
@@ -119,11 +123,15 @@ int dp_leaf_ready(int64_t leaf, int64_t grad) {
   if (items.empty()) return 0;
   MALUS_CUDA(cudaEventRecord(g_ev_ready, stream()));
   MALUS_CUDA(cudaStreamWaitEvent(g_dp_stream, g_ev_ready, 0));
+  double bytes = 0.0;
+  for (auto& pc : items) bytes += 4.0 * (double)pc.second;
+  const int pid = prof_begin_on(3, 0.0, bytes, g_dp_stream);
   ncclResult_t r = ncclGroupStart();
   for (auto& pc : items)
     if (r == ncclSuccess || r == ncclInProgress)
       r = ncclAllReduce(pc.first, pc.first, pc.second, ncclFloat, ncclAvg, g_comm, g_dp_stream);
   ncclResult_t e = ncclGroupEnd();
+  prof_end_on(pid, g_dp_stream);
   items.clear();
   if ((r != ncclSuccess && r != ncclInProgress) || (e != ncclSuccess && e != ncclInProgress)) {
     fprintf(stderr, "malus: bucket all-reduce failed: %s\n", ncclGetErrorString(r != ncclSuccess ? r : e));

@@ -1081,7 +1081,9 @@ void bench_reset(void) {
 // enabled, launches of a class are bracketed by CUDA events on the runtime
 // stream; the report sums the event durations and the algorithmic work the
 // launcher declared.  Classes: 0 = tcgen05 GEMM, 1 = split of GEMM operands,
-// 2 = SIMT GEMM.
+// 2 = SIMT GEMM, 3 = data-parallel all-reduce (on the collective stream;
+// bytes = payload), 4 = the main stream's wait for the all-reduces at the
+// join (the communication the backward pass does not hide).
 namespace malus {
 namespace {
 struct ProfRec { cudaEvent_t a, b; int cls; double flops, bytes; };
@@ -1096,17 +1098,19 @@ cudaEvent_t ev_get() {
 }
 }  // namespace
 bool prof_on() { return g_prof_on; }
-int prof_begin(int cls, double flops, double bytes) {
+int prof_begin_on(int cls, double flops, double bytes, cudaStream_t s) {
   if (!g_prof_on) return -1;
   ProfRec r{ev_get(), ev_get(), cls, flops, bytes};
-  MALUS_CUDA(cudaEventRecord(r.a, stream()));
+  MALUS_CUDA(cudaEventRecord(r.a, s));
   g_prof.push_back(r);
   return (int)g_prof.size() - 1;
 }
-void prof_end(int id) {
+void prof_end_on(int id, cudaStream_t s) {
   if (id < 0) return;
-  MALUS_CUDA(cudaEventRecord(g_prof[id].b, stream()));
+  MALUS_CUDA(cudaEventRecord(g_prof[id].b, s));
 }
+int prof_begin(int cls, double flops, double bytes) { return prof_begin_on(cls, flops, bytes, stream()); }
+void prof_end(int id) { prof_end_on(id, stream()); }
 }  // namespace malus
 
 extern "C" {
