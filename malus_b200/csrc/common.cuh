@@ -54,13 +54,16 @@ struct ViewDim {
 struct View { ViewDim d[kMaxRank]; };
 
 // A deferred elementwise result: value = src * scale[0] (+ addend, broadcast
-// over src's leading dims: its shape is src's trailing dims), with the two f32
-// roundings of the eager multiply and add.  A multiply by a one-element tensor
-// makes one (the attention score scaling, and its VJP), an add of such a
-// product and a tensor of its trailing shape extends it (the causal mask).
-// The softmax and the GEMM operand split read it fused; any raw access
-// materialises it.  It holds references to its operands and no storage.
-struct Lazy { int64_t src, scale, addend; };
+// over src's leading dims: its shape is src's trailing dims), or src * colscale
+// (a vector along the last dim), with the roundings of the eager multiply and
+// add.  A multiply by a one-element tensor makes the first kind (the attention
+// score scaling, and its VJP), an add of such a product and a tensor of its
+// trailing shape extends it (the causal mask); a multiply by a vector of the
+// last dim's length makes the second (the layernorm gain, and its VJP).  The
+// softmax, the layernorm VJP and the GEMM operand split read them fused; any
+// raw access materialises them.  They hold references to their operands and
+// no storage.
+struct Lazy { int64_t src, scale, addend, colscale; };
 
 // A tensor is either contiguous row-major over its storage (view == nullptr)
 // or a strided view of a storage shared with the tensor it was made from
@@ -93,8 +96,10 @@ inline void* vptr(int64_t h) {
   if (t->view || t->lazy) materialize(h);
   return t->st->ptr;
 }
-// A deferred src * scale (+ addend) of the given shape (src's); retains the operands.
-int64_t make_lazy(const size_t* shape, int ndim, int64_t src, int64_t scale, int64_t addend);
+// A deferred src * scale (+ addend), or src * colscale, of the given shape
+// (src's element count); retains the operands.
+int64_t make_lazy(const size_t* shape, int ndim, int64_t src, int64_t scale, int64_t addend,
+                  int64_t colscale = 0);
 // A new handle for the same values (same storage, view or deferred result).
 int64_t alias_of(int64_t h);
 // The view of tensor h's dims (row-major strides when it is contiguous).
@@ -171,6 +176,11 @@ void sigmoid_backward_user(const float* g, const float* s, float* out, size_t n)
 // ---- reductions (reduce.cu) ----
 enum RedOp : int { kRSum = 0, kRMean = 1, kRMax = 2, kRVar = 3 };
 void reduce_axis(int op, const float* x, float* out, size_t outer, size_t axis_sz, size_t inner);
+// Sum over the axis of x[i] * x2[i] (each product rounded to f32), with the
+// same partition and order as reduce_axis(kRSum) of the materialised product,
+// so the result is bit-identical to it; inner > 1 (column sums) only.
+void reduce_axis_sum_product(const float* x, const float* x2, float* out, size_t outer, size_t axis_sz,
+                             size_t inner);
 
 // ---- row kernels (rows.cu) ----
 // x (optionally): each element times scale[0], plus addend[(row % add_rows) * axis + i]
@@ -181,8 +191,9 @@ void softmax_bwd(const float* s, const float* dout, float* dx, size_t outer, siz
                  size_t inner);
 void layernorm_fwd(const float* x, float* y, float* var, size_t outer, size_t axis_sz,
                    size_t inner, float eps);
+// dout_colscale (optional, last axis only): dout is read as dout[i] * dout_colscale[i % axis]
 void layernorm_bwd(const float* y, const float* var, const float* dout, float* dx, size_t outer,
-                   size_t axis_sz, size_t inner, float eps);
+                   size_t axis_sz, size_t inner, float eps, const float* dout_colscale = nullptr);
 // probs [N,V] written; loss[0] = mean nll
 void xent_fwd(const float* logits, const void* targets, int tgt_dtype, float* probs, float* loss,
               size_t n, size_t v);
@@ -220,6 +231,7 @@ struct GemmOperand {
   int64_t nz = 1, rows = 0, cols = 0;
   ViewDim z, r, c;
   const float* scale_dev = nullptr;
+  const float* colscale_dev = nullptr;   // optional: column c (of cols) times colscale_dev[c]
   uint64_t key = 0;
 };
 // A contiguous row-major stack: nz slices of rows x cols, row pitch ld, slice stride sstride.

@@ -816,12 +816,15 @@ __global__ void k_split_tf32(const float* __restrict__ src, int64_t rows, int64_
 
 // ---- operand split through a strided view: planes [nz][n_outer][pitch],
 // element (z, o, i) read at base + z.at(z) + outer.at(o) + inner.at(i) and
-// multiplied by *scale when given (one f32 multiply, as the materialised
-// product would be); pitch padding is zero-filled.  One block row per plane
-// row, 1024 inner elements per block (four per thread).
+// multiplied by *scale, or by colscale[operand column], when given (one f32
+// multiply, as the materialised product would be); pitch padding is
+// zero-filled.  One block row per plane row, 1024 inner elements per block
+// (four per thread).
 struct SplitGeom {
   const float* base;
   const float* scale;
+  const float* colscale;
+  bool cs_inner;   // the operand's columns are the planes' inner index (else the outer)
   int64_t n_outer, n_inner, pitch;
   ViewDim z, outer, inner;
   bool vec;   // inner runs of 4 are contiguous and 16-byte aligned
@@ -846,6 +849,11 @@ __global__ void k_split_view(SplitGeom g, float* __restrict__ hi, float* __restr
 #pragma unroll
     for (int q = 0; q < 4; ++q) x[q] = __fmul_rn(x[q], sc);
   }
+  if (g.colscale) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (c + q < g.n_inner) x[q] = __fmul_rn(x[q], g.colscale[g.cs_inner ? c + q : o]);
+  }
   float h[4], l[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -863,6 +871,7 @@ __global__ void k_operand_gather(GemmOperand o, float* __restrict__ out, int64_t
     const int64_t c = f % o.cols, rz = f / o.cols, r = rz % o.rows, zi = rz / o.rows;
     float x = o.base[o.z.at(zi) + o.r.at(r) + o.c.at(c)];
     if (o.scale_dev) x = __fmul_rn(x, *o.scale_dev);
+    if (o.colscale_dev) x = __fmul_rn(x, o.colscale_dev[c]);
     out[f] = x;
   }
 }
@@ -1296,7 +1305,7 @@ GemmOperand plain_operand(const float* p, int64_t nz, int64_t rows, int64_t cols
 namespace {
 
 bool is_plain(const GemmOperand& o) {
-  return !o.scale_dev && o.z.div == 0 && o.r.div == 0 && o.c.div == 0 && o.c.lo == 1;
+  return !o.scale_dev && !o.colscale_dev && o.z.div == 0 && o.r.div == 0 && o.c.div == 0 && o.c.lo == 1;
 }
 
 // ---------------------------------------------------------- plane cache
@@ -1304,6 +1313,7 @@ struct PlaneEntry {
   int64_t nz, rows, cols;
   ViewDim z, r, c;
   const float* scale;
+  const float* colscale;
   float* mem;          // hi then lo, each nz * n_outer * pitch floats
   int64_t pitch;
   bool transposed;     // planes hold the operand's columns as rows
@@ -1323,7 +1333,7 @@ const PlaneEntry* pc_find(const GemmOperand& o) {
   if (it == g_pc.end()) return nullptr;
   for (const PlaneEntry& e : it->second)
     if (e.nz == o.nz && e.rows == o.rows && e.cols == o.cols && same_dim(e.z, o.z) && same_dim(e.r, o.r) &&
-        same_dim(e.c, o.c) && e.scale == o.scale_dev)
+        same_dim(e.c, o.c) && e.scale == o.scale_dev && e.colscale == o.colscale_dev)
       return &e;
   return nullptr;
 }
@@ -1356,6 +1366,8 @@ Planes operand_planes(const GemmOperand& o, bool* trans) {
   SplitGeom g;
   g.base = o.base;
   g.scale = o.scale_dev;
+  g.colscale = o.colscale_dev;
+  g.cs_inner = !flip;
   g.n_outer = n_outer;
   g.n_inner = n_inner;
   g.pitch = pitch;
@@ -1373,7 +1385,8 @@ Planes operand_planes(const GemmOperand& o, bool* trans) {
     after_launch("k_split_view");
   }
   if (cache) {
-    g_pc[o.key].push_back(PlaneEntry{o.nz, o.rows, o.cols, o.z, o.r, o.c, o.scale_dev, mem, pitch, flip});
+    g_pc[o.key].push_back(PlaneEntry{o.nz, o.rows, o.cols, o.z, o.r, o.c, o.scale_dev, o.colscale_dev, mem, pitch,
+                                     flip});
     return Planes{mem, mem + n, n_outer, n_inner, pitch, nullptr};
   }
   return Planes{mem, mem + n, n_outer, n_inner, pitch, mem};

@@ -125,11 +125,22 @@ int64_t lazy_scale(int64_t a, int64_t b) {
   return make_lazy(ta->shape, ta->ndim, a, b, 0);
 }
 
+// a * w for a vector w along a's last dim (b of shape [C], a [..., C]),
+// deferred; 0 when not applicable.
+int64_t lazy_colscale(int64_t a, int64_t b) {
+  auto *ta = tb(a), *tw = tb(b);
+  if (ta->dtype != MALUS_F32 || ta->len < kLazyMin || ta->lazy || ta->ndim < 1 || tw->dtype != MALUS_F32 ||
+      tw->ndim != 1 || tw->len < 2 || tw->len != ta->shape[ta->ndim - 1])
+    return 0;
+  return make_lazy(ta->shape, ta->ndim, a, 0, 0, b);
+}
+
 // (x * s) + m for a deferred x * s and an m of its trailing shape, deferred; 0
 // when not applicable.
 int64_t lazy_add(int64_t a, int64_t b) {
   auto *ta = tb(a), *tm = tb(b);
-  if (!ta->lazy || !ta->lazy->scale || ta->lazy->addend || tm->dtype != MALUS_F32 || tm->ndim > ta->ndim ||
+  if (!ta->lazy || !ta->lazy->scale || ta->lazy->addend || ta->lazy->colscale || tm->dtype != MALUS_F32 ||
+      tm->ndim > ta->ndim ||
       tm->len == 0)
     return 0;
   for (int i = 0; i < tm->ndim; ++i)
@@ -211,10 +222,17 @@ int64_t permute_impl(int64_t x, const std::vector<int>& perm) {
 // a tensor whose memory cannot be read so is materialised first).
 GemmOperand operand_of(int64_t h, size_t nz, size_t rows, size_t cols) {
   auto* t = tb(h);
-  if (t->lazy && t->lazy->scale && !t->lazy->addend && !tb(t->lazy->src)->lazy) {
+  if (t->lazy && t->lazy->scale && !t->lazy->addend && !t->lazy->colscale && !tb(t->lazy->src)->lazy) {
     // x * s read straight from x: the split applies the multiply
     GemmOperand o = operand_of(t->lazy->src, nz, rows, cols);
     o.scale_dev = fptr(t->lazy->scale);
+    return o;
+  }
+  if (t->lazy && t->lazy->colscale && !t->lazy->scale && !t->lazy->addend && !tb(t->lazy->src)->lazy &&
+      t->ndim > 0 && cols == t->shape[t->ndim - 1]) {
+    // x * w along the last dim (the operand's columns): the split applies it
+    GemmOperand o = operand_of(t->lazy->src, nz, rows, cols);
+    o.colscale_dev = fptr(t->lazy->colscale);
     return o;
   }
   const size_t dims[3] = {nz, rows, cols};
@@ -300,6 +318,7 @@ int64_t __broadcast_add_fwd(int64_t a, int64_t b) {
 int64_t __broadcast_sub_fwd(int64_t a, int64_t b) { return binary_broadcast(kSub, a, b); }
 int64_t __broadcast_mul_fwd(int64_t a, int64_t b) {
   if (int64_t z = lazy_scale(a, b)) return z;
+  if (int64_t z = lazy_colscale(a, b)) return z;
   return binary_broadcast(kMul, a, b);
 }
 int64_t __broadcast_div_fwd(int64_t a, int64_t b) { return binary_broadcast(kDiv, a, b); }
@@ -438,13 +457,25 @@ int64_t __sub_bwd_b(int64_t dout, int64_t b) {
   return r;
 }
 int64_t __mul_bwd_a(int64_t dout, int64_t a, int64_t b) {
-  int64_t full = lazy_scale(dout, b);   // dout * s for a one-element b: deferred
+  int64_t full = lazy_scale(dout, b);   // dout * s for a one-element b, dout * w for a vector: deferred
+  if (!full) full = lazy_colscale(dout, b);
   if (!full) full = binary_broadcast(kMul, dout, b);
   int64_t r = sum_to_shape_alias(full, shape_of(a));
   tensor_release(full);
   return r;
 }
 int64_t __mul_bwd_b(int64_t dout, int64_t a, int64_t b) {
+  auto *td = tb(dout), *tw = tb(b);
+  if (tw->ndim == 1 && tw->len > 1 && td->ndim >= 2 && tw->len == td->shape[td->ndim - 1] && same_shape(dout, a) &&
+      tb(a)->dtype == MALUS_F32 && tw->dtype == MALUS_F32) {
+    // the gradient of a gain vector: column sums of dout * a in one pass (the
+    // products are not written), same partition and order as summing the
+    // materialised product down to [C]
+    int64_t r = alloc_shape(shape_of(b));
+    const size_t C = tw->len;
+    reduce_axis_sum_product(fptr(dout), fptr(a), fptr(r), 1, td->len / C, C);
+    return r;
+  }
   int64_t full = binary_broadcast(kMul, dout, a);
   int64_t r = sum_to_shape(full, shape_of(b));
   tensor_release(full);
@@ -545,6 +576,13 @@ int64_t __layernorm_bwd(int64_t y, int64_t var_h, int64_t dout, int64_t axis) {
     panic("layernorm_bwd: variance has %zu elements, expected %zu (keepdim at axis)",
           tb(var_h)->len, outer * inner);
   int64_t dx = alloc_shape(sh);
+  const Lazy* z = tb(dout)->lazy;
+  if (z && z->colscale && !z->scale && !z->addend && !tb(z->src)->lazy && inner == 1 &&
+      tb(z->colscale)->len == asz && same_shape(dout, y)) {
+    // dout = g * w (the deferred gain VJP): read fused
+    layernorm_bwd(fptr(y), fptr(var_h), fptr(z->src), fptr(dx), outer, asz, inner, 1e-5f, fptr(z->colscale));
+    return dx;
+  }
   layernorm_bwd(fptr(y), fptr(var_h), fptr(dout), fptr(dx), outer, asz, inner, 1e-5f);
   return dx;
 }

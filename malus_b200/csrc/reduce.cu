@@ -118,21 +118,28 @@ __global__ void k_reduce_rows_block(const float* __restrict__ x, float* __restri
 
 // ---- column reduction partials: part[c][o*inner+i] over axis chunk c ----
 // mode 0: sum, 1: max, 2: sum of squared deviation from center[o*inner+i]
+// x2 (mode 0 only, optional): the values summed are x[i] * x2[i], each rounded
 __global__ void k_reduce_cols(const float* __restrict__ x, float* __restrict__ part,
                               const float* __restrict__ center, int mode, size_t outer,
-                              size_t axis_sz, size_t inner, size_t chunk) {
+                              size_t axis_sz, size_t inner, size_t chunk,
+                              const float* __restrict__ x2 = nullptr) {
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   size_t o = blockIdx.y;
   size_t c = blockIdx.z;
   if (i >= inner) return;
   size_t a0 = c * chunk, a1 = a0 + chunk < axis_sz ? a0 + chunk : axis_sz;
   const float* base = x + o * axis_sz * inner + i;
+  const float* base2 = x2 ? x2 + o * axis_sz * inner + i : nullptr;
   float ctr = mode == 2 ? center[o * inner + i] : 0.0f;
   float acc0 = mode == 1 ? -INFINITY : 0.0f, acc1 = acc0, acc2 = acc0, acc3 = acc0;
   size_t a = a0;
   for (; a + 4 <= a1; a += 4) {
     float v0 = base[a * inner], v1 = base[(a + 1) * inner];
     float v2 = base[(a + 2) * inner], v3 = base[(a + 3) * inner];
+    if (base2) {
+      v0 = __fmul_rn(v0, base2[a * inner]); v1 = __fmul_rn(v1, base2[(a + 1) * inner]);
+      v2 = __fmul_rn(v2, base2[(a + 2) * inner]); v3 = __fmul_rn(v3, base2[(a + 3) * inner]);
+    }
     if (mode == 1) {
       acc0 = fmaxf(acc0, v0); acc1 = fmaxf(acc1, v1); acc2 = fmaxf(acc2, v2); acc3 = fmaxf(acc3, v3);
     } else if (mode == 2) {
@@ -144,6 +151,7 @@ __global__ void k_reduce_cols(const float* __restrict__ x, float* __restrict__ p
   }
   for (; a < a1; ++a) {
     float v = base[a * inner];
+    if (base2) v = __fmul_rn(v, base2[a * inner]);
     if (mode == 1) acc0 = fmaxf(acc0, v);
     else if (mode == 2) { v -= ctr; acc0 += v * v; }
     else acc0 += v;
@@ -157,8 +165,17 @@ __global__ void k_reduce_combine(const float* __restrict__ part, float* __restri
                                  size_t m, int nchunks, int mode, float inv_n) {
   size_t j = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (j >= m) return;
+  // in chunk order; eight partials are loaded ahead of their additions
   float acc = part[j];
-  for (int c = 1; c < nchunks; ++c) {
+  int c = 1;
+  for (; c + 8 <= nchunks; c += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = part[(size_t)(c + u) * m + j];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = mode == 1 ? fmaxf(acc, v[u]) : acc + v[u];
+  }
+  for (; c < nchunks; ++c) {
     float v = part[(size_t)c * m + j];
     acc = mode == 1 ? fmaxf(acc, v) : acc + v;
   }
@@ -172,7 +189,7 @@ __global__ void k_div_n(float* __restrict__ v, size_t m, float n) {
 }
 
 void column_pass(const float* x, float* out, const float* center, int mode, size_t outer,
-                 size_t axis_sz, size_t inner, bool divide) {
+                 size_t axis_sz, size_t inner, bool divide, const float* x2 = nullptr) {
   size_t m = outer * inner;
   size_t target = (size_t)kNumSMs * 2048;
   size_t nchunks = 1;
@@ -187,7 +204,7 @@ void column_pass(const float* x, float* out, const float* center, int mode, size
   if (nchunks == 0) nchunks = 1;
   float* part = nchunks == 1 ? out : (float*)scratch_alloc(nchunks * m * sizeof(float));
   dim3 grid((unsigned)((inner + 255) / 256), (unsigned)outer, (unsigned)nchunks);
-  k_reduce_cols<<<grid, 256, 0, stream()>>>(x, part, center, mode, outer, axis_sz, inner, chunk);
+  k_reduce_cols<<<grid, 256, 0, stream()>>>(x, part, center, mode, outer, axis_sz, inner, chunk, x2);
   count_launch();
   after_launch("k_reduce_cols");
   if (nchunks > 1) {
@@ -251,6 +268,18 @@ void reduce_axis(int op, const float* x, float* out, size_t outer, size_t axis_s
     return;
   }
   column_pass(x, out, nullptr, op == kRMax ? 1 : 0, outer, axis_sz, inner, op == kRMean);
+}
+
+void reduce_axis_sum_product(const float* x, const float* x2, float* out, size_t outer, size_t axis_sz,
+                             size_t inner) {
+  if (inner <= 1) panic("reduce_axis_sum_product: column sums only (inner %zu)", inner);
+  const size_t m = outer * inner;
+  if (m == 0) return;
+  if (axis_sz == 0) {
+    scalar_op_imm(kSFill, nullptr, 0.0f, out, m);
+    return;
+  }
+  column_pass(x, out, nullptr, 0, outer, axis_sz, inner, false, x2);
 }
 
 }  // namespace malus

@@ -276,9 +276,11 @@ __global__ void k_layernorm_strided(const float* __restrict__ x, float* __restri
 }
 
 template <int PER>
+// gs (optional): the incoming gradient is read as g[i] * gs[i] (the deferred
+// gain VJP), rounded like the eager multiply.
 __global__ void k_layernorm_bwd_warp(const float* __restrict__ y, const float* __restrict__ var,
                                      const float* __restrict__ g, float* __restrict__ dx,
-                                     size_t rows, int len, float eps) {
+                                     size_t rows, int len, float eps, const float* __restrict__ gs) {
   int lane = threadIdx.x & 31;
   size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
   size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
@@ -291,7 +293,7 @@ __global__ void k_layernorm_bwd_warp(const float* __restrict__ y, const float* _
     for (int k = 0; k < PER; ++k) {
       int i = lane + 32 * k;
       yv[k] = i < len ? yr[i] : 0.0f;
-      gv[k] = i < len ? gr[i] : 0.0f;
+      gv[k] = i < len ? (gs ? __fmul_rn(gr[i], gs[i]) : gr[i]) : 0.0f;
       sg += gv[k];
       sgy += gv[k] * yv[k];
     }
@@ -309,22 +311,24 @@ __global__ void k_layernorm_bwd_warp(const float* __restrict__ y, const float* _
 
 __global__ void k_layernorm_bwd_block(const float* __restrict__ y, const float* __restrict__ var,
                                       const float* __restrict__ g, float* __restrict__ dx,
-                                      size_t rows, size_t len, float eps) {
+                                      size_t rows, size_t len, float eps, const float* __restrict__ gs) {
   __shared__ float sh[32];
   for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* yr = y + r * len;
     const float* gr = g + r * len;
+    auto gat = [&](size_t i) { return gs ? __fmul_rn(gr[i], gs[i]) : gr[i]; };
     float sg = 0.0f, sgy = 0.0f;
     for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
-      sg += gr[i];
-      sgy += gr[i] * yr[i];
+      const float gv = gat(i);
+      sg += gv;
+      sgy += gv * yr[i];
     }
     float mg = bsum(sg, sh) / (float)len;
     float mgy = bsum(sgy, sh) / (float)len;
     float inv = 1.0f / sqrtf(var[r] + eps);
     float* dr = dx + r * len;
     for (size_t i = threadIdx.x; i < len; i += blockDim.x)
-      dr[i] = ((gr[i] - mg) - yr[i] * mgy) * inv;
+      dr[i] = ((gat(i) - mg) - yr[i] * mgy) * inv;
     __syncthreads();
   }
 }
@@ -845,12 +849,13 @@ void layernorm_fwd(const float* x, float* y, float* var, size_t outer, size_t ax
 }
 
 void layernorm_bwd(const float* y, const float* var, const float* g, float* dx, size_t outer,
-                   size_t axis_sz, size_t inner, float eps) {
+                   size_t axis_sz, size_t inner, float eps, const float* gs) {
   if (!outer || !axis_sz || !inner) return;
+  if (gs && inner != 1) panic("layernorm_bwd: a column-scaled gradient needs the last axis");
   if (inner == 1 && axis_sz <= 1024) {
-    LAUNCH_ROWS_WARP(k_layernorm_bwd_warp, axis_sz, outer, y, var, g, dx, outer, (int)axis_sz, eps);
+    LAUNCH_ROWS_WARP(k_layernorm_bwd_warp, axis_sz, outer, y, var, g, dx, outer, (int)axis_sz, eps, gs);
   } else if (inner == 1) {
-    k_layernorm_bwd_block<<<row_blocks(outer), 512, 0, stream()>>>(y, var, g, dx, outer, axis_sz, eps);
+    k_layernorm_bwd_block<<<row_blocks(outer), 512, 0, stream()>>>(y, var, g, dx, outer, axis_sz, eps, gs);
     count_launch();
     after_launch("k_layernorm_bwd_block");
   } else {

@@ -387,20 +387,23 @@ __global__ void k_view_gather(const T* __restrict__ src, T* __restrict__ out, si
   }
 }
 
-// out = src * scale[0] (+ addend[f % add_len]), the eager ops' two roundings
+// out = src * scale[0] (+ addend[f % add_len]), or src * colscale[f % cs_len],
+// the eager ops' roundings
 __global__ void k_lazy_eval(const float* __restrict__ src, const float* __restrict__ scale,
-                            const float* __restrict__ add, size_t add_len, float* __restrict__ out,
-                            size_t n) {
+                            const float* __restrict__ add, size_t add_len, const float* __restrict__ cs,
+                            size_t cs_len, float* __restrict__ out, size_t n) {
   const float sc = scale ? *scale : 1.0f;
   for (size_t f = blockIdx.x * (size_t)blockDim.x + threadIdx.x; f < n; f += (size_t)gridDim.x * blockDim.x) {
     float v = src[f];
     if (scale) v = __fmul_rn(v, sc);
+    if (cs) v = __fmul_rn(v, cs[f % cs_len]);
     if (add) v = __fadd_rn(v, add[f % add_len]);
     out[f] = v;
   }
 }
 
-int64_t make_lazy(const size_t* shape, int ndim, int64_t src, int64_t scale, int64_t addend) {
+int64_t make_lazy(const size_t* shape, int ndim, int64_t src, int64_t scale, int64_t addend,
+                  int64_t colscale) {
   size_t n = 1;
   for (int i = 0; i < ndim; ++i) n *= shape[i];
   if (n != tb(src)->len) panic("make_lazy: %zu elements over a %zu-element source", n, tb(src)->len);
@@ -408,13 +411,15 @@ int64_t make_lazy(const size_t* shape, int ndim, int64_t src, int64_t scale, int
   tensor_retain(src);
   if (scale) tensor_retain(scale);
   if (addend) tensor_retain(addend);
-  tb(h)->lazy = new Lazy{src, scale, addend};
+  if (colscale) tensor_retain(colscale);
+  tb(h)->lazy = new Lazy{src, scale, addend, colscale};
   return h;
 }
 
 int64_t alias_of(int64_t h) {
   auto* t = tb(h);
-  if (t->lazy) return make_lazy(t->shape, t->ndim, t->lazy->src, t->lazy->scale, t->lazy->addend);
+  if (t->lazy)
+    return make_lazy(t->shape, t->ndim, t->lazy->src, t->lazy->scale, t->lazy->addend, t->lazy->colscale);
   if (t->view) return make_view(h, t->shape, t->ndim, *t->view);
   t->st->aliases++;
   return make_handle(t->dtype, t->shape, t->ndim, t->st, t->len);
@@ -424,6 +429,7 @@ static void release_lazy(Lazy* z) {
   tensor_release(z->src);
   if (z->scale) tensor_release(z->scale);
   if (z->addend) tensor_release(z->addend);
+  if (z->colscale) tensor_release(z->colscale);
   delete z;
 }
 
@@ -438,9 +444,10 @@ void materialize(int64_t h) {
     st->id = g_storage_ids.fetch_add(1, std::memory_order_relaxed);
     if (t->len) {
       const float* add = z->addend ? fptr(z->addend) : nullptr;
+      const float* cs = z->colscale ? fptr(z->colscale) : nullptr;
       k_lazy_eval<<<grid_for(t->len, 256), 256, 0, stream()>>>(
-          fptr(z->src), z->scale ? fptr(z->scale) : nullptr, add, add ? tb(z->addend)->len : 1,
-          (float*)st->ptr, t->len);
+          fptr(z->src), z->scale ? fptr(z->scale) : nullptr, add, add ? tb(z->addend)->len : 1, cs,
+          cs ? tb(z->colscale)->len : 1, (float*)st->ptr, t->len);
       count_launch();
       after_launch("k_lazy_eval");
     }
@@ -667,7 +674,7 @@ int64_t tensor_reshape(int64_t h, const size_t* dims, size_t ndims) {
           t->len, n);
   if (ndims > (size_t)kMaxRank) panic("reshape rank %zu exceeds %d", ndims, kMaxRank);
   if (t->lazy) {   // same element order: a deferred result of the new shape
-    return make_lazy(dims, (int)ndims, t->lazy->src, t->lazy->scale, t->lazy->addend);
+    return make_lazy(dims, (int)ndims, t->lazy->src, t->lazy->scale, t->lazy->addend, t->lazy->colscale);
   }
   if (t->view) {   // a strided view: a view again where the memory allows, else copied once
     View v;

@@ -169,3 +169,44 @@ def test_deferred_leaf_gradients(M, rt, rng):
     assert (leaves.value, grads.value) == (1, 1)           # only x remains, with its gradient
     np.testing.assert_array_equal(M.Tensor(rt.tape_get_grad(x.h)).numpy(), np.full(xs.shape, 0.5, np.float32))
     rt.malus_tape_reset()
+
+
+def test_gain_vector_products_equal_eager(M, rt, orc, rng):
+    """The layernorm gain x * w (w along the last dim), its VJPs and its reads:
+    a GEMM operand (the split applies w), the layernorm VJP (reads dout * w
+    fused), and the gain gradient (column sums of dout * y in one pass) are
+    bit-equal to the eager products."""
+    m_, c_ = 2048, 384
+    y = rng.standard_normal((m_, c_)).astype(np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(c_)).astype(np.float32)
+    wq = rng.standard_normal((c_, 3 * c_)).astype(np.float32)
+    ty, tw, twq = T(M, y), T(M, w), T(M, wq)
+    xn = rt.__broadcast_mul_fwd(ty.h, tw.h)
+    np.testing.assert_array_equal(np_of(M, xn), y * w)              # host read (materialised)
+    xn2 = rt.__broadcast_mul_fwd(ty.h, tw.h)                          # a fresh deferred product
+    ex = T(M, y * w)
+    np.testing.assert_array_equal(M.Tensor(rt.tensor_matmul(xn2, twq.h)).numpy(),
+                                  M.Tensor(rt.tensor_matmul(ex.h, twq.h)).numpy())
+    g = rng.standard_normal((m_, 3 * c_)).astype(np.float32)
+    tg = T(M, g)
+    np.testing.assert_array_equal(M.Tensor(rt.__matmul_bwd_b(xn2, twq.h, tg.h)).numpy(),
+                                  M.Tensor(rt.__matmul_bwd_b(ex.h, twq.h, tg.h)).numpy())
+    # backward of xn = y * w: d_y deferred (dout * w), read by the layernorm VJP
+    x = (rng.standard_normal((m_, c_)) * 2 + 0.3).astype(np.float32)
+    ly, lv = orc.layernorm(x, 1)
+    dout = rng.standard_normal((m_, c_)).astype(np.float32)
+    tly, tlv, td = T(M, ly), T(M, lv), T(M, dout)
+    dy = rt.__mul_bwd_a(td.h, tly.h, tw.h)
+    tdw = T(M, dout * w)                                              # the eager product
+    np.testing.assert_array_equal(M.Tensor(rt.__layernorm_bwd(tly.h, tlv.h, dy, 1)).numpy(),
+                                  M.Tensor(rt.__layernorm_bwd(tly.h, tlv.h, tdw.h, 1)).numpy())
+    np.testing.assert_array_equal(np_of(M, dy), dout * w)
+    # the gain gradient: column sums of dout * y, bit-equal to summing the product
+    dw = M.Tensor(rt.__mul_bwd_b(td.h, tly.h, tw.h)).numpy()
+    prod = T(M, dout * ly)
+    ones_c = T(M, np.zeros(c_, np.float32))
+    ref = M.Tensor(rt.__sum_to_shape_bwd(prod.h, ones_c.h)).numpy()
+    np.testing.assert_array_equal(dw, ref)
+    assert np.allclose(dw, (dout.astype(np.float64) * ly).sum(axis=0), rtol=0, atol=1e-5 * np.abs(dout * ly).sum(axis=0).max())
+    for h in (xn, xn2, dy):
+        rt.tensor_release(h)
