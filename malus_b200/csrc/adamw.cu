@@ -55,6 +55,22 @@ __global__ void k_adamw(SegTable t, int nseg, int64_t total4, float lr, float b1
     while (s > 0 && q < t.start[s]) --s;
     const AdamSeg& sg = t.seg[s];
     int64_t e0 = (q - t.start[s]) * 4;
+    const bool vec = e0 + 4 <= sg.n &&
+                     (((uintptr_t)sg.p | (uintptr_t)sg.m | (uintptr_t)sg.v | (uintptr_t)sg.g) & 15) == 0;
+    if (vec) {   // one 16-byte access per array (same per-element arithmetic)
+      float4 pp = *reinterpret_cast<const float4*>(sg.p + e0);
+      float4 mm = *reinterpret_cast<const float4*>(sg.m + e0);
+      float4 vv = *reinterpret_cast<const float4*>(sg.v + e0);
+      const float4 gg = sg.g ? *reinterpret_cast<const float4*>(sg.g + e0) : make_float4(0.f, 0.f, 0.f, 0.f);
+      adam_one(pp.x, gg.x, mm.x, vv.x, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(pp.y, gg.y, mm.y, vv.y, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(pp.z, gg.z, mm.z, vv.z, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(pp.w, gg.w, mm.w, vv.w, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      *reinterpret_cast<float4*>(sg.p + e0) = pp;
+      *reinterpret_cast<float4*>(sg.m + e0) = mm;
+      *reinterpret_cast<float4*>(sg.v + e0) = vv;
+      continue;
+    }
     for (int u = 0; u < 4; ++u) {
       int64_t e = e0 + u;
       if (e >= sg.n) break;

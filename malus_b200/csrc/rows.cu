@@ -105,6 +105,60 @@ __global__ void k_softmax_warp(RowSrc x, float* __restrict__ y, size_t rows, int
   }
 }
 
+// The same with 16-byte accesses: lane l holds chunks l, l + 32, ... of four
+// consecutive elements (rows of a multiple of 4 elements, 16-byte aligned).
+// The per-element arithmetic and the reduction order are those of
+// k_softmax_warp with PER = 4 * PER4, element i of lane l's k-th chunk in
+// place of element l + 32 * k: the row max is exact, the row sum may group
+// differently (within the softmax tolerance).
+template <int PER4>
+__global__ void k_softmax_warp4(RowSrc x, float* __restrict__ y, size_t rows, int len) {
+  int lane = threadIdx.x & 31;
+  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  const float sc = x.scale ? *x.scale : 1.0f;
+  const int n4 = len >> 2;
+  for (size_t r = warp; r < rows; r += nw) {
+    float4 v[PER4];
+    float m = -INFINITY;
+    const float4* xr = reinterpret_cast<const float4*>(x.x + r * (size_t)len);
+    const float4* ar = x.add ? reinterpret_cast<const float4*>(x.add + (r % x.add_rows) * (size_t)len) : nullptr;
+#pragma unroll
+    for (int k = 0; k < PER4; ++k) {
+      const int c = lane + 32 * k;
+      if (c < n4) {
+        float4 t = xr[c];
+        if (x.scale) { t.x = __fmul_rn(t.x, sc); t.y = __fmul_rn(t.y, sc); t.z = __fmul_rn(t.z, sc); t.w = __fmul_rn(t.w, sc); }
+        if (ar) {
+          const float4 a = ar[c];
+          t.x = __fadd_rn(t.x, a.x); t.y = __fadd_rn(t.y, a.y); t.z = __fadd_rn(t.z, a.z); t.w = __fadd_rn(t.w, a.w);
+        }
+        v[k] = t;
+        m = fmaxf(m, fmaxf(fmaxf(t.x, t.y), fmaxf(t.z, t.w)));
+      } else {
+        v[k] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      }
+    }
+    m = wmax(m);
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER4; ++k) {
+      const int c = lane + 32 * k;
+      if (c < n4) {
+        v[k].x = expf(v[k].x - m); v[k].y = expf(v[k].y - m); v[k].z = expf(v[k].z - m); v[k].w = expf(v[k].w - m);
+        s += v[k].x; s += v[k].y; s += v[k].z; s += v[k].w;
+      }
+    }
+    s = wsum(s);
+    float4* yr = reinterpret_cast<float4*>(y + r * (size_t)len);
+#pragma unroll
+    for (int k = 0; k < PER4; ++k) {
+      const int c = lane + 32 * k;
+      if (c < n4) yr[c] = make_float4(v[k].x / s, v[k].y / s, v[k].z / s, v[k].w / s);
+    }
+  }
+}
+
 // Long rows: one block per row, three passes (max, sum, write).
 __global__ void k_softmax_block(RowSrc x, float* __restrict__ y, size_t rows, size_t len) {
   __shared__ float sh[32];
@@ -227,6 +281,48 @@ __global__ void k_layernorm_warp(const float* __restrict__ x, float* __restrict_
     for (int k = 0; k < PER; ++k) {
       int i = lane + 32 * k;
       if (i < len) yr[i] = (v[k] - mean) / sigma;
+    }
+    if (lane == 0 && var_out) var_out[r] = var;
+  }
+}
+
+// The same with 16-byte accesses (rows of a multiple of 4 elements, 16-byte
+// aligned; lane l holds chunks l, l + 32, ...).
+template <int PER4>
+__global__ void k_layernorm_warp4(const float* __restrict__ x, float* __restrict__ y,
+                                  float* __restrict__ var_out, size_t rows, int len, float eps) {
+  int lane = threadIdx.x & 31;
+  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  const int n4 = len >> 2;
+  for (size_t r = warp; r < rows; r += nw) {
+    const float4* xr = reinterpret_cast<const float4*>(x + r * (size_t)len);
+    float4 v[PER4];
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER4; ++k) {
+      const int c = lane + 32 * k;
+      v[k] = c < n4 ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      s += v[k].x; s += v[k].y; s += v[k].z; s += v[k].w;
+    }
+    float mean = wsum(s) / (float)len;
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER4; ++k) {
+      if (lane + 32 * k < n4) {
+        float d0 = v[k].x - mean, d1 = v[k].y - mean, d2 = v[k].z - mean, d3 = v[k].w - mean;
+        q += d0 * d0; q += d1 * d1; q += d2 * d2; q += d3 * d3;
+      }
+    }
+    float var = wsum(q) / (float)len;
+    float sigma = sqrtf(var + eps);
+    float4* yr = reinterpret_cast<float4*>(y + r * (size_t)len);
+#pragma unroll
+    for (int k = 0; k < PER4; ++k) {
+      const int c = lane + 32 * k;
+      if (c < n4)
+        yr[c] = make_float4((v[k].x - mean) / sigma, (v[k].y - mean) / sigma, (v[k].z - mean) / sigma,
+                            (v[k].w - mean) / sigma);
     }
     if (lane == 0 && var_out) var_out[r] = var;
   }
@@ -360,12 +456,16 @@ __device__ __forceinline__ int64_t load_index(const void* p, int dtype, size_t i
 }
 
 template <int PER>
+// part[blockIdx.x]: this block's sum of nll (each warp adds its rows in row
+// order, the block adds its warps in warp order: a fixed order for a given grid)
 __global__ void k_xent_fwd_warp(const float* __restrict__ logits, const void* __restrict__ tgt,
-                                int tdt, float* __restrict__ probs, float* __restrict__ nll,
+                                int tdt, float* __restrict__ probs, float* __restrict__ part,
                                 size_t rows, int V, int32_t* err) {
+  __shared__ float wpart[32];
   int lane = threadIdx.x & 31;
   size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
   size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  float wacc = 0.0f;
   for (size_t r = warp; r < rows; r += nw) {
     const float* xr = logits + r * (size_t)V;
     float v[PER];
@@ -400,17 +500,25 @@ __global__ void k_xent_fwd_warp(const float* __restrict__ logits, const void* __
     }
     pt = wsum(pt);
     if (lane == 0) {
-      if (bad) { atomicExch(err, 3); nll[r] = 0.0f; }
-      else nll[r] = -logf(pt);
+      if (bad) atomicExch(err, 3);
+      else wacc += -logf(pt);
     }
+  }
+  if (lane == 0) wpart[threadIdx.x >> 5] = wacc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b += wpart[w];
+    part[blockIdx.x] = b;
   }
 }
 
 __global__ void k_xent_fwd_block(const float* __restrict__ logits, const void* __restrict__ tgt,
-                                 int tdt, float* __restrict__ probs, float* __restrict__ nll,
+                                 int tdt, float* __restrict__ probs, float* __restrict__ part,
                                  size_t rows, size_t V, int32_t* err) {
   __shared__ float sh[32];
   __shared__ float pt_sh;
+  float bacc = 0.0f;   // thread 0: this block's rows' nll in row order
   for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* xr = logits + r * V;
     float m = -INFINITY;
@@ -429,20 +537,20 @@ __global__ void k_xent_fwd_block(const float* __restrict__ logits, const void* _
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      if (bad) { atomicExch(err, 3); nll[r] = 0.0f; }
-      else nll[r] = -logf(pt_sh);
+      if (bad) atomicExch(err, 3);
+      else bacc += -logf(pt_sh);
     }
     __syncthreads();
   }
+  if (threadIdx.x == 0) part[blockIdx.x] = bacc;
 }
 
-// loss[0] = (sum_i nll[i]) / n  — one block, fixed order, deterministic
-__global__ void k_mean_1block(const float* __restrict__ v, float* __restrict__ out, size_t n) {
-  __shared__ float sh[32];
+// out[0] = (sum of the n partials, in a fixed order) / rows
+__global__ void k_mean_partials(const float* __restrict__ part, int n, float* __restrict__ out, size_t rows) {
   float s = 0.0f;
-  for (size_t i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
-  s = bsum(s, sh);
-  if (threadIdx.x == 0) out[0] = s / (float)n;
+  for (int i = threadIdx.x; i < n; i += 32) s += part[i];
+  s = wsum(s);
+  if (threadIdx.x == 0) out[0] = s / (float)rows;
 }
 
 // cross_entropy.ml:13-16: out[i] = -log(probs[i*V + t_i])
@@ -682,29 +790,41 @@ __global__ void k_emb_scatter(const unsigned long long* __restrict__ keys, size_
 }
 
 // K4: dw[v, :] = sum over the run of v (token order) of dout[t, :].
-__global__ void k_emb_segsum(const float* __restrict__ dout, const int* __restrict__ order,
-                             const int* __restrict__ offs, int nch, size_t V, size_t D,
-                             float* __restrict__ dw) {
-  size_t v = blockIdx.x;
-  size_t c4 = (blockIdx.y * (size_t)blockDim.x + threadIdx.x) * 4;
-  if (v >= V || c4 >= D) return;
-  int beg = offs[v * nch], end = offs[(v + 1) * nch];
-  bool vec = (D % 4 == 0) && (((uintptr_t)dout & 15) == 0) && (((uintptr_t)dw & 15) == 0);
-  if (vec) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int k = beg; k < end; ++k) {
-      float4 x = *reinterpret_cast<const float4*>(dout + (size_t)order[k] * D + c4);
-      acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+// One thread per column of one vocabulary row, so every output element is a
+// single chain of additions in token order (the order of the reference's
+// per-row gather, embedding_bwd.ml via transformer_bwd.ml:83-98).  The run's
+// token indices are staged in shared memory kSegIdx at a time, and each
+// thread keeps kSegPipe row loads in flight ahead of its additions: the
+// chains are few (vocab x dim), so memory parallelism has to come from depth.
+constexpr int kSegIdx = 512;
+constexpr int kSegPipe = 32;
+constexpr int kSegThreads = 128;
+__global__ void __launch_bounds__(kSegThreads)
+k_emb_segsum(const float* __restrict__ dout, const int* __restrict__ order, const int* __restrict__ offs,
+             int nch, size_t V, size_t D, float* __restrict__ dw) {
+  __shared__ int sidx[kSegIdx];
+  const size_t v = blockIdx.x;
+  const size_t d = blockIdx.y * (size_t)blockDim.x + threadIdx.x;
+  const int beg = offs[v * nch], end = offs[(v + 1) * nch];
+  float acc = 0.0f;
+  for (int k0 = beg; k0 < end; k0 += kSegIdx) {
+    const int cnt = min(kSegIdx, end - k0);
+    __syncthreads();
+    for (int j = threadIdx.x; j < cnt; j += blockDim.x) sidx[j] = order[k0 + j];
+    __syncthreads();
+    if (d >= D) continue;
+    const float* col = dout + d;
+    int j = 0;
+    for (; j + kSegPipe <= cnt; j += kSegPipe) {
+      float x[kSegPipe];
+#pragma unroll
+      for (int u = 0; u < kSegPipe; ++u) x[u] = col[(size_t)sidx[j + u] * D];
+#pragma unroll
+      for (int u = 0; u < kSegPipe; ++u) acc += x[u];
     }
-    *reinterpret_cast<float4*>(dw + v * D + c4) = acc;
-  } else {
-    for (int q = 0; q < 4 && c4 + q < D; ++q) {
-      float acc = 0.0f;
-      for (int k = beg; k < end; ++k) acc += dout[(size_t)order[k] * D + c4 + q];
-      dw[v * D + c4 + q] = acc;
-    }
+    for (; j < cnt; ++j) acc += col[(size_t)sidx[j] * D];
   }
+  if (d < D) dw[v * D + d] = acc;
 }
 
 // ------------------------------------------------------------------ permute
@@ -798,7 +918,16 @@ void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t 
   if (!outer || !axis_sz || !inner) return;
   if ((scale || addend) && inner != 1) panic("softmax_fwd: a deferred input needs the last axis");
   const RowSrc src{x, scale, addend, std::max<size_t>(add_rows, 1)};
-  if (inner == 1 && axis_sz <= 1024) {
+  const bool vec4 = axis_sz % 4 == 0 && ((((uintptr_t)x) | ((uintptr_t)y) | ((uintptr_t)addend)) & 15) == 0;
+  if (inner == 1 && axis_sz <= 1024 && vec4 && axis_sz >= 128) {
+    const unsigned blocks = grid_for(outer * 32, 256);
+    if (axis_sz <= 128) k_softmax_warp4<1><<<blocks, 256, 0, stream()>>>(src, y, outer, (int)axis_sz);
+    else if (axis_sz <= 256) k_softmax_warp4<2><<<blocks, 256, 0, stream()>>>(src, y, outer, (int)axis_sz);
+    else if (axis_sz <= 512) k_softmax_warp4<4><<<blocks, 256, 0, stream()>>>(src, y, outer, (int)axis_sz);
+    else k_softmax_warp4<8><<<blocks, 256, 0, stream()>>>(src, y, outer, (int)axis_sz);
+    count_launch();
+    after_launch("k_softmax_warp4");
+  } else if (inner == 1 && axis_sz <= 1024) {
     LAUNCH_ROWS_WARP(k_softmax_warp, axis_sz, outer, src, y, outer, (int)axis_sz);
   } else if (inner == 1) {
     k_softmax_block<<<row_blocks(outer), 512, 0, stream()>>>(src, y, outer, axis_sz);
@@ -833,7 +962,16 @@ void softmax_bwd(const float* s, const float* g, float* dx, size_t outer, size_t
 void layernorm_fwd(const float* x, float* y, float* var, size_t outer, size_t axis_sz,
                    size_t inner, float eps) {
   if (!outer || !axis_sz || !inner) return;
-  if (inner == 1 && axis_sz <= 1024) {
+  const bool vec4 = axis_sz % 4 == 0 && ((((uintptr_t)x) | ((uintptr_t)y)) & 15) == 0;
+  if (inner == 1 && axis_sz <= 1024 && axis_sz >= 128 && vec4) {
+    const unsigned blocks = grid_for(outer * 32, 256);
+    if (axis_sz <= 128) k_layernorm_warp4<1><<<blocks, 256, 0, stream()>>>(x, y, var, outer, (int)axis_sz, eps);
+    else if (axis_sz <= 256) k_layernorm_warp4<2><<<blocks, 256, 0, stream()>>>(x, y, var, outer, (int)axis_sz, eps);
+    else if (axis_sz <= 512) k_layernorm_warp4<4><<<blocks, 256, 0, stream()>>>(x, y, var, outer, (int)axis_sz, eps);
+    else k_layernorm_warp4<8><<<blocks, 256, 0, stream()>>>(x, y, var, outer, (int)axis_sz, eps);
+    count_launch();
+    after_launch("k_layernorm_warp4");
+  } else if (inner == 1 && axis_sz <= 1024) {
     LAUNCH_ROWS_WARP(k_layernorm_warp, axis_sz, outer, x, y, var, outer, (int)axis_sz, eps);
   } else if (inner == 1) {
     k_layernorm_block<<<row_blocks(outer), 512, 0, stream()>>>(x, y, var, outer, axis_sz, eps);
@@ -873,20 +1011,21 @@ void xent_fwd(const float* logits, const void* tgt, int tdt, float* probs, float
     scalar_op_imm(kSFill, nullptr, NAN, loss, 1);
     return;
   }
-  float* nll = (float*)scratch_alloc(n * sizeof(float));
+  const unsigned blocks = v <= 1024 ? grid_for(n * 32, 256) : row_blocks(n);
+  float* part = (float*)scratch_alloc(blocks * sizeof(float));
   if (v <= 1024) {
-    LAUNCH_ROWS_WARP(k_xent_fwd_warp, v, n, logits, tgt, tdt, probs, nll, n, (int)v,
+    LAUNCH_ROWS_WARP(k_xent_fwd_warp, v, n, logits, tgt, tdt, probs, part, n, (int)v,
                      device_error_word());
   } else {
-    k_xent_fwd_block<<<row_blocks(n), 512, 0, stream()>>>(logits, tgt, tdt, probs, nll, n, v,
-                                                          device_error_word());
+    k_xent_fwd_block<<<blocks, 512, 0, stream()>>>(logits, tgt, tdt, probs, part, n, v,
+                                                   device_error_word());
     count_launch();
     after_launch("k_xent_fwd_block");
   }
-  k_mean_1block<<<1, 1024, 0, stream()>>>(nll, loss, n);
+  k_mean_partials<<<1, 32, 0, stream()>>>(part, (int)blocks, loss, n);
   count_launch();
-  after_launch("k_mean_1block");
-  scratch_free(nll);
+  after_launch("k_mean_partials");
+  scratch_free(part);
 }
 
 void xent_nll_gather(const float* probs, const void* tgt, int tdt, float* out, size_t n, size_t v) {
@@ -962,8 +1101,8 @@ void embedding_bwd(const float* dout, const void* idx, int idt, float* dw, size_
   k_emb_scatter<<<nch, 512, 0, stream()>>>(keys, n, nch, offs, order);
   count_launch();
   after_launch("k_emb_scatter");
-  unsigned threads = (unsigned)std::min<size_t>(256, std::max<size_t>(32, ((D + 3) / 4 + 31) / 32 * 32));
-  dim3 grid((unsigned)V, (unsigned)(((D + 3) / 4 + threads - 1) / threads));
+  dim3 grid((unsigned)V, (unsigned)((D + kSegThreads - 1) / kSegThreads));
+  const unsigned threads = kSegThreads;
   k_emb_segsum<<<grid, threads, 0, stream()>>>(dout, order, offs, nch, V, D, dw);
   count_launch();
   after_launch("k_emb_segsum");
@@ -1073,8 +1212,8 @@ int embedding_bwd_ws(const float* dout, const void* idx, int idt, float* dw, siz
   check();
   k_emb_scatter<<<nch, 512, 0, st>>>(keys, n, nch, offs, order);
   check();
-  unsigned threads = (unsigned)std::min<size_t>(256, std::max<size_t>(32, ((D + 3) / 4 + 31) / 32 * 32));
-  dim3 grid((unsigned)V, (unsigned)(((D + 3) / 4 + threads - 1) / threads));
+  dim3 grid((unsigned)V, (unsigned)((D + kSegThreads - 1) / kSegThreads));
+  const unsigned threads = kSegThreads;
   k_emb_segsum<<<grid, threads, 0, st>>>(dout, order, offs, nch, V, D, dw);
   check();
   count_launch(6);
