@@ -830,38 +830,42 @@ struct SplitGeom {
   bool vec;   // inner runs of 4 are contiguous and 16-byte aligned
 };
 
-__global__ void k_split_view(SplitGeom g, float* __restrict__ hi, float* __restrict__ lo) {
-  const int64_t row = blockIdx.x;
-  const int64_t c = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * 4;
-  if (c >= g.pitch) return;
-  const int64_t zi = row / g.n_outer, o = row - zi * g.n_outer;
-  const float* s = g.base + g.z.at(zi) + g.outer.at(o);
-  float x[4];
-  if (g.vec && c + 4 <= g.n_inner) {
-    const float4 v = *reinterpret_cast<const float4*>(s + g.inner.at(c));
-    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
-  } else {
+__global__ void k_split_view(SplitGeom g, float* __restrict__ hi, float* __restrict__ lo, int64_t rows_total) {
+  // one thread per four consecutive plane elements, over all rows (a row of
+  // a narrow operand is only a few chunks wide)
+  const int64_t cpr = g.pitch >> 2;   // chunks per plane row
+  const int64_t total = rows_total * cpr;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = q / cpr, c = (q - row * cpr) * 4;
+    const int64_t zi = row / g.n_outer, o = row - zi * g.n_outer;
+    const float* s = g.base + g.z.at(zi) + g.outer.at(o);
+    float x[4];
+    if (g.vec && c + 4 <= g.n_inner) {
+      const float4 v = *reinterpret_cast<const float4*>(s + g.inner.at(c));
+      x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+    } else {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) x[q] = c + q < g.n_inner ? s[g.inner.at(c + q)] : 0.0f;
-  }
-  if (g.scale) {
-    const float sc = *g.scale;
+      for (int k = 0; k < 4; ++k) x[k] = c + k < g.n_inner ? s[g.inner.at(c + k)] : 0.0f;
+    }
+    if (g.scale) {
+      const float sc = *g.scale;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) x[q] = __fmul_rn(x[q], sc);
-  }
-  if (g.colscale) {
+      for (int k = 0; k < 4; ++k) x[k] = __fmul_rn(x[k], sc);
+    }
+    if (g.colscale) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      if (c + q < g.n_inner) x[q] = __fmul_rn(x[q], g.colscale[g.cs_inner ? c + q : o]);
-  }
-  float h[4], l[4];
+      for (int k = 0; k < 4; ++k)
+        if (c + k < g.n_inner) x[k] = __fmul_rn(x[k], g.colscale[g.cs_inner ? c + k : o]);
+    }
+    float h[4], l[4];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    h[q] = tf32_rn(x[q]);
-    l[q] = tf32_rn(x[q] - h[q]);
+    for (int k = 0; k < 4; ++k) {
+      h[k] = tf32_rn(x[k]);
+      l[k] = tf32_rn(x[k] - h[k]);
+    }
+    *reinterpret_cast<float4*>(hi + row * g.pitch + c) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lo + row * g.pitch + c) = make_float4(l[0], l[1], l[2], l[3]);
   }
-  *reinterpret_cast<float4*>(hi + row * g.pitch + c) = make_float4(h[0], h[1], h[2], h[3]);
-  *reinterpret_cast<float4*>(lo + row * g.pitch + c) = make_float4(l[0], l[1], l[2], l[3]);
 }
 
 // ---- operand gather into a contiguous [nz][rows][cols] stack (the SIMT path
@@ -1379,8 +1383,8 @@ Planes operand_planes(const GemmOperand& o, bool* trans) {
           (outer.div == 0 || m4(outer.hi)) && m4(o.z.lo) && (o.z.div == 0 || m4(o.z.hi)) &&
           ((uintptr_t)o.base & 15) == 0;
   if (o.nz * n_outer > 0 && pitch > 0) {
-    dim3 grid((unsigned)(o.nz * n_outer), (unsigned)((pitch + 1023) / 1024));
-    k_split_view<<<grid, 256, 0, stream()>>>(g, mem, mem + n);
+    const int64_t rows_total = o.nz * n_outer;
+    k_split_view<<<grid_for((size_t)(rows_total * (pitch / 4)), 256), 256, 0, stream()>>>(g, mem, mem + n, rows_total);
     count_launch();
     after_launch("k_split_view");
   }
