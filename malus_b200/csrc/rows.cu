@@ -373,10 +373,12 @@ __global__ void k_layernorm_strided(const float* __restrict__ x, float* __restri
 
 template <int PER>
 // gs (optional): the incoming gradient is read as g[i] * gs[i] (the deferred
-// gain VJP), rounded like the eager multiply.
-__global__ void k_layernorm_bwd_warp(const float* __restrict__ y, const float* __restrict__ var,
-                                     const float* __restrict__ g, float* __restrict__ dx,
-                                     size_t rows, int len, float eps, const float* __restrict__ gs) {
+// gain VJP), rounded like the eager multiply.  The choice is a template
+// parameter so that each variant issues its row loads as one straight run.
+template <int PER, bool SCALED>
+__device__ __forceinline__ void ln_bwd_warp_rows(const float* __restrict__ y, const float* __restrict__ var,
+                                                 const float* __restrict__ g, float* __restrict__ dx,
+                                                 size_t rows, int len, float eps, const float* __restrict__ gs) {
   int lane = threadIdx.x & 31;
   size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
   size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
@@ -384,12 +386,22 @@ __global__ void k_layernorm_bwd_warp(const float* __restrict__ y, const float* _
     const float* yr = y + r * (size_t)len;
     const float* gr = g + r * (size_t)len;
     float yv[PER], gv[PER];
-    float sg = 0.0f, sgy = 0.0f;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int i = lane + 32 * k;
       yv[k] = i < len ? yr[i] : 0.0f;
-      gv[k] = i < len ? (gs ? __fmul_rn(gr[i], gs[i]) : gr[i]) : 0.0f;
+      gv[k] = i < len ? gr[i] : 0.0f;
+    }
+    if (SCALED) {
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        int i = lane + 32 * k;
+        if (i < len) gv[k] = __fmul_rn(gv[k], gs[i]);
+      }
+    }
+    float sg = 0.0f, sgy = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
       sg += gv[k];
       sgy += gv[k] * yv[k];
     }
@@ -403,6 +415,14 @@ __global__ void k_layernorm_bwd_warp(const float* __restrict__ y, const float* _
       if (i < len) dr[i] = ((gv[k] - mg) - yv[k] * mgy) * inv;
     }
   }
+}
+
+template <int PER>
+__global__ void k_layernorm_bwd_warp(const float* __restrict__ y, const float* __restrict__ var,
+                                     const float* __restrict__ g, float* __restrict__ dx,
+                                     size_t rows, int len, float eps, const float* __restrict__ gs) {
+  if (gs) ln_bwd_warp_rows<PER, true>(y, var, g, dx, rows, len, eps, gs);
+  else ln_bwd_warp_rows<PER, false>(y, var, g, dx, rows, len, eps, nullptr);
 }
 
 __global__ void k_layernorm_bwd_block(const float* __restrict__ y, const float* __restrict__ var,

@@ -465,14 +465,31 @@ void backward(int64_t loss) {
   for (auto& kv : grads) tensor_release(kv.second);
   // The thunks hold their leaves, so every pending leaf is alive here.  The
   // tape's references go first; a leaf then held by its thunk alone needs no
-  // gradient (dropping the thunk releases it and its registry entry).
+  // gradient (dropping the thunk releases it and its registry entry).  A
+  // thunk's arguments can hold another pending leaf (the mask's thunk holds
+  // the deferred scores, which hold the scale leaf), so thunks are dropped
+  // until none is left whose leaf nothing else holds, and only then are the
+  // remaining ones evaluated.
   tape_clear();
   std::vector<std::pair<int64_t, Thunk>> due(T.pending.begin(), T.pending.end());
   T.pending.clear();
+  for (bool dropped = true; dropped;) {
+    dropped = false;
+    for (size_t i = 0; i < due.size();) {
+      if (tb(due[i].first)->rc.load() == 1) {
+        Thunk k = due[i].second;
+        due.erase(due.begin() + (ptrdiff_t)i);
+        drop_thunk(k);   // releases the leaf (and with it its registry entry)
+        dropped = true;
+      } else {
+        ++i;
+      }
+    }
+  }
   for (auto& kv : due) {
     const int64_t leaf = kv.first;
     const Thunk& k = kv.second;
-    if (tb(leaf)->rc.load() > 1) {   // held by someone besides the thunk: evaluate now
+    {   // held by someone besides the thunks: evaluate now
       int64_t ng = run_thunk(k);
       auto li = T.leaf_grad.find(leaf);
       if (li == T.leaf_grad.end()) {
