@@ -371,7 +371,6 @@ __global__ void k_layernorm_strided(const float* __restrict__ x, float* __restri
   if (var_out) var_out[g] = var;
 }
 
-template <int PER>
 // gs (optional): the incoming gradient is read as g[i] * gs[i] (the deferred
 // gain VJP), rounded like the eager multiply.  The choice is a template
 // parameter so that each variant issues its row loads as one straight run.
