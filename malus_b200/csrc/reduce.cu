@@ -161,25 +161,24 @@ __global__ void k_reduce_cols(const float* __restrict__ x, float* __restrict__ p
 }
 
 // out[j] = combine over chunks of part[c][j]; then /n for mean/var.
+// One warp per output: lane l combines chunks l, l + 32, ... in order, then a
+// fixed shuffle tree combines the lanes (the same order on every run).
 __global__ void k_reduce_combine(const float* __restrict__ part, float* __restrict__ out,
                                  size_t m, int nchunks, int mode, float inv_n) {
-  size_t j = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t j = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (j >= m) return;
-  // in chunk order; eight partials are loaded ahead of their additions
-  float acc = part[j];
-  int c = 1;
-  for (; c + 8 <= nchunks; c += 8) {
-    float v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = part[(size_t)(c + u) * m + j];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) acc = mode == 1 ? fmaxf(acc, v[u]) : acc + v[u];
-  }
-  for (; c < nchunks; ++c) {
-    float v = part[(size_t)c * m + j];
+  float acc = mode == 1 ? -INFINITY : 0.0f;
+  for (int c = lane; c < nchunks; c += 32) {
+    const float v = part[(size_t)c * m + j];
     acc = mode == 1 ? fmaxf(acc, v) : acc + v;
   }
-  out[j] = inv_n != 0.0f ? acc * inv_n : acc;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, acc, o);
+    acc = mode == 1 ? fmaxf(acc, w) : acc + w;
+  }
+  if (lane == 0) out[j] = inv_n != 0.0f ? acc * inv_n : acc;
 }
 
 // out[j] = part_sum[j] / n, computed with a true division to match s / n_f
@@ -208,8 +207,8 @@ void column_pass(const float* x, float* out, const float* center, int mode, size
   count_launch();
   after_launch("k_reduce_cols");
   if (nchunks > 1) {
-    k_reduce_combine<<<(unsigned)((m + 255) / 256), 256, 0, stream()>>>(part, out, m, (int)nchunks,
-                                                                       mode, 0.0f);
+    k_reduce_combine<<<(unsigned)((m * 32 + 255) / 256), 256, 0, stream()>>>(part, out, m, (int)nchunks,
+                                                                            mode, 0.0f);
     count_launch();
     after_launch("k_reduce_combine");
     scratch_free(part);
