@@ -487,6 +487,7 @@ __global__ void k_xent_fwd_warp(const float* __restrict__ logits, const void* __
   float wacc = 0.0f;
   for (size_t r = warp; r < rows; r += nw) {
     const float* xr = logits + r * (size_t)V;
+    const int64_t t = load_index(tgt, tdt, r);   // issued with the row's loads, used after the reductions
     float v[PER];
     float m = -INFINITY;
 #pragma unroll
@@ -504,7 +505,6 @@ __global__ void k_xent_fwd_warp(const float* __restrict__ logits, const void* __
       s += v[k];
     }
     s = wsum(s);
-    int64_t t = load_index(tgt, tdt, r);
     bool bad = t < 0 || t >= V;
     float pt = 0.0f;
     float* pr = probs + r * (size_t)V;
