@@ -353,6 +353,7 @@ class Runner:
             lib.malus_prof_report(0, C.byref(cnt), C.byref(ms_k), C.byref(fl_k), C.byref(by_k))
             if self.world > 1:
                 out["dp"] = self._dp_report(lib, steps, dt_prof_ms)
+            out["kernels"] = self._kernel_table(lib, steps, dt_prof_ms)
             lib.malus_prof_enable(0)
             out["roofline"] = self._gemm_roofline(cnt.value, ms_k.value, fl_k.value, by_k.value, dt_prof_ms,
                                                   steps, workload, mode)
@@ -373,6 +374,27 @@ class Runner:
         del xd, yd
         torch.cuda.empty_cache()
         return out
+
+    def _kernel_table(self, lib, steps, dt_prof_ms):
+        """The compiled step's non-GEMM kernels from the profiled pass: per label,
+        launches and ms per step, share of the step, and achieved GB/s =
+        algorithmic bytes (one read of each input, one write of each output) /
+        CUDA-event time, as a fraction of the measured HBM copy peak."""
+        need = lib.malus_prof_kernels(None, 0)
+        if need <= 0:
+            return []
+        buf = C.create_string_buffer(need + 1)
+        lib.malus_prof_kernels(buf, need + 1)
+        hbm = peaks()[0]
+        rows = []
+        for ln in buf.value.decode().splitlines():
+            name, n, ms, by = ln.split("\t")
+            n, ms, by = int(n), float(ms), float(by)
+            gbs = by / (ms / 1e3) / 1e9 if ms else 0.0
+            rows.append({"kernel": name, "launches_per_step": n / steps, "ms_per_step": round(ms / steps, 4),
+                         "share_of_step": round(ms / dt_prof_ms, 4), "gbs": round(gbs, 1),
+                         "frac_hbm": round(gbs / hbm, 3)})
+        return sorted(rows, key=lambda r: -r["ms_per_step"])
 
     def _dp_report(self, lib, steps, dt_prof_ms):
         """The gradient all-reduces of the profiled pass (this rank): their time on
@@ -498,6 +520,7 @@ def main():
                 "roofline": head.get("roofline"), "cpu_baseline": cpu, "e2e": head["e2e"],
                 "gpu_launches": head["gpu_launches"], "clocks": clk.summary(), "loss_last": head["loss_last"],
                 **({"dp": head["dp"]} if "dp" in head else {}),
+                **({"kernels": head["kernels"]} if head.get("kernels") else {}),
                 "algorithmic_tflops_per_step": round(step_flops(cfg) / 1e12, 4), **extras}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -447,6 +447,11 @@ int32_t malus_device_error(void);
  * the model step runs without its CUDA graph. */
 void malus_prof_enable(int32_t on);
 void malus_prof_report(int32_t cls, int64_t* count, double* ms, double* flops, double* bytes);
+/* Class 5, the compiled step's other kernels, each timed with its algorithmic
+ * bytes: one text line "label<TAB>launches<TAB>ms<TAB>bytes" per kernel label
+ * (first-launch order) into buf (NUL-terminated, truncated at cap); returns
+ * the length of the whole text. */
+int32_t malus_prof_kernels(char* buf, int32_t cap);
 
 /* Embedding backward that allocates nothing.  This entry point has no
  * counterpart in the reference.  It is for callers that cannot call cudaMalloc

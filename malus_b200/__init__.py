@@ -214,6 +214,7 @@ SIGNATURES: dict[str, tuple] = {
     "malus_embedding_bwd_noalloc": (i32, [vp, vp, i32, sz, sz, sz, vp, vp]),
     "malus_prof_report": (None, [i32, P_i64, C.POINTER(C.c_double), C.POINTER(C.c_double),
                                  C.POINTER(C.c_double)]),
+    "malus_prof_kernels": (i32, [C.c_char_p, i32]),
 }
 
 _lib: C.CDLL | None = None

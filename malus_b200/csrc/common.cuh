@@ -126,6 +126,7 @@ bool prof_on();
 int prof_begin(int cls, double flops, double bytes);
 void prof_end(int id);
 int prof_begin_on(int cls, double flops, double bytes, cudaStream_t s);   // on another stream
+int prof_begin_named(const char* name, double bytes);   // class 5: a labelled kernel (static label)
 void prof_end_on(int id, cudaStream_t s);
 
 // Shape helpers

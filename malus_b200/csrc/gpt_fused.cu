@@ -564,6 +564,23 @@ void gemm(int M, int N, int K, int batch, const TcOperand& a, const TcOperand& b
 
 unsigned rows_grid(int rows) { return grid_for((size_t)rows * 32, 256); }
 
+// CUDA-event timing of one labelled launch (or launch group) with its
+// algorithmic bytes (one read of each input, one write of each output), while
+// the bench's profiled pass has kernel timing on; free otherwise.
+struct KTimer {
+  int id;
+  KTimer(const char* label, double bytes) : id(prof_begin_named(label, bytes)) {}
+  ~KTimer() { prof_end(id); }
+};
+
+// bytes of the causal tiles' rows of a [T][T] head: row i spans the 128-wide
+// tiles up to its own (what the attention kernels read and write)
+double causal_tile_elems(int T) {
+  double e = 0.0;
+  for (int i = 0; i < T; ++i) e += std::min(T, (i / 128 + 1) * 128);
+  return e;
+}
+
 // float4 groups per lane for a row of LEN floats (LEN % 4 == 0, LEN <= 1024)
 #define P4_DISPATCH(LEN, CALL)                                        \
   do {                                                                \
@@ -588,6 +605,8 @@ unsigned rows_grid(int rows) { return grid_for((size_t)rows * 32, 256); }
   } while (0)
 
 void ln_fwd(FusedStep* f, const float* x, const float* g, Planes out, float* mean, float* var) {
+  const double MC = (double)f->M * f->C;
+  KTimer kt("k_ln_fwd_split", 4.0 * (3.0 * MC + f->C + 2.0 * f->M));
   P4_DISPATCH(f->C, (k_ln_fwd_split<P_><<<rows_grid(f->M), 256, 0, stream()>>>(
                           x, g, out.hi, out.lo, mean, var, f->M, f->C)));
   count_launch();
@@ -598,9 +617,17 @@ void ln_bwd(FusedStep* f, const float* x, const float* mean, const float* var, c
             const float* dz, const float* resid, float* gout, Planes gpl, float* dgain) {
   int threads = 256;
   size_t smem = (size_t)(threads / 32) * f->C * sizeof(float);
-  P4_DISPATCH(f->C, (k_ln_bwd_fused<P_><<<f->part_blocks, threads, smem, stream()>>>(
-                          x, mean, var, g, dz, resid, gout, gpl.hi, gpl.lo, f->part, f->M, f->C)));
-  k_colsum<<<(f->C + 31) / 32, 32 * kColGroups, 0, stream()>>>(f->part, dgain, f->part_blocks, f->C);
+  const double MC = (double)f->M * f->C, part = (double)f->part_blocks * f->C;
+  {
+    KTimer kt("k_ln_bwd_fused", 4.0 * (MC + 2.0 * f->M + f->C + MC + (resid ? MC : 0.0) + (gout ? MC : 0.0) +
+                                       (gpl.hi ? 2.0 * MC : 0.0) + part));
+    P4_DISPATCH(f->C, (k_ln_bwd_fused<P_><<<f->part_blocks, threads, smem, stream()>>>(
+                            x, mean, var, g, dz, resid, gout, gpl.hi, gpl.lo, f->part, f->M, f->C)));
+  }
+  {
+    KTimer kt("k_colsum", 4.0 * (part + f->C));
+    k_colsum<<<(f->C + 31) / 32, 32 * kColGroups, 0, stream()>>>(f->part, dgain, f->part_blocks, f->C);
+  }
   count_launch(2);
   after_launch("k_ln_bwd_fused");
 }
@@ -757,10 +784,15 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
   const TcLayout rowC = L(0, 0, 0, 0, C), rowC4 = L(0, 0, 0, 0, C4), unit = L(0, 0, 0, 0, 1);
 
   // ------------------------------------------------------------ forward
-  k_embed2<<<grid_for((size_t)M * 32, 256), 256, 0, stream()>>>(P(top), P(top + 1), xt, f->x[0], M, T,
-                                                               C, V, device_error_word());
-  count_launch();
-  after_launch("k_embed2");
+  {
+    KTimer kt("k_embed2", 4.0 * ((double)MC + (double)(V + T) * C + M));
+    k_embed2<<<grid_for((size_t)M * 32, 256), 256, 0, stream()>>>(P(top), P(top + 1), xt, f->x[0], M, T,
+                                                                 C, V, device_error_word());
+    count_launch();
+    after_launch("k_embed2");
+  }
+  const double attn_elems = (double)BH * causal_tile_elems(T);   // causal-tile P / dS elements per layer
+  const double qkv_elems = 3.0 * MC;
   for (int l = 0; l < Lc; ++l) {
     size_t b = (size_t)l * 8;
     ln_fwd(f, f->x[l], P(b), f->xn1[l], f->mean1[l], f->var1[l]);
@@ -772,10 +804,12 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     if (f->fused_attn_bwd) {
       // S, causal softmax and O = P V in one kernel; the row statistics let the
       // backward recompute P
+      KTimer kt("k_attn_fwd", 4.0 * (2.0 * qkv_elems + 2.0 * MC + 2.0 * BH * T));
       attn_fwd(f->qkv[l].hi, f->qkv[l].lo, B, H, T, hs, f->scale, nullptr, nullptr, f->O[l].hi, f->O[l].lo,
                f->astats[l]);
     } else if (f->fused_attn) {
       // the same kernel, keeping the P planes for the GEMM backward
+      KTimer kt("k_attn_fwd", 4.0 * (2.0 * qkv_elems + 2.0 * MC + 2.0 * attn_elems));
       attn_fwd(f->qkv[l].hi, f->qkv[l].lo, B, H, T, hs, f->scale, f->P[l].hi, f->P[l].lo, f->O[l].hi,
                f->O[l].lo, nullptr);
     } else {
@@ -811,16 +845,19 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
   else
     gemm(M, V, C, 1, op(f->xf, M, C, C, false), op(f->lmpl, C, V, Vp, true), kEpiStore, none,
          L(0, 0, 0, 0, V), unit, f->logits, Planes{}, nullptr);
-  if (Vp <= 1024) {
-    PER_DISPATCH(Vp, (k_xent_fused<P_><<<rows_grid(M), 256, 0, stream()>>>(
-                         f->logits, yt, f->nll, f->dlog.hi, f->dlog.lo, M, V, Vp, device_error_word())));
-  } else {
-    k_xent_fused_wide<<<std::min(M, kNumSMs * 4), 512, 0, stream()>>>(f->logits, yt, f->nll, f->dlog.hi,
-                                                                      f->dlog.lo, M, V, Vp, device_error_word());
+  {
+    KTimer kt("k_xent_fused + k_mean_nll", 4.0 * ((double)M * V + M + 2.0 * M * Vp + M + 1));
+    if (Vp <= 1024) {
+      PER_DISPATCH(Vp, (k_xent_fused<P_><<<rows_grid(M), 256, 0, stream()>>>(
+                           f->logits, yt, f->nll, f->dlog.hi, f->dlog.lo, M, V, Vp, device_error_word())));
+    } else {
+      k_xent_fused_wide<<<std::min(M, kNumSMs * 4), 512, 0, stream()>>>(f->logits, yt, f->nll, f->dlog.hi,
+                                                                        f->dlog.lo, M, V, Vp, device_error_word());
+    }
+    k_mean_nll<<<1, 1024, 0, stream()>>>(f->nll, loss_dev, M);
+    count_launch(2);
+    after_launch("k_xent_fused");
   }
-  k_mean_nll<<<1, 1024, 0, stream()>>>(f->nll, loss_dev, M);
-  count_launch(2);
-  after_launch("k_xent_fused");
 
   // ------------------------------------------------------------ backward
   // LM head
@@ -860,6 +897,7 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
          G(b + 4), Planes{}, nullptr);
     if (f->fused_attn_bwd) {
       // dq | dk | dv planes (head-unfolded into dqkv) with P recomputed
+      KTimer kt("k_attn_bwd (dq, dkdv)", 4.0 * (2.0 * qkv_elems + 2.0 * MC + 2.0 * MC + 2.0 * BH * T + 2.0 * qkv_elems));
       attn_bwd(f->qkv[l].hi, f->qkv[l].lo, f->dO.hi, f->dO.lo, f->O[l].hi, f->O[l].lo, f->astats[l], f->arow,
                B, H, T, hs, f->scale, f->dqkv.hi, f->dqkv.lo);
     } else {
@@ -871,8 +909,11 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
     gemm(T, hs, T, BH, op(f->P[l], T, T, T, true, BH, (int64_t)TT, kZBatch),
          op(f->dO, T, hs, hs, true, BH, (int64_t)T * hs, kZBatch), kEpiStore,
          L(H, (int64_t)T * C, 0, 0, hs), rowC, unit, nullptr, dqkv2, nullptr, 1.0f, kCausalAUpper);
-    P4_DISPATCH(T, (k_softmax_bwd_split<P_><<<rows_grid(BH * T), 256, 0, stream()>>>(
-                        f->P[l].hi, f->P[l].lo, f->dP, f->dS.hi, f->dS.lo, BH * T, T, f->scale)));
+    {
+      KTimer kt("k_softmax_bwd_split", 12.0 * BH * ((double)T * (T + 1) / 2) + 8.0 * attn_elems);
+      P4_DISPATCH(T, (k_softmax_bwd_split<P_><<<rows_grid(BH * T), 256, 0, stream()>>>(
+                          f->P[l].hi, f->P[l].lo, f->dP, f->dS.hi, f->dS.lo, BH * T, T, f->scale)));
+    }
     count_launch();
     after_launch("k_softmax_bwd_split");
     // dQ = dS K ; dK = dS^T Q  (unfolded into dqkv [3][M][C])
@@ -903,16 +944,23 @@ void fused_step(FusedStep* f, const int32_t* xt, const int32_t* yt, float* loss_
   float* dwte = f->cfg.tied ? f->emb_tmp : G(top);
   // a token id outside [0, V) is reported through the runtime's error word,
   // as in __embedding_bwd
-  int er = embedding_bwd_ws(g3, xt, MALUS_I32, dwte, M, V, C, f->emb_ws, stream(), device_error_word());
+  int er;
+  {
+    KTimer kt("embedding VJP (sort, scan, segmented sum)", 4.0 * ((double)MC + M + (double)V * C));
+    er = embedding_bwd_ws(g3, xt, MALUS_I32, dwte, M, V, C, f->emb_ws, stream(), device_error_word());
+  }
   if (er != 0) panic("fused step: embedding backward failed (%d)", er);
   if (f->cfg.tied) {
     k_add_inplace<<<grid_for((size_t)V * C, 256), 256, 0, stream()>>>(G(top), f->emb_tmp, (size_t)V * C);
     count_launch();
     after_launch("k_add_inplace");
   }
-  k_dwpe<<<grid_for((size_t)T * C, 256), 256, 0, stream()>>>(g3, G(top + 1), B, (size_t)T * C);
-  count_launch();
-  after_launch("k_dwpe");
+  {
+    KTimer kt("k_dwpe", 4.0 * ((double)MC + (double)T * C));
+    k_dwpe<<<grid_for((size_t)T * C, 256), 256, 0, stream()>>>(g3, G(top + 1), B, (size_t)T * C);
+    count_launch();
+    after_launch("k_dwpe");
+  }
   if (dp_world() > 1) {
     const auto& bk = f->buckets.back();
     if (dp_allreduce_async(f->gbuf + bk.first, bk.second - bk.first) != 0)
@@ -938,8 +986,11 @@ void fused_body(FusedStep* f, const int32_t* x, const int32_t* y, float* loss) {
   // AdamW over the whole fused buffer, writing the tf32 planes of every updated
   // parameter (the weight planes share the parameter layout); only the padded
   // untied LM head is re-split separately
-  adamw_flat(f->pbuf, f->gbuf, f->mbuf, f->vbuf, (int64_t)f->total, f->cfg.lr, f->cfg.beta1,
-             f->cfg.beta2, f->cfg.eps, f->cfg.wd, gscale, f->bc_tab, f->step_dev, f->wpl.hi, f->wpl.lo);
+  {
+    KTimer kt("k_adamw_flat", 4.0 * 9.0 * (double)f->total);   // p, g, m, v in; p, m, v, hi, lo out
+    adamw_flat(f->pbuf, f->gbuf, f->mbuf, f->vbuf, (int64_t)f->total, f->cfg.lr, f->cfg.beta1,
+               f->cfg.beta2, f->cfg.eps, f->cfg.wd, gscale, f->bc_tab, f->step_dev, f->wpl.hi, f->wpl.lo);
+  }
   if (!f->cfg.tied) {
     size_t top = (size_t)f->L * 8;
     tf32_split(f->params[top + 3], f->C, f->V, f->V, 1, 0, f->lmpl.hi, f->lmpl.lo, f->Vp);

@@ -19,6 +19,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <tuple>
 #include <unordered_map>
 #include <unordered_set>
 #include <vector>
@@ -1093,7 +1094,7 @@ void bench_reset(void) {
 // join (the communication the backward pass does not hide).
 namespace malus {
 namespace {
-struct ProfRec { cudaEvent_t a, b; int cls; double flops, bytes; };
+struct ProfRec { cudaEvent_t a, b; int cls; double flops, bytes; const char* name; };
 bool g_prof_on = false;
 std::vector<ProfRec> g_prof;
 std::vector<cudaEvent_t> g_ev_free;
@@ -1107,7 +1108,7 @@ cudaEvent_t ev_get() {
 bool prof_on() { return g_prof_on; }
 int prof_begin_on(int cls, double flops, double bytes, cudaStream_t s) {
   if (!g_prof_on) return -1;
-  ProfRec r{ev_get(), ev_get(), cls, flops, bytes};
+  ProfRec r{ev_get(), ev_get(), cls, flops, bytes, nullptr};
   MALUS_CUDA(cudaEventRecord(r.a, s));
   g_prof.push_back(r);
   return (int)g_prof.size() - 1;
@@ -1117,6 +1118,11 @@ void prof_end_on(int id, cudaStream_t s) {
   MALUS_CUDA(cudaEventRecord(g_prof[id].b, s));
 }
 int prof_begin(int cls, double flops, double bytes) { return prof_begin_on(cls, flops, bytes, stream()); }
+int prof_begin_named(const char* name, double bytes) {
+  const int id = prof_begin_on(5, 0.0, bytes, stream());
+  if (id >= 0) g_prof[(size_t)id].name = name;
+  return id;
+}
 void prof_end(int id) { prof_end_on(id, stream()); }
 }  // namespace malus
 
@@ -1128,6 +1134,44 @@ void malus_prof_enable(int32_t on) {
   g_prof.clear();
   g_prof_on = on != 0;
 }
+// Per kernel label of class 5 (non-GEMM kernels of the compiled step, each with
+// its algorithmic bytes): one line "label<TAB>launches<TAB>ms<TAB>bytes" per
+// label, in first-launch order, written into buf (NUL-terminated, truncated
+// at cap); returns the length the whole text needs.
+int32_t malus_prof_kernels(char* buf, int32_t cap) {
+  using namespace malus;
+  gpu_barrier();
+  std::vector<std::string> order;
+  std::unordered_map<std::string, std::tuple<int64_t, double, double>> agg;
+  for (auto& r : g_prof) {
+    if (r.cls != 5 || !r.name) continue;
+    float x = 0;
+    MALUS_CUDA(cudaEventElapsedTime(&x, r.a, r.b));
+    auto it = agg.find(r.name);
+    if (it == agg.end()) {
+      order.push_back(r.name);
+      it = agg.emplace(r.name, std::make_tuple((int64_t)0, 0.0, 0.0)).first;
+    }
+    std::get<0>(it->second) += 1;
+    std::get<1>(it->second) += x;
+    std::get<2>(it->second) += r.bytes;
+  }
+  std::string text;
+  char line[256];
+  for (auto& n : order) {
+    auto& a = agg[n];
+    snprintf(line, sizeof line, "%s\t%lld\t%.6f\t%.0f\n", n.c_str(), (long long)std::get<0>(a), std::get<1>(a),
+             std::get<2>(a));
+    text += line;
+  }
+  if (buf && cap > 0) {
+    const size_t k = std::min(text.size(), (size_t)cap - 1);
+    memcpy(buf, text.data(), k);
+    buf[k] = 0;
+  }
+  return (int32_t)text.size();
+}
+
 // Sum over recorded launches of class `cls`: count, total ms, flops, bytes.
 void malus_prof_report(int32_t cls, int64_t* count, double* ms, double* flops, double* bytes) {
   using namespace malus;
