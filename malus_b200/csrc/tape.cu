@@ -451,6 +451,9 @@ void backward(int64_t loss) {
     if (gi == grads.end()) continue;
     int64_t ng = gi->second;
     grads.erase(gi);
+    // a leaf's gradient is kept as plain data: a deferred product would hold
+    // its operands (possibly other leaves) alive as long as the gradient
+    if (tb(ng)->lazy) materialize(ng);
     auto li = T.leaf_grad.find(leaf);
     if (li == T.leaf_grad.end()) {
       T.leaf_grad.emplace(leaf, ng);
