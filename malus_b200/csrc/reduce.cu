@@ -133,6 +133,29 @@ __global__ void k_reduce_cols(const float* __restrict__ x, float* __restrict__ p
   float ctr = mode == 2 ? center[o * inner + i] : 0.0f;
   float acc0 = mode == 1 ? -INFINITY : 0.0f, acc1 = acc0, acc2 = acc0, acc3 = acc0;
   size_t a = a0;
+  // eight rows' loads in flight per step; accumulator k still adds rows
+  // a = k (mod 4) in increasing order (the same sums as four rows per step)
+  for (; a + 8 <= a1; a += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = base[(a + u) * inner];
+    if (base2) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __fmul_rn(v[u], base2[(a + u) * inner]);
+    }
+#pragma unroll
+    for (int h = 0; h < 8; h += 4) {
+      float v0 = v[h], v1 = v[h + 1], v2 = v[h + 2], v3 = v[h + 3];
+      if (mode == 1) {
+        acc0 = fmaxf(acc0, v0); acc1 = fmaxf(acc1, v1); acc2 = fmaxf(acc2, v2); acc3 = fmaxf(acc3, v3);
+      } else if (mode == 2) {
+        v0 -= ctr; v1 -= ctr; v2 -= ctr; v3 -= ctr;
+        acc0 += v0 * v0; acc1 += v1 * v1; acc2 += v2 * v2; acc3 += v3 * v3;
+      } else {
+        acc0 += v0; acc1 += v1; acc2 += v2; acc3 += v3;
+      }
+    }
+  }
   for (; a + 4 <= a1; a += 4) {
     float v0 = base[a * inner], v1 = base[(a + 1) * inner];
     float v2 = base[(a + 2) * inner], v3 = base[(a + 3) * inner];

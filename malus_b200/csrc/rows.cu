@@ -812,11 +812,11 @@ __global__ void k_emb_scatter(const unsigned long long* __restrict__ keys, size_
 // One thread per column of one vocabulary row, so every output element is a
 // single chain of additions in token order (the order of the reference's
 // per-row gather, embedding_bwd.ml via transformer_bwd.ml:83-98).  The run's
-// token indices are staged in shared memory kSegIdx at a time, and each
-// thread keeps kSegPipe row loads in flight ahead of its additions: the
-// chains are few (vocab x dim), so memory parallelism has to come from depth.
-constexpr int kSegIdx = 512;
-constexpr int kSegPipe = 32;
+// token indices are staged in shared memory kSegIdx at a time; each thread
+// loads the next kSegPipe rows while it adds the current ones (two register
+// buffers), so the chains, which are few (vocab x dim), keep memory busy.
+constexpr int kSegIdx = 1024;
+constexpr int kSegPipe = 16;
 constexpr int kSegThreads = 128;
 __global__ void __launch_bounds__(kSegThreads)
 k_emb_segsum(const float* __restrict__ dout, const int* __restrict__ order, const int* __restrict__ offs,
@@ -825,6 +825,7 @@ k_emb_segsum(const float* __restrict__ dout, const int* __restrict__ order, cons
   const size_t v = blockIdx.x;
   const size_t d = blockIdx.y * (size_t)blockDim.x + threadIdx.x;
   const int beg = offs[v * nch], end = offs[(v + 1) * nch];
+  const float* col = dout + (d < D ? d : 0);
   float acc = 0.0f;
   for (int k0 = beg; k0 < end; k0 += kSegIdx) {
     const int cnt = min(kSegIdx, end - k0);
@@ -832,16 +833,26 @@ k_emb_segsum(const float* __restrict__ dout, const int* __restrict__ order, cons
     for (int j = threadIdx.x; j < cnt; j += blockDim.x) sidx[j] = order[k0 + j];
     __syncthreads();
     if (d >= D) continue;
-    const float* col = dout + d;
-    int j = 0;
-    for (; j + kSegPipe <= cnt; j += kSegPipe) {
-      float x[kSegPipe];
+    const int full = cnt / kSegPipe;   // whole batches
+    float xa[kSegPipe], xb[kSegPipe];
+    if (full > 0) {
 #pragma unroll
-      for (int u = 0; u < kSegPipe; ++u) x[u] = col[(size_t)sidx[j + u] * D];
-#pragma unroll
-      for (int u = 0; u < kSegPipe; ++u) acc += x[u];
+      for (int u = 0; u < kSegPipe; ++u) xa[u] = col[(size_t)sidx[u] * D];
     }
-    for (; j < cnt; ++j) acc += col[(size_t)sidx[j] * D];
+    for (int b = 0; b < full; ++b) {
+      const bool more = b + 1 < full;
+      if (more) {
+#pragma unroll
+        for (int u = 0; u < kSegPipe; ++u) xb[u] = col[(size_t)sidx[(b + 1) * kSegPipe + u] * D];
+      }
+#pragma unroll
+      for (int u = 0; u < kSegPipe; ++u) acc += xa[u];
+      if (more) {
+#pragma unroll
+        for (int u = 0; u < kSegPipe; ++u) xa[u] = xb[u];
+      }
+    }
+    for (int j = full * kSegPipe; j < cnt; ++j) acc += col[(size_t)sidx[j] * D];
   }
   if (d < D) dw[v * D + d] = acc;
 }
