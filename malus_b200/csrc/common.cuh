@@ -78,6 +78,15 @@ struct TensorBuffer {
   std::atomic<int64_t> rc;
   View* view = nullptr;
   Lazy* lazy = nullptr;    // st == nullptr while set
+  // Facts about the values the runtime knows from how it made them:
+  //  causal_mask: the [T, T] additive mask of tensor_causal_mask (0 on and below
+  //    the diagonal, -1e9 above);
+  //  causal_zero: every [T, T] slice of the last two dims is exactly 0 above
+  //    the diagonal (a softmax over scores plus that mask, and its VJP).
+  // Both are dropped by writes the runtime cannot see into (host writes, raw
+  // pointers handed out).
+  bool causal_mask = false;
+  bool causal_zero = false;
 };
 
 inline TensorBuffer* tb(int64_t h) {
@@ -244,6 +253,9 @@ struct GemmArgs {
   GemmOperand B; bool b_trans;
   float* C; int64_t ldc; int64_t strideC;
   float alpha = 1.f, beta = 0.f;
+  // A[m][k] is exactly 0 for k > m (kCausalALower) or k < m (kCausalAUpper):
+  // the GEMM clips its K ranges there (the skipped products are exact zeros)
+  int a_zero = 0;
 };
 // Operand planes split from tensors during a step are kept per storage and
 // view and reused by later GEMMs that read the same data (a weight in the

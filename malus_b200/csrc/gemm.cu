@@ -1417,6 +1417,7 @@ void gemm_tc(const GemmArgs& g) {
   pr.out = g.C;
   pr.alpha = g.alpha;
   pr.beta = g.beta;
+  pr.causal = (g.a_zero == kCausalALower || g.a_zero == kCausalAUpper) && g.M == g.K ? g.a_zero : kCausalNone;
   gemm_tc_planes(pr);
   if (pa.tmp) scratch_free(pa.tmp);
   if (pb.tmp) scratch_free(pb.tmp);

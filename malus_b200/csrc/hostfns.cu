@@ -122,7 +122,9 @@ bool one_element_f32(int64_t h) { return tb(h)->len == 1 && tb(h)->dtype == MALU
 int64_t lazy_scale(int64_t a, int64_t b) {
   auto *ta = tb(a), *tb_ = tb(b);
   if (ta->dtype != MALUS_F32 || ta->len < kLazyMin || !one_element_f32(b) || tb_->ndim > ta->ndim) return 0;
-  return make_lazy(ta->shape, ta->ndim, a, b, 0);
+  int64_t z = make_lazy(ta->shape, ta->ndim, a, b, 0);
+  tb(z)->causal_zero = ta->causal_zero;   // 0 * s stays 0 (the multiplier is taken to be finite)
+  return z;
 }
 
 // a * w for a vector w along a's last dim (b of shape [C], a [..., C]),
@@ -299,6 +301,7 @@ int64_t tensor_matmul(int64_t ha, int64_t hb) {
     MALUS_CUDA(cudaMemsetAsync(g.C, 0, o.numel() * 4, stream()));
     return out;
   }
+  if (a.ndim == 3 && tb(ha)->causal_zero && g.M == g.K) g.a_zero = kCausalALower;
   g.A = operand_of(ha, (size_t)g.batch, (size_t)g.M, (size_t)g.K);
   g.B = operand_of(hb, b.ndim == 3 ? (size_t)g.batch : 1, (size_t)g.K, (size_t)g.N);
   gemm(g);
@@ -336,6 +339,11 @@ int64_t __softmax_fwd(int64_t x, int64_t axis) {
     // are never written)
     softmax_fwd(fptr(z->src), fptr(out), outer, asz, inner, z->scale ? fptr(z->scale) : nullptr,
                 z->addend ? fptr(z->addend) : nullptr, z->addend ? tb(z->addend)->len / asz : 1);
+    // over scores plus the causal mask (-1e9 above the diagonal) the
+    // probabilities there underflow to exactly 0 (for scores below ~5e8)
+    const TensorBuffer* m = z->addend ? tb(z->addend) : nullptr;
+    tb(out)->causal_zero = m && m->causal_mask && m->ndim == 2 && m->shape[0] == asz && m->shape[1] == asz &&
+                           s.ndim >= 2 && s.d[s.ndim - 2] == asz;
     return out;
   }
   softmax_fwd(fptr(x), fptr(out), outer, asz, inner);
@@ -564,6 +572,7 @@ int64_t __softmax_bwd(int64_t s, int64_t dout, int64_t axis) {
   split_axis(sh, ax, &outer, &asz, &inner);
   int64_t dx = alloc_shape(sh);
   softmax_bwd(fptr(s), fptr(dout), fptr(dx), outer, asz, inner);
+  tb(dx)->causal_zero = tb(s)->causal_zero && inner == 1;   // s (dout - sum) is 0 where s is
   return dx;
 }
 
@@ -625,6 +634,7 @@ int64_t __matmul_bwd_a(int64_t a, int64_t b, int64_t dout) {
     if (g.K == 0) {
       MALUS_CUDA(cudaMemsetAsync(fptr(da), 0, sa.numel() * 4, stream()));
     } else {
+      if (sb.ndim == 3 && tb(dout)->causal_zero && g.M == g.K) g.a_zero = kCausalALower;
       g.A = operand_of(dout, (size_t)g.batch, (size_t)g.M, (size_t)g.K);
       g.B = operand_of(b, (size_t)g.batch, (size_t)g.N, (size_t)g.K);   // stored [N][K]
       gemm(g);
@@ -655,6 +665,8 @@ int64_t __matmul_bwd_b(int64_t a, int64_t b, int64_t dout) {
     if (g.K == 0) {
       MALUS_CUDA(cudaMemsetAsync(fptr(db), 0, sb.numel() * 4, stream()));
     } else {
+      // A = a^T: zero below the diagonal when a is zero above it
+      if (sa.ndim == 3 && sb.ndim == 3 && tb(a)->causal_zero && g.M == g.K) g.a_zero = kCausalAUpper;
       g.A = operand_of(a, (size_t)g.batch, (size_t)g.K, (size_t)g.M);      // stored [K][M]
       g.B = operand_of(dout, (size_t)g.batch, (size_t)g.K, (size_t)g.N);
       gemm(g);

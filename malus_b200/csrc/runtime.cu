@@ -419,11 +419,18 @@ int64_t make_lazy(const size_t* shape, int ndim, int64_t src, int64_t scale, int
 
 int64_t alias_of(int64_t h) {
   auto* t = tb(h);
+  int64_t out;
   if (t->lazy)
-    return make_lazy(t->shape, t->ndim, t->lazy->src, t->lazy->scale, t->lazy->addend, t->lazy->colscale);
-  if (t->view) return make_view(h, t->shape, t->ndim, *t->view);
-  t->st->aliases++;
-  return make_handle(t->dtype, t->shape, t->ndim, t->st, t->len);
+    out = make_lazy(t->shape, t->ndim, t->lazy->src, t->lazy->scale, t->lazy->addend, t->lazy->colscale);
+  else if (t->view)
+    out = make_view(h, t->shape, t->ndim, *t->view);
+  else {
+    t->st->aliases++;
+    out = make_handle(t->dtype, t->shape, t->ndim, t->st, t->len);
+  }
+  tb(out)->causal_zero = t->causal_zero;
+  tb(out)->causal_mask = t->causal_mask;
+  return out;
 }
 
 static void release_lazy(Lazy* z) {
@@ -674,8 +681,12 @@ int64_t tensor_reshape(int64_t h, const size_t* dims, size_t ndims) {
     panic("reshape element count mismatch: input has %zu elements, target would have %zu",
           t->len, n);
   if (ndims > (size_t)kMaxRank) panic("reshape rank %zu exceeds %d", ndims, kMaxRank);
+  const bool keep_tail = t->ndim >= 2 && ndims >= 2 && dims[ndims - 1] == t->shape[t->ndim - 1] &&
+                         dims[ndims - 2] == t->shape[t->ndim - 2];
   if (t->lazy) {   // same element order: a deferred result of the new shape
-    return make_lazy(dims, (int)ndims, t->lazy->src, t->lazy->scale, t->lazy->addend, t->lazy->colscale);
+    int64_t out = make_lazy(dims, (int)ndims, t->lazy->src, t->lazy->scale, t->lazy->addend, t->lazy->colscale);
+    tb(out)->causal_zero = t->causal_zero && keep_tail;
+    return out;
   }
   if (t->view) {   // a strided view: a view again where the memory allows, else copied once
     View v;
@@ -683,7 +694,9 @@ int64_t tensor_reshape(int64_t h, const size_t* dims, size_t ndims) {
     materialize(h);
   }
   t->st->aliases++;
-  return make_handle(t->dtype, dims, (int)ndims, t->st, t->len);
+  int64_t out = make_handle(t->dtype, dims, (int)ndims, t->st, t->len);
+  tb(out)->causal_zero = t->causal_zero && keep_tail;
+  return out;
 }
 
 // metal.rs:1601-1612 fills the [T,T] additive mask on the host (0 on and
@@ -704,6 +717,7 @@ int64_t tensor_causal_mask(int64_t tsz) {
     count_launch();
     after_launch("k_causal_mask");
   }
+  tb(h)->causal_mask = true;
   return h;
 }
 
@@ -889,7 +903,11 @@ void malus_set_mem_budget(int64_t bytes) {
   g_pool.budget = bytes < 0 ? -1 : bytes;
 }
 
-void* malus_tensor_data(int64_t h) { return vptr(h); }
+void* malus_tensor_data(int64_t h) {
+  auto* t = tb(h);
+  t->causal_zero = t->causal_mask = false;   // the caller may write through the pointer
+  return vptr(h);
+}
 int32_t malus_tensor_dtype(int64_t h) { return tb(h)->dtype; }
 void malus_tensor_read(int64_t h, void* dst, size_t bytes) {
   auto* t = tb(h);
@@ -903,6 +921,7 @@ void malus_tensor_write(int64_t h, const void* src, size_t bytes) {
   size_t have = t->len * dtype_size(t->dtype);
   if (bytes > have) panic("tensor_write of %zu bytes into a %zu-byte tensor", bytes, have);
   plane_cache_clear();   // the data changes in place
+  t->causal_zero = t->causal_mask = false;
   if (bytes) MALUS_CUDA(cudaMemcpyAsync(vptr(h), src, bytes, cudaMemcpyHostToDevice, stream()));
   gpu_barrier();
 }

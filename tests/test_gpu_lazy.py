@@ -210,3 +210,38 @@ def test_gain_vector_products_equal_eager(M, rt, orc, rng):
     assert np.allclose(dw, (dout.astype(np.float64) * ly).sum(axis=0), rtol=0, atol=1e-5 * np.abs(dout * ly).sum(axis=0).max())
     for h in (xn, xn2, dy):
         rt.tensor_release(h)
+
+
+def test_causal_zero_gemms_equal_full(M, rt, rng):
+    """softmax(qk * s + causal mask) is exactly 0 above the diagonal, and so is
+    its VJP; GEMMs that read them as their A operand (P V, P^T dO, dS K) skip
+    those K blocks.  The results equal the same GEMMs on untagged copies of the
+    same values (the skipped products are exact zeros)."""
+    Z, T_, hs = 24, 256, 64
+    qk = (rng.standard_normal((Z, T_, T_)) * 3).astype(np.float32)
+    v = rng.standard_normal((Z, T_, hs)).astype(np.float32)
+    g = rng.standard_normal((Z, T_, hs)).astype(np.float32)
+    tq, tv, tg = T(M, qk), T(M, v), T(M, g)
+    ts = T(M, np.array([[0.125]], np.float32))
+    mask = rt.tensor_causal_mask(T_)
+    sc = rt.__broadcast_mul_fwd(tq.h, ts.h)
+    ms = rt.__broadcast_add_fwd(sc, mask)
+    p = rt.__softmax_fwd(ms, 2)
+    pn = np_of(M, p)
+    assert np.all(pn[:, np.triu_indices(T_, 1)[0], np.triu_indices(T_, 1)[1]] == 0.0)
+    tp_plain = T(M, pn)                                   # the same values, no tag
+    np.testing.assert_array_equal(M.Tensor(rt.tensor_matmul(p, tv.h)).numpy(),
+                                  M.Tensor(rt.tensor_matmul(tp_plain.h, tv.h)).numpy())
+    np.testing.assert_array_equal(M.Tensor(rt.__matmul_bwd_b(p, tv.h, tg.h)).numpy(),
+                                  M.Tensor(rt.__matmul_bwd_b(tp_plain.h, tv.h, tg.h)).numpy())
+    dp = T(M, rng.standard_normal((Z, T_, T_)).astype(np.float32))
+    ds = rt.__softmax_bwd(p, dp.h, 2)
+    dsn = np_of(M, ds)
+    dsc = rt.__mul_bwd_a(ds, tq.h, ts.h)                  # deferred ds * s, still zero above the diagonal
+    plain = T(M, dsn * np.float32(0.125))
+    kk = T(M, rng.standard_normal((Z, T_, hs)).astype(np.float32))
+    kt = rt.tensor_permute(kk.h, (C.c_size_t * 3)(0, 2, 1), 3)
+    np.testing.assert_array_equal(M.Tensor(rt.__matmul_bwd_a(tq.h, kt, dsc)).numpy(),
+                                  M.Tensor(rt.__matmul_bwd_a(tq.h, kt, plain.h)).numpy())
+    for h in (mask, sc, ms, p, ds, dsc, kt):
+        rt.tensor_release(h)
