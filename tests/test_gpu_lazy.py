@@ -239,9 +239,10 @@ def test_causal_zero_gemms_equal_full(M, rt, rng):
     dsn = np_of(M, ds)
     dsc = rt.__mul_bwd_a(ds, tq.h, ts.h)                  # deferred ds * s, still zero above the diagonal
     plain = T(M, dsn * np.float32(0.125))
+    qq = T(M, rng.standard_normal((Z, T_, hs)).astype(np.float32))   # scores = Q @ K^T
     kk = T(M, rng.standard_normal((Z, T_, hs)).astype(np.float32))
     kt = rt.tensor_permute(kk.h, (C.c_size_t * 3)(0, 2, 1), 3)
-    np.testing.assert_array_equal(M.Tensor(rt.__matmul_bwd_a(tq.h, kt, dsc)).numpy(),
-                                  M.Tensor(rt.__matmul_bwd_a(tq.h, kt, plain.h)).numpy())
+    np.testing.assert_array_equal(M.Tensor(rt.__matmul_bwd_a(qq.h, kt, dsc)).numpy(),
+                                  M.Tensor(rt.__matmul_bwd_a(qq.h, kt, plain.h)).numpy())
     for h in (mask, sc, ms, p, ds, dsc, kt):
         rt.tensor_release(h)
