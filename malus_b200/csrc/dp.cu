@@ -62,7 +62,6 @@ int dp_allreduce_async(float* ptr, size_t count) {
   MALUS_CUDA(cudaStreamWaitEvent(g_dp_stream, g_ev_ready, 0));
   const int pid = prof_begin_on(3, 0.0, 4.0 * (double)count, g_dp_stream);
   ncclResult_t r = ncclAllReduce(ptr, ptr, count, ncclFloat, ncclSum, g_comm, g_dp_stream);
-  prof_end_on(pid, g_dp_stream);
   if (r != ncclSuccess && r != ncclInProgress) {
     fprintf(stderr, "malus: ncclAllReduce failed: %s\n", ncclGetErrorString(r));
     return -5;
@@ -71,6 +70,9 @@ int dp_allreduce_async(float* ptr, size_t count) {
     abort_comm();
     return -4;
   }
+  // a non-blocking communicator enqueues the collective's kernel only when the
+  // operation has left ncclInProgress: the closing event goes after that
+  prof_end_on(pid, g_dp_stream);
   return 0;
 }
 
@@ -131,7 +133,6 @@ int dp_leaf_ready(int64_t leaf, int64_t grad) {
     if (r == ncclSuccess || r == ncclInProgress)
       r = ncclAllReduce(pc.first, pc.first, pc.second, ncclFloat, ncclAvg, g_comm, g_dp_stream);
   ncclResult_t e = ncclGroupEnd();
-  prof_end_on(pid, g_dp_stream);
   items.clear();
   if ((r != ncclSuccess && r != ncclInProgress) || (e != ncclSuccess && e != ncclInProgress)) {
     fprintf(stderr, "malus: bucket all-reduce failed: %s\n", ncclGetErrorString(r != ncclSuccess ? r : e));
@@ -141,6 +142,7 @@ int dp_leaf_ready(int64_t leaf, int64_t grad) {
     abort_comm();
     return -4;
   }
+  prof_end_on(pid, g_dp_stream);
   return 0;
 }
 
