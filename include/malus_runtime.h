@@ -309,6 +309,12 @@ int32_t malus_jit_compile_check(const char* msl, char* log, size_t cap);
 int32_t malus_attn_fwd(const float* qkv_hi, const float* qkv_lo, int32_t B, int32_t H, int32_t T,
                        int32_t hs, float scale, float* p_hi, float* p_lo, float* o_hi, float* o_lo,
                        float* stats);
+/* Which kernel serves malus_attn_fwd for T <= 384: 1 (default) keeps the
+ * tile's scores resident in tensor memory and computes them once; 0 recomputes
+ * them in the second softmax pass (the kernel used for longer sequences).  Both
+ * give the same bits.  Returns the previous setting.  Environment:
+ * MALUS_ATTN_RS=0 starts with 0.  New in this build. */
+int32_t malus_attn_set_resident(int32_t on);
 /* Fused causal attention backward (tcgen05, 3xTF32), the VJP of
  * malus_attn_fwd: from the q|k|v planes, the planes of dO (head-folded
  * [B][H][T][hs]) and of O (head-unfolded, as the forward wrote them) and the

@@ -184,6 +184,7 @@ SIGNATURES: dict[str, tuple] = {
     "malus_jit_translate": (i32, [C.c_char_p, C.c_char_p, sz]),
     "malus_jit_compile_check": (i32, [C.c_char_p, C.c_char_p, sz]),
     "malus_attn_fwd": (i32, [vp, vp, i32, i32, i32, i32, f32, vp, vp, vp, vp, vp]),
+    "malus_attn_set_resident": (i32, [i32]),
     "malus_attn_bwd": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, vp, vp]),
     "malus_graph_begin": (i32, []),
     "malus_graph_end": (i64, []),

@@ -60,6 +60,37 @@ def test_attn_fwd_matches_reference(M, rt, rng, B, H, T, hs):
     assert np.max(np.abs(got_o - ref_o) / scale_o) < 1e-5
 
 
+@pytest.mark.parametrize("B,H,T,hs,with_p", [(2, 3, 256, 64, 1), (2, 3, 256, 64, 0), (1, 2, 128, 32, 1),
+                                             (2, 2, 384, 64, 1), (3, 1, 256, 32, 0), (1, 1, 384, 32, 1)])
+def test_resident_scores_kernel_equals_recomputing_kernel(M, rt, rng, B, H, T, hs, with_p):
+    """For T <= 384 the scores of a query tile stay in tensor memory and are
+    computed once; the kernel that recomputes them per pass must give the same
+    bits (same products in the same order, same softmax expressions)."""
+    qkv = (rng.standard_normal((3, B, H, T, hs)) * 0.7).astype(np.float32)
+    src = dev(M, qkv)
+    hi, lo = dev(M, np.zeros_like(qkv)), dev(M, np.zeros_like(qkv))
+    rt.malus_tf32_split(ptr(rt, src), 3 * B * H * T, hs, hs, 1, 0, ptr(rt, hi), ptr(rt, lo), hs)
+    scale = np.float32(1.0 / np.sqrt(hs))
+    outs = []
+    prev = rt.malus_attn_set_resident(1)
+    try:
+        for resident in (1, 0):
+            rt.malus_attn_set_resident(resident)
+            p_hi, p_lo = dev(M, np.zeros((B * H, T, T))), dev(M, np.zeros((B * H, T, T)))
+            o_hi, o_lo = dev(M, np.zeros((B * T, H * hs))), dev(M, np.zeros((B * T, H * hs)))
+            stats = dev(M, np.zeros((B * H * T, 2)))
+            pp = (ptr(rt, p_hi), ptr(rt, p_lo)) if with_p else (None, None)
+            assert rt.malus_attn_fwd(ptr(rt, hi), ptr(rt, lo), B, H, T, hs, scale, *pp, ptr(rt, o_hi),
+                                     ptr(rt, o_lo), ptr(rt, stats)) == 0
+            assert rt.malus_device_error() == 0
+            outs.append([t.numpy() for t in (p_hi, p_lo, o_hi, o_lo, stats)])
+    finally:
+        rt.malus_attn_set_resident(prev)
+    for a, b in zip(*outs):
+        np.testing.assert_array_equal(a, b)
+    assert np.all(np.isfinite(outs[0][2]))
+
+
 def test_attn_fwd_rejects_unsupported_shapes(M, rt):
     z = dev(M, np.zeros(16, np.float32))
     zp = ptr(rt, z)
