@@ -830,6 +830,81 @@ struct SplitGeom {
   bool vec;   // inner runs of 4 are contiguous and 16-byte aligned
 };
 
+// Division of 32-bit indices by a divisor fixed at launch, by multiply and
+// shift (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", 1994, the round-up variant): with s = ceil(log2 d) and
+// m = floor(2^32 (2^s - d) / d) + 1, n / d = (umulhi(n, m) + n) >> s for all
+// n, d < 2^31.  A 64-bit division costs dozens of instructions; the split of a
+// viewed operand does three or four per four elements.
+struct FastDiv {
+  uint32_t d = 1, m = 1, s = 0;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t dv) : d(dv) {
+    while (s < 32 && (1ull << s) < dv) ++s;
+    m = (uint32_t)(((1ull << 32) * ((1ull << s) - dv)) / dv + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> s; }
+};
+struct ViewDim32 {
+  FastDiv fd;
+  bool has_div = false;
+  int64_t hi = 0, lo = 0;
+  ViewDim32() = default;
+  explicit ViewDim32(const ViewDim& v) : fd(v.div ? (uint32_t)v.div : 1u), has_div(v.div != 0), hi(v.hi), lo(v.lo) {}
+  __device__ __forceinline__ int64_t at(uint32_t i) const {
+    if (!has_div) return (int64_t)i * lo;
+    const uint32_t q = fd.div(i);
+    return (int64_t)q * hi + (int64_t)(i - q * fd.d) * lo;
+  }
+};
+struct SplitGeom32 {
+  const float* base;
+  const float* scale;
+  const float* colscale;
+  bool cs_inner;
+  uint32_t n_inner, pitch;
+  FastDiv cpr, n_outer;
+  ViewDim32 z, outer, inner;
+  bool vec;
+};
+
+// k_split_view with every index below 2^31: the same elements, values and
+// plane layout, indexed by FastDiv.
+__global__ void k_split_view32(SplitGeom32 g, float* __restrict__ hi, float* __restrict__ lo, uint32_t total) {
+  for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < total; q += gridDim.x * blockDim.x) {
+    const uint32_t row = g.cpr.div(q), c = (q - row * g.cpr.d) * 4;
+    const uint32_t zi = g.n_outer.div(row), o = row - zi * g.n_outer.d;
+    const float* s = g.base + g.z.at(zi) + g.outer.at(o);
+    float x[4];
+    if (g.vec && c + 4 <= g.n_inner) {
+      const float4 v = *reinterpret_cast<const float4*>(s + g.inner.at(c));
+      x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) x[k] = c + k < g.n_inner ? s[g.inner.at(c + k)] : 0.0f;
+    }
+    if (g.scale) {
+      const float sc = *g.scale;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) x[k] = __fmul_rn(x[k], sc);
+    }
+    if (g.colscale) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (c + k < g.n_inner) x[k] = __fmul_rn(x[k], g.colscale[g.cs_inner ? c + k : o]);
+    }
+    float h[4], l[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      h[k] = tf32_rn(x[k]);
+      l[k] = tf32_rn(x[k] - h[k]);
+    }
+    const size_t at = (size_t)row * g.pitch + c;
+    *reinterpret_cast<float4*>(hi + at) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lo + at) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
 __global__ void k_split_view(SplitGeom g, float* __restrict__ hi, float* __restrict__ lo, int64_t rows_total) {
   // one thread per four consecutive plane elements, over all rows (a row of
   // a narrow operand is only a few chunks wide)
@@ -1384,9 +1459,31 @@ Planes operand_planes(const GemmOperand& o, bool* trans) {
           ((uintptr_t)o.base & 15) == 0;
   if (o.nz * n_outer > 0 && pitch > 0) {
     const int64_t rows_total = o.nz * n_outer;
-    k_split_view<<<grid_for((size_t)(rows_total * (pitch / 4)), 256), 256, 0, stream()>>>(g, mem, mem + n, rows_total);
-    count_launch();
-    after_launch("k_split_view");
+    const int64_t total = rows_total * (pitch / 4);
+    constexpr int64_t k31 = (int64_t)1 << 31;
+    auto fits = [&](const ViewDim& v) { return v.div >= 0 && v.div < k31; };
+    if (rows_total * pitch < k31 && n_outer < k31 && fits(o.z) && fits(outer) && fits(inner)) {
+      SplitGeom32 h;
+      h.base = g.base;
+      h.scale = g.scale;
+      h.colscale = g.colscale;
+      h.cs_inner = g.cs_inner;
+      h.n_inner = (uint32_t)n_inner;
+      h.pitch = (uint32_t)pitch;
+      h.cpr = FastDiv((uint32_t)(pitch / 4));
+      h.n_outer = FastDiv((uint32_t)n_outer);
+      h.z = ViewDim32(o.z);
+      h.outer = ViewDim32(outer);
+      h.inner = ViewDim32(inner);
+      h.vec = g.vec;
+      k_split_view32<<<grid_for((size_t)total, 256), 256, 0, stream()>>>(h, mem, mem + n, (uint32_t)total);
+      count_launch();
+      after_launch("k_split_view32");
+    } else {
+      k_split_view<<<grid_for((size_t)total, 256), 256, 0, stream()>>>(g, mem, mem + n, rows_total);
+      count_launch();
+      after_launch("k_split_view");
+    }
   }
   if (cache) {
     g_pc[o.key].push_back(PlaneEntry{o.nz, o.rows, o.cols, o.z, o.r, o.c, o.scale_dev, o.colscale_dev, mem, pitch,

@@ -19,6 +19,8 @@
 // shuffles, and every pass is a coalesced stream over HBM.
 #include "common.cuh"
 
+#include <unordered_map>
+
 namespace malus {
 namespace {
 
@@ -105,28 +107,32 @@ __global__ void k_softmax_warp(RowSrc x, float* __restrict__ y, size_t rows, int
   }
 }
 
-// The same with 16-byte accesses: lane l holds chunks l, l + 32, ... of four
-// consecutive elements (rows of a multiple of 4 elements, 16-byte aligned).
-// The per-element arithmetic and the reduction order are those of
-// k_softmax_warp with PER = 4 * PER4, element i of lane l's k-th chunk in
-// place of element l + 32 * k: the row max is exact, the row sum may group
-// differently (within the softmax tolerance).
-template <int PER4>
-__global__ void k_softmax_warp4(RowSrc x, float* __restrict__ y, size_t rows, int len) {
-  int lane = threadIdx.x & 31;
-  size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
-  size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+// Rows of 128..1024 elements (a multiple of 4, 16-byte aligned sources):
+// LPR lanes per row, so a warp works on 32 / LPR rows at once and each lane
+// has eight 16-byte loads in flight.  Lane j of a row holds chunks j, j + LPR,
+// ... of four elements; max and sum combine the lane's values in chunk order,
+// then across the row's lanes by a fixed xor tree; p = e * (1 / sum).  A
+// deferred x * s + m reads through RowSrc with the eager roundings, and plain
+// and deferred rows take this same kernel, so they give the same bits.
+template <int LPR>
+__global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restrict__ y, uint32_t rows, int len) {
+  constexpr int PER4 = 8, RPW = 32 / LPR;
+  const int lane = threadIdx.x & 31, sub = lane % LPR;
+  const uint32_t gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
   const float sc = x.scale ? *x.scale : 1.0f;
   const int n4 = len >> 2;
-  for (size_t r = warp; r < rows; r += nw) {
+  for (uint32_t base = gwarp * RPW; base < rows; base += nwarps * RPW) {
+    const uint32_t r = base + (uint32_t)(lane / LPR);
+    const bool live = r < rows;
+    const float4* xr = reinterpret_cast<const float4*>(x.x + (size_t)r * len);
+    const float4* ar = x.add ? reinterpret_cast<const float4*>(x.add + (size_t)(r % (uint32_t)x.add_rows) * len) : nullptr;
     float4 v[PER4];
     float m = -INFINITY;
-    const float4* xr = reinterpret_cast<const float4*>(x.x + r * (size_t)len);
-    const float4* ar = x.add ? reinterpret_cast<const float4*>(x.add + (r % x.add_rows) * (size_t)len) : nullptr;
 #pragma unroll
     for (int k = 0; k < PER4; ++k) {
-      const int c = lane + 32 * k;
-      if (c < n4) {
+      const int c = sub + LPR * k;
+      if (live && c < n4) {
         float4 t = xr[c];
         if (x.scale) { t.x = __fmul_rn(t.x, sc); t.y = __fmul_rn(t.y, sc); t.z = __fmul_rn(t.z, sc); t.w = __fmul_rn(t.w, sc); }
         if (ar) {
@@ -139,24 +145,40 @@ __global__ void k_softmax_warp4(RowSrc x, float* __restrict__ y, size_t rows, in
         v[k] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
       }
     }
-    m = wmax(m);
-    float s = 0.0f;
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.0f;
 #pragma unroll
     for (int k = 0; k < PER4; ++k) {
-      const int c = lane + 32 * k;
-      if (c < n4) {
+      const int c = sub + LPR * k;
+      if (live && c < n4) {
         v[k].x = expf(v[k].x - m); v[k].y = expf(v[k].y - m); v[k].z = expf(v[k].z - m); v[k].w = expf(v[k].w - m);
-        s += v[k].x; s += v[k].y; s += v[k].z; s += v[k].w;
+        sum += v[k].x; sum += v[k].y; sum += v[k].z; sum += v[k].w;
       }
     }
-    s = wsum(s);
-    float4* yr = reinterpret_cast<float4*>(y + r * (size_t)len);
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = 1.0f / sum;
+    float4* yr = reinterpret_cast<float4*>(y + (size_t)r * len);
 #pragma unroll
     for (int k = 0; k < PER4; ++k) {
-      const int c = lane + 32 * k;
-      if (c < n4) yr[c] = make_float4(v[k].x / s, v[k].y / s, v[k].z / s, v[k].w / s);
+      const int c = sub + LPR * k;
+      if (live && c < n4) yr[c] = make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv);
     }
   }
+}
+
+// Blocks of 256 threads that stay resident together: the SM count times what
+// the occupancy calculator allows for `kern` (once per kernel), at most `need`.
+template <typename K>
+unsigned resident_blocks(K kern, size_t need) {
+  static std::unordered_map<const void*, int> per_sm;
+  int& n = per_sm[(const void*)kern];
+  if (!n) {
+    MALUS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 256, 0));
+    if (n < 1) n = 1;
+  }
+  return (unsigned)std::max<size_t>(1, std::min<size_t>(need, (size_t)kNumSMs * n));
 }
 
 // Long rows: one block per row, three passes (max, sum, write).
@@ -948,17 +970,22 @@ void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t 
   if (!outer || !axis_sz || !inner) return;
   if ((scale || addend) && inner != 1) panic("softmax_fwd: a deferred input needs the last axis");
   const RowSrc src{x, scale, addend, std::max<size_t>(add_rows, 1)};
-  // 16-byte rows for plain inputs (measured faster there); a deferred scaled
-  // and masked input keeps the scalar kernel, which measured faster on it
-  const bool vec4 = !scale && !addend && axis_sz % 4 == 0 && ((((uintptr_t)x) | ((uintptr_t)y)) & 15) == 0;
-  if (inner == 1 && axis_sz <= 1024 && vec4 && axis_sz >= 128) {
-    const unsigned blocks = grid_for(outer * 32, 256);
-    if (axis_sz <= 128) k_softmax_warp4<1><<<blocks, 256, 0, stream()>>>(src, y, outer, (int)axis_sz);
-    else if (axis_sz <= 256) k_softmax_warp4<2><<<blocks, 256, 0, stream()>>>(src, y, outer, (int)axis_sz);
-    else if (axis_sz <= 512) k_softmax_warp4<4><<<blocks, 256, 0, stream()>>>(src, y, outer, (int)axis_sz);
-    else k_softmax_warp4<8><<<blocks, 256, 0, stream()>>>(src, y, outer, (int)axis_sz);
+  // 16-byte rows whenever the row and every source are 16-byte aligned: a
+  // deferred x * s + m must take the same kernel as its materialised value
+  // (the row sum's grouping follows the kernel), so both give the same bits
+  const bool vec4 = axis_sz % 4 == 0 && ((((uintptr_t)x) | ((uintptr_t)y) | ((uintptr_t)addend)) & 15) == 0;
+  if (inner == 1 && axis_sz <= 1024 && vec4 && axis_sz >= 128 && outer < ((size_t)1 << 31)) {
+    const uint32_t rows = (uint32_t)outer;
+    const int len = (int)axis_sz;
+    auto go = [&](auto kern, int rpw) {
+      kern<<<resident_blocks(kern, (outer + 8 * rpw - 1) / (8 * rpw)), 256, 0, stream()>>>(src, y, rows, len);
+    };
+    if (axis_sz <= 128) go(k_softmax_rows<4>, 8);
+    else if (axis_sz <= 256) go(k_softmax_rows<8>, 4);
+    else if (axis_sz <= 512) go(k_softmax_rows<16>, 2);
+    else go(k_softmax_rows<32>, 1);
     count_launch();
-    after_launch("k_softmax_warp4");
+    after_launch("k_softmax_rows");
   } else if (inner == 1 && axis_sz <= 1024) {
     LAUNCH_ROWS_WARP(k_softmax_warp, axis_sz, outer, src, y, outer, (int)axis_sz);
   } else if (inner == 1) {

@@ -94,6 +94,18 @@ def cases(b: Bench, rng):
     sm = M.Tensor(lib.__softmax_fwd(a.h, 1))
     b.keep.append(sm)
     yield "softmax bwd 65536x768", lambda: lib.__softmax_bwd(sm.h, g.h, 1), 3 * r * c * F, 0
+    # the attention scores of the reference's call sequence at C4: (QK^T * scale) + causal
+    # mask, deferred, read by the softmax ([384, 256, 256]; the mask stays in L2)
+    z, t = 384, 256
+    qk = b.T(rng.standard_normal((z, t, t), dtype=np.float32))
+    sc1 = b.T(np.array([[0.125]], np.float32))
+    mask = b.T(np.where(np.arange(t)[None, :] > np.arange(t)[:, None], -1e9, 0).astype(np.float32))
+    scaled = lib.__broadcast_mul_fwd(qk.h, sc1.h)
+    masked = M.Tensor(lib.__broadcast_add_fwd(scaled, mask.h))
+    lib.tensor_release(scaled)
+    b.keep.append(masked)
+    yield "softmax (x*s+mask deferred) 98304x256", lambda: lib.__softmax_fwd(masked.h, 2), 2 * z * t * t * F, 0
+    yield "softmax 98304x256", lambda: lib.__softmax_fwd(qk.h, 2), 2 * z * t * t * F, 0
 
     def ln():
         box = lib.__layernorm_fwd(a.h, 1)
@@ -224,6 +236,26 @@ def plane_cases(b: Bench, rng):
     causal = 0.5 * (1 + 128 / T)   # score entries up to each query's 128-wide tile
     yield ("attn fwd fused (causal, C4)", attn,
            8 * 3 * Mt * Cc + 8 * Mt * Cc + 8 * Bz * H * T,
+           2.0 * 2 * Bz * H * T * T * hs * 0.5)
+    # the fused step's form at T = 256: P planes written for the GEMM backward
+    # (score entries up to each query's 128-wide tile)
+    ph, pl = buf(Bz * H, T, T, rand=False), buf(Bz * H, T, T, rand=False)
+    pbytes = 8 * Bz * H * T * T * causal
+
+    def attn_p():
+        lib.malus_attn_fwd(qh, ql, Bz, H, T, hs, C.c_float(0.125), ph, pl, oh, ol, st)
+        return 0
+
+    def attn_p_recompute():
+        prev = lib.malus_attn_set_resident(0)
+        attn_p()
+        lib.malus_attn_set_resident(prev)
+        return 0
+    yield ("attn fwd fused + P planes (C4 step)", attn_p,
+           8 * 3 * Mt * Cc + 8 * Mt * Cc + 8 * Bz * H * T + pbytes,
+           2.0 * 2 * Bz * H * T * T * hs * 0.5)
+    yield ("attn fwd + P planes, scores recomputed", attn_p_recompute,
+           8 * 3 * Mt * Cc + 8 * Mt * Cc + 8 * Bz * H * T + pbytes,
            2.0 * 2 * Bz * H * T * T * hs * 0.5)
     # backward: dq | dk | dv planes from q|k|v, dO and O planes and the statistics
     dh, dl = buf(Bz * H, T, hs), buf(Bz * H, T, hs)
