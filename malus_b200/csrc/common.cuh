@@ -194,11 +194,19 @@ void reduce_axis_sum_product(const float* x, const float* x2, float* out, size_t
 
 // ---- row kernels (rows.cu) ----
 // x (optionally): each element times scale[0], plus addend[(row % add_rows) * axis + i]
-// (same roundings as the eager multiply and add; rows along the last axis only)
+// (same roundings as the eager multiply and add; rows along the last axis only).
+// causal_T > 0: the addend is the causal mask of [causal_T, causal_T] scores
+// (-1e9 above the diagonal), so in row r the elements past r % causal_T give
+// exactly 0 and need not be read (the same bits as reading them, for scores
+// below ~1e8 in magnitude).
 void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner,
-                 const float* scale = nullptr, const float* addend = nullptr, size_t add_rows = 1);
+                 const float* scale = nullptr, const float* addend = nullptr, size_t add_rows = 1,
+                 int causal_T = 0);
+// causal_T > 0: s is zero past the diagonal of [causal_T, causal_T] blocks, so
+// dx is zero there and those elements of s and dout are not read (the same
+// values; a zero may differ in sign)
 void softmax_bwd(const float* s, const float* dout, float* dx, size_t outer, size_t axis_sz,
-                 size_t inner);
+                 size_t inner, int causal_T = 0);
 void layernorm_fwd(const float* x, float* y, float* var, size_t outer, size_t axis_sz,
                    size_t inner, float eps);
 // dout_colscale (optional, last axis only): dout is read as dout[i] * dout_colscale[i % axis]

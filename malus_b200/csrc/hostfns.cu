@@ -336,14 +336,17 @@ int64_t __softmax_fwd(int64_t x, int64_t axis) {
   const Lazy* z = tb(x)->lazy;
   if (z && inner == 1 && !tb(z->src)->lazy && (!z->addend || tb(z->addend)->len % asz == 0)) {
     // softmax(src * s + m): one pass over src (the scaled and masked scores
-    // are never written)
-    softmax_fwd(fptr(z->src), fptr(out), outer, asz, inner, z->scale ? fptr(z->scale) : nullptr,
-                z->addend ? fptr(z->addend) : nullptr, z->addend ? tb(z->addend)->len / asz : 1);
-    // over scores plus the causal mask (-1e9 above the diagonal) the
-    // probabilities there underflow to exactly 0 (for scores below ~5e8)
+    // are never written).  Over scores plus the causal mask (-1e9 above the
+    // diagonal) the probabilities there underflow to exactly 0 (for scores
+    // below ~1e8 in magnitude): those elements are not read, and the result
+    // is tagged so that the GEMMs reading it clip their K ranges.
     const TensorBuffer* m = z->addend ? tb(z->addend) : nullptr;
-    tb(out)->causal_zero = m && m->causal_mask && m->ndim == 2 && m->shape[0] == asz && m->shape[1] == asz &&
-                           s.ndim >= 2 && s.d[s.ndim - 2] == asz;
+    const bool causal = m && m->causal_mask && m->ndim == 2 && m->shape[0] == asz && m->shape[1] == asz &&
+                        s.ndim >= 2 && s.d[s.ndim - 2] == asz;
+    softmax_fwd(fptr(z->src), fptr(out), outer, asz, inner, z->scale ? fptr(z->scale) : nullptr,
+                z->addend ? fptr(z->addend) : nullptr, z->addend ? tb(z->addend)->len / asz : 1,
+                causal ? (int)asz : 0);
+    tb(out)->causal_zero = causal;
     return out;
   }
   softmax_fwd(fptr(x), fptr(out), outer, asz, inner);
@@ -571,8 +574,11 @@ int64_t __softmax_bwd(int64_t s, int64_t dout, int64_t axis) {
   size_t outer, asz, inner;
   split_axis(sh, ax, &outer, &asz, &inner);
   int64_t dx = alloc_shape(sh);
-  softmax_bwd(fptr(s), fptr(dout), fptr(dx), outer, asz, inner);
-  tb(dx)->causal_zero = tb(s)->causal_zero && inner == 1;   // s (dout - sum) is 0 where s is
+  // s (dout - sum) is 0 where s is: past the diagonal of a causal-zero s,
+  // which is then not read (nor dout there)
+  const bool causal = tb(s)->causal_zero && inner == 1 && sh.ndim >= 2 && sh.d[sh.ndim - 2] == asz;
+  softmax_bwd(fptr(s), fptr(dout), fptr(dx), outer, asz, inner, causal ? (int)asz : 0);
+  tb(dx)->causal_zero = causal;
   return dx;
 }
 

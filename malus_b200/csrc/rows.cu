@@ -65,6 +65,7 @@ struct RowSrc {
   const float* scale;
   const float* add;
   size_t add_rows;
+  uint32_t causal_T;   // > 0: elements past row % causal_T are masked (read by k_softmax_rows only)
   __device__ __forceinline__ float at(size_t r, size_t i, size_t len, float sc) const {
     float v = x[r * len + i];
     if (scale) v = __fmul_rn(v, sc);
@@ -127,12 +128,14 @@ __global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restric
     const bool live = r < rows;
     const float4* xr = reinterpret_cast<const float4*>(x.x + (size_t)r * len);
     const float4* ar = x.add ? reinterpret_cast<const float4*>(x.add + (size_t)(r % (uint32_t)x.add_rows) * len) : nullptr;
+    // chunks wholly past the diagonal of a causal mask: exp gives exactly 0 there
+    const uint32_t last = x.causal_T ? r % x.causal_T : 0xffffffffu;
     float4 v[PER4];
     float m = -INFINITY;
 #pragma unroll
     for (int k = 0; k < PER4; ++k) {
       const int c = sub + LPR * k;
-      if (live && c < n4) {
+      if (live && c < n4 && (uint32_t)(4 * c) <= last) {
         float4 t = xr[c];
         if (x.scale) { t.x = __fmul_rn(t.x, sc); t.y = __fmul_rn(t.y, sc); t.z = __fmul_rn(t.z, sc); t.w = __fmul_rn(t.w, sc); }
         if (ar) {
@@ -151,7 +154,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restric
 #pragma unroll
     for (int k = 0; k < PER4; ++k) {
       const int c = sub + LPR * k;
-      if (live && c < n4) {
+      if (live && c < n4 && (uint32_t)(4 * c) <= last) {
         v[k].x = expf(v[k].x - m); v[k].y = expf(v[k].y - m); v[k].z = expf(v[k].z - m); v[k].w = expf(v[k].w - m);
         sum += v[k].x; sum += v[k].y; sum += v[k].z; sum += v[k].w;
       }
@@ -163,7 +166,9 @@ __global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restric
 #pragma unroll
     for (int k = 0; k < PER4; ++k) {
       const int c = sub + LPR * k;
-      if (live && c < n4) yr[c] = make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv);
+      if (live && c < n4)
+        yr[c] = (uint32_t)(4 * c) <= last ? make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv)
+                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
   }
 }
@@ -213,22 +218,26 @@ __global__ void k_softmax_strided(const float* __restrict__ x, float* __restrict
   for (size_t a = 0; a < axis_sz; ++a) yb[a * inner] = expf(b[a * inner] - m) / s;
 }
 
+// causal_T > 0: s is zero past column r % causal_T of row r; those terms add
+// (signed) zeros to the dot product and give zero gradients, so they are not read.
 template <int PER>
 __global__ void k_softmax_bwd_warp(const float* __restrict__ s, const float* __restrict__ g,
-                                   float* __restrict__ dx, size_t rows, int len) {
+                                   float* __restrict__ dx, size_t rows, int len, int causal_T) {
   int lane = threadIdx.x & 31;
   size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
   size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
   for (size_t r = warp; r < rows; r += nw) {
     const float* sr = s + r * (size_t)len;
     const float* gr = g + r * (size_t)len;
+    const int last = causal_T ? (int)(r % (size_t)causal_T) : len;
     float sv[PER], gv[PER];
     float dot = 0.0f;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int i = lane + 32 * k;
-      sv[k] = i < len ? sr[i] : 0.0f;
-      gv[k] = i < len ? gr[i] : 0.0f;
+      const bool rd = i < len && i <= last;
+      sv[k] = rd ? sr[i] : 0.0f;
+      gv[k] = rd ? gr[i] : 0.0f;
       dot += gv[k] * sv[k];
     }
     dot = wsum(dot);
@@ -236,7 +245,7 @@ __global__ void k_softmax_bwd_warp(const float* __restrict__ s, const float* __r
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int i = lane + 32 * k;
-      if (i < len) dr[i] = sv[k] * (gv[k] - dot);
+      if (i < len) dr[i] = i <= last ? sv[k] * (gv[k] - dot) : 0.0f;
     }
   }
 }
@@ -966,10 +975,12 @@ static unsigned row_blocks(size_t rows) {
 }
 
 void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner,
-                 const float* scale, const float* addend, size_t add_rows) {
+                 const float* scale, const float* addend, size_t add_rows, int causal_T) {
   if (!outer || !axis_sz || !inner) return;
   if ((scale || addend) && inner != 1) panic("softmax_fwd: a deferred input needs the last axis");
-  const RowSrc src{x, scale, addend, std::max<size_t>(add_rows, 1)};
+  if (causal_T && (!addend || inner != 1 || (size_t)causal_T != axis_sz))
+    panic("softmax_fwd: causal skipping needs the [T, T] mask as the addend");
+  const RowSrc src{x, scale, addend, std::max<size_t>(add_rows, 1), (uint32_t)causal_T};
   // 16-byte rows whenever the row and every source are 16-byte aligned: a
   // deferred x * s + m must take the same kernel as its materialised value
   // (the row sum's grouping follows the kernel), so both give the same bits
@@ -1001,10 +1012,10 @@ void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t 
 }
 
 void softmax_bwd(const float* s, const float* g, float* dx, size_t outer, size_t axis_sz,
-                 size_t inner) {
+                 size_t inner, int causal_T) {
   if (!outer || !axis_sz || !inner) return;
   if (inner == 1 && axis_sz <= 1024) {
-    LAUNCH_ROWS_WARP(k_softmax_bwd_warp, axis_sz, outer, s, g, dx, outer, (int)axis_sz);
+    LAUNCH_ROWS_WARP(k_softmax_bwd_warp, axis_sz, outer, s, g, dx, outer, (int)axis_sz, causal_T);
   } else if (inner == 1) {
     k_softmax_bwd_block<<<row_blocks(outer), 512, 0, stream()>>>(s, g, dx, outer, axis_sz);
     count_launch();

@@ -237,6 +237,9 @@ def test_causal_zero_gemms_equal_full(M, rt, rng):
     dp = T(M, rng.standard_normal((Z, T_, T_)).astype(np.float32))
     ds = rt.__softmax_bwd(p, dp.h, 2)
     dsn = np_of(M, ds)
+    # the VJP of a tagged P skips the zero half: the same values as over an untagged copy
+    np.testing.assert_array_equal(dsn, M.Tensor(rt.__softmax_bwd(tp_plain.h, dp.h, 2)).numpy())
+    assert np.all(dsn[:, np.triu_indices(T_, 1)[0], np.triu_indices(T_, 1)[1]] == 0.0)
     dsc = rt.__mul_bwd_a(ds, tq.h, ts.h)                  # deferred ds * s, still zero above the diagonal
     plain = T(M, dsn * np.float32(0.125))
     qq = T(M, rng.standard_normal((Z, T_, hs)).astype(np.float32))   # scores = Q @ K^T
