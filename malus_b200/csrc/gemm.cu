@@ -869,11 +869,15 @@ struct SplitGeom32 {
 };
 
 // k_split_view with every index below 2^31: the same elements, values and
-// plane layout, indexed by FastDiv.
-__global__ void k_split_view32(SplitGeom32 g, float* __restrict__ hi, float* __restrict__ lo, uint32_t total) {
+// plane layout, indexed by FastDiv.  causal_T > 0 (the operand is a [T, T]
+// causal-zero block read by a GEMM that clips its K ranges to 128-row tiles):
+// row o's columns from (o / 128 + 1) * 128 on are never read and not written.
+__global__ void k_split_view32(SplitGeom32 g, float* __restrict__ hi, float* __restrict__ lo, uint32_t total,
+                               uint32_t causal_T) {
   for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < total; q += gridDim.x * blockDim.x) {
     const uint32_t row = g.cpr.div(q), c = (q - row * g.cpr.d) * 4;
     const uint32_t zi = g.n_outer.div(row), o = row - zi * g.n_outer.d;
+    if (causal_T && c >= ((o >> 7) + 1) * 128) continue;
     const float* s = g.base + g.z.at(zi) + g.outer.at(o);
     float x[4];
     if (g.vec && c + 4 <= g.n_inner) {
@@ -1396,6 +1400,7 @@ struct PlaneEntry {
   float* mem;          // hi then lo, each nz * n_outer * pitch floats
   int64_t pitch;
   bool transposed;     // planes hold the operand's columns as rows
+  int64_t causal_T;    // > 0: only the part a causally clipped GEMM reads was written
 };
 std::mutex g_pc_mu;
 std::unordered_map<uint64_t, std::vector<PlaneEntry>> g_pc;
@@ -1407,12 +1412,15 @@ bool plane_cache_on() {
 
 bool same_dim(const ViewDim& a, const ViewDim& b) { return a.div == b.div && a.hi == b.hi && a.lo == b.lo; }
 
-const PlaneEntry* pc_find(const GemmOperand& o) {
+// A cached entry of the same operand; partially written planes serve only a
+// consumer that clips its K ranges the same way (causal_T equal).
+const PlaneEntry* pc_find(const GemmOperand& o, int64_t causal_T) {
   auto it = g_pc.find(o.key);
   if (it == g_pc.end()) return nullptr;
   for (const PlaneEntry& e : it->second)
     if (e.nz == o.nz && e.rows == o.rows && e.cols == o.cols && same_dim(e.z, o.z) && same_dim(e.r, o.r) &&
-        same_dim(e.c, o.c) && e.scale == o.scale_dev && e.colscale == o.colscale_dev)
+        same_dim(e.c, o.c) && e.scale == o.scale_dev && e.colscale == o.colscale_dev &&
+        (e.causal_T == 0 || e.causal_T == causal_T))
       return &e;
   return nullptr;
 }
@@ -1427,16 +1435,24 @@ struct Planes {
   void* tmp;                   // scratch to free after the GEMM (null: cached)
 };
 
-Planes operand_planes(const GemmOperand& o, bool* trans) {
+// causal_T > 0: the operand is the A of a GEMM clipped to the causal
+// triangle of [causal_T, causal_T] blocks (128-row tiles); when the planes hold
+// it as (query row, key column), the part past each tile's diagonal block is
+// skipped.
+Planes operand_planes(const GemmOperand& o, bool* trans, int64_t causal_T = 0) {
   const bool flip = o.c.lo != 1 && o.r.lo == 1;
   const int64_t n_outer = flip ? o.cols : o.rows, n_inner = flip ? o.rows : o.cols;
   const ViewDim outer = flip ? o.c : o.r, inner = flip ? o.r : o.c;
   const int64_t pitch = (n_inner + 3) & ~int64_t(3);
   if (flip) *trans = !*trans;
+  // rows of the planes are the T queries, each with its T keys contiguous
+  if (!(causal_T > 0 && n_outer == causal_T && n_inner == causal_T && inner.div == 0 && inner.lo == 1 &&
+        outer.div == 0 && outer.lo == causal_T && causal_T % 128 == 0))
+    causal_T = 0;
   std::lock_guard<std::mutex> lk(g_pc_mu);
   const bool cache = o.key != 0 && plane_cache_on();
   if (cache)
-    if (const PlaneEntry* e = pc_find(o)) {
+    if (const PlaneEntry* e = pc_find(o, causal_T)) {
       const int64_t n = o.nz * n_outer * e->pitch;
       return Planes{e->mem, e->mem + n, n_outer, n_inner, e->pitch, nullptr};
     }
@@ -1476,10 +1492,12 @@ Planes operand_planes(const GemmOperand& o, bool* trans) {
       h.outer = ViewDim32(outer);
       h.inner = ViewDim32(inner);
       h.vec = g.vec;
-      k_split_view32<<<grid_for((size_t)total, 256), 256, 0, stream()>>>(h, mem, mem + n, (uint32_t)total);
+      k_split_view32<<<grid_for((size_t)total, 256), 256, 0, stream()>>>(h, mem, mem + n, (uint32_t)total,
+                                                                           (uint32_t)causal_T);
       count_launch();
       after_launch("k_split_view32");
     } else {
+      causal_T = 0;   // the 64-bit-index split writes every element
       k_split_view<<<grid_for((size_t)total, 256), 256, 0, stream()>>>(g, mem, mem + n, rows_total);
       count_launch();
       after_launch("k_split_view");
@@ -1487,7 +1505,7 @@ Planes operand_planes(const GemmOperand& o, bool* trans) {
   }
   if (cache) {
     g_pc[o.key].push_back(PlaneEntry{o.nz, o.rows, o.cols, o.z, o.r, o.c, o.scale_dev, o.colscale_dev, mem, pitch,
-                                     flip});
+                                     flip, causal_T});
     return Planes{mem, mem + n, n_outer, n_inner, pitch, nullptr};
   }
   return Planes{mem, mem + n, n_outer, n_inner, pitch, mem};
@@ -1497,8 +1515,9 @@ Planes operand_planes(const GemmOperand& o, bool* trans) {
 // their views), then one persistent GEMM with a plain row-major (batched) output.
 void gemm_tc(const GemmArgs& g) {
   bool at = g.a_trans, bt = g.b_trans;
+  const int causal = (g.a_zero == kCausalALower || g.a_zero == kCausalAUpper) && g.M == g.K ? g.a_zero : kCausalNone;
   int pid = prof_begin(1, 0.0, 12.0 * (double)(g.A.nz * g.A.rows * g.A.cols + g.B.nz * g.B.rows * g.B.cols));
-  const Planes pa = operand_planes(g.A, &at);
+  const Planes pa = operand_planes(g.A, &at, causal != kCausalNone ? g.M : 0);
   const Planes pb = operand_planes(g.B, &bt);
   prof_end(pid);
   TcProblem pr{};
@@ -1514,7 +1533,7 @@ void gemm_tc(const GemmArgs& g) {
   pr.out = g.C;
   pr.alpha = g.alpha;
   pr.beta = g.beta;
-  pr.causal = (g.a_zero == kCausalALower || g.a_zero == kCausalAUpper) && g.M == g.K ? g.a_zero : kCausalNone;
+  pr.causal = causal;
   gemm_tc_planes(pr);
   if (pa.tmp) scratch_free(pa.tmp);
   if (pb.tmp) scratch_free(pb.tmp);

@@ -234,6 +234,11 @@ def test_causal_zero_gemms_equal_full(M, rt, rng):
                                   M.Tensor(rt.tensor_matmul(tp_plain.h, tv.h)).numpy())
     np.testing.assert_array_equal(M.Tensor(rt.__matmul_bwd_b(p, tv.h, tg.h)).numpy(),
                                   M.Tensor(rt.__matmul_bwd_b(tp_plain.h, tv.h, tg.h)).numpy())
+    # the clipped products above cached only the planes they read; P as the
+    # B operand of an unclipped product needs (and gets) all of them
+    xw = T(M, rng.standard_normal((Z, hs, T_)).astype(np.float32))
+    np.testing.assert_array_equal(M.Tensor(rt.tensor_matmul(xw.h, p)).numpy(),
+                                  M.Tensor(rt.tensor_matmul(xw.h, tp_plain.h)).numpy())
     dp = T(M, rng.standard_normal((Z, T_, T_)).astype(np.float32))
     ds = rt.__softmax_bwd(p, dp.h, 2)
     dsn = np_of(M, ds)
