@@ -52,9 +52,9 @@ constexpr int AQ = 128;  // query rows per CTA
 constexpr int AK = 64;   // keys per block
 constexpr int kAttnThreads = 64 + 256;   // producer, MMA, 8 softmax warps
 
-// The persistent resident-score kernel (k_attn_fwd_ps) serves T <= 384 unless
-// switched off (MALUS_ATTN_RS=0, or malus_attn_set_resident(0)); both kernels
-// give the same bits.
+// The resident-score kernel (k_attn_fwd_rs) serves T <= 384 unless switched
+// off (MALUS_ATTN_RS=0, or malus_attn_set_resident(0)); both kernels give the
+// same bits.
 int g_attn_rs = -1;
 bool attn_resident_on() {
   if (g_attn_rs < 0) {
@@ -415,75 +415,58 @@ k_attn_fwd(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUt
 }
 
 // ---------------------------------------------------------------------------
-// Persistent variant for T <= 384 (k_attn_fwd_ps): one CTA per SM works
-// through a list of (head, query tile) units, heaviest tiles first in a
-// zigzag over the CTAs, and overlaps consecutive units.
-//  * A tile's score blocks (at most 384 keys up to its diagonal) stay in
-//    tensor memory, 64 columns per 64-key block, so S = Q K^T is computed once
-//    and read by both softmax passes.  Two O accumulators (64 columns each)
-//    follow the score columns, so unit j + 1's P V never waits for unit j's
-//    epilogue to drain O.
-//  * Q has its own shared region, freed as soon as the unit's last S product
-//    is done (the producer then loads the next unit's Q).  K blocks and then
-//    V blocks of every unit stream through one three-stage ring.
-//  * The MMA warp issues unit j's P V products as the softmax hands over P,
-//    and in between the next unit's S products whose K block has landed and
-//    whose tensor-memory block unit j's second pass has already read (a
-//    score block is released by the eight softmax warps right after their
-//    pass-2 load of it).
-//  * Each softmax group has one P stage, at once the A operand of its half
-//    of P V and the source of the TMA store of the P planes; the row
-//    statistics of the pass-1 combine share group 0's stage, written only
-//    after its last P V and store have read it.
-// Per unit the products and their order (S per block with the same three
-// tf32 MMAs per k-step; O over blocks, halves and k-steps) and the softmax
-// expressions are those of k_attn_fwd, so both kernels give the same bits.
-// Every wait is bounded; the softmax warps take every exit decision
-// collectively, and a failed wait drains the copies and MMAs in flight.
+// Resident-score variant (T <= 384).  A 128-query tile has at most 384 keys up
+// to its diagonal, so all its score blocks fit in tensor memory at once (64
+// columns per 64-key block) beside O.  S = Q K^T is then computed once: pass 1
+// reads the resident blocks for the row max and sum, pass 2 reads them again
+// for P.  K blocks and then V blocks stream through one three-stage ring, so V
+// is prefetched while pass 1 runs, and each softmax group has two P stages
+// (the second one in Q's shared memory once every S product is done, for
+// hs = 64), so a block's P is written while the previous block's P V runs and
+// its TMA store drains.  The products and their order (S per block with the
+// same three tf32 MMAs per k-step; O accumulated over blocks, halves and
+// k-steps in the same order) and the softmax expressions are those of
+// k_attn_fwd, so both kernels give the same bits.
 constexpr int kRsMaxBlocks = 6;   // 384 keys
 constexpr int kRsRing = 3;
-constexpr int kPsOCol = kRsMaxBlocks * AK;   // two O accumulators after the score columns
+constexpr int kRsOCol = kRsMaxBlocks * AK;   // O after the score columns
 
 template <int HS>
-struct AttnPsCfg {
+struct AttnRsCfg {
   static constexpr int kQBytes = AQ * HS * 4;
   static constexpr int kKBytes = AK * HS * 4;              // one plane of a K or V block
   static constexpr int kStage = 2 * kKBytes;               // hi + lo
   static constexpr int kPBytes = AQ * 32 * 4;              // one plane of a 32-key P half
   static constexpr int kPStage = 2 * kPBytes;              // hi + lo
   static constexpr int kOffRing = 2 * kQBytes;
-  static constexpr int kOffP = kOffRing + kRsRing * kStage;   // group g's stage at kOffP + g * kPStage
-  static constexpr int kOffStats = kOffP;                     // [2][128] float2 in group 0's stage
-  static constexpr int kOffBar = kOffP + 2 * kPStage;
-  static constexpr int kSmem = kOffBar + 256 + 1024;
+  static constexpr int kOffP0 = kOffRing + kRsRing * kStage;          // P buffer 0 of both groups
+  static constexpr bool kP1InQ = 2 * kQBytes >= 2 * kPStage;         // buffer 1 reuses Q (hs = 64)
+  static constexpr int kOffP1 = kP1InQ ? 0 : kOffP0 + 2 * kPStage;
+  static constexpr int kOffStats = kOffP0;                 // as in k_attn_fwd: read before any P write
+  static constexpr int kOffBar = (kP1InQ ? kOffP0 + 2 * kPStage : kOffP1 + 2 * kPStage);
+  static constexpr int kSmem = kOffBar + 512 + 1024;
   static_assert(kSmem <= 232448, "shared memory");
 };
 
-// The k-th unit of CTA c (zigzag over the G CTAs: c, 2G-1-c, 2G+c, ...);
-// units are numbered heaviest first: u -> query tile nq-1-u/BH of head u%BH.
-__device__ __forceinline__ int ps_unit(int k, int c, int G) { return k * G + ((k & 1) ? G - 1 - c : c); }
-
 template <int HS>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-k_attn_fwd_ps(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUtensorMap mQKl,
+k_attn_fwd_rs(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ CUtensorMap mQKl,
               const __grid_constant__ CUtensorMap mVh, const __grid_constant__ CUtensorMap mVl,
               const __grid_constant__ CUtensorMap mPh, const __grid_constant__ CUtensorMap mPl,
-              const AttnArgs a, int BH) {
-  using CF = AttnPsCfg<HS>;
+              const __grid_constant__ CUtensorMap mOh, const __grid_constant__ CUtensorMap mOl,
+              const AttnArgs a) {
+  using CF = AttnRsCfg<HS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bar = (uint64_t*)(smem + CF::kOffBar);
   uint64_t* q_full = bar;
-  uint64_t* q_empty = bar + 1;
-  uint64_t* r_full = bar + 2;                    // [kRsRing]
-  uint64_t* r_empty = r_full + kRsRing;          // [kRsRing]
-  uint64_t* s_full = r_empty + kRsRing;          // [kRsMaxBlocks]
-  uint64_t* s_free = s_full + kRsMaxBlocks;      // [kRsMaxBlocks], 8 softmax warps each
-  uint64_t* p_full = s_free + kRsMaxBlocks;      // [2 groups]
-  uint64_t* p_empty = p_full + 2;                // [2]
-  uint64_t* o_full = p_empty + 2;                // [2 accumulators]
-  uint64_t* o_free = o_full + 2;                 // [2], 8 softmax warps each
-  uint64_t* drain = o_free + 2;
+  uint64_t* r_full = bar + 1;                    // [kRsRing]
+  uint64_t* r_empty = bar + 1 + kRsRing;         // [kRsRing]
+  uint64_t* s_full = bar + 1 + 2 * kRsRing;      // [kRsMaxBlocks], one use each
+  uint64_t* p_full = s_full + kRsMaxBlocks;      // [2 groups][2 buffers]
+  uint64_t* p_empty = p_full + 4;                // [2][2]
+  uint64_t* o_full = p_empty + 4;
+  uint64_t* drain = o_full + 1;
   uint64_t* done = drain + 1;
   uint32_t* tmem_slot = (uint32_t*)(done + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
@@ -491,25 +474,25 @@ k_attn_fwd_ps(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = a.T / AQ;
-  const int U = BH * nq, G = (int)gridDim.x, c = (int)blockIdx.x;
+  const int qb = nq - 1 - (int)(blockIdx.x % nq);   // heavy (late) query blocks first
+  const int z = (int)(blockIdx.x / nq);
+  const int q0 = qb * AQ;
+  const int nkb = (q0 + AQ) / AK;                     // key blocks up to the diagonal (<= 6)
+  const int items = 2 * nkb;                          // ring items: K blocks, then V blocks
+  const int row_base = z * a.T;
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
-    mbar_init(smem_u32(q_empty), 1);
     for (int i = 0; i < kRsRing; ++i) {
       mbar_init(smem_u32(&r_full[i]), 1);
       mbar_init(smem_u32(&r_empty[i]), 1);
     }
-    for (int i = 0; i < kRsMaxBlocks; ++i) {
-      mbar_init(smem_u32(&s_full[i]), 1);
-      mbar_init(smem_u32(&s_free[i]), 8);
-    }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kRsMaxBlocks; ++i) mbar_init(smem_u32(&s_full[i]), 1);
+    for (int i = 0; i < 4; ++i) {
       mbar_init(smem_u32(&p_full[i]), 1);
       mbar_init(smem_u32(&p_empty[i]), 1);
-      mbar_init(smem_u32(&o_full[i]), 1);
-      mbar_init(smem_u32(&o_free[i]), 8);
     }
+    mbar_init(smem_u32(o_full), 1);
     mbar_init(smem_u32(drain), 1);
     mbar_init(smem_u32(done), 8);
     *abort_flag = 0;
@@ -524,7 +507,7 @@ k_attn_fwd_ps(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ 
   __syncwarp();
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = *tmem_slot;   // score block b at columns 64 b, O accumulators at kPsOCol (+64)
+  const uint32_t tmem = *tmem_slot;   // S block b at columns 64 b, O at kRsOCol
 
   uint8_t* q_h = smem;
   uint8_t* q_l = smem + CF::kQBytes;
@@ -532,48 +515,40 @@ k_attn_fwd_ps(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int it = 0, nq_loads = 0;
-      bool ok = true;
-      for (int k = 0; ok; ++k) {
-        const int u = ps_unit(k, c, G);
-        if (u >= U) break;
-        const int z = u % BH, q0 = (nq - 1 - u / BH) * AQ, nkb = (q0 + AQ) / AK, row_base = z * a.T;
-        if (k > 0 && !mbar_wait(smem_u32(q_empty), (k - 1) & 1, abort_flag, a.err, 51)) { ok = false; break; }
-        mbar_expect_tx(smem_u32(q_full), 2 * CF::kQBytes);
-        for (int sl = 0; sl < HS / 32; ++sl)
-          for (int rh = 0; rh < 2; ++rh) {
-            const uint32_t off = sl * (AQ * 128) + rh * (64 * 128);
-            tma_load_3d(smem_u32(q_h + off), &mQKh, smem_u32(q_full), sl * 32, row_base + q0 + rh * 64, 0);
-            tma_load_3d(smem_u32(q_l + off), &mQKl, smem_u32(q_full), sl * 32, row_base + q0 + rh * 64, 0);
+      mbar_expect_tx(smem_u32(q_full), 2 * CF::kQBytes);
+      for (int sl = 0; sl < HS / 32; ++sl)
+        for (int rh = 0; rh < 2; ++rh) {
+          const uint32_t off = sl * (AQ * 128) + rh * (64 * 128);
+          tma_load_3d(smem_u32(q_h + off), &mQKh, smem_u32(q_full), sl * 32, row_base + q0 + rh * 64, 0);
+          tma_load_3d(smem_u32(q_l + off), &mQKl, smem_u32(q_full), sl * 32, row_base + q0 + rh * 64, 0);
+        }
+      int it = 0;
+      for (; it < items; ++it) {
+        const int st = it % kRsRing, use = it / kRsRing;
+        if (use > 0 && !mbar_wait(smem_u32(&r_empty[st]), (use - 1) & 1, abort_flag, a.err, 41)) break;
+        uint8_t* base = smem + CF::kOffRing + st * CF::kStage;
+        const uint32_t fb = smem_u32(&r_full[st]);
+        mbar_expect_tx(fb, CF::kStage);
+        if (it < nkb) {
+          const int kb = it;
+          for (int sl = 0; sl < HS / 32; ++sl) {
+            tma_load_3d(smem_u32(base + sl * (AK * 128)), &mQKh, fb, sl * 32, row_base + kb * AK, 1);
+            tma_load_3d(smem_u32(base + CF::kKBytes + sl * (AK * 128)), &mQKl, fb, sl * 32, row_base + kb * AK, 1);
           }
-        ++nq_loads;
-        for (int i = 0; i < 2 * nkb; ++i, ++it) {
-          const int st = it % kRsRing, use = it / kRsRing;
-          if (use > 0 && !mbar_wait(smem_u32(&r_empty[st]), (use - 1) & 1, abort_flag, a.err, 52)) { ok = false; break; }
-          uint8_t* base = smem + CF::kOffRing + st * CF::kStage;
-          const uint32_t fb = smem_u32(&r_full[st]);
-          mbar_expect_tx(fb, CF::kStage);
-          if (i < nkb) {
-            for (int sl = 0; sl < HS / 32; ++sl) {
-              tma_load_3d(smem_u32(base + sl * (AK * 128)), &mQKh, fb, sl * 32, row_base + i * AK, 1);
-              tma_load_3d(smem_u32(base + CF::kKBytes + sl * (AK * 128)), &mQKl, fb, sl * 32, row_base + i * AK, 1);
-            }
-          } else {
-            const int kb = i - nkb;
-            for (int half = 0; half < 2; ++half) {
-              const uint32_t voff = half * (HS / 32) * 4096;
-              tma_load_4d(smem_u32(base + voff), &mVh, fb, 0, row_base + kb * AK + 32 * half, 0, 2);
-              tma_load_4d(smem_u32(base + CF::kKBytes + voff), &mVl, fb, 0, row_base + kb * AK + 32 * half, 0, 2);
-            }
+        } else {
+          const int kb = it - nkb;
+          for (int half = 0; half < 2; ++half) {
+            const uint32_t voff = half * (HS / 32) * 4096;
+            tma_load_4d(smem_u32(base + voff), &mVh, fb, 0, row_base + kb * AK + 32 * half, 0, 2);
+            tma_load_4d(smem_u32(base + CF::kKBytes + voff), &mVl, fb, 0, row_base + kb * AK + 32 * half, 0, 2);
           }
         }
       }
       if (*abort_flag) {
-        // every issued load must land before the CTA exits: the last Q and the
-        // last kRsRing ring items (distinct stages, each at its latest phase)
+        // every issued load must land before the CTA exits (the last kRsRing
+        // items are in distinct stages, each at its latest phase)
         uint64_t t0 = gtimer();
-        if (nq_loads > 0)
-          while (!mbar_try(smem_u32(q_full), (nq_loads - 1) & 1) && gtimer() - t0 < kWaitNs) {}
+        while (!mbar_try(smem_u32(q_full), 0) && gtimer() - t0 < kWaitNs) {}
         for (int qi = it > kRsRing ? it - kRsRing : 0; qi < it; ++qi) {
           t0 = gtimer();
           while (!mbar_try(smem_u32(&r_full[qi % kRsRing]), (qi / kRsRing) & 1) && gtimer() - t0 < kWaitNs) {}
@@ -585,29 +560,15 @@ k_attn_fwd_ps(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ 
     if (lane == 0) {
       const uint32_t id_s = idesc_tf32(false, false, AK);
       const uint32_t id_o = idesc_tf32(false, true, HS);
+      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, a.err, 42);
+      bool issued = false;
       const uint64_t dqh = desc_kmajor(smem_u32(q_h), 0), dql = desc_kmajor(smem_u32(q_l), 0);
       const uint64_t dr0 = desc_kmajor(smem_u32(smem + CF::kOffRing), 0);
       const uint64_t dv0 = desc_mnmajor(smem_u32(smem + CF::kOffRing), 0);
-      int cnt_s[kRsMaxBlocks];
-#pragma unroll
-      for (int i = 0; i < kRsMaxBlocks; ++i) cnt_s[i] = 0;
-      bool ok = true, issued = false;
-      // S_b = Q K_b^T of unit k (ring item `item`) into score block b.  A poll
-      // (block = false) issues it only if everything it needs is ready.
-      auto issue_s = [&](int k, int b, int item, bool block) -> bool {
-        const int st = item % kRsRing;
-        const uint32_t qpar = k & 1, rpar = (item / kRsRing) & 1;
-        if (block) {
-          if (!mbar_wait(smem_u32(q_full), qpar, abort_flag, a.err, 53)) { ok = false; return false; }
-          if (!mbar_wait(smem_u32(&r_full[st]), rpar, abort_flag, a.err, 54)) { ok = false; return false; }
-          if (cnt_s[b] > 0 && !mbar_wait(smem_u32(&s_free[b]), (cnt_s[b] - 1) & 1, abort_flag, a.err, 55)) {
-            ok = false;
-            return false;
-          }
-        } else if (!mbar_try(smem_u32(q_full), qpar) || !mbar_try(smem_u32(&r_full[st]), rpar) ||
-                   (cnt_s[b] > 0 && !mbar_try(smem_u32(&s_free[b]), (cnt_s[b] - 1) & 1))) {
-          return false;
-        }
+      // S_b = Q K_b^T for every block, as the K blocks land
+      for (int b = 0; b < nkb && ok; ++b) {
+        const int st = b % kRsRing;
+        if (!mbar_wait(smem_u32(&r_full[st]), (b / kRsRing) & 1, abort_flag, a.err, 43)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t kh = dr0 + (uint64_t)(st * (CF::kStage / 16)), kl = kh + CF::kKBytes / 16;
         const uint32_t dS = tmem + b * AK;
@@ -622,72 +583,34 @@ k_attn_fwd_ps(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ 
         issued = true;
         mma_commit(smem_u32(&s_full[b]));
         mma_commit(smem_u32(&r_empty[st]));
-        ++cnt_s[b];
-        return true;
-      };
-      auto nkb_of = [&](int u) { return ((nq - 1 - u / BH) * AQ + AQ) / AK; };
-      int it_base = 0, pcount = 0;
-      // unit 0's scores
-      if (ps_unit(0, c, G) < U) {
-        const int n0 = nkb_of(ps_unit(0, c, G));
-        for (int b = 0; b < n0 && ok; ++b) issue_s(0, b, b, true);
-        if (ok) mma_commit(smem_u32(q_empty));
       }
-      for (int k = 0; ok; ++k) {
-        const int u = ps_unit(k, c, G);
-        if (u >= U) break;
-        const int nkb = nkb_of(u);
-        const int un = ps_unit(k + 1, c, G);
-        const bool has_next = un < U;
-        const int nkb_n = has_next ? nkb_of(un) : 0, base_n = it_base + 2 * nkb;
-        int sn = 0;   // scores of unit k + 1 issued so far
-        const int ob = k & 1;
-        if (k >= 2 && !mbar_wait(smem_u32(&o_free[ob]), ((k >> 1) - 1) & 1, abort_flag, a.err, 56)) { ok = false; break; }
-        const uint32_t dO = tmem + kPsOCol + 64 * ob;
-        for (int b = 0; b < nkb && ok; ++b) {
-          // O += P_b V_b, half g from group g's P stage
-          const int item = it_base + nkb + b, st = item % kRsRing;
-          if (!mbar_wait(smem_u32(&r_full[st]), (item / kRsRing) & 1, abort_flag, a.err, 57)) { ok = false; break; }
-          for (int g = 0; g < 2; ++g) {
-            if (!mbar_wait(smem_u32(&p_full[g]), pcount & 1, abort_flag, a.err, 58)) { ok = false; break; }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint64_t ph0 = desc_kmajor(smem_u32(smem + CF::kOffP + g * CF::kPStage), 0);
-            const uint64_t pl0 = ph0 + CF::kPBytes / 16;
-            const uint64_t vh0 = dv0 + (uint64_t)(st * (CF::kStage / 16)) + (uint64_t)(g * (HS / 32) * (4096 / 16));
-            const uint64_t vl0 = vh0 + CF::kKBytes / 16;
+      // O += P_b V_b, half g from group g's P buffer b & 1
+      for (int b = 0; b < nkb && ok; ++b) {
+        const int it = nkb + b, st = it % kRsRing;
+        if (!mbar_wait(smem_u32(&r_full[st]), (it / kRsRing) & 1, abort_flag, a.err, 44)) { ok = false; break; }
+        const int buf = b & 1, use = b >> 1;
+        for (int g = 0; g < 2; ++g) {
+          if (!mbar_wait(smem_u32(&p_full[g * 2 + buf]), use & 1, abort_flag, a.err, 45)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t poff = (buf ? CF::kOffP1 : CF::kOffP0) + g * CF::kPStage;
+          const uint64_t ph0 = desc_kmajor(smem_u32(smem + poff), 0), pl0 = ph0 + CF::kPBytes / 16;
+          const uint64_t vh0 = dv0 + (uint64_t)(st * (CF::kStage / 16)) + (uint64_t)(g * (HS / 32) * (4096 / 16));
+          const uint64_t vl0 = vh0 + CF::kKBytes / 16;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t dph = ph0 + (uint64_t)(kk * 2), dpl = pl0 + (uint64_t)(kk * 2);
-              const uint64_t dvh = vh0 + (uint64_t)(kk * 64), dvl = vl0 + (uint64_t)(kk * 64);
-              const uint32_t acc0 = (b > 0 || g > 0 || kk > 0) ? 1u : 0u;
-              mma_tf32(dO, dpl, dvh, id_o, acc0);
-              mma_tf32(dO, dph, dvl, id_o, 1u);
-              mma_tf32(dO, dph, dvh, id_o, 1u);
-            }
-            mma_commit(smem_u32(&p_empty[g]));
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t dph = ph0 + (uint64_t)(kk * 2), dpl = pl0 + (uint64_t)(kk * 2);
+            const uint64_t dvh = vh0 + (uint64_t)(kk * 64), dvl = vl0 + (uint64_t)(kk * 64);
+            const uint32_t acc0 = (b > 0 || g > 0 || kk > 0) ? 1u : 0u;
+            mma_tf32(tmem + kRsOCol, dpl, dvh, id_o, acc0);
+            mma_tf32(tmem + kRsOCol, dph, dvl, id_o, 1u);
+            mma_tf32(tmem + kRsOCol, dph, dvh, id_o, 1u);
           }
-          if (!ok) break;
-          mma_commit(smem_u32(&r_empty[st]));
-          ++pcount;
-          // the next unit's scores whose K block has landed: its ring stage was
-          // last used by the item three before it, which must be consumed
-          // before that stage's barrier is polled
-          while (has_next && sn < nkb_n) {
-            const int vprev = nkb + sn - 3;   // V block of unit k three items earlier (if any)
-            if (sn < 3 && vprev >= 0 && vprev > b) break;
-            if (!issue_s(k + 1, sn, base_n + sn, false)) break;
-            ++sn;
-          }
+          mma_commit(smem_u32(&p_empty[g * 2 + buf]));
         }
         if (!ok) break;
-        mma_commit(smem_u32(&o_full[ob]));
-        if (has_next) {
-          for (; sn < nkb_n && ok; ++sn) issue_s(k + 1, sn, base_n + sn, true);
-          if (!ok) break;
-          mma_commit(smem_u32(q_empty));
-        }
-        it_base = base_n;
+        mma_commit(smem_u32(&r_empty[st]));
       }
+      if (ok) mma_commit(smem_u32(o_full));
       if (!ok && issued) {
         mma_commit(smem_u32(drain));
         uint64_t t0 = gtimer();
@@ -696,94 +619,113 @@ k_attn_fwd_ps(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ 
       if (!ok) *abort_flag = 1;
     }
   } else {
+
     // ---------------- softmax warps: group g owns keys 32g..32g+31 of each block ----------------
     const int quarter = warp & 3;
     const int g = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;      // TMEM lane == tile row
+    const int q = q0 + row;
     const bool issuer = (warp == 2 + 4 * g) && lane == 0;
+    float m = -INFINITY, l = 0.0f, inv_l = 0.0f;
     const float sl2e = a.scale * kLog2e;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    int cnt_s[kRsMaxBlocks];
-#pragma unroll
-    for (int i = 0; i < kRsMaxBlocks; ++i) cnt_s[i] = 0;
-    int pcount = 0;
     bool ok = true;
-    uint8_t* p_h = smem + CF::kOffP + g * CF::kPStage;
-    uint8_t* p_l = p_h + CF::kPBytes;
-    for (int k = 0; ok; ++k) {
-      const int u = ps_unit(k, c, G);
-      if (u >= U) break;
-      const int z = u % BH, q0 = (nq - 1 - u / BH) * AQ, nkb = (q0 + AQ) / AK, row_base = z * a.T;
-      const int q = q0 + row;
-      float m = -INFINITY, l = 0.0f, inv_l = 0.0f;
-      // pass 1: row max and sum of this group's keys, block by block as S lands
-      for (int b = 0; b < nkb && ok; ++b) {
-        const bool failed = !mbar_wait(smem_u32(&s_full[b]), cnt_s[b] & 1, abort_flag, a.err, 61);
-        if (any256(failed)) { ok = false; break; }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        uint32_t r[32];
-        tmem_ld32(tmem + b * AK + 32 * g + lane_off, r);
-        const int key0 = b * AK + 32 * g;
-        float bm = -INFINITY;
+    // pass 1: row max and sum of this group's keys, block by block as S lands
+    for (int b = 0; b < nkb && ok; ++b) {
+      const bool failed = !mbar_wait(smem_u32(&s_full[b]), 0, abort_flag, a.err, 46);
+      if (any256(failed)) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t r[32];
+      tmem_ld32(tmem + b * AK + 32 * g + lane_off, r);
+      const int key0 = b * AK + 32 * g;
+      float bm = -INFINITY;
 #pragma unroll
-        for (int cc = 0; cc < 32; ++cc)
-          if (key0 + cc <= q) bm = fmaxf(bm, __uint_as_float(r[cc]) * sl2e);
-        const float mn = fmaxf(m, bm);
-        if (mn != -INFINITY) {
-          float sum = 0.0f;
+      for (int c = 0; c < 32; ++c)
+        if (key0 + c <= q) bm = fmaxf(bm, __uint_as_float(r[c]) * sl2e);
+      const float mn = fmaxf(m, bm);
+      if (mn != -INFINITY) {
+        float sum = 0.0f;
 #pragma unroll
-          for (int cc = 0; cc < 32; ++cc)
-            sum += key0 + cc <= q ? exp2_hw(fmaf(__uint_as_float(r[cc]), sl2e, -mn)) : 0.0f;
-          l = (m == -INFINITY ? 0.0f : l * exp2_hw(m - mn)) + sum;
-          m = mn;
-        }
+        for (int c = 0; c < 32; ++c)
+          sum += key0 + c <= q ? exp2_hw(fmaf(__uint_as_float(r[c]), sl2e, -mn)) : 0.0f;
+        l = (m == -INFINITY ? 0.0f : l * exp2_hw(m - mn)) + sum;
+        m = mn;
       }
-      if (!ok) break;
-      // combine the two groups' row statistics in group 0's P stage, once the
-      // previous unit's last P V and P store have read it
-      {
-        bool failed = false;
-        if (issuer && g == 0) {
-          if (pcount > 0) failed = !mbar_wait(smem_u32(&p_empty[0]), (pcount - 1) & 1, abort_flag, a.err, 62);
-          bulk_wait_read<0>();
-        }
-        if (any256(failed)) { ok = false; break; }
-        stats[g * AQ + row] = make_float2(m, l);
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        const float2 o = stats[(1 - g) * AQ + row];
-        const float mm = fmaxf(m, o.x);
-        l = (m == -INFINITY ? 0.0f : l * exp2_hw(m - mm)) + (o.x == -INFINITY ? 0.0f : o.y * exp2_hw(o.x - mm));
-        m = mm;
-        inv_l = 1.0f / l;
-        if (g == 0 && a.stats) a.stats[row_base + q] = make_float2(m, inv_l);
-      }
-      // pass 2: P from the resident scores; each score block is released to
-      // the MMA warp (the next unit's S) right after it is read
-      for (int b = 0; b < nkb && ok; ++b) {
-        uint32_t r[32];
-        tmem_ld32(tmem + b * AK + 32 * g + lane_off, r);
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&s_free[b]));
-        ++cnt_s[b];
-        const int key0 = b * AK + 32 * g;
-        float sv[32];
+    }
+    if (ok) {
+      // combine the two groups' row statistics
+      stats[g * AQ + row] = make_float2(m, l);
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const float2 o = stats[(1 - g) * AQ + row];
+      const float mm = fmaxf(m, o.x);
+      l = (m == -INFINITY ? 0.0f : l * exp2_hw(m - mm)) + (o.x == -INFINITY ? 0.0f : o.y * exp2_hw(o.x - mm));
+      m = mm;
+      inv_l = 1.0f / l;
+      if (g == 0 && a.stats) a.stats[row_base + q] = make_float2(m, inv_l);
+    }
+    // pass 2: P from the resident scores, into buffer b & 1 of this group
+    for (int b = 0; b < nkb && ok; ++b) {
+      uint32_t r[32];
+      tmem_ld32(tmem + b * AK + 32 * g + lane_off, r);
+      const int key0 = b * AK + 32 * g;
+      float sv[32];
 #pragma unroll
-        for (int cc = 0; cc < 32; ++cc)
-          sv[cc] = key0 + cc <= q ? exp2_hw(fmaf(__uint_as_float(r[cc]), sl2e, -m)) * inv_l : 0.0f;
-        bool failed2 = false;
-        if (issuer) {
-          if (pcount > 0) failed2 = !mbar_wait(smem_u32(&p_empty[g]), (pcount - 1) & 1, abort_flag, a.err, 63);
-          bulk_wait_read<0>();   // the previous P store has read the stage
+      for (int c = 0; c < 32; ++c)
+        sv[c] = key0 + c <= q ? exp2_hw(fmaf(__uint_as_float(r[c]), sl2e, -m)) * inv_l : 0.0f;
+      const int buf = b & 1, use = b >> 1;
+      bool failed2 = false;
+      if (issuer) {
+        if (use > 0) failed2 = !mbar_wait(smem_u32(&p_empty[g * 2 + buf]), (use - 1) & 1, abort_flag, a.err, 47);
+        bulk_wait_read<1>();   // the store of this buffer's previous block has read it
+      }
+      if (any256(failed2)) { ok = false; break; }
+      uint8_t* p_h = smem + (buf ? CF::kOffP1 : CF::kOffP0) + g * CF::kPStage;
+      uint8_t* p_l = p_h + CF::kPBytes;
+      float4* rh = reinterpret_cast<float4*>(p_h + row * 128);
+      float4* rl = reinterpret_cast<float4*>(p_l + row * 128);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 v = make_float4(sv[4 * j], sv[4 * j + 1], sv[4 * j + 2], sv[4 * j + 3]);
+        const float4 h4 = make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
+        rh[j ^ (row & 7)] = h4;
+        rl[j ^ (row & 7)] = make_float4(tf32_rn(v.x - h4.x), tf32_rn(v.y - h4.y), tf32_rn(v.z - h4.z),
+                                        tf32_rn(v.w - h4.w));
+      }
+      fence_async_smem();
+      group_sync(g);
+      if (issuer) {
+        mbar_arrive(smem_u32(&p_full[g * 2 + buf]));
+        if (a.store_p) {
+          tma_store_2d(&mPh, smem_u32(p_h), key0, row_base + q0);
+          tma_store_2d(&mPl, smem_u32(p_l), key0, row_base + q0);
         }
-        // every thread has read the statistics (before the first collective
-        // of pass 2) and the stage is free for the whole group
-        if (any256(failed2)) { ok = false; break; }
-        float4* rh = reinterpret_cast<float4*>(p_h + row * 128);
-        float4* rl = reinterpret_cast<float4*>(p_l + row * 128);
+        bulk_commit();
+      }
+    }
+    // O = P V: group g takes columns [32g, 32g + 32) of each 64 (hs = 32: group
+    // 0 only) and stores them as head-unfolded tf32 planes [B*T][H*hs] by TMA,
+    // staged in its P buffer 0 (every MMA and P store has read it by then)
+    if (ok) {
+      const bool failed = !mbar_wait(smem_u32(o_full), 0, abort_flag, a.err, 48);
+      ok = !any256(failed);
+    }
+    if (ok) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int bb = z / a.H, h = z % a.H;
+      uint8_t* o_h = smem + CF::kOffP0 + g * CF::kPStage;
+      uint8_t* o_l = o_h + CF::kPBytes;
+#pragma unroll
+      for (int c0 = g * 32; c0 < HS; c0 += 64) {
+        uint32_t o[32];
+        tmem_ld32(tmem + kRsOCol + lane_off + (uint32_t)c0, o);
+        if (issuer) bulk_wait_read<0>();
+        group_sync(g);
+        float4* rh = reinterpret_cast<float4*>(o_h + row * 128);
+        float4* rl = reinterpret_cast<float4*>(o_l + row * 128);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 v = make_float4(sv[4 * j], sv[4 * j + 1], sv[4 * j + 2], sv[4 * j + 3]);
+          const float4 v = make_float4(__uint_as_float(o[4 * j]), __uint_as_float(o[4 * j + 1]),
+                                       __uint_as_float(o[4 * j + 2]), __uint_as_float(o[4 * j + 3]));
           const float4 h4 = make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
           rh[j ^ (row & 7)] = h4;
           rl[j ^ (row & 7)] = make_float4(tf32_rn(v.x - h4.x), tf32_rn(v.y - h4.y), tf32_rn(v.z - h4.z),
@@ -792,47 +734,13 @@ k_attn_fwd_ps(const __grid_constant__ CUtensorMap mQKh, const __grid_constant__ 
         fence_async_smem();
         group_sync(g);
         if (issuer) {
-          mbar_arrive(smem_u32(&p_full[g]));
-          if (a.store_p) {
-            tma_store_2d(&mPh, smem_u32(p_h), key0, row_base + q0);
-            tma_store_2d(&mPl, smem_u32(p_l), key0, row_base + q0);
-          }
+          tma_store_2d(&mOh, smem_u32(o_h), h * HS + c0, bb * a.T + q0);
+          tma_store_2d(&mOl, smem_u32(o_l), h * HS + c0, bb * a.T + q0);
           bulk_commit();
         }
-        ++pcount;
       }
-      if (!ok) break;
-      // O = P V from accumulator k & 1: group g writes columns [g*HS/2, (g+1)*HS/2)
-      // as head-unfolded tf32 planes, then releases the accumulator
-      const int ob = k & 1;
-      const bool failed3 = !mbar_wait(smem_u32(&o_full[ob]), (k >> 1) & 1, abort_flag, a.err, 64);
-      if (any256(failed3)) { ok = false; break; }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      {
-        const int bb = z / a.H, h = z % a.H;
-        const size_t C = (size_t)a.H * HS;
-        float* oh = a.o_hi + ((size_t)bb * a.T + q) * C + (size_t)h * HS;
-        float* ol = a.o_lo + ((size_t)bb * a.T + q) * C + (size_t)h * HS;
-#pragma unroll
-        for (int c0 = g * 32; c0 < HS; c0 += 64) {
-          uint32_t o[32];
-          tmem_ld32(tmem + kPsOCol + 64 * ob + lane_off + (uint32_t)c0, o);
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 v = make_float4(__uint_as_float(o[j]), __uint_as_float(o[j + 1]),
-                                         __uint_as_float(o[j + 2]), __uint_as_float(o[j + 3]));
-            const float4 h4 = make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
-            *reinterpret_cast<float4*>(oh + c0 + j) = h4;
-            *reinterpret_cast<float4*>(ol + c0 + j) =
-                make_float4(tf32_rn(v.x - h4.x), tf32_rn(v.y - h4.y), tf32_rn(v.z - h4.z), tf32_rn(v.w - h4.w));
-          }
-        }
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&o_free[ob]));
     }
-    if (issuer) bulk_wait<0>();   // the P stores have landed before the CTA exits
+    if (issuer) bulk_wait<0>();   // the P and O stores have landed before the CTA exits
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(done));
@@ -874,19 +782,20 @@ void launch_attn(const float* qkv_hi, const float* qkv_lo, int B, int H, int T, 
                 device_error_word()};
   const unsigned grid = (unsigned)(B * H * (T / AQ));
   if (attn_resident_on() && T <= kRsMaxBlocks * AK) {
-    using PF = AttnPsCfg<HS>;
-    static bool attr_ps = false;
-    if (!attr_ps) {
-      MALUS_CUDA(cudaFuncSetAttribute(k_attn_fwd_ps<HS>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF::kSmem));
-      attr_ps = true;
+    using RF = AttnRsCfg<HS>;
+    static bool attr_rs = false;
+    if (!attr_rs) {
+      MALUS_CUDA(cudaFuncSetAttribute(k_attn_fwd_rs<HS>, cudaFuncAttributeMaxDynamicSharedMemorySize, RF::kSmem));
+      attr_rs = true;
     }
-    // one CTA per SM (the shared memory allows no second), each working
-    // through its share of the B*H*(T/128) units
-    const unsigned units = grid;
-    const unsigned ctas = std::min<unsigned>(units, (unsigned)kNumSMs);
-    k_attn_fwd_ps<HS><<<ctas, kAttnThreads, PF::kSmem, stream()>>>(qh, ql, vh, vl, ph, pl, args, B * H);
+    // O planes [B*T][H*hs], box {32 columns, 128 rows}: the layout of a P stage
+    const uint64_t dO[2] = {(uint64_t)H * HS, (uint64_t)B * T}, sO[1] = {(uint64_t)H * HS * 4};
+    const uint32_t bO[2] = {32, 128};
+    CUtensorMap oh = encode_f32_map(2, o_hi, dO, sO, bO, CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap ol = encode_f32_map(2, o_lo, dO, sO, bO, CU_TENSOR_MAP_SWIZZLE_128B);
+    k_attn_fwd_rs<HS><<<grid, kAttnThreads, RF::kSmem, stream()>>>(qh, ql, vh, vl, ph, pl, oh, ol, args);
     count_launch();
-    after_launch("k_attn_fwd_ps");
+    after_launch("k_attn_fwd_rs");
     return;
   }
   static bool attr = false;
