@@ -115,7 +115,7 @@ __global__ void k_softmax_warp(RowSrc x, float* __restrict__ y, size_t rows, int
 // then across the row's lanes by a fixed xor tree; p = e * (1 / sum).  A
 // deferred x * s + m reads through RowSrc with the eager roundings, and plain
 // and deferred rows take this same kernel, so they give the same bits.
-template <int LPR>
+template <int LPR, bool CAUSAL>
 __global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restrict__ y, uint32_t rows, int len) {
   constexpr int PER4 = 8, RPW = 32 / LPR;
   const int lane = threadIdx.x & 31, sub = lane % LPR;
@@ -129,13 +129,13 @@ __global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restric
     const float4* xr = reinterpret_cast<const float4*>(x.x + (size_t)r * len);
     const float4* ar = x.add ? reinterpret_cast<const float4*>(x.add + (size_t)(r % (uint32_t)x.add_rows) * len) : nullptr;
     // chunks wholly past the diagonal of a causal mask: exp gives exactly 0 there
-    const uint32_t last = x.causal_T ? r % x.causal_T : 0xffffffffu;
+    const uint32_t last = CAUSAL ? r % x.causal_T : 0xffffffffu;
     float4 v[PER4];
     float m = -INFINITY;
 #pragma unroll
     for (int k = 0; k < PER4; ++k) {
       const int c = sub + LPR * k;
-      if (live && c < n4 && (uint32_t)(4 * c) <= last) {
+      if (live && c < n4 && (!CAUSAL || (uint32_t)(4 * c) <= last)) {
         float4 t = xr[c];
         if (x.scale) { t.x = __fmul_rn(t.x, sc); t.y = __fmul_rn(t.y, sc); t.z = __fmul_rn(t.z, sc); t.w = __fmul_rn(t.w, sc); }
         if (ar) {
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restric
 #pragma unroll
     for (int k = 0; k < PER4; ++k) {
       const int c = sub + LPR * k;
-      if (live && c < n4 && (uint32_t)(4 * c) <= last) {
+      if (live && c < n4 && (!CAUSAL || (uint32_t)(4 * c) <= last)) {
         v[k].x = expf(v[k].x - m); v[k].y = expf(v[k].y - m); v[k].z = expf(v[k].z - m); v[k].w = expf(v[k].w - m);
         sum += v[k].x; sum += v[k].y; sum += v[k].z; sum += v[k].w;
       }
@@ -167,8 +167,9 @@ __global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restric
     for (int k = 0; k < PER4; ++k) {
       const int c = sub + LPR * k;
       if (live && c < n4)
-        yr[c] = (uint32_t)(4 * c) <= last ? make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv)
-                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        yr[c] = !CAUSAL || (uint32_t)(4 * c) <= last
+                    ? make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv)
+                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
   }
 }
@@ -991,10 +992,19 @@ void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t 
     auto go = [&](auto kern, int rpw) {
       kern<<<resident_blocks(kern, (outer + 8 * rpw - 1) / (8 * rpw)), 256, 0, stream()>>>(src, y, rows, len);
     };
-    if (axis_sz <= 128) go(k_softmax_rows<4>, 8);
-    else if (axis_sz <= 256) go(k_softmax_rows<8>, 4);
-    else if (axis_sz <= 512) go(k_softmax_rows<16>, 2);
-    else go(k_softmax_rows<32>, 1);
+    // the causal variant skips the chunks past the diagonal; its results are
+    // those of the plain one (the skipped terms are exact zeros)
+    if (causal_T) {
+      if (axis_sz <= 128) go(k_softmax_rows<4, true>, 8);
+      else if (axis_sz <= 256) go(k_softmax_rows<8, true>, 4);
+      else if (axis_sz <= 512) go(k_softmax_rows<16, true>, 2);
+      else go(k_softmax_rows<32, true>, 1);
+    } else {
+      if (axis_sz <= 128) go(k_softmax_rows<4, false>, 8);
+      else if (axis_sz <= 256) go(k_softmax_rows<8, false>, 4);
+      else if (axis_sz <= 512) go(k_softmax_rows<16, false>, 2);
+      else go(k_softmax_rows<32, false>, 1);
+    }
     count_launch();
     after_launch("k_softmax_rows");
   } else if (inner == 1 && axis_sz <= 1024) {
