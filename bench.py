@@ -428,7 +428,8 @@ class Runner:
         f32_sus = 0.5 * (bf16_sus or bf16) / 3.0
         return {"bound": "tensor", "kernel": "k_gemm_tc (3xTF32 tcgen05)",
                 "achieved": round(algo, 2), "peak": round(f32_burst, 2), "unit": "TFLOP/s",
-                "frac": round(algo / f32_burst, 4), "frac_sustained": round(algo / f32_sus, 4),
+                "frac": round(algo / f32_burst, 4), "frac_burst": round(algo / f32_burst, 4),
+                "frac_sustained": round(algo / f32_sus, 4),
                 "peak_sustained": round(f32_sus, 2),
                 "traffic": traffic_from_profiles("k_gemm_tc", workload, mode),
                 "algorithmic_bytes_per_launch": round(by_k / cnt),

@@ -564,6 +564,76 @@ __global__ void k_xent_fwd_warp(const float* __restrict__ logits, const void* __
   }
 }
 
+// Short rows (V <= 12 * LPR): LPR lanes per row, 32 / LPR rows per warp at
+// once (k_xent_fwd_warp keeps one row per warp and leaves most of each row's
+// latency exposed).  Lane j of a row holds elements j, j + LPR, ...; max, sum
+// and the target's probability combine across the row's lanes by a fixed xor
+// tree; each row group's first lane adds its rows' -log p in row order, and a
+// block's partial is its warps' group sums in a fixed order.
+template <int LPR>
+__global__ void k_xent_fwd_rows(const float* __restrict__ logits, const void* __restrict__ tgt,
+                                int tdt, float* __restrict__ probs, float* __restrict__ part,
+                                size_t rows, int V, int32_t* err) {
+  constexpr int PER = 12, RPW = 32 / LPR;
+  __shared__ float wpart[32];
+  const int lane = threadIdx.x & 31, sub = lane % LPR, grp = lane / LPR;
+  const size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+  const size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+  float wacc = 0.0f;
+  for (size_t base = warp * RPW; base < rows; base += nw * RPW) {
+    const size_t r = base + (size_t)grp;
+    const bool live = r < rows;
+    const float* xr = logits + r * (size_t)V;
+    const int64_t t = live ? load_index(tgt, tdt, r) : 0;   // issued with the row's loads
+    float v[PER];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = sub + LPR * k;
+      v[k] = live && i < V ? xr[i] : -INFINITY;
+      m = fmaxf(m, v[k]);
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = sub + LPR * k;
+      v[k] = live && i < V ? expf(v[k] - m) : 0.0f;
+      s += v[k];
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    float pt = 0.0f;
+    float* pr = probs + r * (size_t)V;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = sub + LPR * k;
+      if (live && i < V) {
+        const float pv = v[k] / s;
+        pr[i] = pv;
+        if (i == t) pt = pv;
+      }
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) pt += __shfl_xor_sync(0xffffffffu, pt, o);
+    if (sub == 0 && live) {
+      if (t < 0 || t >= V) atomicExch(err, 3);
+      else wacc += -logf(pt);
+    }
+  }
+  float w = 0.0f;
+#pragma unroll
+  for (int g = 0; g < RPW; ++g) w += __shfl_sync(0xffffffffu, wacc, g * LPR);
+  if (lane == 0) wpart[threadIdx.x >> 5] = w;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) b += wpart[i];
+    part[blockIdx.x] = b;
+  }
+}
+
 __global__ void k_xent_fwd_block(const float* __restrict__ logits, const void* __restrict__ tgt,
                                  int tdt, float* __restrict__ probs, float* __restrict__ part,
                                  size_t rows, size_t V, int32_t* err) {
@@ -1091,9 +1161,19 @@ void xent_fwd(const float* logits, const void* tgt, int tdt, float* probs, float
     scalar_op_imm(kSFill, nullptr, NAN, loss, 1);
     return;
   }
-  const unsigned blocks = v <= 1024 ? grid_for(n * 32, 256) : row_blocks(n);
+  const int lpr = v <= 96 ? 8 : v <= 192 ? 16 : 0;   // lanes per row of k_xent_fwd_rows
+  const unsigned blocks = lpr ? grid_for((n + 32 / lpr - 1) / (32 / lpr) * 32, 256)
+                              : v <= 1024 ? grid_for(n * 32, 256) : row_blocks(n);
   float* part = (float*)scratch_alloc(blocks * sizeof(float));
-  if (v <= 1024) {
+  if (lpr == 8) {
+    k_xent_fwd_rows<8><<<blocks, 256, 0, stream()>>>(logits, tgt, tdt, probs, part, n, (int)v, device_error_word());
+    count_launch();
+    after_launch("k_xent_fwd_rows");
+  } else if (lpr == 16) {
+    k_xent_fwd_rows<16><<<blocks, 256, 0, stream()>>>(logits, tgt, tdt, probs, part, n, (int)v, device_error_word());
+    count_launch();
+    after_launch("k_xent_fwd_rows");
+  } else if (v <= 1024) {
     LAUNCH_ROWS_WARP(k_xent_fwd_warp, v, n, logits, tgt, tdt, probs, part, n, (int)v,
                      device_error_word());
   } else {
