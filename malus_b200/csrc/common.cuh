@@ -199,9 +199,17 @@ void reduce_axis_sum_product(const float* x, const float* x2, float* out, size_t
 // (-1e9 above the diagonal), so in row r the elements past r % causal_T give
 // exactly 0 and need not be read (the same bits as reading them, for scores
 // below ~1e8 in magnitude).
+// p_hi / p_lo: with causal_T, also the result's tf32 planes (row pitch
+// axis_sz) up to each 128-row tile's diagonal block; only the row kernel
+// (softmax_rows_path) writes them.
 void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner,
                  const float* scale = nullptr, const float* addend = nullptr, size_t add_rows = 1,
-                 int causal_T = 0);
+                 int causal_T = 0, float* p_hi = nullptr, float* p_lo = nullptr);
+bool softmax_rows_path(const float* x, const float* y, const float* addend, size_t outer, size_t axis_sz,
+                       size_t inner);
+// GELU (g null) or its VJP (dout g) over n elements, also writing the result's
+// tf32 planes hi / lo (n % 4 == 0, 16-byte-aligned arrays)
+void gelu_planes(const float* x, const float* g, float* out, float* hi, float* lo, size_t n);
 // causal_T > 0: s is zero past the diagonal of [causal_T, causal_T] blocks, so
 // dx is zero there and those elements of s and dout are not read (the same
 // values; a zero may differ in sign)
@@ -274,6 +282,21 @@ struct GemmArgs {
 // storage is freed.  MALUS_PLANE_CACHE=0 disables it.
 void plane_cache_clear();
 void plane_cache_drop(uint64_t storage_id);
+// Planes for an operand that the kernel producing it writes as it stores the
+// f32 values (hi = tf32_rn(x), lo = tf32_rn(x - hi), the split's own
+// expressions): registers a cache entry for `o` (a plain row-major stack, no
+// deferred scale) and returns its memory (hi, then lo after nz*rows*cols
+// floats, row pitch = cols), or null when the cache is off, the layout is not
+// plain, or an entry exists.  causal_T > 0: only the part a causally clipped
+// GEMM reads need be written, and only such GEMMs use the entry.
+float* plane_cache_prime(const GemmOperand& o, int64_t causal_T);
+// x rounded to tf32 (round to nearest, ties away from zero), as the operand
+// split does for the hi plane
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
 void gemm(const GemmArgs& g);
 
 // Low-level tcgen05 GEMM on pre-split tf32 planes (hi/lo), for callers that

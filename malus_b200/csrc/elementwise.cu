@@ -185,6 +185,24 @@ __global__ void k_unary(const float* __restrict__ a, float* __restrict__ out, si
   }
 }
 
+// The same, also writing the result's tf32 planes (hi, lo; the operand
+// split's expressions) for a GEMM that reads it next; 16-byte-aligned arrays
+// of a multiple of 4 elements.
+template <int OP>
+__global__ void k_unary_planes(const float* __restrict__ a, float* __restrict__ out, float* __restrict__ hi,
+                               float* __restrict__ lo, size_t n4) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 x = reinterpret_cast<const float4*>(a)[i];
+    const float4 y = make_float4(uop<OP>(x.x, 0.f), uop<OP>(x.y, 0.f), uop<OP>(x.z, 0.f), uop<OP>(x.w, 0.f));
+    const float4 h = make_float4(tf32_round(y.x), tf32_round(y.y), tf32_round(y.z), tf32_round(y.w));
+    reinterpret_cast<float4*>(out)[i] = y;
+    reinterpret_cast<float4*>(hi)[i] = h;
+    reinterpret_cast<float4*>(lo)[i] =
+        make_float4(tf32_round(y.x - h.x), tf32_round(y.y - h.y), tf32_round(y.z - h.z), tf32_round(y.w - h.w));
+  }
+}
+
 // ---- unary VJPs: out = f(x or y, dout) ----
 template <int OP>
 __device__ __forceinline__ float ubwd(float x, float g) {
@@ -401,6 +419,42 @@ void scalar_op_imm(int op, const float* a, float s, float* out, size_t n) {
 
 void fill_from_dev_scalar(float* out, const float* s_dev, size_t n) {
   scalar_op_dev(kSFill, nullptr, s_dev, out, n);
+}
+
+template <int OP>
+__global__ void k_unary_bwd_planes(const float* __restrict__ x, const float* __restrict__ g,
+                                   float* __restrict__ out, float* __restrict__ hi, float* __restrict__ lo,
+                                   size_t n4) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 xv = reinterpret_cast<const float4*>(x)[i];
+    const float4 gv = reinterpret_cast<const float4*>(g)[i];
+    const float4 y = make_float4(ubwd<OP>(xv.x, gv.x), ubwd<OP>(xv.y, gv.y), ubwd<OP>(xv.z, gv.z),
+                                 ubwd<OP>(xv.w, gv.w));
+    const float4 h = make_float4(tf32_round(y.x), tf32_round(y.y), tf32_round(y.z), tf32_round(y.w));
+    reinterpret_cast<float4*>(out)[i] = y;
+    reinterpret_cast<float4*>(hi)[i] = h;
+    reinterpret_cast<float4*>(lo)[i] =
+        make_float4(tf32_round(y.x - h.x), tf32_round(y.y - h.y), tf32_round(y.z - h.z), tf32_round(y.w - h.w));
+  }
+}
+
+// GELU and its VJP with the result's tf32 planes (see k_unary_planes); n % 4
+// == 0 and every array 16-byte aligned.
+void gelu_planes(const float* x, const float* g, float* out, float* hi, float* lo, size_t n) {
+  if (!n) return;
+  if (n % 4 || !aligned16(x) || (g && !aligned16(g)) || !aligned16(out) || !aligned16(hi) || !aligned16(lo))
+    panic("gelu_planes: needs 16-byte-aligned arrays of a multiple of 4 elements");
+  const size_t n4 = n / 4;
+  if (g) {
+    k_unary_bwd_planes<kGeluBwd><<<grid_for(n4, kThreads), kThreads, 0, stream()>>>(x, g, out, hi, lo, n4);
+    count_launch();
+    after_launch("k_unary_bwd_planes");
+  } else {
+    k_unary_planes<kGelu><<<grid_for(n4, kThreads), kThreads, 0, stream()>>>(x, out, hi, lo, n4);
+    count_launch();
+    after_launch("k_unary_planes");
+  }
 }
 
 void unary_op(int op, const float* a, float* out, size_t n, float p) {

@@ -1585,6 +1585,20 @@ void plane_cache_clear() {
   for (float* m : mem) scratch_free(m);
 }
 
+float* plane_cache_prime(const GemmOperand& o, int64_t causal_T) {
+  if (!plane_cache_on() || o.key == 0 || o.scale_dev || o.colscale_dev || o.cols % 4 != 0) return nullptr;
+  const bool plain = o.c.div == 0 && o.c.lo == 1 && o.r.div == 0 && o.r.lo == o.cols &&
+                     (o.nz == 1 || (o.z.div == 0 && o.z.lo == o.rows * o.cols));
+  if (!plain) return nullptr;
+  std::lock_guard<std::mutex> lk(g_pc_mu);
+  if (pc_find(o, causal_T)) return nullptr;
+  const int64_t n = o.nz * o.rows * o.cols;
+  float* mem = (float*)scratch_alloc((size_t)(2 * n) * sizeof(float) + 256);
+  g_pc[o.key].push_back(PlaneEntry{o.nz, o.rows, o.cols, o.z, o.r, o.c, nullptr, nullptr, mem, o.cols, false,
+                                   causal_T});
+  return mem;
+}
+
 void plane_cache_drop(uint64_t sid) {
   std::vector<float*> mem;
   {

@@ -255,6 +255,17 @@ GemmOperand operand_of(int64_t h, size_t nz, size_t rows, size_t cols) {
   return o;
 }
 
+// tf32 planes of `out` ([rows, C], C its last dim) primed in the GEMM operand
+// cache, for a result that a GEMM reads next (the MLP activation and its VJP);
+// null when it is small, 1-D, or not 16-byte friendly.
+float* prime_row_planes(int64_t out, const float* src, const float* src2) {
+  const TensorBuffer* t = tb(out);
+  if (t->len < kLazyMin || t->ndim < 2 || t->len % 4) return nullptr;
+  const size_t C = t->shape[t->ndim - 1];
+  if (C % 4 || ((uintptr_t)src | (uintptr_t)src2 | (uintptr_t)fptr(out)) & 15) return nullptr;
+  return plane_cache_prime(operand_of(out, 1, t->len / C, C), 0);
+}
+
 void check_f32(int64_t h, const char* what) {
   if (tb(h)->dtype != MALUS_F32) panic("%s expects an f32 tensor, got dtype %d", what, tb(h)->dtype);
 }
@@ -343,9 +354,18 @@ int64_t __softmax_fwd(int64_t x, int64_t axis) {
     const TensorBuffer* m = z->addend ? tb(z->addend) : nullptr;
     const bool causal = m && m->causal_mask && m->ndim == 2 && m->shape[0] == asz && m->shape[1] == asz &&
                         s.ndim >= 2 && s.d[s.ndim - 2] == asz;
-    softmax_fwd(fptr(z->src), fptr(out), outer, asz, inner, z->scale ? fptr(z->scale) : nullptr,
-                z->addend ? fptr(z->addend) : nullptr, z->addend ? tb(z->addend)->len / asz : 1,
-                causal ? (int)asz : 0);
+    const float* src = fptr(z->src);
+    const float* add = z->addend ? fptr(z->addend) : nullptr;
+    // the probabilities feed P V (and P^T dO in the backward), which read
+    // them as tf32 planes: the kernel writes those as it goes, for the part
+    // the causally clipped GEMMs read, instead of a later split re-reading P
+    float* planes = nullptr;
+    if (causal && asz % 128 == 0 && tb(out)->len >= kLazyMin &&
+        softmax_rows_path(src, fptr(out), add, outer, asz, inner))
+      planes = plane_cache_prime(operand_of(out, outer / asz, asz, asz), (int64_t)asz);
+    softmax_fwd(src, fptr(out), outer, asz, inner, z->scale ? fptr(z->scale) : nullptr, add,
+                z->addend ? tb(z->addend)->len / asz : 1, causal ? (int)asz : 0, planes,
+                planes ? planes + tb(out)->len : nullptr);
     tb(out)->causal_zero = causal;
     return out;
   }
@@ -394,7 +414,9 @@ int64_t __embedding_fwd(int64_t weight, int64_t indices) {
 
 int64_t __gelu_fwd(int64_t x) {
   int64_t out = alloc_like(x);
-  unary_op(kGelu, fptr(x), fptr(out), tb(x)->len);
+  const float* a = fptr(x);
+  if (float* pl = prime_row_planes(out, a, a)) gelu_planes(a, nullptr, fptr(out), pl, pl + tb(out)->len, tb(out)->len);
+  else unary_op(kGelu, a, fptr(out), tb(x)->len);
   return out;
 }
 
@@ -521,8 +543,16 @@ UBWD(__relu_bwd, kReluBwd)
 UBWD(__tanh_bwd, kTanhBwd)
 UBWD(__sqrt_bwd, kSqrtBwd)
 UBWD(__abs_bwd, kAbsBwd)
-UBWD(__gelu_bwd, kGeluBwd)
 #undef UBWD
+
+int64_t __gelu_bwd(int64_t x, int64_t dout) {
+  int64_t out = alloc_like(x);
+  const float* a = fptr(x);
+  const float* g = fptr(dout);
+  if (float* pl = prime_row_planes(out, a, g)) gelu_planes(a, g, fptr(out), pl, pl + tb(out)->len, tb(out)->len);
+  else unary_bwd(kGeluBwd, a, g, fptr(out), tb(x)->len);
+  return out;
+}
 
 int64_t __sum_bwd(int64_t x, int64_t dout) {
   int64_t out = alloc_like(x);

@@ -115,8 +115,13 @@ __global__ void k_softmax_warp(RowSrc x, float* __restrict__ y, size_t rows, int
 // then across the row's lanes by a fixed xor tree; p = e * (1 / sum).  A
 // deferred x * s + m reads through RowSrc with the eager roundings, and plain
 // and deferred rows take this same kernel, so they give the same bits.
+// With CAUSAL and phi (the result's tf32 planes, registered in the operand
+// cache for the P V product that follows), each row also writes hi / lo of
+// its values up to the end of its 128-row tile's diagonal block, the part that
+// the causally clipped GEMMs read.
 template <int LPR, bool CAUSAL>
-__global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restrict__ y, uint32_t rows, int len) {
+__global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restrict__ y, uint32_t rows, int len,
+                                                      float* __restrict__ phi, float* __restrict__ plo) {
   constexpr int PER4 = 8, RPW = 32 / LPR;
   const int lane = threadIdx.x & 31, sub = lane % LPR;
   const uint32_t gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -166,10 +171,19 @@ __global__ void __launch_bounds__(256) k_softmax_rows(RowSrc x, float* __restric
 #pragma unroll
     for (int k = 0; k < PER4; ++k) {
       const int c = sub + LPR * k;
-      if (live && c < n4)
-        yr[c] = !CAUSAL || (uint32_t)(4 * c) <= last
-                    ? make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv)
-                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (live && c < n4) {
+        const float4 pv = !CAUSAL || (uint32_t)(4 * c) <= last
+                              ? make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv)
+                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        yr[c] = pv;
+        if (CAUSAL && phi && (uint32_t)(4 * c) < ((last >> 7) + 1) * 128) {
+          const float4 h = make_float4(tf32_round(pv.x), tf32_round(pv.y), tf32_round(pv.z), tf32_round(pv.w));
+          const size_t at = (size_t)r * (len >> 2) + c;
+          reinterpret_cast<float4*>(phi)[at] = h;
+          reinterpret_cast<float4*>(plo)[at] = make_float4(tf32_round(pv.x - h.x), tf32_round(pv.y - h.y),
+                                                           tf32_round(pv.z - h.z), tf32_round(pv.w - h.w));
+        }
+      }
     }
   }
 }
@@ -1045,9 +1059,18 @@ static unsigned row_blocks(size_t rows) {
   return (unsigned)std::max<size_t>(1, std::min<size_t>(rows, (size_t)kNumSMs * 8));
 }
 
+bool softmax_rows_path(const float* x, const float* y, const float* addend, size_t outer, size_t axis_sz,
+                       size_t inner) {
+  const bool vec4 = axis_sz % 4 == 0 && ((((uintptr_t)x) | ((uintptr_t)y) | ((uintptr_t)addend)) & 15) == 0;
+  return inner == 1 && axis_sz <= 1024 && vec4 && axis_sz >= 128 && outer < ((size_t)1 << 31);
+}
+
 void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t inner,
-                 const float* scale, const float* addend, size_t add_rows, int causal_T) {
+                 const float* scale, const float* addend, size_t add_rows, int causal_T, float* p_hi,
+                 float* p_lo) {
   if (!outer || !axis_sz || !inner) return;
+  if (p_hi && (!causal_T || !p_lo || !softmax_rows_path(x, y, addend, outer, axis_sz, inner)))
+    panic("softmax_fwd: planes are written only by the row kernel over a causal mask");
   if ((scale || addend) && inner != 1) panic("softmax_fwd: a deferred input needs the last axis");
   if (causal_T && (!addend || inner != 1 || (size_t)causal_T != axis_sz))
     panic("softmax_fwd: causal skipping needs the [T, T] mask as the addend");
@@ -1055,12 +1078,12 @@ void softmax_fwd(const float* x, float* y, size_t outer, size_t axis_sz, size_t 
   // 16-byte rows whenever the row and every source are 16-byte aligned: a
   // deferred x * s + m must take the same kernel as its materialised value
   // (the row sum's grouping follows the kernel), so both give the same bits
-  const bool vec4 = axis_sz % 4 == 0 && ((((uintptr_t)x) | ((uintptr_t)y) | ((uintptr_t)addend)) & 15) == 0;
-  if (inner == 1 && axis_sz <= 1024 && vec4 && axis_sz >= 128 && outer < ((size_t)1 << 31)) {
+  if (softmax_rows_path(x, y, addend, outer, axis_sz, inner)) {
     const uint32_t rows = (uint32_t)outer;
     const int len = (int)axis_sz;
     auto go = [&](auto kern, int rpw) {
-      kern<<<resident_blocks(kern, (outer + 8 * rpw - 1) / (8 * rpw)), 256, 0, stream()>>>(src, y, rows, len);
+      kern<<<resident_blocks(kern, (outer + 8 * rpw - 1) / (8 * rpw)), 256, 0, stream()>>>(src, y, rows, len,
+                                                                                          p_hi, p_lo);
     };
     // the causal variant skips the chunks past the diagonal; its results are
     // those of the plain one (the skipped terms are exact zeros)

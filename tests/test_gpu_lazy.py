@@ -254,3 +254,30 @@ def test_causal_zero_gemms_equal_full(M, rt, rng):
                                   M.Tensor(rt.__matmul_bwd_a(qq.h, kt, plain.h)).numpy())
     for h in (mask, sc, ms, p, ds, dsc, kt):
         rt.tensor_release(h)
+
+
+def test_gelu_results_carry_their_planes(M, rt, rng):
+    """GELU and its VJP write the tf32 planes of a large result as they store
+    it, for the GEMMs that read it next (the MLP's down product and both VJPs
+    of the up product).  Those GEMMs equal the same GEMMs over copies of the
+    values, whose planes the operand split makes."""
+    m_, c4, c_ = 2048, 1536, 384
+    x = rng.standard_normal((m_, c4)).astype(np.float32)
+    w2 = rng.standard_normal((c4, c_)).astype(np.float32)
+    g2 = rng.standard_normal((m_, c_)).astype(np.float32)
+    dh_in = rng.standard_normal((m_, c4)).astype(np.float32)
+    xn = rng.standard_normal((m_, c_)).astype(np.float32)
+    w1 = rng.standard_normal((c_, c4)).astype(np.float32)
+    tx, tw2, tg2, tdh, txn, tw1 = (T(M, a) for a in (x, w2, g2, dh_in, xn, w1))
+    h = rt.__gelu_fwd(tx.h)
+    d = rt.__gelu_bwd(tx.h, tdh.h)
+    got = [M.Tensor(rt.tensor_matmul(h, tw2.h)).numpy(), M.Tensor(rt.__matmul_bwd_b(h, tw2.h, tg2.h)).numpy(),
+           M.Tensor(rt.__matmul_bwd_a(txn.h, tw1.h, d)).numpy(), M.Tensor(rt.__matmul_bwd_b(txn.h, tw1.h, d)).numpy()]
+    hc, dc = T(M, np_of(M, h)), T(M, np_of(M, d))
+    ref = [M.Tensor(rt.tensor_matmul(hc.h, tw2.h)).numpy(), M.Tensor(rt.__matmul_bwd_b(hc.h, tw2.h, tg2.h)).numpy(),
+           M.Tensor(rt.__matmul_bwd_a(txn.h, tw1.h, dc.h)).numpy(),
+           M.Tensor(rt.__matmul_bwd_b(txn.h, tw1.h, dc.h)).numpy()]
+    for a, b in zip(got, ref):
+        np.testing.assert_array_equal(a, b)
+    for hh in (h, d):
+        rt.tensor_release(hh)
