@@ -767,15 +767,16 @@ __global__ void k_splitk_reduce(const TcKernelParams kp) {
     const size_t sstep = (size_t)(tsz / 4);
     float4 v = src[0];
     int sl = 1;
-    // four slices' loads in flight at a time, added in slice order (the same
+    // eight slices' loads in flight at a time, added in slice order (the same
     // sums, bit for bit, as one slice at a time)
-    for (; sl + 4 <= kp.splits; sl += 4) {
-      const float4 t0 = src[(size_t)sl * sstep], t1 = src[(size_t)(sl + 1) * sstep];
-      const float4 t2 = src[(size_t)(sl + 2) * sstep], t3 = src[(size_t)(sl + 3) * sstep];
-      v.x += t0.x; v.y += t0.y; v.z += t0.z; v.w += t0.w;
-      v.x += t1.x; v.y += t1.y; v.z += t1.z; v.w += t1.w;
-      v.x += t2.x; v.y += t2.y; v.z += t2.z; v.w += t2.w;
-      v.x += t3.x; v.y += t3.y; v.z += t3.z; v.w += t3.w;
+    for (; sl + 8 <= kp.splits; sl += 8) {
+      float4 t[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] = src[(size_t)(sl + j) * sstep];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v.x += t[j].x; v.y += t[j].y; v.z += t[j].z; v.w += t[j].w;
+      }
     }
     for (; sl < kp.splits; ++sl) {
       const float4 t = src[(size_t)sl * sstep];
@@ -1537,7 +1538,12 @@ void gemm_tc(const GemmArgs& g) {
   bool at = g.a_trans, bt = g.b_trans;
   const int causal = (g.a_zero == kCausalALower || g.a_zero == kCausalAUpper) && g.M == g.K ? g.a_zero : kCausalNone;
   int pid = prof_begin(1, 0.0, 12.0 * (double)(g.A.nz * g.A.rows * g.A.cols + g.B.nz * g.B.rows * g.B.cols));
-  const Planes pa = operand_planes(g.A, &at, causal != kCausalNone ? g.M : 0);
+  // A partial split serves clipped consumers only.  The probabilities P are
+  // read only so (their planes come from the softmax itself); the scaled
+  // score gradient dS * s is also the B operand of d(K^T) = Q^T (dS * s),
+  // which reads it whole, so it is split whole once for both.
+  const bool partial = causal != kCausalNone && !g.A.scale_dev;
+  const Planes pa = operand_planes(g.A, &at, partial ? g.M : 0);
   const Planes pb = operand_planes(g.B, &bt);
   prof_end(pid);
   TcProblem pr{};

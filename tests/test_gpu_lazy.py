@@ -252,6 +252,11 @@ def test_causal_zero_gemms_equal_full(M, rt, rng):
     kt = rt.tensor_permute(kk.h, (C.c_size_t * 3)(0, 2, 1), 3)
     np.testing.assert_array_equal(M.Tensor(rt.__matmul_bwd_a(qq.h, kt, dsc)).numpy(),
                                   M.Tensor(rt.__matmul_bwd_a(qq.h, kt, plain.h)).numpy())
+    # dS itself (tagged, unscaled) as the A of a clipped product: its planes are
+    # split only where the 128-row tiles read them
+    ds_plain = T(M, dsn)
+    np.testing.assert_array_equal(M.Tensor(rt.tensor_matmul(ds, kk.h)).numpy(),
+                                  M.Tensor(rt.tensor_matmul(ds_plain.h, kk.h)).numpy())
     for h in (mask, sc, ms, p, ds, dsc, kt):
         rt.tensor_release(h)
 
