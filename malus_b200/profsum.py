@@ -30,12 +30,13 @@ _BYTES = {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "B": 1.0, "KB":
 
 def short_name(name: str) -> str:
     """Kernel name without its argument list, return type and namespaces."""
-    n = re.sub(r"\(.*$", "", name)
-    n = re.sub(r"^void ", "", n)
-    n = re.sub(r"malus::", "", n)
     # ncu writes anonymous namespaces as "(anonymous namespace)::", "<unnamed>::"
-    # or, truncated, "unnamed>::"
-    n = re.sub(r"^(\(anonymous namespace\)|<?unnamed>)::", "", n.strip())
+    # or, truncated, "unnamed>::"; drop them before the argument list, whose
+    # "(" would otherwise match the namespace's
+    n = re.sub(r"\(anonymous namespace\)::|<?unnamed>::", "", name)
+    n = re.sub(r"\(.*$", "", n)
+    n = re.sub(r"^void ", "", n.strip())
+    n = re.sub(r"malus::", "", n)
     return n.strip()
 
 
