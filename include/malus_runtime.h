@@ -315,6 +315,31 @@ int32_t malus_attn_fwd(const float* qkv_hi, const float* qkv_lo, int32_t B, int3
  * give the same bits.  Returns the previous setting.  Environment:
  * MALUS_ATTN_RS=0 starts with 0.  New in this build. */
 int32_t malus_attn_set_resident(int32_t on);
+
+/* ---- SafeTensors files (malus's interop spec, docs/spec/08-interop.md:
+ * `load(path)` / `save(tensors, path)` of named tensor sets).  An 8-byte
+ * little-endian header length, a JSON header mapping each name to its dtype
+ * ("F32", "I32", "I64"), shape and [begin, end) byte offsets, then the data.
+ * Negative codes: -1 I/O, -2 header length, -3 JSON, -4 a name or field
+ * (empty, duplicate, "__metadata__", unsupported dtype, rank above 8), -5
+ * offsets (outside the file, not matching the shape, overlapping), -6 no such
+ * name.  New in this build. */
+/* Write n tensors held in host memory (dtype codes 0, 5, 6). */
+int32_t malus_safetensors_write_host(const char* path, size_t n, const char* const* names, const int32_t* dtypes,
+                                     const size_t* const* shapes, const size_t* ndims, const void* const* data);
+/* The names in header order, newline-separated (NUL-terminated, truncated at
+ * cap); returns the length the whole list needs, or a negative code. */
+int32_t malus_safetensors_names(const char* path, char* buf, int32_t cap);
+/* One tensor into host memory: dtype, rank, shape (up to 8 dims) always, its
+ * bytes when cap holds them; returns the byte count or a negative code. */
+int64_t malus_safetensors_read_host(const char* path, const char* name, int32_t* dtype, size_t* shape,
+                                    size_t* ndim, void* data, size_t cap);
+/* Save device tensors under the given names (views and deferred results are
+ * materialised); returns 0 or a negative code. */
+int32_t malus_save_safetensors(const char* path, size_t n, const char* const* names, const int64_t* handles);
+/* Load one tensor onto the GPU as a new handle (refcount 1); 0 when the name
+ * is absent or the file invalid (the reason goes to stderr). */
+int64_t malus_load_safetensors(const char* path, const char* name);
 /* Fused causal attention backward (tcgen05, 3xTF32), the VJP of
  * malus_attn_fwd: from the q|k|v planes, the planes of dO (head-folded
  * [B][H][T][hs]) and of O (head-unfolded, as the forward wrote them) and the

@@ -185,6 +185,13 @@ SIGNATURES: dict[str, tuple] = {
     "malus_jit_compile_check": (i32, [C.c_char_p, C.c_char_p, sz]),
     "malus_attn_fwd": (i32, [vp, vp, i32, i32, i32, i32, f32, vp, vp, vp, vp, vp]),
     "malus_attn_set_resident": (i32, [i32]),
+    "malus_safetensors_write_host": (i32, [C.c_char_p, sz, C.POINTER(C.c_char_p), C.POINTER(i32),
+                                             C.POINTER(C.POINTER(sz)), C.POINTER(sz), C.POINTER(vp)]),
+    "malus_safetensors_names": (i32, [C.c_char_p, C.c_char_p, i32]),
+    "malus_safetensors_read_host": (i64, [C.c_char_p, C.c_char_p, C.POINTER(i32), C.POINTER(sz), C.POINTER(sz),
+                                          vp, sz]),
+    "malus_save_safetensors": (i32, [C.c_char_p, sz, C.POINTER(C.c_char_p), C.POINTER(i64)]),
+    "malus_load_safetensors": (i64, [C.c_char_p, C.c_char_p]),
     "malus_attn_bwd": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, vp, vp]),
     "malus_graph_begin": (i32, []),
     "malus_graph_end": (i64, []),
@@ -292,6 +299,42 @@ class Tensor:
             self.close()
         except Exception:
             pass
+
+
+def save_safetensors(path: str | os.PathLike, tensors: dict) -> None:
+    """Write named tensors (Tensor objects or raw handles) to a SafeTensors
+    file, as malus's interop spec's `save(tensors, path)`."""
+    lib = load()
+    names = list(tensors)
+    hs = [t.h if isinstance(t, Tensor) else int(t) for t in tensors.values()]
+    arr_n = (C.c_char_p * len(names))(*[n.encode() for n in names])
+    arr_h = (C.c_int64 * len(hs))(*hs)
+    rc = lib.malus_save_safetensors(os.fsencode(path), len(names), arr_n, arr_h)
+    if rc != 0:
+        raise OSError(f"malus_save_safetensors({path}) failed with code {rc}")
+
+
+def safetensors_names(path: str | os.PathLike) -> list[str]:
+    lib = load()
+    need = lib.malus_safetensors_names(os.fsencode(path), None, 0)
+    if need < 0:
+        raise ValueError(f"{path}: not a valid SafeTensors file (code {need})")
+    buf = C.create_string_buffer(need + 1)
+    lib.malus_safetensors_names(os.fsencode(path), buf, need + 1)
+    return [n for n in buf.value.decode().split("\n") if n]
+
+
+def load_safetensors(path: str | os.PathLike) -> dict:
+    """Every tensor of a SafeTensors file on the GPU, by name (the spec's
+    `load(path)`)."""
+    lib = load()
+    out = {}
+    for n in safetensors_names(path):
+        h = lib.malus_load_safetensors(os.fsencode(path), n.encode())
+        if not h:
+            raise ValueError(f"{path}: loading {n} failed")
+        out[n] = Tensor(h)
+    return out
 
 
 def tuple_fields(box: int) -> tuple[int, int]:
