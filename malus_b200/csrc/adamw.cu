@@ -55,8 +55,35 @@ __global__ void k_adamw(SegTable t, int nseg, int64_t total4, float lr, float b1
     while (s > 0 && q < t.start[s]) --s;
     const AdamSeg& sg = t.seg[s];
     int64_t e0 = (q - t.start[s]) * 4;
-    const bool vec = e0 + 4 <= sg.n &&
-                     (((uintptr_t)sg.p | (uintptr_t)sg.m | (uintptr_t)sg.v | (uintptr_t)sg.g) & 15) == 0;
+    const bool aligned = (((uintptr_t)sg.p | (uintptr_t)sg.m | (uintptr_t)sg.v | (uintptr_t)sg.g) & 15) == 0;
+    const bool vec = e0 + 4 <= sg.n && aligned;
+    // this thread's next chunk in the same segment: both chunks' loads are
+    // issued before either is computed (the same per-element arithmetic)
+    const int64_t q2 = q + step, e2 = e0 + 4 * step;
+    if (vec && q2 < total4 && (s + 1 >= nseg || q2 < t.start[s + 1]) && e2 + 4 <= sg.n) {
+      float4 pp = *reinterpret_cast<const float4*>(sg.p + e0), p2 = *reinterpret_cast<const float4*>(sg.p + e2);
+      float4 mm = *reinterpret_cast<const float4*>(sg.m + e0), m2 = *reinterpret_cast<const float4*>(sg.m + e2);
+      float4 vv = *reinterpret_cast<const float4*>(sg.v + e0), v2 = *reinterpret_cast<const float4*>(sg.v + e2);
+      const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 gg = sg.g ? *reinterpret_cast<const float4*>(sg.g + e0) : z4;
+      const float4 g2 = sg.g ? *reinterpret_cast<const float4*>(sg.g + e2) : z4;
+      adam_one(pp.x, gg.x, mm.x, vv.x, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(pp.y, gg.y, mm.y, vv.y, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(pp.z, gg.z, mm.z, vv.z, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(pp.w, gg.w, mm.w, vv.w, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(p2.x, g2.x, m2.x, v2.x, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(p2.y, g2.y, m2.y, v2.y, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(p2.z, g2.z, m2.z, v2.z, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      adam_one(p2.w, g2.w, m2.w, v2.w, lr, b1, b2, eps, wd, c1, c2, bc1, bc2, gs);
+      *reinterpret_cast<float4*>(sg.p + e0) = pp;
+      *reinterpret_cast<float4*>(sg.m + e0) = mm;
+      *reinterpret_cast<float4*>(sg.v + e0) = vv;
+      *reinterpret_cast<float4*>(sg.p + e2) = p2;
+      *reinterpret_cast<float4*>(sg.m + e2) = m2;
+      *reinterpret_cast<float4*>(sg.v + e2) = v2;
+      q = q2;   // the loop's increment then moves past both
+      continue;
+    }
     if (vec) {   // one 16-byte access per array (same per-element arithmetic)
       float4 pp = *reinterpret_cast<const float4*>(sg.p + e0);
       float4 mm = *reinterpret_cast<const float4*>(sg.m + e0);

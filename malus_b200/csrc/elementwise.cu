@@ -136,9 +136,12 @@ __global__ void k_scalar(const float* __restrict__ a, const float* __restrict__ 
     size_t n4 = n >> 2;
     float4* o4 = reinterpret_cast<float4*>(out);
     const float4* a4 = reinterpret_cast<const float4*>(a);
-    for (size_t i = tid; i < n4; i += stride) {
-      float4 x = OP == kSFill ? make_float4(0, 0, 0, 0) : a4[i];
+    for (size_t i = tid; i < n4; i += 2 * stride) {   // two chunks' loads in flight
+      const size_t i2 = i + stride;
+      const float4 x = OP == kSFill ? make_float4(0, 0, 0, 0) : a4[i];
+      const float4 x2 = OP == kSFill || i2 >= n4 ? x : a4[i2];
       o4[i] = make_float4(sop<OP>(x.x, s), sop<OP>(x.y, s), sop<OP>(x.z, s), sop<OP>(x.w, s));
+      if (i2 < n4) o4[i2] = make_float4(sop<OP>(x2.x, s), sop<OP>(x2.y, s), sop<OP>(x2.z, s), sop<OP>(x2.w, s));
     }
     for (size_t i = (n4 << 2) + tid; i < n; i += stride)
       out[i] = sop<OP>(OP == kSFill ? 0.f : a[i], s);
@@ -175,9 +178,13 @@ __global__ void k_unary(const float* __restrict__ a, float* __restrict__ out, si
     size_t n4 = n >> 2;
     const float4* a4 = reinterpret_cast<const float4*>(a);
     float4* o4 = reinterpret_cast<float4*>(out);
-    for (size_t i = tid; i < n4; i += stride) {
-      float4 x = a4[i];
+    // two chunks per iteration, both loads issued before either is computed
+    for (size_t i = tid; i < n4; i += 2 * stride) {
+      const size_t i2 = i + stride;
+      const float4 x = a4[i];
+      const float4 x2 = i2 < n4 ? a4[i2] : x;
       o4[i] = make_float4(uop<OP>(x.x, p), uop<OP>(x.y, p), uop<OP>(x.z, p), uop<OP>(x.w, p));
+      if (i2 < n4) o4[i2] = make_float4(uop<OP>(x2.x, p), uop<OP>(x2.y, p), uop<OP>(x2.z, p), uop<OP>(x2.w, p));
     }
     for (size_t i = (n4 << 2) + tid; i < n; i += stride) out[i] = uop<OP>(a[i], p);
   } else {
