@@ -87,6 +87,9 @@ struct TensorBuffer {
   // pointers handed out).
   bool causal_mask = false;
   bool causal_zero = false;
+  // made by tensor_matmul: an activation of such a product (the MLP's GELU)
+  // is read by the next GEMM, so its kernel writes the tf32 planes too
+  bool gemm_out = false;
 };
 
 inline TensorBuffer* tb(int64_t h) {

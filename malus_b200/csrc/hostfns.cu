@@ -304,6 +304,7 @@ int64_t tensor_matmul(int64_t ha, int64_t hb) {
           a.ndim, b.ndim);
   }
   int64_t out = alloc_shape(o);
+  tb(out)->gemm_out = true;
   g.C = fptr(out);
   g.ldc = g.N;
   g.strideC = g.batch > 1 ? (int64_t)g.M * g.N : 0;
@@ -415,7 +416,8 @@ int64_t __embedding_fwd(int64_t weight, int64_t indices) {
 int64_t __gelu_fwd(int64_t x) {
   int64_t out = alloc_like(x);
   const float* a = fptr(x);
-  if (float* pl = prime_row_planes(out, a, a)) gelu_planes(a, nullptr, fptr(out), pl, pl + tb(out)->len, tb(out)->len);
+  // the MLP's activation (GELU of a GEMM's output) feeds the down product
+  if (float* pl = tb(x)->gemm_out ? prime_row_planes(out, a, a) : nullptr) gelu_planes(a, nullptr, fptr(out), pl, pl + tb(out)->len, tb(out)->len);
   else unary_op(kGelu, a, fptr(out), tb(x)->len);
   return out;
 }
@@ -549,7 +551,8 @@ int64_t __gelu_bwd(int64_t x, int64_t dout) {
   int64_t out = alloc_like(x);
   const float* a = fptr(x);
   const float* g = fptr(dout);
-  if (float* pl = prime_row_planes(out, a, g)) gelu_planes(a, g, fptr(out), pl, pl + tb(out)->len, tb(out)->len);
+  // its VJP at a GEMM's output feeds both VJPs of that GEMM
+  if (float* pl = tb(x)->gemm_out ? prime_row_planes(out, a, g) : nullptr) gelu_planes(a, g, fptr(out), pl, pl + tb(out)->len, tb(out)->len);
   else unary_bwd(kGeluBwd, a, g, fptr(out), tb(x)->len);
   return out;
 }

@@ -262,18 +262,18 @@ def test_causal_zero_gemms_equal_full(M, rt, rng):
 
 
 def test_gelu_results_carry_their_planes(M, rt, rng):
-    """GELU and its VJP write the tf32 planes of a large result as they store
-    it, for the GEMMs that read it next (the MLP's down product and both VJPs
-    of the up product).  Those GEMMs equal the same GEMMs over copies of the
+    """GELU and its VJP at a GEMM's output (the MLP's pre-activation) write the
+    tf32 planes of their large results as they store them, for the GEMMs that
+    read them next (the MLP's down product and both VJPs of the up product).  Those GEMMs equal the same GEMMs over copies of the
     values, whose planes the operand split makes."""
     m_, c4, c_ = 2048, 1536, 384
-    x = rng.standard_normal((m_, c4)).astype(np.float32)
     w2 = rng.standard_normal((c4, c_)).astype(np.float32)
     g2 = rng.standard_normal((m_, c_)).astype(np.float32)
     dh_in = rng.standard_normal((m_, c4)).astype(np.float32)
     xn = rng.standard_normal((m_, c_)).astype(np.float32)
-    w1 = rng.standard_normal((c_, c4)).astype(np.float32)
-    tx, tw2, tg2, tdh, txn, tw1 = (T(M, a) for a in (x, w2, g2, dh_in, xn, w1))
+    w1 = (rng.standard_normal((c_, c4)) * 0.1).astype(np.float32)
+    tw2, tg2, tdh, txn, tw1 = (T(M, a) for a in (w2, g2, dh_in, xn, w1))
+    tx = M.Tensor(rt.tensor_matmul(txn.h, tw1.h))          # the pre-activation: a GEMM's output
     h = rt.__gelu_fwd(tx.h)
     d = rt.__gelu_bwd(tx.h, tdh.h)
     got = [M.Tensor(rt.tensor_matmul(h, tw2.h)).numpy(), M.Tensor(rt.__matmul_bwd_b(h, tw2.h, tg2.h)).numpy(),
