@@ -178,13 +178,20 @@ __global__ void k_unary(const float* __restrict__ a, float* __restrict__ out, si
     size_t n4 = n >> 2;
     const float4* a4 = reinterpret_cast<const float4*>(a);
     float4* o4 = reinterpret_cast<float4*>(out);
-    // two chunks per iteration, both loads issued before either is computed
-    for (size_t i = tid; i < n4; i += 2 * stride) {
-      const size_t i2 = i + stride;
-      const float4 x = a4[i];
-      const float4 x2 = i2 < n4 ? a4[i2] : x;
-      o4[i] = make_float4(uop<OP>(x.x, p), uop<OP>(x.y, p), uop<OP>(x.z, p), uop<OP>(x.w, p));
-      if (i2 < n4) o4[i2] = make_float4(uop<OP>(x2.x, p), uop<OP>(x2.y, p), uop<OP>(x2.z, p), uop<OP>(x2.w, p));
+    if (OP == kGelu) {   // compute-heavy: one chunk per iteration measured faster
+      for (size_t i = tid; i < n4; i += stride) {
+        const float4 x = a4[i];
+        o4[i] = make_float4(uop<OP>(x.x, p), uop<OP>(x.y, p), uop<OP>(x.z, p), uop<OP>(x.w, p));
+      }
+    } else {
+      // two chunks per iteration, both loads issued before either is computed
+      for (size_t i = tid; i < n4; i += 2 * stride) {
+        const size_t i2 = i + stride;
+        const float4 x = a4[i];
+        const float4 x2 = i2 < n4 ? a4[i2] : x;
+        o4[i] = make_float4(uop<OP>(x.x, p), uop<OP>(x.y, p), uop<OP>(x.z, p), uop<OP>(x.w, p));
+        if (i2 < n4) o4[i2] = make_float4(uop<OP>(x2.x, p), uop<OP>(x2.y, p), uop<OP>(x2.z, p), uop<OP>(x2.w, p));
+      }
     }
     for (size_t i = (n4 << 2) + tid; i < n; i += stride) out[i] = uop<OP>(a[i], p);
   } else {
