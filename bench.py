@@ -412,7 +412,10 @@ class Runner:
                 "payload_mb_per_step": round(by.value / steps / 1e6, 2),
                 "bus_gbs": round(bus, 1) if bus else None,
                 "profiled_step_ms": round(dt_prof_ms / steps, 4),
-                "note": "rank 0's profiled pass (eager, CUDA events on the collective stream and at the join)"}
+                "note": "rank 0's profiled pass (eager): allreduce_ms_per_step spans each all-reduce on the "
+                        "collective stream from its gradients being ready to its completion, overlapped with the "
+                        "backward (bus_gbs is payload over that span, so it reflects contention for SMs, not "
+                        "link bandwidth); exposed_ms_per_step is the main stream's wait at the join"}
 
     def _gemm_roofline(self, cnt, ms_k, fl_k, by_k, dt_prof_ms, steps, workload, mode):
         if not cnt:
